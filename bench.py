@@ -1,0 +1,355 @@
+"""Benchmark of the B200 render + train hot path (driver contract: one JSON line).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload train|sort]
+
+Workloads (BASELINE.json metric "train-step Mpix/s (fwd+bwd+Adam) and sort keys/s"):
+  train -- config C5 (6M Gaussians, SH3, 32 views of 1920x1080 split over the ranks,
+           gradients summed by an NCCL allreduce, sparse Adam on every rank); a step is
+           one full training step. Metric: Mpix/s = 32 * 1920 * 1080 / step time.
+  sort  -- config C2 (2^24 Zipf (uint64 key, uint32 value) pairs, 45 key bits); a step is
+           one stable sort per rank (independent per-GPU sorts, weak scaling).
+           Metric: sorted pairs/s over all ranks.
+
+Timing: W untimed steps, then K steps between barrier + synchronize, CUDA events on the
+launching stream, max over ranks. `value` has inputs resident in HBM; `e2e` goes through
+the public API with pinned host buffers and the host<->device copies inside the timed
+region. `roofline` is computed from the dominant kernel's average launch time, measured
+with the library's CUDA-event kernel timer (gs_timing_*) in a separate loop after the
+timed one. `cpu_baseline` times the reference's CPU implementation on this host.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+L2_BYTES = 126 * 1024 * 1024
+
+
+def measured_peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", str(self.gpu), "-lms", "200"], stdout=open(self.path, "w"),
+                stderr=subprocess.DEVNULL)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in rows if num(r[1]) is not None]
+        mx = [num(r[2]) for r in rows if num(r[2]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[5 + i]
+                          and "Not" not in r[5 + i]})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+# ---------------------------------------------------------------- distributed
+
+def dist_setup(args):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "b200":
+        torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        backend = "nccl" if args.impl == "b200" else "gloo"
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- sort workload
+
+SORT_N = 1 << 24
+SORT_KEY_BITS = 45
+
+
+def sort_algorithmic_bytes(n: int, key_bits: int) -> tuple[float, float]:
+    """(bytes per onesweep pass launch, bytes per sort) of this implementation's passes:
+    every pass reads 12 B/pair (key + value); all but the last write 12 B/pair, the last
+    writes 4 B/pair (values only); the histogram kernel reads 8 B/pair."""
+    npass = (key_bits + 7) // 8
+    pass_bytes = n * (npass * 12 + (npass - 1) * 12 + 4)
+    return pass_bytes / npass, pass_bytes + 8.0 * n
+
+
+def cpu_sort_baseline(keys, vals, budget_s: float = 15.0) -> dict:
+    """The reference's sort_and_bin (oracle/_ref) on this host's cores, else the C port."""
+    os.environ.setdefault("GSPLAT_TT_NUM_THREADS", str(os.cpu_count()))
+    from oracle import display as od
+    ref = od.reference_module()
+    n = keys.size
+    if ref is not None:
+        tiles = (keys >> np.uint64(32)).astype(np.int64)
+        depth = (keys & np.uint64(0xFFFFFFFF)).astype(np.uint32).view(np.float32)
+        dv = np.empty(n, np.float32)
+        dv[vals] = depth
+        gids = vals.astype(np.int64)
+        fn = lambda: ref.sort(gids, tiles, dv, 120, 68)  # noqa: E731
+        kind, cores = "reference", int(os.environ.get("GSPLAT_TT_NUM_THREADS", os.cpu_count()))
+    else:
+        fn = lambda: od.sort_pairs(keys, vals)  # noqa: E731
+        kind, cores = "port", 1
+    fn()
+    t0, iters = time.perf_counter(), 0
+    while True:
+        fn()
+        iters += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or iters >= 20:
+            break
+    return {"value": n * iters / el, "unit": "pairs/s", "cores": cores, "kind": kind,
+            "sample": f"{iters} full C2 sorts of {n} pairs"}
+
+
+def run_sort(args, rank, world, local) -> dict:
+    import torch
+    from gsplat_tt_b200 import scenes
+    from gsplat_tt_b200._lib import lib, check, timing_report
+    dev = torch.device("cuda", local)
+    keys, vals = scenes.c2_pairs(seed=rank)  # one independent C2 instance per rank
+    n = keys.size
+    kd = torch.from_numpy(keys.view(np.int64)).to(dev)
+    vd = torch.from_numpy(vals.view(np.int32)).to(dev)
+    vo = torch.empty_like(vd)
+    ws = torch.empty(lib.gs_sort_pairs_workspace_size(n, SORT_KEY_BITS), dtype=torch.uint8,
+                     device=dev)
+    st = torch.cuda.current_stream()
+
+    def step():
+        check(lib.gs_sort_pairs(kd.data_ptr(), vd.data_ptr(), n, SORT_KEY_BITS, None,
+                                vo.data_ptr(), ws.data_ptr(), ws.numel(), st.cuda_stream))
+
+    for _ in range(args.warmup):
+        step()
+    check(lib.gs_workspace_error(ws.data_ptr(), st.cuda_stream))
+    torch.cuda.synchronize()
+    # correctness guard on the benchmarked data: values are a permutation of 0..n-1, so
+    # key_by_value[sorted values] must be non-decreasing.
+    key_by_value = torch.empty_like(kd)
+    key_by_value[vd.long()] = kd
+    ks = key_by_value[vo.long()]
+    if not bool((ks[1:] >= ks[:-1]).all()):
+        raise RuntimeError("sort output is not sorted")
+    del key_by_value, ks
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    check(lib.gs_workspace_error(ws.data_ptr(), st.cuda_stream))
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    total_pairs = sum_over_ranks(float(n), world)
+    value = total_pairs / (ms / 1e3)
+
+    # e2e through the public API: pinned host in, sorted values back to the host.
+    kh = torch.from_numpy(keys.view(np.int64)).pin_memory()
+    vh = torch.from_numpy(vals.view(np.int32)).pin_memory()
+    oh = torch.empty(n, dtype=torch.int32).pin_memory()
+    for _ in range(2):
+        kd.copy_(kh, non_blocking=True); vd.copy_(vh, non_blocking=True); step()
+        oh.copy_(vo, non_blocking=True)
+    barrier(world)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(args.steps):
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        step()
+        oh.copy_(vo, non_blocking=True)
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+
+    # dominant kernel (onesweep pass) launch times, live, with CUDA events
+    lib.gs_timing_reset()
+    lib.gs_timing_enable(1)
+    for _ in range(args.steps):
+        step()
+    torch.cuda.synchronize()
+    lib.gs_timing_enable(0)
+    rep = timing_report()
+    lib.gs_timing_reset()
+    pass_ms, pass_launches = rep.get("radix_pass", (float("nan"), 1))
+    per_launch_bytes, _ = sort_algorithmic_bytes(n, SORT_KEY_BITS)
+    avg_ms = pass_ms / pass_launches
+    peaks = measured_peaks()
+    achieved = per_launch_bytes / (avg_ms / 1e3) / 1e9
+    out = {
+        "metric": "sort keys/s (C2: 2^24 Zipf uint64/uint32 pairs, 45 key bits)",
+        "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
+        "config": {"workload": "C2 radix sort, one 2^24-pair instance per GPU",
+                   "pairs_per_gpu": n, "key_bits": SORT_KEY_BITS, "tiles": 8160,
+                   "l2": "inputs larger than L2 (201 MB keys+values per GPU)",
+                   "parallelism": f"independent sorts x{world}"},
+        "e2e": {"value": sum_over_ranks(float(n), world) / (e2e_ms / 1e3), "unit": "pairs/s",
+                "h2d_bytes_per_step": 12 * n, "d2h_bytes_per_step": 4 * n},
+        "gpu_launches": int(args.steps * (2 + (SORT_KEY_BITS + 7) // 8)),
+        "roofline": {"bound": "hbm", "kernel": "k_radix_pass", "achieved": achieved,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "peak_source": peaks["source"], "avg_launch_ms": avg_ms,
+                     "algorithmic_bytes_per_launch": per_launch_bytes},
+        "kernel_ms": {k: v[0] / v[1] for k, v in rep.items()},
+        "clocks": clk.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_sort_baseline(keys, vals)
+    return out
+
+
+def run_sort_reference(args) -> dict:
+    from gsplat_tt_b200 import scenes
+    keys, vals = scenes.c2_pairs()
+    b = cpu_sort_baseline(keys, vals, budget_s=max(5.0, 2.0 * args.steps))
+    return {"impl": "reference", "metric": "sort keys/s (C2: 2^24 Zipf uint64/uint32 pairs, 45 key bits)",
+            "value": b["value"], "unit": "pairs/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": keys.size / b["value"] * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u64",
+            "data": "synthetic", "config": {"workload": "C2 radix sort", "pairs": int(keys.size)},
+            "cpu_baseline": b,
+            "e2e": {"value": b["value"], "unit": "pairs/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------- main
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", choices=["train", "sort"], default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    workload = args.workload
+    if workload is None:
+        try:
+            from gsplat_tt_b200 import train  # noqa: F401
+            workload = "train"
+        except ImportError:
+            workload = "sort"
+    rank, world, local = dist_setup(args)
+    if args.impl == "reference":
+        if rank == 0:
+            if workload == "sort":
+                out = run_sort_reference(args)
+            else:
+                from gsplat_tt_b200 import train_bench
+                out = train_bench.run_reference(args)
+            print(json.dumps(out), flush=True)
+        return
+    if workload == "sort":
+        out = run_sort(args, rank, world, local)
+    else:
+        from gsplat_tt_b200 import train_bench
+        out = train_bench.run(args, rank, world, local)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,68 @@
+"""libgs200.so host-side checks that need no GPU: it loads, exports every entry point
+include/gs200.h declares, sizes workspaces, and rejects bad arguments before touching
+the device (the reference's std::invalid_argument cases map to GS_ERR_ARG)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    names = set()
+    for f in os.listdir(os.path.join(ROOT, "include")):
+        if f.endswith(".h"):
+            text = open(os.path.join(ROOT, "include", f)).read()
+            text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+            names |= set(re.findall(r"\b(gs_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = declared_symbols()
+    assert "gs_sort_pairs" in names and "gs_project" in names and len(names) >= 10
+
+
+def test_library_exports_every_declared_symbol():
+    from gsplat_tt_b200 import _lib
+    missing = [n for n in declared_symbols() if not hasattr(_lib.lib, n)]
+    assert not missing, missing
+    assert _lib.version().startswith("gs200")
+
+
+def test_workspace_queries():
+    from gsplat_tt_b200._lib import lib
+    assert lib.gs_sort_pairs_workspace_size(1 << 24, 45) > (1 << 24) * 24
+    assert lib.gs_project_workspace_size(10000) > 0
+    assert lib.gs_tile_assign_workspace_size(10000, 1 << 20) > (1 << 20) * 8
+    assert lib.gs_sort_and_bin_workspace_size(1000, 16, 16) > 1000 * 24
+
+
+def test_argument_errors_need_no_device():
+    from gsplat_tt_b200._lib import lib, GS_ERR_ARG, GS_ERR_UNSUPPORTED
+    assert lib.gs_sort_pairs(None, None, -1, 45, None, None, None, 0, None) == GS_ERR_ARG
+    assert b"n must be" in lib.gs_last_error()
+    assert lib.gs_sort_pairs(None, None, 10, 0, None, None, None, 0, None) == GS_ERR_ARG
+    assert lib.gs_blend(None, None, None, None, None, None, 0, 64, 64, 33, None, None,
+                        None) == GS_ERR_ARG
+    e = (ctypes.c_float * 16)()
+    k = (ctypes.c_float * 9)()
+    assert lib.gs_project(None, None, e, k, None, None, 0.0, 0, 8, 8, 0, 1e-4, 3.0, 1,
+                          None, None, None, None, None, None, None, None, None, None, 0,
+                          None) == GS_ERR_UNSUPPORTED
+    assert lib.gs_tile_assign(None, None, 0, 8, 8, 16, ctypes.c_void_p(1), None, 0.0, None,
+                              None, 0, None, ctypes.c_void_p(1), None, None, 0,
+                              None) == GS_ERR_ARG
+
+
+def test_product_path_fails_loudly_without_library(tmp_path, monkeypatch):
+    import importlib
+    import gsplat_tt_b200._lib as L
+    monkeypatch.setattr(L, "LIB_PATH", str(tmp_path / "missing.so"))
+    src = open(L.__file__).read()
+    ns = {"__file__": str(tmp_path / "_lib.py"), "__name__": "x"}
+    with pytest.raises(ImportError):
+        exec(compile(src, "x", "exec"), ns)
+    importlib.reload(L)
