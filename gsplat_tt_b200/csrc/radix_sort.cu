@@ -81,7 +81,7 @@ __device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
 __device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) { *(volatile uint32_t*)p = v; }
 
 // One onesweep pass over digit `shift`.
-__global__ void __launch_bounds__(kSortThreads)
+__global__ void __launch_bounds__(kSortThreads, 3)
 k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
              uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
              const int64_t* __restrict__ n_dev, int64_t n_host, int shift,
@@ -100,38 +100,43 @@ k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ 
     if (base >= n) return;
     const int valid = (int)min((int64_t)kTileItems, n - base);
 
-    // Load (warp-striped: warp w owns items [512 w, 512 w + 512) of the tile).
+    // Load (warp-striped: warp w owns items [512 w, 512 w + 512) of the tile). Pads
+    // past the end get an all-ones digit so they rank after every real item.
     uint64_t key[kSortItems];
     uint32_t val[kSortItems];
-    uint32_t dig[kSortItems];
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
         const int li = warp * (kSortItems * 32) + j * 32 + lane;
         if (li < valid) {
             key[j] = keys_in[base + li];
             val[j] = vals_in[base + li];
-            dig[j] = (uint32_t)(key[j] >> shift) & (kRadix - 1);
         } else {
-            key[j] = 0;
+            key[j] = (uint64_t)(kRadix - 1) << shift;
             val[j] = 0;
-            dig[j] = kRadix - 1;  // pads rank after every real item of the last digit
         }
     }
+#define GS_DIGIT(k) ((uint32_t)((k) >> shift) & (uint32_t)(kRadix - 1))
 
     // Warp-level multisplit: rank of each item among the warp's items of its digit.
+    // Peers are found with one ballot per digit bit (pure ALU, pipelines across items);
+    // each peer group's leader claims the group's slots with one shared atomic, kept in
+    // item order by __syncwarp.
     uint32_t rank[kSortItems];
     const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
-        const uint32_t peers = __match_any_sync(0xffffffffu, dig[j]);
-        const int leader = __ffs(peers) - 1;
-        uint32_t old = 0;
-        if (lane == leader) {
-            old = S.warp_hist[warp][dig[j]];
-            S.warp_hist[warp][dig[j]] = old + __popc(peers);
+        const uint32_t d = GS_DIGIT(key[j]);
+        uint32_t peers = 0xffffffffu;
+#pragma unroll
+        for (int b = 0; b < kRadixBits; ++b) {
+            const uint32_t bit = (d >> b) & 1u;
+            const uint32_t m = __ballot_sync(0xffffffffu, bit);
+            peers &= bit ? m : ~m;
         }
-        old = __shfl_sync(peers, old, leader);
-        rank[j] = old + __popc(peers & lt_mask);
+        const int leader = 31 - __clz(peers);
+        uint32_t old = 0;
+        if (lane == leader) old = atomicAdd(&S.warp_hist[warp][d], (uint32_t)__popc(peers));
+        rank[j] = __shfl_sync(0xffffffffu, old, leader) + __popc(peers & lt_mask);
         __syncwarp();
     }
     __syncthreads();
@@ -194,7 +199,8 @@ k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ 
     // Scatter into shared memory in digit-sorted order.
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
-        const uint32_t pos = S.local_off[dig[j]] + S.warp_hist[warp][dig[j]] + rank[j];
+        const uint32_t d = GS_DIGIT(key[j]);
+        const uint32_t pos = S.local_off[d] + S.warp_hist[warp][d] + rank[j];
         S.keys[pos] = key[j];
         S.vals[pos] = val[j];
     }
@@ -204,11 +210,12 @@ k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ 
 #pragma unroll 4
     for (int i = tid; i < valid; i += kSortThreads) {
         const uint64_t k = S.keys[i];
-        const uint32_t dd = (uint32_t)(k >> shift) & (kRadix - 1);
+        const uint32_t dd = GS_DIGIT(k);
         const uint32_t out = S.gbase[dd] + ((uint32_t)i - S.local_off[dd]);
         if (keys_out) keys_out[out] = k;
         vals_out[out] = S.vals[i];
     }
+#undef GS_DIGIT
 }
 
 size_t radix_workspace_bytes(int64_t n, int key_bits) {
