@@ -42,7 +42,7 @@ struct SortSmem {
 __global__ void k_radix_hist(const uint64_t* __restrict__ keys, const int64_t* __restrict__ n_dev,
                              int64_t n_host, int npass, uint32_t* __restrict__ hist) {
     __shared__ uint32_t sh[8][kRadix];
-    const int64_t n = n_dev ? *n_dev : n_host;
+    const int64_t n = n_dev ? min(*n_dev, n_host) : n_host;  // device count, capped
     for (int i = threadIdx.x; i < 8 * kRadix; i += blockDim.x) (&sh[0][0])[i] = 0;
     __syncthreads();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
@@ -90,7 +90,7 @@ k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ 
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SortSmem& S = *reinterpret_cast<SortSmem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t n = n_dev ? *n_dev : n_host;
+    const int64_t n = n_dev ? min(*n_dev, n_host) : n_host;  // device count, capped
 
     if (tid == 0) S.tile = atomicAdd(tile_counter, 1u);
     for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads) (&S.warp_hist[0][0])[i] = 0;
@@ -236,7 +236,7 @@ int radix_num_passes(int key_bits) { return (key_bits + kRadixBits - 1) / kRadix
 gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int64_t* n_dev,
                            int64_t n_cap, int key_bits, uint64_t* keys_out, uint32_t* vals_out,
                            void* workspace, size_t workspace_bytes, cudaStream_t st,
-                           unsigned int** err_out) {
+                           unsigned int** err_out, unsigned int* err_ext) {
     const int npass = radix_num_passes(key_bits);
     const int64_t ntiles = (n_cap + kTileItems - 1) / kTileItems + 1;
     Workspace ws(workspace, workspace_bytes);
@@ -253,9 +253,11 @@ gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int
                   radix_workspace_bytes(n_cap, key_bits));
         return GS_ERR_ARG;
     }
-    if (err_out) *err_out = err;
-    // err .. counters are contiguous: one memset clears all of them.
+    // err .. counters are contiguous: one memset clears all of them. A caller-owned
+    // error word (err_ext) is OR-ed into, never cleared here.
     GS_CUDA_CHECK(cudaMemsetAsync(err, 0, (char*)(counters + npass) - (char*)err, st));
+    if (err_ext) err = err_ext;
+    if (err_out) *err_out = err;
     const int hist_blocks = (int)std::min<int64_t>(kNumSMs * 4, std::max<int64_t>(1, (n_cap + 4095) / 4096));
     {
         KernelTimer kt("radix_hist", st);

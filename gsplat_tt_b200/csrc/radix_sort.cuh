@@ -18,6 +18,6 @@ int bits_for(int64_t v);
 gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int64_t* n_dev,
                            int64_t n_cap, int key_bits, uint64_t* keys_out, uint32_t* vals_out,
                            void* workspace, size_t workspace_bytes, cudaStream_t st,
-                           unsigned int** err_out);
+                           unsigned int** err_out, unsigned int* err_ext = nullptr);
 
 }  // namespace gs

@@ -1,0 +1,1220 @@
+// train.cu -- training path: rasterisers, loss, projection backward, sparse Adam and
+// the gs_train_step orchestration (one stream, no host synchronisation inside a step).
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "radix_sort.cuh"
+#include "scan.cuh"
+#include "train.cuh"
+
+namespace gs {
+
+// ------------------------------------------------------------------ host helpers
+
+TCam make_tcam(const gs_camera& c) {
+    TCam t;
+    const float* w = c.w2c;
+    const float R[9] = {w[0], w[1], w[2], w[4], w[5], w[6], w[8], w[9], w[10]};
+    memcpy(t.R, R, sizeof(R));
+    t.t[0] = w[3];
+    t.t[1] = w[7];
+    t.t[2] = w[11];
+    t.fx = c.K[0];
+    t.fy = c.K[4];
+    t.cx = c.K[2];
+    t.cy = c.K[5];
+    for (int j = 0; j < 3; ++j) {  // camera centre -R^T t, in double, rounded once
+        double acc = 0.0;
+        for (int i = 0; i < 3; ++i) acc += (double)R[3 * i + j] * (double)t.t[i];
+        t.cc[j] = (float)(-acc);
+    }
+    t.H = c.height;
+    t.W = c.width;
+    return t;
+}
+
+TCfg make_tcfg(const gs_train_config& c, int H, int W) {
+    TCfg t;
+    t.sh_degree = c.sh_degree;
+    t.K = (c.sh_degree + 1) * (c.sh_degree + 1);
+    t.tile = c.tile_size;
+    t.tiles_x = (W + c.tile_size - 1) / c.tile_size;
+    t.tiles_y = (H + c.tile_size - 1) / c.tile_size;
+    t.near_plane = c.near_plane;
+    t.lowpass = c.lowpass;
+    t.amax = c.alpha_max;
+    t.amin = c.alpha_min;
+    t.tmin = c.t_min;
+    for (int i = 0; i < 3; ++i) t.bg[i] = c.background[i];
+    return t;
+}
+
+// ------------------------------------------------------------------ tile ranges
+
+// [start, end) of each tile in the sorted keys (binary search), (0, 0) when empty.
+__global__ void k_train_ranges(const uint64_t* __restrict__ skeys, const int64_t* __restrict__ p_dev,
+                               int64_t cap, int ntiles, int2* __restrict__ ranges) {
+    const int t = blockIdx.x * blockDim.x + threadIdx.x;
+    if (t >= ntiles) return;
+    const int64_t p = min(*p_dev, cap);
+    auto lower = [&](uint64_t target) {
+        int64_t lo = 0, hi = p;
+        while (lo < hi) {
+            const int64_t mid = (lo + hi) >> 1;
+            if (skeys[mid] < target) lo = mid + 1; else hi = mid;
+        }
+        return lo;
+    };
+    const int64_t s = lower((uint64_t)t << 32), e = lower((uint64_t)(t + 1) << 32);
+    ranges[t] = (e > s) ? make_int2((int)s, (int)e) : make_int2(0, 0);
+}
+
+// ------------------------------------------------------------------ rasterisers
+
+// One pair staged in shared memory: the tile-centred power polynomial
+// (gsplat/blend_backward_ref.py:68-92), opacity and colour.
+struct RPair {
+    float Af, Bf, Cf, P0, Lx, Ly, op, r, g, b;
+};
+
+// Coefficients in float64 from the fp32 conic and tile-local mean, rounded once.
+__device__ __forceinline__ RPair stage_pair(float4 p0, float4 p1, float p2, float ox, float oy,
+                                            float centre, float& mxl, float& myl) {
+    RPair q;
+    mxl = p0.x - ox;
+    myl = p0.y - oy;
+    q.Af = -0.5f * p0.z;
+    q.Bf = -p0.w;
+    q.Cf = -0.5f * p1.x;
+    const double a = q.Af, b = q.Bf, c = q.Cf;
+    const double U0 = (double)centre - (double)mxl, V0 = (double)centre - (double)myl;
+    q.P0 = (float)(a * U0 * U0 + b * U0 * V0 + c * V0 * V0);
+    q.Lx = (float)(2.0 * a * U0 + b * V0);
+    q.Ly = (float)(b * U0 + 2.0 * c * V0);
+    q.op = p1.y;
+    q.r = p1.z;
+    q.g = p1.w;
+    q.b = p2;
+    return q;
+}
+
+// power = P0 + du (Lx + Af du + Bf dv) + dv (Ly + Cf dv), with explicit FMAs so the forward
+// and backward kernels evaluate bit-identical alphas and hence identical decisions.
+__device__ __forceinline__ float centred_power(const RPair& q, float du, float dv) {
+    const float t2 = __fmaf_rn(q.Bf, dv, __fmaf_rn(q.Af, du, q.Lx));
+    const float t3 = __fmaf_rn(q.Cf, dv, q.Ly);
+    return __fmaf_rn(dv, t3, __fmaf_rn(du, t2, q.P0));
+}
+
+template <int TILE>
+__global__ void __launch_bounds__(TILE * TILE)
+k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals, ProjView pv,
+            TCfg cfg, int H, int W, float* __restrict__ image, float* __restrict__ final_T,
+            int32_t* __restrict__ n_contrib) {
+    constexpr int NB = 256;  // pairs staged per batch
+    __shared__ RPair sp[NB];
+    const int tile = blockIdx.x;
+    const int tx = tile % cfg.tiles_x, ty = tile / cfg.tiles_x;
+    const int lx = threadIdx.x % TILE, ly = threadIdx.x / TILE;
+    const int x = tx * TILE + lx, y = ty * TILE + ly;
+    const bool inside = (x < W) && (y < H);
+    const float centre = 0.5f * TILE;
+    const float du = ((float)lx + 0.5f) - centre, dv = ((float)ly + 0.5f) - centre;
+    const float ox = (float)(tx * TILE), oy = (float)(ty * TILE);
+    const int2 rg = ranges[tile];
+    const float amax = cfg.amax, amin = cfg.amin, tmin = cfg.tmin;
+    float T = 1.0f, c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;
+    bool done = !inside;
+    int last = 0;
+    for (int b0 = rg.x; b0 < rg.y; b0 += NB) {
+        __syncthreads();
+        const int i = b0 + threadIdx.x;
+        if (threadIdx.x < NB && i < rg.y) {
+            const uint32_t g = svals[i];
+            float mxl, myl;
+            sp[threadIdx.x] = stage_pair(pv.p0[g], pv.p1[g], pv.p2[g], ox, oy, centre, mxl, myl);
+        }
+        __syncthreads();
+        const int nb = min(NB, rg.y - b0);
+        for (int j = 0; j < nb && !done; ++j) {
+            const RPair q = sp[j];
+            const float power = centred_power(q, du, dv);
+            const float w = __expf(fminf(power, 0.0f));
+            const float alpha = fminf(q.op * w, amax);
+            if (alpha >= amin) {
+                const float Tn = T * (1.0f - alpha);
+                if (Tn < tmin) {
+                    done = true;
+                } else {
+                    const float at = alpha * T;
+                    c0 = __fmaf_rn(at, q.r, c0);
+                    c1 = __fmaf_rn(at, q.g, c1);
+                    c2 = __fmaf_rn(at, q.b, c2);
+                    T = Tn;
+                    last = b0 - rg.x + j + 1;
+                }
+            }
+        }
+        if (__syncthreads_count(!done) == 0) break;
+    }
+    if (!inside) return;
+    const size_t o = (size_t)y * W + x;
+    image[3 * o] = c0 + T * cfg.bg[0];
+    image[3 * o + 1] = c1 + T * cfg.bg[1];
+    image[3 * o + 2] = c2 + T * cfg.bg[2];
+    final_T[o] = T;
+    n_contrib[o] = last;
+}
+
+struct BPair {
+    RPair q;
+    float mxl, myl, A, B, C;
+    uint32_t gid;
+};
+
+// Back-to-front replay (gsplat/blend_backward_ref.py:134-249 terms, recomputed from the
+// stored final T and count of processed pairs): per pixel and live pair
+//   T_i = T_{i+1} / (1 - a_i),  da = T_i (c.g) - behind / (1 - a_i),  behind += a T_i (c.g)
+// with behind starting at T_final (bg.g). The nine per-pixel terms (dopacity, dcolour,
+// G u^2, G uv, G v^2, G u, G v with G = dL/dpower) are reduced per warp with shuffles,
+// per tile in shared memory, and added once per pair into the view's per-Gaussian rows.
+template <int TILE>
+__global__ void __launch_bounds__(TILE * TILE)
+k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals, ProjView pv,
+            TCfg cfg, int H, int W, const float* __restrict__ dimg,
+            const float* __restrict__ final_T, const int32_t* __restrict__ n_contrib,
+            float* __restrict__ grad2d) {
+    constexpr int NB = 256;  // pairs staged per batch
+    __shared__ BPair sp[NB];
+    __shared__ float acc[9][NB];
+    __shared__ int s_max;
+    const int tile = blockIdx.x;
+    const int tx = tile % cfg.tiles_x, ty = tile / cfg.tiles_x;
+    const int lx = threadIdx.x % TILE, ly = threadIdx.x / TILE;
+    const int x = tx * TILE + lx, y = ty * TILE + ly;
+    const bool inside = (x < W) && (y < H);
+    const float centre = 0.5f * TILE;
+    const float du = ((float)lx + 0.5f) - centre, dv = ((float)ly + 0.5f) - centre;
+    const float xx = (float)lx + 0.5f, yy = (float)ly + 0.5f;
+    const float ox = (float)(tx * TILE), oy = (float)(ty * TILE);
+    const int2 rg = ranges[tile];
+    const int lane = threadIdx.x & 31;
+    const float amax = cfg.amax, amin = cfg.amin;
+    float T = 1.0f, g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, behind = 0.0f;
+    int last = 0;
+    if (inside) {
+        const size_t o = (size_t)y * W + x;
+        T = final_T[o];
+        last = n_contrib[o];
+        g0 = dimg[3 * o];
+        g1 = dimg[3 * o + 1];
+        g2 = dimg[3 * o + 2];
+        behind = T * (cfg.bg[0] * g0 + cfg.bg[1] * g1 + cfg.bg[2] * g2);
+    }
+    if (threadIdx.x == 0) s_max = 0;
+    __syncthreads();
+    if (last > 0) atomicMax(&s_max, last);
+    __syncthreads();
+    const int maxl = s_max;
+    for (int hi = maxl; hi > 0; hi -= NB) {
+        const int lo = max(0, hi - NB);
+        const int nb = hi - lo;
+        __syncthreads();
+        if (threadIdx.x < nb) {
+            const uint32_t g = svals[rg.x + lo + threadIdx.x];
+            const float4 p0 = pv.p0[g], p1 = pv.p1[g];
+            BPair bp;
+            bp.q = stage_pair(p0, p1, pv.p2[g], ox, oy, centre, bp.mxl, bp.myl);
+            bp.A = p0.z;
+            bp.B = p0.w;
+            bp.C = p1.x;
+            bp.gid = g;
+            sp[threadIdx.x] = bp;
+#pragma unroll
+            for (int k = 0; k < 9; ++k) acc[k][threadIdx.x] = 0.0f;
+        }
+        __syncthreads();
+        for (int j = nb - 1; j >= 0; --j) {
+            float v[9];
+#pragma unroll
+            for (int k = 0; k < 9; ++k) v[k] = 0.0f;
+            bool live = false;
+            if (lo + j < last) {
+                const BPair& bp = sp[j];
+                const float power = centred_power(bp.q, du, dv);
+                const float w = __expf(fminf(power, 0.0f));
+                const float raw = bp.q.op * w;
+                const bool clamp = raw > amax;
+                const float alpha = fminf(raw, amax);
+                if (alpha >= amin) {
+                    live = true;
+                    const float one_m = 1.0f - alpha;
+                    T = T / one_m;
+                    const float cg = bp.q.r * g0 + bp.q.g * g1 + bp.q.b * g2;
+                    const float dalpha = T * cg - behind / one_m;
+                    const float at = alpha * T;
+                    behind = __fmaf_rn(at, cg, behind);
+                    const float G = (!clamp && power <= 0.0f) ? dalpha * alpha : 0.0f;
+                    const float u = xx - bp.mxl, vv = yy - bp.myl;
+                    v[0] = clamp ? 0.0f : dalpha * w;
+                    v[1] = at * g0;
+                    v[2] = at * g1;
+                    v[3] = at * g2;
+                    v[4] = G * u * u;
+                    v[5] = G * u * vv;
+                    v[6] = G * vv * vv;
+                    v[7] = G * u;
+                    v[8] = G * vv;
+                }
+            }
+            if (__any_sync(0xffffffffu, live)) {
+#pragma unroll
+                for (int k = 0; k < 9; ++k) {
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) v[k] += __shfl_xor_sync(0xffffffffu, v[k], o);
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int k = 0; k < 9; ++k) atomicAdd(&acc[k][j], v[k]);
+                }
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x < nb) {
+            const BPair& bp = sp[threadIdx.x];
+            const float s0 = acc[0][threadIdx.x], s1 = acc[1][threadIdx.x], s2 = acc[2][threadIdx.x];
+            const float s3 = acc[3][threadIdx.x], Suu = acc[4][threadIdx.x], Suv = acc[5][threadIdx.x];
+            const float Svv = acc[6][threadIdx.x], Su = acc[7][threadIdx.x], Sv = acc[8][threadIdx.x];
+            if (s0 != 0.0f || s1 != 0.0f || s2 != 0.0f || s3 != 0.0f || Su != 0.0f || Sv != 0.0f ||
+                Suu != 0.0f || Suv != 0.0f || Svv != 0.0f) {
+                float4* gr = reinterpret_cast<float4*>(grad2d + (size_t)bp.gid * kGradStride);
+                atomicAdd(&gr[0], make_float4(bp.A * Su + bp.B * Sv, bp.B * Su + bp.C * Sv,
+                                              -0.5f * Suu, -Suv));
+                atomicAdd(&gr[1], make_float4(-0.5f * Svv, s0, s1, s2));
+                atomicAdd(&gr[2], make_float4(s3, 0.0f, 0.0f, 0.0f));
+            }
+        }
+    }
+}
+
+// ------------------------------------------------------------------ loss
+
+constexpr int kLossTile = 16;
+constexpr int kHalo = 5;
+constexpr int kSpan = kLossTile + 2 * kHalo;  // 26
+
+struct LossCfg {
+    float taps[11];
+    float lambda;   // lambda_dssim
+    float inv_n;    // 1 / (3 H W)
+    int H, W;
+};
+
+// Pure L1 (gsplat/train_loss.py:166-171): grad = (1 - lambda) / n sign(x - y).
+__global__ void k_loss_l1(const float* __restrict__ img, const float* __restrict__ tgt, int64_t n3,
+                          LossCfg L, float* __restrict__ dimg, double* __restrict__ acc) {
+    __shared__ double red[32];
+    double s = 0.0;
+    const float w = (1.0f - L.lambda) * L.inv_n;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n3;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float d = img[i] - tgt[i];
+        s += fabsf(d);
+        dimg[i] = w * (float)((d > 0.0f) - (d < 0.0f));
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < (int)(blockDim.x >> 5); ++k) t += red[k];
+        atomicAdd(&acc[0], t);
+    }
+}
+
+// Separable 11-tap Gaussian of one 16x16 output tile of one channel from a
+// (26 x 26) shared patch; `hbuf` holds the 26 x 16 horizontal pass.
+__device__ __forceinline__ float filt_v(const float (*hbuf)[kLossTile], const float* taps, int ly, int lx) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 11; ++k) s = __fmaf_rn(taps[k], hbuf[ly + k][lx], s);
+    return s;
+}
+
+// SSIM forward + its partial derivatives (gsplat/train_loss.py:126-165): per pixel and
+// channel mu_x, mu_y, E_xx, E_yy, E_xy (zero padding), S, and the maps d_mu, d_xx, d_xy
+// (scaled by -lambda / n) that the second pass filters. Sums |x - y| and S.
+__global__ void __launch_bounds__(kLossTile * kLossTile)
+k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg L,
+           float* __restrict__ dmu, float* __restrict__ dxx, float* __restrict__ dxy,
+           double* __restrict__ acc) {
+    __shared__ float px[kSpan][kSpan], py[kSpan][kSpan];
+    __shared__ float h[5][kSpan][kLossTile];
+    __shared__ double red[2][8];
+    const int lx = threadIdx.x % kLossTile, ly = threadIdx.x / kLossTile;
+    const int x0 = blockIdx.x * kLossTile, y0 = blockIdx.y * kLossTile;
+    const int x = x0 + lx, y = y0 + ly;
+    const bool inside = x < L.W && y < L.H;
+    double s_l1 = 0.0, s_ssim = 0.0;
+    const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
+    const float w = -L.lambda * L.inv_n;
+    for (int ch = 0; ch < 3; ++ch) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < kSpan * kSpan; i += blockDim.x) {
+            const int yy = y0 - kHalo + i / kSpan, xx = x0 - kHalo + i % kSpan;
+            const bool in = yy >= 0 && yy < L.H && xx >= 0 && xx < L.W;
+            const size_t o = ((size_t)yy * L.W + xx) * 3 + ch;
+            px[i / kSpan][i % kSpan] = in ? img[o] : 0.0f;
+            py[i / kSpan][i % kSpan] = in ? tgt[o] : 0.0f;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < kSpan * kLossTile; i += blockDim.x) {
+            const int r = i / kLossTile, c = i % kLossTile;
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 11; ++k) {
+                const float xv = px[r][c + k], yv = py[r][c + k], t = L.taps[k];
+                a0 = __fmaf_rn(t, xv, a0);
+                a1 = __fmaf_rn(t, yv, a1);
+                a2 = __fmaf_rn(t, xv * xv, a2);
+                a3 = __fmaf_rn(t, yv * yv, a3);
+                a4 = __fmaf_rn(t, xv * yv, a4);
+            }
+            h[0][r][c] = a0; h[1][r][c] = a1; h[2][r][c] = a2; h[3][r][c] = a3; h[4][r][c] = a4;
+        }
+        __syncthreads();
+        if (inside) {
+            const float mx = filt_v(h[0], L.taps, ly, lx), my = filt_v(h[1], L.taps, ly, lx);
+            const float exx = filt_v(h[2], L.taps, ly, lx), eyy = filt_v(h[3], L.taps, ly, lx);
+            const float exy = filt_v(h[4], L.taps, ly, lx);
+            const float mxy = mx * my;
+            const float A = 2.0f * mxy + C1;
+            const float B = 2.0f * (exy - mxy) + C2;
+            const float C = mx * mx + my * my + C1;
+            const float D = (exx - mx * mx) + (eyy - my * my) + C2;
+            const float S = (A * B) / (C * D);
+            const float Sw = S * w;
+            const size_t o = ((size_t)y * L.W + x) * 3 + ch;
+            dmu[o] = Sw * (2.0f * my / A - 2.0f * my / B - 2.0f * mx / C + 2.0f * mx / D);
+            dxx[o] = -Sw / D;
+            dxy[o] = 2.0f * Sw / B;
+            s_ssim += S;
+            s_l1 += fabsf(px[ly + kHalo][lx + kHalo] - py[ly + kHalo][lx + kHalo]);
+        }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+        s_l1 += __shfl_xor_sync(0xffffffffu, s_l1, o);
+        s_ssim += __shfl_xor_sync(0xffffffffu, s_ssim, o);
+    }
+    if ((threadIdx.x & 31) == 0) {
+        red[0][threadIdx.x >> 5] = s_l1;
+        red[1][threadIdx.x >> 5] = s_ssim;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        double a = 0.0, b = 0.0;
+        for (int k = 0; k < 8; ++k) { a += red[0][k]; b += red[1][k]; }
+        atomicAdd(&acc[0], a);
+        atomicAdd(&acc[1], b);
+    }
+}
+
+// dL/dx = G*d_mu + 2 x G*d_xx + y G*d_xy + (1 - lambda)/n sign(x - y).
+__global__ void __launch_bounds__(kLossTile * kLossTile)
+k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt,
+           const float* __restrict__ dmu, const float* __restrict__ dxx,
+           const float* __restrict__ dxy, LossCfg L, float* __restrict__ dimg) {
+    __shared__ float p[3][kSpan][kSpan];
+    __shared__ float h[3][kSpan][kLossTile];
+    const int lx = threadIdx.x % kLossTile, ly = threadIdx.x / kLossTile;
+    const int x0 = blockIdx.x * kLossTile, y0 = blockIdx.y * kLossTile;
+    const int x = x0 + lx, y = y0 + ly;
+    const bool inside = x < L.W && y < L.H;
+    const float wl1 = (1.0f - L.lambda) * L.inv_n;
+    for (int ch = 0; ch < 3; ++ch) {
+        __syncthreads();
+        for (int i = threadIdx.x; i < kSpan * kSpan; i += blockDim.x) {
+            const int yy = y0 - kHalo + i / kSpan, xx = x0 - kHalo + i % kSpan;
+            const bool in = yy >= 0 && yy < L.H && xx >= 0 && xx < L.W;
+            const size_t o = ((size_t)yy * L.W + xx) * 3 + ch;
+            p[0][i / kSpan][i % kSpan] = in ? dmu[o] : 0.0f;
+            p[1][i / kSpan][i % kSpan] = in ? dxx[o] : 0.0f;
+            p[2][i / kSpan][i % kSpan] = in ? dxy[o] : 0.0f;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < kSpan * kLossTile; i += blockDim.x) {
+            const int r = i / kLossTile, c = i % kLossTile;
+            float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+#pragma unroll
+            for (int k = 0; k < 11; ++k) {
+                const float t = L.taps[k];
+                a0 = __fmaf_rn(t, p[0][r][c + k], a0);
+                a1 = __fmaf_rn(t, p[1][r][c + k], a1);
+                a2 = __fmaf_rn(t, p[2][r][c + k], a2);
+            }
+            h[0][r][c] = a0; h[1][r][c] = a1; h[2][r][c] = a2;
+        }
+        __syncthreads();
+        if (inside) {
+            const size_t o = ((size_t)y * L.W + x) * 3 + ch;
+            const float P = filt_v(h[0], L.taps, ly, lx), Q = filt_v(h[1], L.taps, ly, lx);
+            const float Rr = filt_v(h[2], L.taps, ly, lx);
+            const float xv = img[o], yv = tgt[o];
+            const float d = xv - yv;
+            dimg[o] = P + 2.0f * xv * Q + yv * Rr + wl1 * (float)((d > 0.0f) - (d < 0.0f));
+        }
+    }
+}
+
+__global__ void k_loss_finalize(const double* __restrict__ acc, LossCfg L, int use_ssim,
+                                float* __restrict__ out) {
+    const double n = 1.0 / (double)L.inv_n;
+    const double l1 = acc[0] / n;
+    double loss = (1.0 - (double)L.lambda) * l1;
+    if (use_ssim) loss += (double)L.lambda * (1.0 - acc[1] / n);
+    *out = (float)loss;
+}
+
+// ------------------------------------------------------------------ projection backward
+
+constexpr float kC0 = 0.28209479177387814f, kC1 = 0.4886025119029199f;
+__constant__ float c_C2[5] = {1.0925484305920792f, -1.0925484305920792f, 0.31539156525252005f,
+                              -1.0925484305920792f, 0.5462742152960396f};
+__constant__ float c_C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.4570457994644658f,
+                              0.3731763325901154f, -0.4570457994644658f, 1.445305721320277f,
+                              -0.5900435899266435f};
+
+__device__ __forceinline__ void sh_basis_and_grad(int deg, float x, float y, float z, float* b,
+                                                  float (*db)[3]) {
+    b[0] = kC0;
+    db[0][0] = db[0][1] = db[0][2] = 0.0f;
+    if (deg < 1) return;
+    b[1] = -kC1 * y; db[1][0] = 0.f; db[1][1] = -kC1; db[1][2] = 0.f;
+    b[2] = kC1 * z; db[2][0] = 0.f; db[2][1] = 0.f; db[2][2] = kC1;
+    b[3] = -kC1 * x; db[3][0] = -kC1; db[3][1] = 0.f; db[3][2] = 0.f;
+    if (deg < 2) return;
+    const float xx = x * x, yy = y * y, zz = z * z;
+    const float* c = c_C2;
+    b[4] = c[0] * (x * y); db[4][0] = c[0] * y; db[4][1] = c[0] * x; db[4][2] = 0.f;
+    b[5] = c[1] * (y * z); db[5][0] = 0.f; db[5][1] = c[1] * z; db[5][2] = c[1] * y;
+    b[6] = c[2] * (2.0f * zz - xx - yy);
+    db[6][0] = -2.0f * c[2] * x; db[6][1] = -2.0f * c[2] * y; db[6][2] = 4.0f * c[2] * z;
+    b[7] = c[3] * (x * z); db[7][0] = c[3] * z; db[7][1] = 0.f; db[7][2] = c[3] * x;
+    b[8] = c[4] * (xx - yy); db[8][0] = 2.0f * c[4] * x; db[8][1] = -2.0f * c[4] * y; db[8][2] = 0.f;
+    if (deg < 3) return;
+    const float* e = c_C3;
+    b[9] = e[0] * y * (3.0f * xx - yy);
+    db[9][0] = e[0] * 6.0f * x * y; db[9][1] = e[0] * (3.0f * xx - 3.0f * yy); db[9][2] = 0.f;
+    b[10] = e[1] * (x * y) * z;
+    db[10][0] = e[1] * y * z; db[10][1] = e[1] * x * z; db[10][2] = e[1] * x * y;
+    b[11] = e[2] * y * (4.0f * zz - xx - yy);
+    db[11][0] = -2.0f * e[2] * x * y; db[11][1] = e[2] * (4.0f * zz - xx - 3.0f * yy);
+    db[11][2] = 8.0f * e[2] * y * z;
+    b[12] = e[3] * z * (2.0f * zz - 3.0f * xx - 3.0f * yy);
+    db[12][0] = -6.0f * e[3] * x * z; db[12][1] = -6.0f * e[3] * y * z;
+    db[12][2] = e[3] * (6.0f * zz - 3.0f * xx - 3.0f * yy);
+    b[13] = e[4] * x * (4.0f * zz - xx - yy);
+    db[13][0] = e[4] * (4.0f * zz - 3.0f * xx - yy); db[13][1] = -2.0f * e[4] * x * y;
+    db[13][2] = 8.0f * e[4] * x * z;
+    b[14] = e[5] * z * (xx - yy);
+    db[14][0] = 2.0f * e[5] * x * z; db[14][1] = -2.0f * e[5] * y * z; db[14][2] = e[5] * (xx - yy);
+    b[15] = e[6] * x * (xx - 3.0f * yy);
+    db[15][0] = e[6] * (3.0f * xx - 3.0f * yy); db[15][1] = -6.0f * e[6] * x * y; db[15][2] = 0.f;
+}
+
+struct GMut {
+    float* means;
+    float* ls;
+    float* q;
+    float* ol;
+    float* sh;
+};
+
+// Per Gaussian, over every view that gave it 2D gradients: the analytic projection
+// backward of gsplat/t2_param_backward.py:123-192 extended with SH bands 1-3 and the
+// view-direction term, summed over views. dL/dcov3d, dL/dopacity and the SH gradient
+// accumulate across views; the log-scale, quaternion and logit gradients are formed once.
+template <int DEG>
+__global__ void __launch_bounds__(128)
+k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCfg cfg,
+            const float* __restrict__ grad2d, const uint64_t* __restrict__ touch, GMut G) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    constexpr int K = (DEG + 1) * (DEG + 1);
+    const uint64_t mask = touch[g];
+    float gm[3] = {0.f, 0.f, 0.f};
+    float G3[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 00 01 02 11 12 22
+    float gop = 0.0f;
+    float gsh[3 * K];
+#pragma unroll
+    for (int k = 0; k < 3 * K; ++k) gsh[k] = 0.0f;
+    const float m0 = P.means[3 * g], m1 = P.means[3 * g + 1], m2 = P.means[3 * g + 2];
+    const float4 q = reinterpret_cast<const float4*>(P.q)[g];
+    const float qinv = 1.0f / sqrtf(q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w);
+    const float qw = q.x * qinv, qx = q.y * qinv, qy = q.z * qinv, qz = q.w * qinv;
+    float Rq[9];
+    Rq[0] = 1.0f - 2.0f * (qy * qy + qz * qz);
+    Rq[1] = 2.0f * (qx * qy - qw * qz);
+    Rq[2] = 2.0f * (qx * qz + qw * qy);
+    Rq[3] = 2.0f * (qx * qy + qw * qz);
+    Rq[4] = 1.0f - 2.0f * (qx * qx + qz * qz);
+    Rq[5] = 2.0f * (qy * qz - qw * qx);
+    Rq[6] = 2.0f * (qx * qz - qw * qy);
+    Rq[7] = 2.0f * (qy * qz + qw * qx);
+    Rq[8] = 1.0f - 2.0f * (qx * qx + qy * qy);
+    const float s[3] = {__expf(P.ls[3 * g]), __expf(P.ls[3 * g + 1]), __expf(P.ls[3 * g + 2])};
+    float M[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) M[3 * i + j] = Rq[3 * i + j] * s[j];
+    float S[3][3];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int k = i; k < 3; ++k) {
+            S[i][k] = M[3 * i] * M[3 * k] + M[3 * i + 1] * M[3 * k + 1] + M[3 * i + 2] * M[3 * k + 2];
+            S[k][i] = S[i][k];
+        }
+    const float* shg = P.sh + (size_t)g * K * 3;
+    for (int v = 0; v < n_views; ++v) {
+        if (!((mask >> v) & 1ull)) continue;
+        const float* gr = grad2d + ((size_t)v * n + g) * kGradStride;
+        const float4 ga4 = reinterpret_cast<const float4*>(gr)[0];
+        const float4 gb4 = reinterpret_cast<const float4*>(gr)[1];
+        const float gbl = gr[8];
+        const float gmx = ga4.x, gmy = ga4.y, gA = ga4.z, gB = ga4.w, gC = gb4.x;
+        if (gmx == 0.f && gmy == 0.f && gA == 0.f && gB == 0.f && gC == 0.f && gb4.y == 0.f &&
+            gb4.z == 0.f && gb4.w == 0.f && gbl == 0.f)
+            continue;
+        const TCam& cam = cams[v];
+        const float* R = cam.R;
+        const float x = R[0] * m0 + R[1] * m1 + R[2] * m2 + cam.t[0];
+        const float y = R[3] * m0 + R[4] * m1 + R[5] * m2 + cam.t[1];
+        const float z = R[6] * m0 + R[7] * m1 + R[8] * m2 + cam.t[2];
+        if (!(z > cfg.near_plane)) continue;
+        const float iz = 1.0f / z, iz2 = iz * iz;
+        const float j00 = cam.fx * iz, j02 = -cam.fx * x * iz2;
+        const float j11 = cam.fy * iz, j12 = -cam.fy * y * iz2;
+        float T0[3], T1[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            T0[k] = j00 * R[k] + j02 * R[6 + k];
+            T1[k] = j11 * R[3 + k] + j12 * R[6 + k];
+        }
+        float TC0[3], TC1[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            TC0[k] = T0[0] * S[0][k] + T0[1] * S[1][k] + T0[2] * S[2][k];
+            TC1[k] = T1[0] * S[0][k] + T1[1] * S[1][k] + T1[2] * S[2][k];
+        }
+        const float a = T0[0] * TC0[0] + T0[1] * TC0[1] + T0[2] * TC0[2] + cfg.lowpass;
+        const float b = T1[0] * TC0[0] + T1[1] * TC0[1] + T1[2] * TC0[2];
+        const float c = T1[0] * TC1[0] + T1[1] * TC1[1] + T1[2] * TC1[2] + cfg.lowpass;
+        const float idet = 1.0f / (a * c - b * b);
+        const float A = c * idet, B = -b * idet, C = a * idet;
+        // conic -> 2D covariance
+        const float ga = -(A * A * gA + A * B * gB + B * B * gC);
+        const float gc = -(B * B * gA + B * C * gB + C * C * gC);
+        const float gbb = -(2.0f * A * B * gA + (A * C + B * B) * gB + 2.0f * B * C * gC);
+        const float hb = 0.5f * gbb;
+        // dL/dcov3d += T^T Gs T
+        G3[0] += ga * T0[0] * T0[0] + hb * 2.0f * T0[0] * T1[0] + gc * T1[0] * T1[0];
+        G3[1] += ga * T0[0] * T0[1] + hb * (T0[0] * T1[1] + T1[0] * T0[1]) + gc * T1[0] * T1[1];
+        G3[2] += ga * T0[0] * T0[2] + hb * (T0[0] * T1[2] + T1[0] * T0[2]) + gc * T1[0] * T1[2];
+        G3[3] += ga * T0[1] * T0[1] + hb * 2.0f * T0[1] * T1[1] + gc * T1[1] * T1[1];
+        G3[4] += ga * T0[1] * T0[2] + hb * (T0[1] * T1[2] + T1[1] * T0[2]) + gc * T1[1] * T1[2];
+        G3[5] += ga * T0[2] * T0[2] + hb * 2.0f * T0[2] * T1[2] + gc * T1[2] * T1[2];
+        // dL/dT = 2 Gs T Sigma -> Jacobian entries -> camera-space mean
+        float dT0[3], dT1[3];
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            dT0[k] = 2.0f * (ga * TC0[k] + hb * TC1[k]);
+            dT1[k] = 2.0f * (hb * TC0[k] + gc * TC1[k]);
+        }
+        const float gj00 = dT0[0] * R[0] + dT0[1] * R[1] + dT0[2] * R[2];
+        const float gj02 = dT0[0] * R[6] + dT0[1] * R[7] + dT0[2] * R[8];
+        const float gj11 = dT1[0] * R[3] + dT1[1] * R[4] + dT1[2] * R[5];
+        const float gj12 = dT1[0] * R[6] + dT1[1] * R[7] + dT1[2] * R[8];
+        const float fx = cam.fx, fy = cam.fy;
+        const float gx = gmx * fx * iz - gj02 * fx * iz2;
+        const float gy = gmy * fy * iz - gj12 * fy * iz2;
+        const float gz = -(gmx * fx * x + gmy * fy * y + gj00 * fx + gj11 * fy) * iz2 +
+                         2.0f * (gj02 * fx * x + gj12 * fy * y) * iz2 * iz;
+        gm[0] += R[0] * gx + R[3] * gy + R[6] * gz;
+        gm[1] += R[1] * gx + R[4] * gy + R[7] * gz;
+        gm[2] += R[2] * gx + R[5] * gy + R[8] * gz;
+        gop += gb4.y;
+        // SH colour backward (colour = max(raw, 0)) and the view-direction term.
+        const float d0 = m0 - cam.cc[0], d1 = m1 - cam.cc[1], d2 = m2 - cam.cc[2];
+        const float dn = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
+        const float idn = 1.0f / dn;
+        const float dx = d0 * idn, dy = d1 * idn, dz = d2 * idn;
+        float basis[16], db[16][3];
+        sh_basis_and_grad(DEG, dx, dy, dz, basis, db);
+        const float gcol_in[3] = {gb4.z, gb4.w, gbl};
+        float gcol[3];
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+            float raw = 0.5f;
+#pragma unroll
+            for (int k = 0; k < K; ++k) raw += basis[k] * shg[3 * k + ch];
+            gcol[ch] = (raw >= 0.0f) ? gcol_in[ch] : 0.0f;
+        }
+        float gdir[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+        for (int k = 0; k < K; ++k) {
+            const float s0 = shg[3 * k], s1 = shg[3 * k + 1], s2 = shg[3 * k + 2];
+            gsh[3 * k] += basis[k] * gcol[0];
+            gsh[3 * k + 1] += basis[k] * gcol[1];
+            gsh[3 * k + 2] += basis[k] * gcol[2];
+            const float gbk = s0 * gcol[0] + s1 * gcol[1] + s2 * gcol[2];
+            gdir[0] += db[k][0] * gbk;
+            gdir[1] += db[k][1] * gbk;
+            gdir[2] += db[k][2] * gbk;
+        }
+        if (K > 1) {
+            const float pd = dx * gdir[0] + dy * gdir[1] + dz * gdir[2];
+            gm[0] += (gdir[0] - dx * pd) * idn;
+            gm[1] += (gdir[1] - dy * pd) * idn;
+            gm[2] += (gdir[2] - dz * pd) * idn;
+        }
+    }
+    // cov3d = M M^T: dM = 2 G3 M, M = Rq diag(s).
+    const float Gf[3][3] = {{G3[0], G3[1], G3[2]}, {G3[1], G3[3], G3[4]}, {G3[2], G3[4], G3[5]}};
+    float dM[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j)
+            dM[3 * i + j] = 2.0f * (Gf[i][0] * M[j] + Gf[i][1] * M[3 + j] + Gf[i][2] * M[6 + j]);
+    float gls[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) gls[j] = (dM[j] * Rq[j] + dM[3 + j] * Rq[3 + j] + dM[6 + j] * Rq[6 + j]) * s[j];
+    float gR[9];
+#pragma unroll
+    for (int i = 0; i < 3; ++i)
+#pragma unroll
+        for (int j = 0; j < 3; ++j) gR[3 * i + j] = dM[3 * i + j] * s[j];
+    const float g00 = gR[0], g01 = gR[1], g02 = gR[2], g10 = gR[3], g11 = gR[4], g12 = gR[5];
+    const float g20 = gR[6], g21 = gR[7], g22 = gR[8];
+    const float gqn0 = 2.0f * (-qz * g01 + qy * g02 + qz * g10 - qx * g12 - qy * g20 + qx * g21);
+    const float gqn1 = 2.0f * (qy * g01 + qz * g02 + qy * g10 - 2.0f * qx * g11 - qw * g12 + qz * g20 +
+                               qw * g21 - 2.0f * qx * g22);
+    const float gqn2 = 2.0f * (-2.0f * qy * g00 + qx * g01 + qw * g02 + qx * g10 + qz * g12 - qw * g20 +
+                               qz * g21 - 2.0f * qy * g22);
+    const float gqn3 = 2.0f * (-2.0f * qz * g00 - qw * g01 + qx * g02 + qw * g10 - 2.0f * qz * g11 +
+                               qy * g12 + qx * g20 + qy * g21);
+    const float dot = qw * gqn0 + qx * gqn1 + qy * gqn2 + qz * gqn3;
+    const float op = 1.0f / (1.0f + __expf(-P.ol[g]));
+    G.means[3 * g] = gm[0];
+    G.means[3 * g + 1] = gm[1];
+    G.means[3 * g + 2] = gm[2];
+    G.ls[3 * g] = gls[0];
+    G.ls[3 * g + 1] = gls[1];
+    G.ls[3 * g + 2] = gls[2];
+    reinterpret_cast<float4*>(G.q)[g] =
+        make_float4((gqn0 - qw * dot) * qinv, (gqn1 - qx * dot) * qinv, (gqn2 - qy * dot) * qinv,
+                    (gqn3 - qz * dot) * qinv);
+    G.ol[g] = gop * op * (1.0f - op);
+    float* gshg = G.sh + (size_t)g * K * 3;
+#pragma unroll
+    for (int k = 0; k < 3 * K; ++k) gshg[k] = gsh[k];
+}
+
+// View v's 2D gradient rows in the reference's (N, 9) layout (zero where untouched).
+__global__ void k_export_grad2d(const float* __restrict__ grad2d, const uint64_t* __restrict__ touch,
+                                int64_t n, int view, float* __restrict__ out) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    const bool t = (touch[g] >> view) & 1ull;
+    const float* src = grad2d + ((size_t)view * n + g) * kGradStride;
+#pragma unroll
+    for (int k = 0; k < 9; ++k) out[9 * g + k] = t ? src[k] : 0.0f;
+}
+
+// ------------------------------------------------------------------ sparse Adam
+
+struct AdamGroup {
+    float* p;
+    float* m;
+    float* v;
+    const float* g;
+    int64_t count;       // elements
+    int width;           // elements per Gaussian row
+    float step_size;     // lr / (1 - beta1^t)
+    float step_size_rest;
+    int sh_band_split;   // 1 for the SH group: element j of a row is band j / 3
+};
+
+struct AdamParams {
+    AdamGroup grp[5];
+    float b1, b2, isq_bc2, eps;
+    int bf16;
+};
+
+__device__ __forceinline__ float bf16_round(float x) {
+    uint32_t u = __float_as_uint(x);
+    u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+    return __uint_as_float(u);
+}
+
+__global__ void k_sparse_adam(AdamParams A, const float* __restrict__ vis,
+                              const unsigned int* __restrict__ err, int group) {
+    if (err != nullptr && *err != 0u) return;
+    const AdamGroup& G = A.grp[group];
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < G.count;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t row = e / G.width;
+        if (!(vis[row] > 0.0f)) continue;
+        const float g = G.g[e];
+        const float m1 = A.b1 * G.m[e] + (1.0f - A.b1) * g;
+        const float v1 = A.b2 * G.v[e] + (1.0f - A.b2) * g * g;
+        const float den = sqrtf(v1) * A.isq_bc2 + A.eps;
+        float ss = G.step_size;
+        if (G.sh_band_split && (e % G.width) >= 3) ss = G.step_size_rest;
+        G.p[e] = G.p[e] - ss * (m1 / den);
+        G.m[e] = A.bf16 ? bf16_round(m1) : m1;
+        G.v[e] = A.bf16 ? bf16_round(v1) : v1;
+    }
+}
+
+// ------------------------------------------------------------------ workspace layout
+
+struct TrainWs {
+    unsigned int* err;
+    uint64_t* touch;
+    TCam* cams;
+    float* grad2d;
+    int64_t* blk;
+    int64_t* pairs;
+    ProjView pv;
+    uint64_t* keys;
+    uint32_t* vals;
+    uint64_t* skeys;
+    uint32_t* svals;
+    char* radix;
+    size_t radix_bytes;
+    int2* ranges;
+    float* image;
+    float* final_T;
+    int32_t* ncon;
+    float* dimg;
+    float* dmu;
+    float* dxx;
+    float* dxy;
+    double* loss_acc;
+};
+
+template <typename WS>
+static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int W, int tile,
+                         int64_t cap) {
+    const int tiles = ((W + tile - 1) / tile) * ((H + tile - 1) / tile);
+    const int key_bits = 32 + bits_for(tiles > 1 ? tiles - 1 : 1);
+    const int64_t nb = div_up(n, kProjThreads) + 1;
+    const int64_t px = (int64_t)H * W;
+    L.err = ws.template take<unsigned int>(1);
+    L.touch = ws.template take<uint64_t>(n);
+    L.cams = ws.template take<TCam>(n_views);
+    L.grad2d = ws.template take<float>((size_t)n_views * n * kGradStride);
+    L.blk = ws.template take<int64_t>(nb);
+    L.pairs = ws.template take<int64_t>(n_views);
+    L.pv.p0 = ws.template take<float4>(n);
+    L.pv.p1 = ws.template take<float4>(n);
+    L.pv.p2 = ws.template take<float>(n);
+    L.pv.dkey = ws.template take<uint32_t>(n);
+    L.pv.rect = ws.template take<ushort4>(n);
+    L.pv.cnt = ws.template take<uint32_t>(n);
+    L.keys = ws.template take<uint64_t>(cap);
+    L.vals = ws.template take<uint32_t>(cap);
+    L.skeys = ws.template take<uint64_t>(cap);
+    L.svals = ws.template take<uint32_t>(cap);
+    L.radix_bytes = radix_workspace_bytes(cap, key_bits);
+    L.radix = ws.template take<char>(L.radix_bytes);
+    L.ranges = ws.template take<int2>(tiles);
+    L.image = ws.template take<float>(px * 3);
+    L.final_T = ws.template take<float>(px);
+    L.ncon = ws.template take<int32_t>(px);
+    L.dimg = ws.template take<float>(px * 3);
+    L.dmu = ws.template take<float>(px * 3);
+    L.dxx = ws.template take<float>(px * 3);
+    L.dxy = ws.template take<float>(px * 3);
+    L.loss_acc = ws.template take<double>(2 * (size_t)n_views);
+}
+
+struct SizerAdapter {
+    WorkspaceSizer s;
+    template <typename T>
+    T* take(size_t c) {
+        s.take<T>(c);
+        return nullptr;
+    }
+};
+
+static gs_status check_cfg(const gs_train_config* cfg) {
+    GS_ARG_CHECK(cfg != nullptr, "train: null config");
+    GS_ARG_CHECK(cfg->sh_degree >= 0 && cfg->sh_degree <= 3, "train: sh_degree must be 0..3");
+    GS_ARG_CHECK(cfg->tile_size == 16 || cfg->tile_size == 32, "train: tile_size must be 16 or 32");
+    return GS_OK;
+}
+
+static GConst gconst(const gs_gaussians* p) {
+    return GConst{p->means, p->log_scales, p->quats, p->opacity_logits, p->sh};
+}
+
+}  // namespace gs
+
+using namespace gs;
+
+extern "C" size_t gs_train_workspace_size(int64_t n, int32_t sh_degree, int32_t n_views,
+                                          int32_t height, int32_t width, int32_t tile_size,
+                                          int64_t pair_capacity) {
+    (void)sh_degree;
+    if (n < 1) n = 1;
+    if (n_views < 1) n_views = 1;
+    if (tile_size < 1) tile_size = 16;
+    if (pair_capacity < 1) pair_capacity = 1;
+    SizerAdapter s;
+    TrainWs L;
+    train_layout(s, L, n, n_views, height, width, tile_size, pair_capacity);
+    return s.s.bytes();
+}
+
+static gs_status project_and_sort_view(const GConst& P, int64_t n, const TCam& cam, const TCfg& cfg,
+                                       int view, TrainWs& L, int64_t cap, float* vis_counts,
+                                       bool with_grad, cudaStream_t st) {
+    const unsigned int nb = div_up(n, kProjThreads);
+    {
+        KernelTimer kt("train_project", st);
+        launch_project(P, n, cam, cfg, view, L.pv, L.blk, L.touch, vis_counts,
+                       with_grad ? L.grad2d + (size_t)view * n * kGradStride : nullptr, st);
+        GS_CHECK_LAUNCH();
+    }
+    scan_block_totals<int64_t><<<1, 1024, 0, st>>>(L.blk, nb, L.pairs + view);
+    GS_CHECK_LAUNCH();
+    {
+        KernelTimer kt("train_emit", st);
+        launch_emit(L.pv, n, cfg, L.blk, cap, L.keys, L.vals, L.err, st);
+        GS_CHECK_LAUNCH();
+    }
+    const int tiles = cfg.tiles_x * cfg.tiles_y;
+    const int key_bits = 32 + bits_for(tiles > 1 ? tiles - 1 : 1);
+    unsigned int* rerr = nullptr;
+    gs_status s = radix_sort_pairs(L.keys, L.vals, L.pairs + view, cap, key_bits, L.skeys, L.svals,
+                                   L.radix, L.radix_bytes, st, &rerr, L.err);
+    if (s != GS_OK) return s;
+    k_train_ranges<<<div_up(tiles, 256), 256, 0, st>>>(L.skeys, L.pairs + view, cap, tiles, L.ranges);
+    GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
+extern "C" gs_status gs_train_count_pairs(const gs_gaussians* params, int64_t n,
+                                          const gs_camera* cams, int32_t n_views,
+                                          const gs_train_config* cfg, int64_t* pairs_host,
+                                          void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(params && cams && pairs_host && n > 0 && n_views > 0 && n_views <= 64,
+                 "gs_train_count_pairs: bad arguments");
+    int H = 0, W = 0;
+    for (int v = 0; v < n_views; ++v) {
+        H = std::max(H, (int)cams[v].height);
+        W = std::max(W, (int)cams[v].width);
+    }
+    Workspace ws(workspace, workspace_bytes);
+    TrainWs L;
+    train_layout(ws, L, n, n_views, H, W, cfg->tile_size, 1);
+    GS_ARG_CHECK(ws.ok(), "gs_train_count_pairs: workspace too small");
+    const GConst P = gconst(params);
+    const unsigned int nb = div_up(n, kProjThreads);
+    for (int v = 0; v < n_views; ++v) {
+        const TCam cam = make_tcam(cams[v]);
+        const TCfg c = make_tcfg(*cfg, cams[v].height, cams[v].width);
+        launch_project(P, n, cam, c, v, L.pv, L.blk, L.touch, nullptr, nullptr, st);
+        GS_CHECK_LAUNCH();
+        scan_block_totals<int64_t><<<1, 1024, 0, st>>>(L.blk, nb, L.pairs + v);
+        GS_CHECK_LAUNCH();
+    }
+    GS_CUDA_CHECK(cudaMemcpyAsync(pairs_host, L.pairs, n_views * sizeof(int64_t),
+                                  cudaMemcpyDeviceToHost, st));
+    GS_CUDA_CHECK(cudaStreamSynchronize(st));
+    return GS_OK;
+}
+
+__global__ void k_export_projection(ProjView pv, int64_t n, float* __restrict__ means2d,
+                                    float* __restrict__ conic, float* __restrict__ opacity,
+                                    float* __restrict__ colors, float* __restrict__ depth,
+                                    int32_t* __restrict__ rects) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    const float4 p0 = pv.p0[g], p1 = pv.p1[g];
+    means2d[2 * g] = p0.x;
+    means2d[2 * g + 1] = p0.y;
+    conic[3 * g] = p0.z;
+    conic[3 * g + 1] = p0.w;
+    conic[3 * g + 2] = p1.x;
+    opacity[g] = p1.y;
+    colors[3 * g] = p1.z;
+    colors[3 * g + 1] = p1.w;
+    colors[3 * g + 2] = pv.p2[g];
+    depth[g] = __uint_as_float(pv.dkey[g]);
+    const ushort4 r = pv.rect[g];
+    const bool any = pv.cnt[g] > 0;
+    rects[4 * g] = any ? r.x : 0;
+    rects[4 * g + 1] = any ? r.y : -1;
+    rects[4 * g + 2] = any ? r.z : 0;
+    rects[4 * g + 3] = any ? r.w : -1;
+}
+
+extern "C" gs_status gs_train_project_view(const gs_gaussians* params, int64_t n,
+                                           const gs_camera* cam, const gs_train_config* cfg,
+                                           float* means2d, float* conic, float* opacity,
+                                           float* colors, float* depth, int32_t* rects,
+                                           float* vis_counts, uint32_t* sorted_ids,
+                                           int32_t* tile_ranges, int64_t pair_capacity,
+                                           int64_t* pairs_host, void* workspace,
+                                           size_t workspace_bytes, void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(params && cam && means2d && conic && opacity && colors && depth && rects &&
+                 vis_counts && sorted_ids && tile_ranges && pairs_host && n > 0,
+                 "gs_train_project_view: bad arguments");
+    GS_ARG_CHECK(pair_capacity >= 1 && pair_capacity < (1ll << 30),
+                 "gs_train_project_view: bad pair_capacity");
+    Workspace ws(workspace, workspace_bytes);
+    TrainWs L;
+    train_layout(ws, L, n, 1, cam->height, cam->width, cfg->tile_size, pair_capacity);
+    GS_ARG_CHECK(ws.ok(), "gs_train_project_view: workspace too small");
+    GS_CUDA_CHECK(cudaMemsetAsync(L.err, 0, sizeof(unsigned int), st));
+    GS_CUDA_CHECK(cudaMemsetAsync(L.touch, 0, n * sizeof(uint64_t), st));
+    GS_CUDA_CHECK(cudaMemsetAsync(vis_counts, 0, n * sizeof(float), st));
+    const TCam tc = make_tcam(*cam);
+    const TCfg c = make_tcfg(*cfg, cam->height, cam->width);
+    gs_status s = project_and_sort_view(gconst(params), n, tc, c, 0, L, pair_capacity, vis_counts,
+                                        false, st);
+    if (s != GS_OK) return s;
+    k_export_projection<<<div_up(n, 256), 256, 0, st>>>(L.pv, n, means2d, conic, opacity, colors,
+                                                        depth, rects);
+    GS_CHECK_LAUNCH();
+    const int tiles = c.tiles_x * c.tiles_y;
+    GS_CUDA_CHECK(cudaMemcpyAsync(tile_ranges, L.ranges, tiles * sizeof(int2), cudaMemcpyDeviceToDevice, st));
+    unsigned int herr = 0;
+    GS_CUDA_CHECK(cudaMemcpyAsync(pairs_host, L.pairs, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
+    GS_CUDA_CHECK(cudaMemcpyAsync(&herr, L.err, sizeof(unsigned int), cudaMemcpyDeviceToHost, st));
+    GS_CUDA_CHECK(cudaStreamSynchronize(st));
+    if (herr & DEV_OVERFLOW) {
+        set_error("gs_train_project_view: %lld pairs exceed capacity %lld", (long long)*pairs_host,
+                  (long long)pair_capacity);
+        return GS_ERR_OVERFLOW;
+    }
+    if (herr & DEV_TIMEOUT) {
+        set_error("gs_train_project_view: radix sort look-back timed out");
+        return GS_ERR_TIMEOUT;
+    }
+    if (*pairs_host > 0)
+        GS_CUDA_CHECK(cudaMemcpyAsync(sorted_ids, L.svals, *pairs_host * sizeof(uint32_t),
+                                      cudaMemcpyDeviceToDevice, st));
+    return GS_OK;
+}
+
+static AdamParams make_adam(const gs_gaussians* p, const gs_gaussians* m, const gs_gaussians* v,
+                            const gs_gaussians* g, int64_t n, int64_t step,
+                            const gs_train_config* cfg) {
+    AdamParams A;
+    const int K = (cfg->sh_degree + 1) * (cfg->sh_degree + 1);
+    const double t = (double)step + 1.0;
+    const double bc1 = 1.0 - std::pow((double)cfg->beta1, t);
+    const double bc2 = 1.0 - std::pow((double)cfg->beta2, t);
+    A.b1 = cfg->beta1;
+    A.b2 = cfg->beta2;
+    A.isq_bc2 = (float)(1.0 / std::sqrt(bc2));
+    A.eps = cfg->eps;
+    A.bf16 = cfg->bf16_moments;
+    float* P[5] = {p->means, p->log_scales, p->quats, p->opacity_logits, p->sh};
+    float* Mm[5] = {m->means, m->log_scales, m->quats, m->opacity_logits, m->sh};
+    float* Vv[5] = {v->means, v->log_scales, v->quats, v->opacity_logits, v->sh};
+    const float* Gg[5] = {g->means, g->log_scales, g->quats, g->opacity_logits, g->sh};
+    const int width[5] = {3, 3, 4, 1, 3 * K};
+    const double lr[5] = {cfg->lr_means, cfg->lr_log_scales, cfg->lr_quats, cfg->lr_opacity,
+                          cfg->lr_sh_dc};
+    for (int i = 0; i < 5; ++i) {
+        A.grp[i].p = P[i];
+        A.grp[i].m = Mm[i];
+        A.grp[i].v = Vv[i];
+        A.grp[i].g = Gg[i];
+        A.grp[i].count = n * width[i];
+        A.grp[i].width = width[i];
+        A.grp[i].step_size = (float)(lr[i] / bc1);
+        A.grp[i].step_size_rest = (float)((double)cfg->lr_sh_rest / bc1);
+        A.grp[i].sh_band_split = (i == 4) ? 1 : 0;
+    }
+    return A;
+}
+
+static gs_status launch_adam(const AdamParams& A, const float* vis, const unsigned int* err,
+                             cudaStream_t st) {
+    KernelTimer kt("sparse_adam", st);
+    for (int i = 0; i < 5; ++i) {
+        const int64_t cnt = A.grp[i].count;
+        const unsigned int blocks = (unsigned int)std::min<int64_t>(div_up(cnt, 256), kNumSMs * 16);
+        k_sparse_adam<<<blocks, 256, 0, st>>>(A, vis, err, i);
+        GS_CHECK_LAUNCH();
+    }
+    return GS_OK;
+}
+
+extern "C" gs_status gs_sparse_adam(const gs_gaussians* params, const gs_gaussians* exp_avg,
+                                    const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
+                                    const float* vis_counts, int64_t n, int64_t step,
+                                    const gs_train_config* cfg, const unsigned int* error_word,
+                                    void* stream) {
+    clear_error();
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(params && exp_avg && exp_avg_sq && grads && vis_counts && n >= 0 && step >= 0,
+                 "gs_sparse_adam: bad arguments");
+    if (n == 0) return GS_OK;
+    const AdamParams A = make_adam(params, exp_avg, exp_avg_sq, grads, n, step, cfg);
+    return launch_adam(A, vis_counts, error_word, (cudaStream_t)stream);
+}
+
+extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussians* exp_avg,
+                                   const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
+                                   float* vis_counts, int64_t n, int64_t step,
+                                   const gs_camera* cams, const float* const* targets,
+                                   int32_t n_views, const gs_train_config* cfg,
+                                   int32_t apply_adam, float* view_losses, float* images,
+                                   float* grad2d_out, int64_t* pairs, int64_t pair_capacity,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(params && grads && vis_counts && cams && targets && view_losses,
+                 "gs_train_step: null argument");
+    GS_ARG_CHECK(!apply_adam || (exp_avg && exp_avg_sq), "gs_train_step: Adam needs moments");
+    GS_ARG_CHECK(n > 0 && n < (1ll << 32), "gs_train_step: n must be in [1, 2^32)");
+    GS_ARG_CHECK(n_views >= 1 && n_views <= 64, "gs_train_step: n_views must be in [1, 64]");
+    GS_ARG_CHECK(pair_capacity >= 1 && pair_capacity < (1ll << 30),
+                 "gs_train_step: pair_capacity must be in [1, 2^30)");
+    GS_ARG_CHECK(((uintptr_t)params->quats & 15) == 0 && ((uintptr_t)grads->quats & 15) == 0,
+                 "gs_train_step: quats must be 16-byte aligned");
+    int H = 0, W = 0;
+    for (int v = 0; v < n_views; ++v) {
+        GS_ARG_CHECK(cams[v].height > 0 && cams[v].width > 0, "gs_train_step: bad image size");
+        GS_ARG_CHECK(targets[v] != nullptr, "gs_train_step: null target");
+        H = std::max(H, (int)cams[v].height);
+        W = std::max(W, (int)cams[v].width);
+    }
+    Workspace ws(workspace, workspace_bytes);
+    TrainWs L;
+    train_layout(ws, L, n, n_views, H, W, cfg->tile_size, pair_capacity);
+    GS_ARG_CHECK(ws.ok(), "gs_train_step: workspace too small (%zu < %zu)", workspace_bytes,
+                 gs_train_workspace_size(n, cfg->sh_degree, n_views, H, W, cfg->tile_size,
+                                         pair_capacity));
+    const GConst P = gconst(params);
+    GS_CUDA_CHECK(cudaMemsetAsync(L.err, 0, sizeof(unsigned int), st));
+    GS_CUDA_CHECK(cudaMemsetAsync(L.touch, 0, n * sizeof(uint64_t), st));
+    GS_CUDA_CHECK(cudaMemsetAsync(vis_counts, 0, n * sizeof(float), st));
+    GS_CUDA_CHECK(cudaMemsetAsync(L.loss_acc, 0, 2 * n_views * sizeof(double), st));
+    std::vector<TCam> hc(n_views);
+    for (int v = 0; v < n_views; ++v) hc[v] = make_tcam(cams[v]);
+    // A copy from pageable memory returns once the source has been staged, so the host
+    // vector may go out of scope afterwards.
+    GS_CUDA_CHECK(cudaMemcpyAsync(L.cams, hc.data(), n_views * sizeof(TCam), cudaMemcpyHostToDevice, st));
+
+    LossCfg LC;
+    {
+        double taps[11], sum = 0.0;
+        for (int k = 0; k < 11; ++k) {
+            const double xk = k - 5;
+            taps[k] = std::exp(-(xk * xk) / (2.0 * 1.5 * 1.5));
+            sum += taps[k];
+        }
+        for (int k = 0; k < 11; ++k) LC.taps[k] = (float)(taps[k] / sum);
+        // (1 - lambda) L1 [+ lambda (1 - SSIM)]; a pure L1 loss is lambda = 0 without SSIM.
+        LC.lambda = cfg->lambda_dssim;
+    }
+
+    for (int v = 0; v < n_views; ++v) {
+        const int vh = cams[v].height, vw = cams[v].width;
+        const TCfg c = make_tcfg(*cfg, vh, vw);
+        gs_status s = project_and_sort_view(P, n, hc[v], c, v, L, pair_capacity, vis_counts, true, st);
+        if (s != GS_OK) return s;
+        float* img = images ? images + (size_t)v * vh * vw * 3 : L.image;
+        const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
+        {
+            KernelTimer kt("raster_fwd", st);
+            if (c.tile == 16)
+                k_train_fwd<16><<<tiles, 256, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
+            else
+                k_train_fwd<32><<<tiles, 1024, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
+            GS_CHECK_LAUNCH();
+        }
+        LC.H = vh;
+        LC.W = vw;
+        LC.inv_n = (float)(1.0 / (3.0 * vh * vw));
+        {
+            KernelTimer kt("loss", st);
+            const int64_t n3 = (int64_t)vh * vw * 3;
+            if (cfg->use_ssim) {
+                dim3 grid(div_up(vw, kLossTile), div_up(vh, kLossTile));
+                k_ssim_fwd<<<grid, kLossTile * kLossTile, 0, st>>>(img, targets[v], LC, L.dmu, L.dxx,
+                                                                   L.dxy, L.loss_acc + 2 * v);
+                GS_CHECK_LAUNCH();
+                k_ssim_bwd<<<grid, kLossTile * kLossTile, 0, st>>>(img, targets[v], L.dmu, L.dxx, L.dxy,
+                                                                   LC, L.dimg);
+            } else {
+                k_loss_l1<<<(unsigned int)std::min<int64_t>(div_up(n3, 256), kNumSMs * 8), 256, 0, st>>>(
+                    img, targets[v], n3, LC, L.dimg, L.loss_acc + 2 * v);
+            }
+            GS_CHECK_LAUNCH();
+            k_loss_finalize<<<1, 1, 0, st>>>(L.loss_acc + 2 * v, LC, cfg->use_ssim, view_losses + v);
+            GS_CHECK_LAUNCH();
+        }
+        {
+            KernelTimer kt("raster_bwd", st);
+            float* g2 = L.grad2d + (size_t)v * n * kGradStride;
+            if (c.tile == 16)
+                k_train_bwd<16><<<tiles, 256, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
+                                                       L.final_T, L.ncon, g2);
+            else
+                k_train_bwd<32><<<tiles, 1024, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
+                                                        L.final_T, L.ncon, g2);
+            GS_CHECK_LAUNCH();
+        }
+        if (grad2d_out) {
+            k_export_grad2d<<<div_up(n, 256), 256, 0, st>>>(L.grad2d, L.touch, n, v,
+                                                            grad2d_out + (size_t)v * n * 9);
+            GS_CHECK_LAUNCH();
+        }
+    }
+    if (pairs) {
+        GS_CUDA_CHECK(cudaMemcpyAsync(pairs, L.pairs, n_views * sizeof(int64_t),
+                                      cudaMemcpyDeviceToDevice, st));
+    }
+    {
+        KernelTimer kt("param_bwd", st);
+        TCfg c = make_tcfg(*cfg, H, W);
+        GMut G{grads->means, grads->log_scales, grads->quats, grads->opacity_logits, grads->sh};
+        const unsigned int nb = div_up(n, 128);
+        switch (cfg->sh_degree) {
+            case 0: k_param_bwd<0><<<nb, 128, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            case 1: k_param_bwd<1><<<nb, 128, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            case 2: k_param_bwd<2><<<nb, 128, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            default: k_param_bwd<3><<<nb, 128, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+        }
+        GS_CHECK_LAUNCH();
+    }
+    if (apply_adam) {
+        const AdamParams A = make_adam(params, exp_avg, exp_avg_sq, grads, n, step, cfg);
+        gs_status s = launch_adam(A, vis_counts, L.err, st);
+        if (s != GS_OK) return s;
+    }
+    return GS_OK;
+}

@@ -1,0 +1,336 @@
+"""Training step on the B200: torch front end of the libgs200 training C ABI.
+
+Names follow the reference trainer (gsplat/train_oracle.py): optimizer-space params
+``means, log_scales, quats, opacity_logits, sh``; ``RenderConfig``-style render rules;
+``DEFAULT_LR``; ``sparse_adam_step``. One ``Trainer.step`` runs, for every view of this
+rank, projection + SH -> key emission -> radix sort -> tile ranges -> forward raster ->
+loss -> backward raster, then one fused projection backward over all views and (on one
+GPU) the sparse Adam update, all on one CUDA stream through ``gs_train_step``.
+
+Multi-GPU (data parallel over views): each rank renders its own views; the per-Gaussian
+gradients and visibility counts -- one contiguous fp32 buffer -- are summed with an NCCL
+allreduce (torch.distributed), then every rank applies the identical sparse Adam step.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._lib import check, lib
+
+PARAM_NAMES = ("means", "log_scales", "quats", "opacity_logits", "sh")
+DEFAULT_LR = {"means": 1.6e-4, "log_scales": 5e-3, "quats": 1e-3, "opacity_logits": 0.05,
+              "sh_dc": 2.5e-3, "sh_rest": 2.5e-3 / 20.0}
+
+
+class GsGaussians(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_void_p) for n in PARAM_NAMES]
+
+
+class GsCamera(ctypes.Structure):
+    _fields_ = [("w2c", ctypes.c_float * 16), ("K", ctypes.c_float * 9),
+                ("height", ctypes.c_int32), ("width", ctypes.c_int32)]
+
+
+class GsTrainConfig(ctypes.Structure):
+    _fields_ = [("sh_degree", ctypes.c_int32), ("tile_size", ctypes.c_int32),
+                ("near_plane", ctypes.c_float), ("lowpass", ctypes.c_float),
+                ("alpha_max", ctypes.c_float), ("alpha_min", ctypes.c_float),
+                ("t_min", ctypes.c_float), ("background", ctypes.c_float * 3),
+                ("use_ssim", ctypes.c_int32), ("lambda_dssim", ctypes.c_float),
+                ("lr_means", ctypes.c_float), ("lr_log_scales", ctypes.c_float),
+                ("lr_quats", ctypes.c_float), ("lr_opacity", ctypes.c_float),
+                ("lr_sh_dc", ctypes.c_float), ("lr_sh_rest", ctypes.c_float),
+                ("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("eps", ctypes.c_float),
+                ("bf16_moments", ctypes.c_int32)]
+
+
+_G = ctypes.POINTER(GsGaussians)
+_C = ctypes.POINTER(GsCamera)
+_CFG = ctypes.POINTER(GsTrainConfig)
+_vp, _i64, _i32, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32, ctypes.c_size_t
+lib.gs_train_step.restype = ctypes.c_int
+lib.gs_train_step.argtypes = [_G, _G, _G, _G, _vp, _i64, _i64, _C, ctypes.POINTER(_vp), _i32,
+                              _CFG, _i32, _vp, _vp, _vp, _vp, _i64, _vp, _sz, _vp]
+lib.gs_train_workspace_size.restype = _sz
+lib.gs_train_workspace_size.argtypes = [_i64, _i32, _i32, _i32, _i32, _i32, _i64]
+lib.gs_train_count_pairs.restype = ctypes.c_int
+lib.gs_train_count_pairs.argtypes = [_G, _i64, _C, _i32, _CFG, ctypes.POINTER(_i64), _vp, _sz, _vp]
+lib.gs_sparse_adam.restype = ctypes.c_int
+lib.gs_sparse_adam.argtypes = [_G, _G, _G, _G, _vp, _i64, _i64, _CFG, _vp, _vp]
+lib.gs_train_project_view.restype = ctypes.c_int
+lib.gs_train_project_view.argtypes = [_G, _i64, _C, _CFG, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                      _vp, _vp, _i64, ctypes.POINTER(_i64), _vp, _sz, _vp]
+
+
+@dataclass
+class TrainConfig:
+    """gsplat/train_oracle.py:64-71 RenderConfig + loss + Adam settings."""
+    sh_degree: int = 3
+    tile_size: int = 16
+    near: float = 0.2
+    lowpass: float = 0.3
+    alpha_max: float = 0.99
+    alpha_min: float = 1.0 / 255.0
+    t_min: float = 1e-4
+    background: tuple = (0.0, 0.0, 0.0)
+    use_ssim: bool = True
+    lambda_dssim: float = 0.2
+    lr: dict = field(default_factory=lambda: dict(DEFAULT_LR))
+    betas: tuple = (0.9, 0.999)
+    eps: float = 1e-15
+    bf16_moments: bool = False
+
+    def c_struct(self) -> GsTrainConfig:
+        c = GsTrainConfig()
+        c.sh_degree, c.tile_size = int(self.sh_degree), int(self.tile_size)
+        c.near_plane, c.lowpass = self.near, self.lowpass
+        c.alpha_max, c.alpha_min, c.t_min = self.alpha_max, self.alpha_min, self.t_min
+        for i in range(3):
+            c.background[i] = float(self.background[i])
+        c.use_ssim, c.lambda_dssim = int(bool(self.use_ssim)), float(self.lambda_dssim)
+        c.lr_means, c.lr_log_scales = self.lr["means"], self.lr["log_scales"]
+        c.lr_quats, c.lr_opacity = self.lr["quats"], self.lr["opacity_logits"]
+        c.lr_sh_dc, c.lr_sh_rest = self.lr["sh_dc"], self.lr["sh_rest"]
+        c.beta1, c.beta2, c.eps = self.betas[0], self.betas[1], self.eps
+        c.bf16_moments = int(bool(self.bf16_moments))
+        return c
+
+
+def camera_struct(w2c, K, height, width) -> GsCamera:
+    c = GsCamera()
+    w = np.asarray(w2c, np.float32).reshape(16)
+    k = np.asarray(K, np.float32).reshape(9)
+    for i in range(16):
+        c.w2c[i] = float(w[i])
+    for i in range(9):
+        c.K[i] = float(k[i])
+    c.height, c.width = int(height), int(width)
+    return c
+
+
+def _group_sizes(n: int, K: int) -> list[int]:
+    return [3 * n, 3 * n, 4 * n, n, 3 * K * n]
+
+
+class GroupBuffer:
+    """The five parameter groups (or moments, or gradients) of N Gaussians in one flat
+    fp32 device buffer, each group starting on a 16-byte boundary. ``extra`` floats after
+    the groups hold the visibility counts of a gradient buffer, so one allreduce covers
+    gradients and counts."""
+
+    def __init__(self, n: int, sh_degree: int, device, extra: int = 0):
+        self.n, self.K = n, (sh_degree + 1) ** 2
+        sizes = _group_sizes(n, self.K)
+        self.offsets = []
+        off = 0
+        for s in sizes:
+            self.offsets.append(off)
+            off += (s + 3) // 4 * 4
+        self.extra_offset = off
+        self.flat = torch.zeros(off + extra, dtype=torch.float32, device=device)
+        shapes = [(n, 3), (n, 3), (n, 4), (n,), (n, self.K, 3)]
+        self.views = {name: self.flat[o:o + s].view(*shape)
+                      for name, o, s, shape in zip(PARAM_NAMES, self.offsets, sizes, shapes)}
+        self.extra = self.flat[off:off + extra]
+
+    def __getitem__(self, k):
+        return self.views[k]
+
+    def c_struct(self) -> GsGaussians:
+        return GsGaussians(*[self.views[k].data_ptr() for k in PARAM_NAMES])
+
+    def load(self, params: dict) -> None:
+        for k in PARAM_NAMES:
+            src = params[k]
+            src = torch.from_numpy(np.ascontiguousarray(src, np.float32)) if isinstance(src, np.ndarray) else src
+            self.views[k].copy_(src.reshape(self.views[k].shape))
+
+    def numpy(self) -> dict:
+        return {k: v.detach().cpu().numpy() for k, v in self.views.items()}
+
+
+class Trainer:
+    """Training state (params, Adam moments, gradients, workspace) of one rank.
+
+    ``step(cams, targets)`` runs one step over this rank's views; cams is a list of
+    (w2c, K, H, W) and targets a list of (H, W, 3) fp32 device tensors (or numpy arrays).
+    Returns the per-view losses as a device tensor (no host synchronisation unless
+    ``check`` is set, which also retries with a larger pair capacity on overflow).
+    """
+
+    def __init__(self, params: dict, cfg: TrainConfig, n_views: int, height: int, width: int,
+                 pair_capacity: int | None = None, device=None, process_group=None):
+        if not torch.cuda.is_available():
+            raise RuntimeError("Trainer needs a CUDA device")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        self.cfg = cfg
+        self.ccfg = cfg.c_struct()
+        self.n = int(np.asarray(params["means"]).shape[0]) if not isinstance(params["means"], torch.Tensor) \
+            else int(params["means"].shape[0])
+        self.n_views, self.H, self.W = int(n_views), int(height), int(width)
+        self.params = GroupBuffer(self.n, cfg.sh_degree, self.device)
+        self.params.load(params)
+        self.m = GroupBuffer(self.n, cfg.sh_degree, self.device)
+        self.v = GroupBuffer(self.n, cfg.sh_degree, self.device)
+        self.grads = GroupBuffer(self.n, cfg.sh_degree, self.device, extra=self.n + 1)
+        self.vis_counts = self.grads.extra[:self.n]
+        self.err_slot = self.grads.extra[self.n:]
+        self.losses = torch.zeros(self.n_views, dtype=torch.float32, device=self.device)
+        self.pairs = torch.zeros(self.n_views, dtype=torch.int64, device=self.device)
+        self.step_count = 0
+        self.pg = process_group
+        self.world = torch.distributed.get_world_size(process_group) \
+            if torch.distributed.is_available() and torch.distributed.is_initialized() else 1
+        self._err_i32 = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.capacity = int(pair_capacity) if pair_capacity else 0
+        self.ws = None
+        self._alloc(max(self.capacity, 1))
+
+    def _alloc(self, capacity: int) -> None:
+        self.capacity = capacity
+        nb = lib.gs_train_workspace_size(self.n, self.cfg.sh_degree, self.n_views, self.H, self.W,
+                                         self.cfg.tile_size, capacity)
+        self.ws = None
+        torch.cuda.empty_cache()
+        self.ws = torch.empty(nb, dtype=torch.uint8, device=self.device)
+
+    def _cams(self, cams):
+        arr = (GsCamera * len(cams))()
+        for i, (w2c, K, H, W) in enumerate(cams):
+            arr[i] = camera_struct(w2c, K, H, W)
+        return arr
+
+    def count_pairs(self, cams) -> list[int]:
+        arr = self._cams(cams)
+        out = (_i64 * len(cams))()
+        p = self.params.c_struct()
+        check(lib.gs_train_count_pairs(ctypes.byref(p), self.n, arr, len(cams), ctypes.byref(self.ccfg),
+                                       out, self.ws.data_ptr(), self.ws.numel(),
+                                       torch.cuda.current_stream().cuda_stream))
+        return [int(x) for x in out]
+
+    def ensure_capacity(self, cams, headroom: float = 1.2) -> None:
+        need = max(self.count_pairs(cams))
+        if need > self.capacity:
+            self._alloc(int(need * headroom) + 4096)
+
+    def _targets(self, targets):
+        ts = []
+        for t in targets:
+            if isinstance(t, np.ndarray):
+                t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
+            ts.append(t.to(self.device, torch.float32).contiguous())
+        return ts
+
+    def step(self, cams, targets, check_errors: bool = False, images=None, grad2d=None):
+        if len(cams) != self.n_views:
+            raise ValueError(f"expected {self.n_views} views, got {len(cams)}")
+        tg = self._targets(targets)
+        self._keep = tg
+        tptr = (ctypes.c_void_p * len(tg))(*[t.data_ptr() for t in tg])
+        arr = self._cams(cams)
+        st = torch.cuda.current_stream().cuda_stream
+        p, m, v, g = (b.c_struct() for b in (self.params, self.m, self.v, self.grads))
+        single = self.world == 1
+        while True:
+            code = lib.gs_train_step(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
+                                     self.vis_counts.data_ptr(), self.n, self.step_count, arr, tptr,
+                                     len(cams), ctypes.byref(self.ccfg), int(single),
+                                     self.losses.data_ptr(),
+                                     None if images is None else images.data_ptr(),
+                                     None if grad2d is None else grad2d.data_ptr(),
+                                     self.pairs.data_ptr(), self.capacity, self.ws.data_ptr(),
+                                     self.ws.numel(), st)
+            check(code)
+            if not single:
+                self._allreduce_and_adam(st)
+            if not check_errors:
+                break
+            if single:
+                code = lib.gs_workspace_error(self.ws.data_ptr(), st)
+                failed = code != _lib.GS_OK
+            else:  # the reduced flag: every rank takes the same branch
+                failed = bool(self.err_slot.item() > 0)
+                code = lib.gs_workspace_error(self.ws.data_ptr(), st) if failed else _lib.GS_OK
+            if failed and (code in (_lib.GS_ERR_OVERFLOW, _lib.GS_OK)):
+                # Adam was skipped on the device: grow the pair buffers and redo the step.
+                self._alloc(max(int(self.pairs.max().item() * 1.25) + 4096, self.capacity))
+                continue
+            check(code)
+            break
+        self.step_count += 1
+        return self.losses
+
+    def _allreduce_and_adam(self, st) -> None:
+        import torch.distributed as dist
+        # error word of this rank's step (first 4 bytes at the workspace's first 256-byte
+        # boundary) rides along in the reduced buffer so every rank agrees on skipping Adam
+        off = (-self.ws.data_ptr()) % 256
+        errw = self.ws[off:off + 4].view(torch.int32)
+        self.err_slot.copy_((errw != 0).to(torch.float32))
+        dist.all_reduce(self.grads.flat, group=self.pg)
+        self._err_i32.copy_((self.err_slot > 0).to(torch.int32))
+        p, m, v, g = (b.c_struct() for b in (self.params, self.m, self.v, self.grads))
+        check(lib.gs_sparse_adam(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
+                                 self.vis_counts.data_ptr(), self.n, self.step_count,
+                                 ctypes.byref(self.ccfg), self._err_i32.data_ptr(), st))
+
+    def project_view(self, w2c, K, H, W) -> dict:
+        """Projection, intersections, sorted pairs and tile ranges of one view (parity API)."""
+        n, d = self.n, self.device
+        out = {"means2d": torch.empty((n, 2), device=d), "conic": torch.empty((n, 3), device=d),
+               "opacity": torch.empty(n, device=d), "colors": torch.empty((n, 3), device=d),
+               "depth": torch.empty(n, device=d),
+               "rects": torch.empty((n, 4), dtype=torch.int32, device=d),
+               "visible": torch.empty(n, device=d)}
+        ts = self.cfg.tile_size
+        tiles = ((W + ts - 1) // ts) * ((H + ts - 1) // ts)
+        cap = max(self.capacity, 1)
+        sids = torch.empty(cap, dtype=torch.int32, device=d)
+        rng = torch.empty((tiles, 2), dtype=torch.int32, device=d)
+        P = _i64(0)
+        ws = torch.empty(lib.gs_train_workspace_size(n, self.cfg.sh_degree, 1, H, W, ts, cap),
+                         dtype=torch.uint8, device=d)
+        p = self.params.c_struct()
+        cam = camera_struct(w2c, K, H, W)
+        check(lib.gs_train_project_view(
+            ctypes.byref(p), n, ctypes.byref(cam), ctypes.byref(self.ccfg),
+            *[out[k].data_ptr() for k in ("means2d", "conic", "opacity", "colors", "depth", "rects",
+                                          "visible")],
+            sids.data_ptr(), rng.data_ptr(), cap, ctypes.byref(P), ws.data_ptr(), ws.numel(),
+            torch.cuda.current_stream().cuda_stream))
+        out["sorted_ids"] = sids[:P.value]
+        out["tile_ranges"] = rng
+        out["pairs"] = P.value
+        return out
+
+
+def smoke_step() -> None:
+    """One small SH3 training step on cuda:0 checked against the oracle (used by smoke())."""
+    from oracle import train as ot
+    from . import scenes
+    params = scenes.cluster_scene(3000, sh_degree=3, seed=5)
+    params["means"] = (params["means"] * 0.5).astype(np.float32)
+    params["log_scales"] = (params["log_scales"] + 1.5).astype(np.float32)
+    H, W = 64, 96
+    cams = [(scenes.look_at((0.2, -0.1, -3.5)), scenes.intrinsics(90.0, W, H), H, W)]
+    tg = [np.random.default_rng(3).uniform(0, 1, (H, W, 3)).astype(np.float32)]
+    cfg = TrainConfig(sh_degree=3, tile_size=16)
+    tr = Trainer(params, cfg, 1, H, W)
+    tr.ensure_capacity(cams)
+    images = torch.empty((1, H, W, 3), device=tr.device)
+    tr.step(cams, tg, check_errors=True, images=images)
+    ocfg = ot.Cfg(sh_degree=3, tile=16)
+    pr = ot.project(params, cams[0][0], cams[0][1], H, W, ocfg)
+    fw = ot.forward(pr, H, W, ocfg)
+    ok = ~fw["ties"]
+    err = float(np.abs(images[0].cpu().numpy() - fw["image"])[ok].max())
+    L, _ = ot.loss_ssim(fw["image"], tg[0])
+    lerr = abs(float(tr.losses[0].item()) - L) / max(abs(L), 1e-12)
+    assert err <= 1e-4, f"train forward image max-abs {err}"
+    assert lerr <= 1e-4, f"train loss rel err {lerr}"

@@ -1,0 +1,238 @@
+"""Training-step benchmark (bench.py --workload train).
+
+Config ("C5"): 6,000,000 Gaussians, SH degree 3, 64-cluster
+distributions of gsplat_tt_b200.scenes; 32 views of 1920x1080 (f = 1500) on a sphere of
+radius 5 looking at the origin; loss 0.8 L1 + 0.2 (1 - SSIM); sparse Adam with betas
+(0.9, 0.999), eps 1e-15 and the per-group learning rates of configs[3]. The views are split
+evenly over the ranks (strong scaling: the step's total work is fixed); gradients are summed
+with one NCCL allreduce. ``GS_BENCH_CONFIG=c4`` selects configs[3] (3M Gaussians, 8 views of
+1600x1056, f = 1300, radius 4) instead.
+"""
+from __future__ import annotations
+
+import os
+import time
+
+import numpy as np
+import torch
+
+from . import scenes
+from ._lib import check, lib, timing_report
+from .train import TrainConfig, Trainer
+
+LR_BASELINE = {"means": 1.6e-4, "log_scales": 5e-3, "quats": 1e-3, "opacity_logits": 5e-2,
+               "sh_dc": 2.5e-3, "sh_rest": 2.5e-3 / 20.0}
+
+
+def config_name() -> str:
+    return os.environ.get("GS_BENCH_CONFIG", "c5")
+
+
+def view_targets(cams, first_index: int) -> list[np.ndarray]:
+    out = []
+    for i, c in enumerate(cams):
+        rng = np.random.default_rng(1000 + first_index + i)
+        out.append(rng.uniform(0.0, 1.0, (c.height, c.width, 3)).astype(np.float32))
+    return out
+
+
+def train_cfg() -> TrainConfig:
+    return TrainConfig(sh_degree=3, tile_size=16, use_ssim=True, lambda_dssim=0.2,
+                       lr=dict(LR_BASELINE), betas=(0.9, 0.999), eps=1e-15)
+
+
+def _kernel_bytes(name: str, n: int, views: int, pairs: float, px: int) -> float | None:
+    """Algorithmic DRAM bytes of one launch of the HBM-bound kernels (per view unless
+    noted): projection reads the SH3 params (236 B) and writes the 2D record, key and rect
+    (48 + 16 B) per Gaussian; the sparse Adam (one launch per parameter group, averaged)
+    reads p, m, v, g and writes p, m, v for the 59 values of each row; the emission writes
+    12 B per pair."""
+    if name == "train_project":
+        return n * (236.0 + 64.0)
+    if name == "sparse_adam":
+        return n * 59 * 28.0
+    if name == "train_emit":
+        return pairs * 12.0 + n * 16.0
+    return None
+
+
+def run(args, rank: int, world: int, local: int) -> dict:
+    from bench import ClockSampler, barrier, max_over_ranks, measured_peaks  # noqa: E402
+    name = config_name()
+    c = scenes.CONFIGS[name]
+    dev = torch.device("cuda", local)
+    V = c["views"]
+    if V % world != 0:
+        raise SystemExit(f"{V} views do not split evenly over {world} GPUs")
+    per = V // world
+    cams_all = scenes.training_cameras(name)
+    mine = cams_all[rank * per:(rank + 1) * per]
+    H, W = c["height"], c["width"]
+    params = scenes.cluster_scene(c["n"], sh_degree=3, seed=0)
+    targets_host = view_targets(mine, rank * per)
+    cfg = train_cfg()
+    tr = Trainer(params, cfg, per, H, W, device=dev)
+    del params
+    cams = [(cm.w2c, cm.K, H, W) for cm in mine]
+    pairs0 = tr.count_pairs(cams)
+    tr._alloc(int(max(pairs0) * 1.3) + 4096)
+    targets = [torch.from_numpy(t).to(dev) for t in targets_host]
+    st = torch.cuda.current_stream()
+
+    for i in range(args.warmup):
+        tr.step(cams, targets, check_errors=(i == 0))
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier(world)
+        torch.cuda.synchronize()
+        e0.record()
+        for _ in range(args.steps):
+            tr.step(cams, targets)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier(world)
+    if lib.gs_workspace_error(tr.ws.data_ptr(), st.cuda_stream) != 0:
+        raise RuntimeError("a timed step overflowed its pair buffers or timed out")
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    total_px = V * H * W
+    value = total_px / (ms / 1e3) / 1e6
+    loss_now = float(tr.losses.sum().item())
+
+    # e2e: the public API with the step's inputs (target images) copied from pinned host
+    # memory every step and the loss read back to the host.
+    pinned = [torch.from_numpy(t).pin_memory() for t in targets_host]
+    for _ in range(2):
+        for t, h in zip(targets, pinned):
+            t.copy_(h, non_blocking=True)
+        tr.step(cams, targets)
+        loss_host = tr.losses.sum().item()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    e0.record()
+    for _ in range(args.steps):
+        for t, h in zip(targets, pinned):
+            t.copy_(h, non_blocking=True)
+        tr.step(cams, targets)
+        loss_host = tr.losses.sum().item()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    del loss_host, t0
+
+    # per-kernel device times (CUDA events on the launching stream), one more short loop
+    lib.gs_timing_reset()
+    lib.gs_timing_enable(1)
+    ksteps = max(2, min(args.steps, 5))
+    for _ in range(ksteps):
+        tr.step(cams, targets)
+    torch.cuda.synchronize()
+    lib.gs_timing_enable(0)
+    rep = timing_report()
+    lib.gs_timing_reset()
+    pairs = tr.pairs.float().mean().item()
+    peaks = measured_peaks()
+    per_kernel = {}
+    for k, (tot, cnt) in rep.items():
+        avg = tot / cnt
+        entry = {"ms_per_launch": avg, "launches_per_step": cnt / ksteps,
+                 "ms_per_step": tot / ksteps}
+        b = _kernel_bytes(k, tr.n, per, pairs, H * W)
+        if k == "sparse_adam":
+            b = b / 1.0  # one timer covers the five group launches
+        if b is not None:
+            gbs = b / (avg / 1e3) / 1e9
+            entry.update({"algorithmic_bytes": b, "achieved_gbs": gbs,
+                          "frac_hbm": gbs / peaks["hbm_gbs"]})
+        per_kernel[k] = entry
+    dom = max(per_kernel.items(), key=lambda kv: kv[1]["ms_per_step"])
+    radix_pass = per_kernel.get("radix_pass")
+    out = {
+        "metric": "train-step Mpix/s (fwd+bwd+Adam)",
+        "value": value, "unit": "Mpix/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{name.upper()} train step: {c['n']} Gaussians SH3, {V} views "
+                               f"{W}x{H} ({per} per GPU), L1+SSIM, sparse Adam",
+                   "gaussians": c["n"], "views": V, "width": W, "height": H, "tile": 16,
+                   "parallelism": f"dp{world} over views + NCCL allreduce",
+                   "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},
+        "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
+                "h2d_bytes_per_step": int(sum(t.numel() * 4 for t in targets_host)),
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": int(sum(v["launches_per_step"] for v in per_kernel.values())),
+        "pairs_per_view": pairs, "loss": loss_now,
+        "kernels": per_kernel,
+        "clocks": clk.summary(),
+    }
+    dom_name, d = dom
+    if "achieved_gbs" in d:
+        out["roofline"] = {"bound": "hbm", "kernel": dom_name, "achieved": d["achieved_gbs"],
+                           "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": d["frac_hbm"],
+                           "traffic": None, "peak_source": peaks["source"]}
+    else:
+        # The rasterisers are not DRAM-bound (their pair records and pixel state stay in
+        # L2 / shared memory); report the dominant kernel's DRAM fraction honestly from
+        # its own algorithmic bytes: per pair 36 B of record reads, per pixel 48 B (fwd:
+        # image, T, count writes; bwd: T, count, dL/dimage reads) and 48 B of atomics.
+        px = H * W
+        b = pairs * 36.0 + px * 48.0 + (pairs * 48.0 if "bwd" in dom_name else 0.0)
+        gbs = b / (d["ms_per_launch"] / 1e3) / 1e9
+        out["roofline"] = {"bound": "hbm", "kernel": dom_name, "achieved": gbs,
+                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                           "frac": gbs / peaks["hbm_gbs"], "traffic": None,
+                           "peak_source": peaks["source"],
+                           "note": "issue-bound rasteriser; DRAM fraction of its algorithmic bytes"}
+    if radix_pass is not None:
+        out["sort_in_step"] = radix_pass
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(name)
+    return out
+
+
+def _oracle_sample(name: str, scale: int):
+    """The config at 1/scale^2 of the pixels and Gaussians (same density), one view."""
+    c = scenes.CONFIGS[name]
+    n = c["n"] // (scale * scale)
+    H, W = c["height"] // scale, c["width"] // scale
+    f = c["f"] / scale
+    cam = scenes.sphere_cameras(1, c["radius"], f, W, H)[0]
+    params = scenes.cluster_scene(n, sh_degree=3, seed=0)
+    tgt = np.random.default_rng(1000).uniform(0, 1, (H, W, 3)).astype(np.float32)
+    return params, cam, tgt, n, H, W
+
+
+def cpu_baseline(name: str, budget_s: float = 20.0) -> dict:
+    """The oracle port of the reference's numpy training models (the reference's CPU
+    implementation of this path is numpy; it cannot run here) on one view at reduced size."""
+    from oracle import train as ot
+    scale = 8
+    params, cam, tgt, n, H, W = _oracle_sample(name, scale)
+    cfg = ot.Cfg(sh_degree=3, tile=16)
+    zeros = {k: np.zeros_like(v) for k, v in params.items()}
+    t0 = time.perf_counter()
+    iters = 0
+    while True:
+        ot.train_step(params, zeros, zeros, 0, [(cam.w2c, cam.K, H, W)], [tgt], cfg,
+                      lr=LR_BASELINE, ssim=True)
+        iters += 1
+        el = time.perf_counter() - t0
+        if el > budget_s or iters >= 3:
+            break
+    return {"value": H * W * iters / el / 1e6, "unit": "Mpix/s", "cores": 1, "kind": "port",
+            "sample": f"{iters} oracle steps of 1 view {W}x{H} with {n} Gaussians "
+                      f"({name.upper()} at 1/{scale * scale} pixels and Gaussians)"}
+
+
+def run_reference(args) -> dict:
+    name = config_name()
+    b = cpu_baseline(name, budget_s=max(10.0, 3.0 * args.steps))
+    return {"impl": "reference", "metric": "train-step Mpix/s (fwd+bwd+Adam)", "value": b["value"],
+            "unit": "Mpix/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{name.upper()} train step (oracle port, reduced sample)"},
+            "cpu_baseline": b,
+            "e2e": {"value": b["value"], "unit": "Mpix/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}

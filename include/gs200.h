@@ -149,6 +149,114 @@ gs_status gs_blend(const float* means_2d, const float* covs_2d, const float* col
                    const int64_t* tile_ranges, int64_t m, int32_t height, int32_t width,
                    int32_t tile_size, float* image, float* alpha, void* stream);
 
+/* ------------------------------------------------------------------------------
+ * Training path: per view project -> key emission -> sort -> ranges -> forward raster
+ * -> loss -> backward raster; then one projection backward over all views and a
+ * sparse Adam step.
+ * ------------------------------------------------------------------------------ */
+
+/* Optimizer-space Gaussian parameters (or Adam moments, or gradients), device fp32, in
+ * the reference trainer's layouts (gsplat/train_oracle.py:8-20): means N*3, log_scales
+ * N*3, quats N*4 (w, x, y, z; unnormalised), opacity_logits N, sh N*K*3 with
+ * K = (sh_degree + 1)^2. The five arrays may live anywhere; quats must be 16-byte aligned. */
+typedef struct gs_gaussians {
+    float* means;
+    float* log_scales;
+    float* quats;
+    float* opacity_logits;
+    float* sh;
+} gs_gaussians;
+
+/* One pinhole view: world-to-camera w2c (row-major 4x4) and intrinsics K (row-major
+ * 3x3), image size (gsplat/train_oracle.py:56-61 Camera). Host memory. */
+typedef struct gs_camera {
+    float w2c[16];
+    float K[9];
+    int32_t height;
+    int32_t width;
+} gs_camera;
+
+/* Render rules (gsplat/train_oracle.py:64-71 RenderConfig), loss (train_oracle.py:276-279
+ * loss_fn, gsplat/train_loss.py:126-171) and Adam settings
+ * (train_oracle.py:422-470 DEFAULT_LR / sparse_adam_step). */
+typedef struct gs_train_config {
+    int32_t sh_degree;       /* 0..3 */
+    int32_t tile_size;       /* 16 or 32 */
+    float near_plane;        /* 0.2 */
+    float lowpass;           /* 0.3 */
+    float alpha_max;         /* 0.99 */
+    float alpha_min;         /* 1/255 */
+    float t_min;             /* 1e-4 */
+    float background[3];
+    int32_t use_ssim;        /* 0: loss = (1 - lambda) L1; 1: (1 - lambda) L1 + lambda (1 - SSIM) */
+    float lambda_dssim;      /* 0.2 */
+    float lr_means, lr_log_scales, lr_quats, lr_opacity, lr_sh_dc, lr_sh_rest;
+    float beta1, beta2, eps;
+    int32_t bf16_moments;    /* moments stored as bf16 values (round to nearest even) */
+} gs_train_config;
+
+/* One training step over n_views views (<= 64) of one rank.
+ *   params / exp_avg / exp_avg_sq: parameters and Adam moments, updated in place when
+ *   apply_adam != 0 (rows visible in at least one view only, bias correction with
+ *   step + 1). grads: written with the gradients summed over the views;
+ *   vis_counts (N floats): number of views in which each Gaussian is visible. These two
+ *   are the buffers a multi-GPU caller sums across ranks before calling gs_sparse_adam
+ *   (apply_adam = 0 here).
+ *   targets: n_views device pointers to H*W*3 fp32 target images (host array of pointers).
+ *   view_losses (device, n_views floats): per-view loss. images (nullable, device,
+ *   n_views*H*W*3) and grad2d (nullable, device, n_views*N*9 of dmx, dmy, dA, dB, dC,
+ *   dopacity, dr, dg, db) export intermediates for parity tests. pairs (nullable, device
+ *   int64, n_views): pair count of each view.
+ *   pair_capacity bounds the (Gaussian, tile) pairs of one view; if a view needs more,
+ *   the step leaves params and moments untouched and gs_workspace_error() reports
+ *   GS_ERR_OVERFLOW (grow the capacity with gs_train_count_pairs and retry).
+ * No counterpart in one reference call: it chains gsplat/blend_backward_dev.py:404
+ * forward_fast, gsplat/train_loss.py:126 loss_and_grad_device, blend_backward_dev.py:444
+ * ref_slots_fast, gsplat/t2_param_backward.py:244 t2_step (extended to SH1-3 and
+ * multiple views) and gsplat/train_oracle.py:434 sparse_adam_step. */
+gs_status gs_train_step(const gs_gaussians* params, const gs_gaussians* exp_avg,
+                        const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
+                        float* vis_counts, int64_t n, int64_t step, const gs_camera* cams,
+                        const float* const* targets, int32_t n_views,
+                        const gs_train_config* cfg, int32_t apply_adam, float* view_losses,
+                        float* images, float* grad2d, int64_t* pairs, int64_t pair_capacity,
+                        void* workspace, size_t workspace_bytes, void* stream);
+size_t gs_train_workspace_size(int64_t n, int32_t sh_degree, int32_t n_views, int32_t height,
+                               int32_t width, int32_t tile_size, int64_t pair_capacity);
+
+/* Pair count of each view (projection + tile rectangles only), synchronising, to size
+ * pair_capacity. pairs_host: n_views int64 in host memory. */
+gs_status gs_train_count_pairs(const gs_gaussians* params, int64_t n, const gs_camera* cams,
+                               int32_t n_views, const gs_train_config* cfg,
+                               int64_t* pairs_host, void* workspace, size_t workspace_bytes,
+                               void* stream);
+
+/* One view's projection and intersections with every intermediate exported, for parity
+ * checks of the training path: means2d N*2, conic N*3 (A, B, C of the inverse low-passed
+ * 2D covariance), opacity N, colors N*3 (max(SH + 0.5, 0)), depth N (camera z), rects
+ * N*4 int32 (inclusive tile rectangle x0, x1, y0, y1; x1 < x0 when the Gaussian has no
+ * pairs), vis_counts N (1 where visible for sparse Adam), sorted_ids (pair_capacity
+ * uint32: Gaussian ids sorted by tile then depth bits), tile_ranges (tiles*2 int32
+ * [start, end)), P in *pairs_host (synchronises). Mirrors gsplat/t2_param_backward.py:81-120
+ * forward_lanes, gsplat/blend_backward_dev.py:76-112 tile_rects_vec / pair_lists. */
+gs_status gs_train_project_view(const gs_gaussians* params, int64_t n, const gs_camera* cam,
+                                const gs_train_config* cfg, float* means2d, float* conic,
+                                float* opacity, float* colors, float* depth, int32_t* rects,
+                                float* vis_counts, uint32_t* sorted_ids, int32_t* tile_ranges,
+                                int64_t pair_capacity, int64_t* pairs_host, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
+/* Sparse Adam over rows with vis_counts > 0 (gsplat/train_oracle.py:434-470
+ * sparse_adam_step; gsplat/t2_param_backward.py:195-223 adam_step): fp32 arithmetic,
+ * moments stored fp32 or bf16 per cfg->bf16_moments, lr per group with SH band 0 at
+ * lr_sh_dc and bands >= 1 at lr_sh_rest. `error_word` (nullable, device) is checked
+ * first: a non-zero value (a failed gs_train_step) skips the update. */
+gs_status gs_sparse_adam(const gs_gaussians* params, const gs_gaussians* exp_avg,
+                         const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
+                         const float* vis_counts, int64_t n, int64_t step,
+                         const gs_train_config* cfg, const unsigned int* error_word,
+                         void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -36,6 +36,7 @@ SH_C3 = (-0.5900435899266435, 2.890611442640554, -0.4570457994644658,
          0.3731763325901154, -0.4570457994644658, 1.445305721320277,
          -0.5900435899266435)
 PARAM_NAMES = ("means", "log_scales", "quats", "opacity_logits", "sh")
+TIE_RTOL = 4e-6  # gsplat/blend_backward_dev.py:441 (about 32 fp32 ulp)
 DEFAULT_LR = {"means": 1.6e-4, "log_scales": 5e-3, "quats": 1e-3, "opacity_logits": 0.05,
               "sh_dc": 2.5e-3, "sh_rest": 2.5e-3 / 20.0}
 
@@ -53,13 +54,13 @@ class Cfg:
     tile: int = 16
 
 
-def _cam(w2c, K):
+def _cam(w2c, K, ft=f32):
     w = np.asarray(w2c, np.float64)
     k = np.asarray(K, np.float64)
-    R = w[:3, :3].astype(f32)
-    t = w[:3, 3].astype(f32)
-    cc = (-(w[:3, :3].T @ w[:3, 3])).astype(f32)   # camera centre, float64 then rounded
-    return R, t, f32(k[0, 0]), f32(k[1, 1]), f32(k[0, 2]), f32(k[1, 2]), cc
+    R = w[:3, :3].astype(ft)
+    t = w[:3, 3].astype(ft)
+    cc = (-(w[:3, :3].T @ w[:3, 3])).astype(ft)   # camera centre, float64 then rounded
+    return R, t, ft(k[0, 0]), ft(k[1, 1]), ft(k[0, 2]), ft(k[1, 2]), cc
 
 
 def _quat_rot(w, x, y, z):
@@ -117,22 +118,27 @@ def sh_basis_grad(dirs, degree):
     return np.stack([np.stack(v, 1) for v in g], 1)
 
 
+def _exp(x, ft):
+    """exp rounded once to `ft` (computed in float64): the correctly rounded value the
+    device reproduces, in place of numpy's float32 exp."""
+    return np.exp(np.asarray(x, np.float64)).astype(ft)
+
+
 def project(params, w2c, K, H, W, cfg: Cfg, ft=f32) -> dict:
-    """Per-Gaussian projection for one view (fp32 lanes)."""
-    R, t, fx, fy, cx, cy, cc = _cam(w2c, K)
-    if ft is not f32:
-        R, t, cc = R.astype(ft), t.astype(ft), cc.astype(ft)
-        fx, fy, cx, cy = ft(fx), ft(fy), ft(cx), ft(cy)
+    """Per-Gaussian projection for one view (fp32 lanes). Every sum is written out in
+    order so the device kernel (compiled without FMA contraction) rounds identically."""
+    R, t, fx, fy, cx, cy, cc = _cam(w2c, K, ft)
     m = np.asarray(params["means"], ft)
     x, y, z = (R[i, 0] * m[:, 0] + R[i, 1] * m[:, 1] + R[i, 2] * m[:, 2] + t[i] for i in range(3))
     valid = z > ft(cfg.near)
     iz = ft(1) / np.where(valid, z, ft(1))
     mx, my = fx * x * iz + cx, fy * y * iz + cy
     q = np.asarray(params["quats"], ft)
-    qinv = ft(1) / np.sqrt((q * q).sum(1, dtype=ft))
+    qinv = ft(1) / np.sqrt(q[:, 0] * q[:, 0] + q[:, 1] * q[:, 1] + q[:, 2] * q[:, 2]
+                           + q[:, 3] * q[:, 3])
     qn = [q[:, i] * qinv for i in range(4)]
     Rq = _quat_rot(*qn)
-    s = np.exp(np.asarray(params["log_scales"], ft))
+    s = _exp(params["log_scales"], ft)
     M = [Rq[3 * i + j] * s[:, j] for i in range(3) for j in range(3)]
     S = {(i, k): M[3 * i] * M[3 * k] + M[3 * i + 1] * M[3 * k + 1] + M[3 * i + 2] * M[3 * k + 2]
          for i in range(3) for k in range(i, 3)}
@@ -151,13 +157,16 @@ def project(params, w2c, K, H, W, cfg: Cfg, ft=f32) -> dict:
     rx = np.ceil(ft(3) * np.sqrt(np.maximum(a, ft(0))))
     ry = np.ceil(ft(3) * np.sqrt(np.maximum(c, ft(0))))
     visible = valid & (mx + rx > 0) & (mx - rx < W) & (my + ry > 0) & (my - ry < H)
-    op = ft(1) / (ft(1) + np.exp(-np.asarray(params["opacity_logits"], ft)))
+    op = ft(1) / (ft(1) + _exp(-np.asarray(params["opacity_logits"], ft), ft))
     d = m - cc
-    dn = np.sqrt((d * d).sum(1, dtype=ft))
+    dn = np.sqrt(d[:, 0] * d[:, 0] + d[:, 1] * d[:, 1] + d[:, 2] * d[:, 2])
     dirs = d / dn[:, None]
     basis = sh_basis(dirs, cfg.sh_degree)
     sh = np.asarray(params["sh"], ft)[:, :basis.shape[1]]
-    raw = (basis[:, :, None] * sh).sum(1, dtype=ft) + ft(0.5)
+    raw = basis[:, 0, None] * sh[:, 0]
+    for k in range(1, basis.shape[1]):
+        raw = raw + basis[:, k, None] * sh[:, k]
+    raw = raw + ft(0.5)
     colors = np.maximum(raw, ft(0))
     out = dict(R=R, t=t, fx=fx, fy=fy, x=x, y=y, z=z, iz=iz, valid=valid, visible=visible,
                qn=qn, qinv=qinv, Rq=Rq, s=s, M=M, c3=c3, T0=T0, T1=T1, A=A, B=B, C=C,
@@ -169,7 +178,8 @@ def project(params, w2c, K, H, W, cfg: Cfg, ft=f32) -> dict:
 
 def tile_rects(means2d, valid, conic, H, W, tile):
     """(N,4) inclusive tile rectangle [x0, x1, y0, y1] (x1 < x0: none), computed in float64
-    from the conic as gsplat/blend_backward_dev.py:76-92 does."""
+    from the conic as gsplat/blend_backward_dev.py:76-92 does; a degenerate conic (non-finite
+    radius) gets no rectangle."""
     con = np.asarray(conic, np.float64)
     A, B, C = con[:, 0], con[:, 1], con[:, 2]
     with np.errstate(divide="ignore", invalid="ignore"):
@@ -180,7 +190,7 @@ def tile_rects(means2d, valid, conic, H, W, tile):
         m = np.asarray(means2d, np.float64)
         px, py = m[:, 0], m[:, 1]
         ok = (np.asarray(valid, bool) & ~(px + rx <= 0) & ~(px - rx >= W)
-              & ~(py + ry <= 0) & ~(py - ry >= H))
+              & ~(py + ry <= 0) & ~(py - ry >= H) & np.isfinite(rx) & np.isfinite(ry))
     tx, ty = (W + tile - 1) // tile, (H + tile - 1) // tile
     out = np.zeros((m.shape[0], 4), np.int64)
     out[:, 1] = -1
@@ -245,8 +255,11 @@ def _untile(a, utid, tx, ty, tile, H, W, fill):
 
 
 def forward(proj, H, W, cfg: Cfg) -> dict:
-    """Tiled fp32 forward with the training rules; image (H,W,3), final_T (H,W) and the
-    per-pixel count of processed pairs up to the last blended one (n_contrib)."""
+    """Tiled fp32 forward with the training rules; image (H,W,3), final_T (H,W), the
+    per-pixel count of processed pairs up to the last blended one (n_contrib), and `ties`
+    (H,W): pixels where a decision (alpha >= alpha_min, the alpha clamp, the t_min stop)
+    came within TIE_RTOL of its threshold, where either outcome is a valid fp32 result
+    (gsplat/blend_backward_dev.py:441-449)."""
     tile = cfg.tile
     m2, con = np.asarray(proj["means2d"], f32), np.asarray(proj["conic"], f32)
     op, col = np.asarray(proj["opacity"], f32), np.asarray(proj["colors"], f32)
@@ -259,6 +272,8 @@ def forward(proj, H, W, cfg: Cfg) -> dict:
     ncon = np.zeros((nt, tile, tile), np.int32)
     amax, amin, tmin, one = f32(cfg.alpha_max), f32(cfg.alpha_min), f32(cfg.t_min), f32(1)
     n_live = 0
+    taint = np.zeros((nt, tile, tile), bool)
+    near = lambda q, th: np.abs(q / th - 1.0) < TIE_RTOL  # noqa: E731
     for k in range(int(cnt.max()) if nt else 0):
         n = int(np.searchsorted(-cnt, -k, side="left"))
         g = pl["g"][start[:n] + k]
@@ -267,8 +282,11 @@ def forward(proj, H, W, cfg: Cfg) -> dict:
         Af, Bf, Cf, P0, Lx, Ly = cf
         du, dv = xx - centre, yy - centre
         pw = (P0 + du * (Lx + Af * du + Bf * dv) + dv * (Ly + Cf * dv)).astype(f32)
-        al = np.minimum(op[g][:, None, None] * np.exp(np.minimum(pw, f32(0))), amax).astype(f32)
+        raw = op[g][:, None, None] * np.exp(np.minimum(pw, f32(0)))
+        al = np.minimum(raw, amax).astype(f32)
         Tn = T[:n] * (one - al)
+        taint[:n] |= ~done[:n] & (near(al, amin) | near(raw, amax)
+                                  | ((al >= amin) & near(Tn, tmin)))
         act = (al >= amin) & ~done[:n]
         live = act & (Tn >= tmin)
         n_live += int(live.sum())
@@ -280,6 +298,7 @@ def forward(proj, H, W, cfg: Cfg) -> dict:
     img = _untile(Cc + T[..., None] * bg, utid, tx, ty, tile, H, W, bg)
     return {"image": img, "final_T": _untile(T, utid, tx, ty, tile, H, W, f32(1)),
             "n_contrib": _untile(ncon, utid, tx, ty, tile, H, W, 0),
+            "ties": _untile(taint, utid, tx, ty, tile, H, W, False),
             "n_pairs": int(pl["g"].size), "n_live": n_live}
 
 
@@ -310,7 +329,7 @@ def backward_2d(proj, image, dL_dimage, H, W, cfg: Cfg, ties: bool = False):
     tie_g = np.zeros(N, bool)
     taint = np.zeros((nt, tile, tile), bool)
     amax, amin, tmin, one = f32(cfg.alpha_max), f32(cfg.alpha_min), f32(cfg.t_min), f32(1)
-    near = lambda q, th: np.abs(q / th - one) < 4e-6  # noqa: E731
+    near = lambda q, th: np.abs(q / th - one) < TIE_RTOL  # noqa: E731
     for k in range(int(cnt.max()) if nt else 0):
         n = int(np.searchsorted(-cnt, -k, side="left"))
         g = pl["g"][start[:n] + k]
@@ -329,7 +348,7 @@ def backward_2d(proj, image, dL_dimage, H, W, cfg: Cfg, ties: bool = False):
         if ties:
             taint[:n] |= alive[:n] & (near(alpha, amin) | near(raw, amax)
                                       | (live & near(Tk * (one - alpha), tmin)))
-            tie_g[g[(taint[:n] & (alpha >= amin * (one - f32(4e-6)))).any((1, 2))]] = True
+            tie_g[g[(taint[:n] & (alpha >= amin * (one - f32(TIE_RTOL)))).any((1, 2))]] = True
         stop = live & (Tk * (one - alpha) < tmin)
         live &= ~stop
         alive[:n] &= ~stop
