@@ -5,8 +5,9 @@
 Steps: generate the host-logf exception table (csrc/gen_logf_table.c, run with this
 host's C library), compile every csrc/*.cu for sm_100a, and link
 gsplat_tt_b200/libgs200.so (static cudart, so the library only needs the driver).
-display.cu is compiled with -fmad=false so its float arithmetic rounds like the
-reference's -ffp-contract=off CPU build; the other units keep FMA contraction.
+display.cu and train_project.cu are compiled with -fmad=false so their float arithmetic
+rounds like the reference's -ffp-contract=off CPU build and the oracle's numpy lanes; the
+other units keep FMA contraction.
 """
 from __future__ import annotations
 
@@ -25,7 +26,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-O2",
           "--expt-relaxed-constexpr", f"-I{CSRC}", f"-I{GEN}",
           f"-I{os.path.join(os.path.dirname(HERE), 'include')}"]
-PER_FILE = {"display.cu": ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]}
+NO_FMA = ["-fmad=false", "-prec-div=true", "-prec-sqrt=true"]
+PER_FILE = {"display.cu": NO_FMA, "train_project.cu": NO_FMA}
 
 
 def _newer(target: str, deps: list[str]) -> bool:

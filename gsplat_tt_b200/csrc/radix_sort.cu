@@ -29,8 +29,9 @@ constexpr int kSpinLimit = 1 << 22;
 
 static_assert(kSortThreads == kRadix, "one thread per digit in the look-back");
 
+template <typename KeyT>
 struct SortSmem {
-    uint64_t keys[kTileItems];
+    KeyT keys[kTileItems];
     uint32_t vals[kTileItems];
     uint32_t warp_hist[kSortWarps][kRadix];
     uint32_t local_off[kRadix];
@@ -39,7 +40,8 @@ struct SortSmem {
 };
 
 // Digit histograms of every pass in one read of the keys.
-__global__ void k_radix_hist(const uint64_t* __restrict__ keys, const int64_t* __restrict__ n_dev,
+template <typename KeyT>
+__global__ void k_radix_hist(const KeyT* __restrict__ keys, const int64_t* __restrict__ n_dev,
                              int64_t n_host, int npass, uint32_t* __restrict__ hist) {
     __shared__ uint32_t sh[8][kRadix];
     const int64_t n = n_dev ? min(*n_dev, n_host) : n_host;  // device count, capped
@@ -47,8 +49,8 @@ __global__ void k_radix_hist(const uint64_t* __restrict__ keys, const int64_t* _
     __syncthreads();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
-        const uint64_t k = keys[i];
-        for (int p = 0; p < npass; ++p) atomicAdd(&sh[p][(k >> (p * kRadixBits)) & (kRadix - 1)], 1u);
+        const KeyT k = keys[i];
+        for (int p = 0; p < npass; ++p) atomicAdd(&sh[p][(uint32_t)(k >> (p * kRadixBits)) & (kRadix - 1)], 1u);
     }
     __syncthreads();
     for (int i = threadIdx.x; i < npass * kRadix; i += blockDim.x) {
@@ -81,14 +83,15 @@ __device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
 __device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) { *(volatile uint32_t*)p = v; }
 
 // One onesweep pass over digit `shift`.
+template <typename KeyT>
 __global__ void __launch_bounds__(kSortThreads, 3)
-k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
-             uint64_t* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
+k_radix_pass(const KeyT* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
+             KeyT* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
              const int64_t* __restrict__ n_dev, int64_t n_host, int shift,
              const uint32_t* __restrict__ digit_offsets, uint32_t* __restrict__ lookback,
              uint32_t* __restrict__ tile_counter, unsigned int* __restrict__ err) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    SortSmem& S = *reinterpret_cast<SortSmem*>(smem_raw);
+    SortSmem<KeyT>& S = *reinterpret_cast<SortSmem<KeyT>*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int64_t n = n_dev ? min(*n_dev, n_host) : n_host;  // device count, capped
 
@@ -102,16 +105,16 @@ k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ 
 
     // Load (warp-striped: warp w owns items [512 w, 512 w + 512) of the tile). Pads
     // past the end get an all-ones digit so they rank after every real item.
-    uint64_t key[kSortItems];
+    KeyT key[kSortItems];
     uint32_t val[kSortItems];
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
         const int li = warp * (kSortItems * 32) + j * 32 + lane;
         if (li < valid) {
             key[j] = keys_in[base + li];
-            val[j] = vals_in[base + li];
+            val[j] = vals_in ? vals_in[base + li] : (uint32_t)(base + li);  // null: iota
         } else {
-            key[j] = (uint64_t)(kRadix - 1) << shift;
+            key[j] = (KeyT)(kRadix - 1) << shift;
             val[j] = 0;
         }
     }
@@ -209,7 +212,7 @@ k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ 
     // Coalesced write-out: consecutive threads write consecutive items of a digit run.
 #pragma unroll 4
     for (int i = tid; i < valid; i += kSortThreads) {
-        const uint64_t k = S.keys[i];
+        const KeyT k = S.keys[i];
         const uint32_t dd = GS_DIGIT(k);
         const uint32_t out = S.gbase[dd] + ((uint32_t)i - S.local_off[dd]);
         if (keys_out) keys_out[out] = k;
@@ -218,7 +221,7 @@ k_radix_pass(const uint64_t* __restrict__ keys_in, const uint32_t* __restrict__ 
 #undef GS_DIGIT
 }
 
-size_t radix_workspace_bytes(int64_t n, int key_bits) {
+size_t radix_workspace_bytes(int64_t n, int key_bits, int key_bytes) {
     const int npass = (key_bits + kRadixBits - 1) / kRadixBits;
     const int64_t ntiles = (n + kTileItems - 1) / kTileItems + 1;
     WorkspaceSizer s;
@@ -226,17 +229,18 @@ size_t radix_workspace_bytes(int64_t n, int key_bits) {
     s.take<uint32_t>((size_t)npass * kRadix);          // histograms / offsets
     s.take<uint32_t>((size_t)npass * ntiles * kRadix);  // look-back words
     s.take<uint32_t>(npass);                            // tile counters
-    s.take<uint64_t>(n); s.take<uint32_t>(n);           // ping
-    s.take<uint64_t>(n); s.take<uint32_t>(n);           // pong
+    s.take<char>((size_t)n * key_bytes); s.take<uint32_t>(n);  // ping
+    s.take<char>((size_t)n * key_bytes); s.take<uint32_t>(n);  // pong
     return s.bytes();
 }
 
 int radix_num_passes(int key_bits) { return (key_bits + kRadixBits - 1) / kRadixBits; }
 
-gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int64_t* n_dev,
-                           int64_t n_cap, int key_bits, uint64_t* keys_out, uint32_t* vals_out,
-                           void* workspace, size_t workspace_bytes, cudaStream_t st,
-                           unsigned int** err_out, unsigned int* err_ext) {
+template <typename KeyT>
+gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64_t* n_dev,
+                             int64_t n_cap, int key_bits, KeyT* keys_out, uint32_t* vals_out,
+                             void* workspace, size_t workspace_bytes, cudaStream_t st,
+                             unsigned int** err_out, unsigned int* err_ext) {
     const int npass = radix_num_passes(key_bits);
     const int64_t ntiles = (n_cap + kTileItems - 1) / kTileItems + 1;
     Workspace ws(workspace, workspace_bytes);
@@ -244,13 +248,13 @@ gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int
     uint32_t* hist = ws.take<uint32_t>((size_t)npass * kRadix);
     uint32_t* look = ws.take<uint32_t>((size_t)npass * ntiles * kRadix);
     uint32_t* counters = ws.take<uint32_t>(npass);
-    uint64_t* ka = ws.take<uint64_t>(n_cap);
+    KeyT* ka = (KeyT*)ws.take<char>((size_t)n_cap * sizeof(KeyT));
     uint32_t* va = ws.take<uint32_t>(n_cap);
-    uint64_t* kb = ws.take<uint64_t>(n_cap);
+    KeyT* kb = (KeyT*)ws.take<char>((size_t)n_cap * sizeof(KeyT));
     uint32_t* vb = ws.take<uint32_t>(n_cap);
     if (!ws.ok()) {
         set_error("radix sort: workspace too small (%zu < %zu)", workspace_bytes,
-                  radix_workspace_bytes(n_cap, key_bits));
+                  radix_workspace_bytes(n_cap, key_bits, (int)sizeof(KeyT)));
         return GS_ERR_ARG;
     }
     // err .. counters are contiguous: one memset clears all of them. A caller-owned
@@ -261,21 +265,21 @@ gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int
     const int hist_blocks = (int)std::min<int64_t>(kNumSMs * 4, std::max<int64_t>(1, (n_cap + 4095) / 4096));
     {
         KernelTimer kt("radix_hist", st);
-        k_radix_hist<<<hist_blocks, 512, 0, st>>>(keys, n_dev, n_cap, npass, hist);
+        k_radix_hist<KeyT><<<hist_blocks, 512, 0, st>>>(keys, n_dev, n_cap, npass, hist);
         GS_CHECK_LAUNCH();
         k_radix_hist_scan<<<1, kRadix, 0, st>>>(hist, npass);
         GS_CHECK_LAUNCH();
     }
-    const size_t smem = sizeof(SortSmem);
-    GS_CUDA_CHECK(cudaFuncSetAttribute(k_radix_pass, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    const uint64_t* kin = keys;
+    const size_t smem = sizeof(SortSmem<KeyT>);
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_radix_pass<KeyT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const KeyT* kin = keys;
     const uint32_t* vin = vals;
     for (int p = 0; p < npass; ++p) {
         const bool last = (p == npass - 1);
-        uint64_t* kout = last ? keys_out : ((p & 1) ? kb : ka);
+        KeyT* kout = last ? keys_out : ((p & 1) ? kb : ka);
         uint32_t* vout = last ? vals_out : ((p & 1) ? vb : va);
-        KernelTimer kt("radix_pass", st);
-        k_radix_pass<<<(unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1), kSortThreads, smem, st>>>(
+        KernelTimer kt(sizeof(KeyT) == 8 ? "radix_pass" : "radix_pass32", st);
+        k_radix_pass<KeyT><<<(unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1), kSortThreads, smem, st>>>(
             kin, vin, kout, vout, n_dev, n_cap, p * kRadixBits, hist + p * kRadix,
             look + (size_t)p * ntiles * kRadix, counters + p, err);
         GS_CHECK_LAUNCH();
@@ -283,6 +287,22 @@ gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int
         vin = vout;
     }
     return GS_OK;
+}
+
+gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int64_t* n_dev,
+                           int64_t n_cap, int key_bits, uint64_t* keys_out, uint32_t* vals_out,
+                           void* workspace, size_t workspace_bytes, cudaStream_t st,
+                           unsigned int** err_out, unsigned int* err_ext) {
+    return radix_sort_pairs_t<uint64_t>(keys, vals, n_dev, n_cap, key_bits, keys_out, vals_out,
+                                        workspace, workspace_bytes, st, err_out, err_ext);
+}
+
+gs_status radix_sort_pairs32(const uint32_t* keys, const uint32_t* vals, const int64_t* n_dev,
+                             int64_t n_cap, int key_bits, uint32_t* keys_out, uint32_t* vals_out,
+                             void* workspace, size_t workspace_bytes, cudaStream_t st,
+                             unsigned int** err_out, unsigned int* err_ext) {
+    return radix_sort_pairs_t<uint32_t>(keys, vals, n_dev, n_cap, key_bits, keys_out, vals_out,
+                                        workspace, workspace_bytes, st, err_out, err_ext);
 }
 
 // ------------------------------------------------------------------ sort_and_bin
@@ -334,7 +354,7 @@ using namespace gs;
 extern "C" size_t gs_sort_pairs_workspace_size(int64_t n, int32_t key_bits) {
     if (n < 1) n = 1;
     if (key_bits < 1) key_bits = 1;
-    return radix_workspace_bytes(n, key_bits);
+    return radix_workspace_bytes(n, key_bits, 8);
 }
 
 extern "C" gs_status gs_sort_pairs(const uint64_t* keys, const uint32_t* values, int64_t n,
@@ -356,7 +376,7 @@ extern "C" size_t gs_sort_and_bin_workspace_size(int64_t p, int32_t tiles_x, int
     if (p < 1) p = 1;
     const int kb = 32 + bits_for((int64_t)tiles_x * tiles_y - 1);
     WorkspaceSizer s;
-    s.take<char>(radix_workspace_bytes(p, kb));  // first, so its error word leads
+    s.take<char>(radix_workspace_bytes(p, kb, 8));  // first, so its error word leads
     s.take<uint64_t>(p);  // keys
     s.take<uint32_t>(p);  // values
     s.take<uint64_t>(p);  // sorted keys
@@ -384,7 +404,7 @@ extern "C" gs_status gs_sort_and_bin(const int64_t* gaussian_ids, const int64_t*
                  "gs_sort_and_bin: null pointer");
     const int kb = 32 + bits_for(ntiles - 1);
     Workspace ws(workspace, workspace_bytes);
-    const size_t rbytes = radix_workspace_bytes(p, kb);
+    const size_t rbytes = radix_workspace_bytes(p, kb, 8);
     char* rws = ws.take<char>(rbytes);
     uint64_t* keys = ws.take<uint64_t>(p);
     uint32_t* vals = ws.take<uint32_t>(p);

@@ -7,11 +7,11 @@ namespace gs {
 
 // Bytes of scratch for sorting up to n pairs on the low key_bits bits. The first
 // word of the scratch is the sort's device error word.
-size_t radix_workspace_bytes(int64_t n, int key_bits);
+size_t radix_workspace_bytes(int64_t n, int key_bits, int key_bytes);
 int radix_num_passes(int key_bits);
 int bits_for(int64_t v);
 
-// Enqueue a stable sort of (keys, vals). The element count is *n_dev when n_dev is
+// Enqueue a stable sort of (keys, vals); vals == null sorts (key, index) pairs. The element count is *n_dev when n_dev is
 // non-null (device-resident, at most n_cap), else n_cap. keys_out may be null
 // (values only). *err_out receives the device error word (DEV_TIMEOUT on a
 // look-back timeout).
@@ -19,5 +19,9 @@ gs_status radix_sort_pairs(const uint64_t* keys, const uint32_t* vals, const int
                            int64_t n_cap, int key_bits, uint64_t* keys_out, uint32_t* vals_out,
                            void* workspace, size_t workspace_bytes, cudaStream_t st,
                            unsigned int** err_out, unsigned int* err_ext = nullptr);
+gs_status radix_sort_pairs32(const uint32_t* keys, const uint32_t* vals, const int64_t* n_dev,
+                             int64_t n_cap, int key_bits, uint32_t* keys_out, uint32_t* vals_out,
+                             void* workspace, size_t workspace_bytes, cudaStream_t st,
+                             unsigned int** err_out, unsigned int* err_ext = nullptr);
 
 }  // namespace gs

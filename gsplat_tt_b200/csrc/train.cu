@@ -53,12 +53,12 @@ TCfg make_tcfg(const gs_train_config& c, int H, int W) {
 // ------------------------------------------------------------------ tile ranges
 
 // [start, end) of each tile in the sorted keys (binary search), (0, 0) when empty.
-__global__ void k_train_ranges(const uint64_t* __restrict__ skeys, const int64_t* __restrict__ p_dev,
+__global__ void k_train_ranges(const uint32_t* __restrict__ skeys, const int64_t* __restrict__ p_dev,
                                int64_t cap, int ntiles, int2* __restrict__ ranges) {
     const int t = blockIdx.x * blockDim.x + threadIdx.x;
     if (t >= ntiles) return;
     const int64_t p = min(*p_dev, cap);
-    auto lower = [&](uint64_t target) {
+    auto lower = [&](uint32_t target) {
         int64_t lo = 0, hi = p;
         while (lo < hi) {
             const int64_t mid = (lo + hi) >> 1;
@@ -66,7 +66,7 @@ __global__ void k_train_ranges(const uint64_t* __restrict__ skeys, const int64_t
         }
         return lo;
     };
-    const int64_t s = lower((uint64_t)t << 32), e = lower((uint64_t)(t + 1) << 32);
+    const int64_t s = lower((uint32_t)t), e = lower((uint32_t)t + 1u);
     ranges[t] = (e > s) ? make_int2((int)s, (int)e) : make_int2(0, 0);
 }
 
@@ -535,6 +535,9 @@ struct GMut {
 // backward of gsplat/t2_param_backward.py:123-192 extended with SH bands 1-3 and the
 // view-direction term, summed over views. dL/dcov3d, dL/dopacity and the SH gradient
 // accumulate across views; the log-scale, quaternion and logit gradients are formed once.
+// The geometric part runs in fp64: the covariance gradient cancels strongly along the
+// viewing direction (the part of cov3d a view cannot see), and fp32 there leaves errors
+// of ~1e-2 relative to the group's largest gradient. SH terms stay fp32.
 template <int DEG>
 __global__ void __launch_bounds__(128)
 k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCfg cfg,
@@ -543,33 +546,35 @@ k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCf
     if (g >= n) return;
     constexpr int K = (DEG + 1) * (DEG + 1);
     const uint64_t mask = touch[g];
-    float gm[3] = {0.f, 0.f, 0.f};
-    float G3[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 00 01 02 11 12 22
+    double gm[3] = {0.0, 0.0, 0.0};
+    double G3[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // 00 01 02 11 12 22
     float gop = 0.0f;
     float gsh[3 * K];
 #pragma unroll
     for (int k = 0; k < 3 * K; ++k) gsh[k] = 0.0f;
-    const float m0 = P.means[3 * g], m1 = P.means[3 * g + 1], m2 = P.means[3 * g + 2];
+    const double m0 = P.means[3 * g], m1 = P.means[3 * g + 1], m2 = P.means[3 * g + 2];
     const float4 q = reinterpret_cast<const float4*>(P.q)[g];
-    const float qinv = 1.0f / sqrtf(q.x * q.x + q.y * q.y + q.z * q.z + q.w * q.w);
-    const float qw = q.x * qinv, qx = q.y * qinv, qy = q.z * qinv, qz = q.w * qinv;
-    float Rq[9];
-    Rq[0] = 1.0f - 2.0f * (qy * qy + qz * qz);
-    Rq[1] = 2.0f * (qx * qy - qw * qz);
-    Rq[2] = 2.0f * (qx * qz + qw * qy);
-    Rq[3] = 2.0f * (qx * qy + qw * qz);
-    Rq[4] = 1.0f - 2.0f * (qx * qx + qz * qz);
-    Rq[5] = 2.0f * (qy * qz - qw * qx);
-    Rq[6] = 2.0f * (qx * qz - qw * qy);
-    Rq[7] = 2.0f * (qy * qz + qw * qx);
-    Rq[8] = 1.0f - 2.0f * (qx * qx + qy * qy);
-    const float s[3] = {__expf(P.ls[3 * g]), __expf(P.ls[3 * g + 1]), __expf(P.ls[3 * g + 2])};
-    float M[9];
+    const double qinv = 1.0 / sqrt((double)q.x * q.x + (double)q.y * q.y + (double)q.z * q.z +
+                                   (double)q.w * q.w);
+    const double qw = q.x * qinv, qx = q.y * qinv, qy = q.z * qinv, qz = q.w * qinv;
+    double Rq[9];
+    Rq[0] = 1.0 - 2.0 * (qy * qy + qz * qz);
+    Rq[1] = 2.0 * (qx * qy - qw * qz);
+    Rq[2] = 2.0 * (qx * qz + qw * qy);
+    Rq[3] = 2.0 * (qx * qy + qw * qz);
+    Rq[4] = 1.0 - 2.0 * (qx * qx + qz * qz);
+    Rq[5] = 2.0 * (qy * qz - qw * qx);
+    Rq[6] = 2.0 * (qx * qz - qw * qy);
+    Rq[7] = 2.0 * (qy * qz + qw * qx);
+    Rq[8] = 1.0 - 2.0 * (qx * qx + qy * qy);
+    const double s[3] = {exp((double)P.ls[3 * g]), exp((double)P.ls[3 * g + 1]),
+                         exp((double)P.ls[3 * g + 2])};
+    double M[9];
 #pragma unroll
     for (int i = 0; i < 3; ++i)
 #pragma unroll
         for (int j = 0; j < 3; ++j) M[3 * i + j] = Rq[3 * i + j] * s[j];
-    float S[3][3];
+    double S[3][3];
 #pragma unroll
     for (int i = 0; i < 3; ++i)
 #pragma unroll
@@ -584,73 +589,74 @@ k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCf
         const float4 ga4 = reinterpret_cast<const float4*>(gr)[0];
         const float4 gb4 = reinterpret_cast<const float4*>(gr)[1];
         const float gbl = gr[8];
-        const float gmx = ga4.x, gmy = ga4.y, gA = ga4.z, gB = ga4.w, gC = gb4.x;
-        if (gmx == 0.f && gmy == 0.f && gA == 0.f && gB == 0.f && gC == 0.f && gb4.y == 0.f &&
-            gb4.z == 0.f && gb4.w == 0.f && gbl == 0.f)
+        if (ga4.x == 0.f && ga4.y == 0.f && ga4.z == 0.f && ga4.w == 0.f && gb4.x == 0.f &&
+            gb4.y == 0.f && gb4.z == 0.f && gb4.w == 0.f && gbl == 0.f)
             continue;
+        const double gmx = ga4.x, gmy = ga4.y, gA = ga4.z, gB = ga4.w, gC = gb4.x;
         const TCam& cam = cams[v];
-        const float* R = cam.R;
-        const float x = R[0] * m0 + R[1] * m1 + R[2] * m2 + cam.t[0];
-        const float y = R[3] * m0 + R[4] * m1 + R[5] * m2 + cam.t[1];
-        const float z = R[6] * m0 + R[7] * m1 + R[8] * m2 + cam.t[2];
-        if (!(z > cfg.near_plane)) continue;
-        const float iz = 1.0f / z, iz2 = iz * iz;
-        const float j00 = cam.fx * iz, j02 = -cam.fx * x * iz2;
-        const float j11 = cam.fy * iz, j12 = -cam.fy * y * iz2;
-        float T0[3], T1[3];
+        double R[9];
+#pragma unroll
+        for (int k = 0; k < 9; ++k) R[k] = cam.R[k];
+        const double x = R[0] * m0 + R[1] * m1 + R[2] * m2 + (double)cam.t[0];
+        const double y = R[3] * m0 + R[4] * m1 + R[5] * m2 + (double)cam.t[1];
+        const double z = R[6] * m0 + R[7] * m1 + R[8] * m2 + (double)cam.t[2];
+        if (!(z > (double)cfg.near_plane)) continue;
+        const double fx = cam.fx, fy = cam.fy;
+        const double iz = 1.0 / z, iz2 = iz * iz;
+        const double j00 = fx * iz, j02 = -fx * x * iz2;
+        const double j11 = fy * iz, j12 = -fy * y * iz2;
+        double T0[3], T1[3];
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
             T0[k] = j00 * R[k] + j02 * R[6 + k];
             T1[k] = j11 * R[3 + k] + j12 * R[6 + k];
         }
-        float TC0[3], TC1[3];
+        double TC0[3], TC1[3];
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
             TC0[k] = T0[0] * S[0][k] + T0[1] * S[1][k] + T0[2] * S[2][k];
             TC1[k] = T1[0] * S[0][k] + T1[1] * S[1][k] + T1[2] * S[2][k];
         }
-        const float a = T0[0] * TC0[0] + T0[1] * TC0[1] + T0[2] * TC0[2] + cfg.lowpass;
-        const float b = T1[0] * TC0[0] + T1[1] * TC0[1] + T1[2] * TC0[2];
-        const float c = T1[0] * TC1[0] + T1[1] * TC1[1] + T1[2] * TC1[2] + cfg.lowpass;
-        const float idet = 1.0f / (a * c - b * b);
-        const float A = c * idet, B = -b * idet, C = a * idet;
+        const double lp = cfg.lowpass;
+        const double a = T0[0] * TC0[0] + T0[1] * TC0[1] + T0[2] * TC0[2] + lp;
+        const double b = T1[0] * TC0[0] + T1[1] * TC0[1] + T1[2] * TC0[2];
+        const double c = T1[0] * TC1[0] + T1[1] * TC1[1] + T1[2] * TC1[2] + lp;
+        const double idet = 1.0 / (a * c - b * b);
+        const double A = c * idet, B = -b * idet, C = a * idet;
         // conic -> 2D covariance
-        const float ga = -(A * A * gA + A * B * gB + B * B * gC);
-        const float gc = -(B * B * gA + B * C * gB + C * C * gC);
-        const float gbb = -(2.0f * A * B * gA + (A * C + B * B) * gB + 2.0f * B * C * gC);
-        const float hb = 0.5f * gbb;
+        const double ga = -(A * A * gA + A * B * gB + B * B * gC);
+        const double gc = -(B * B * gA + B * C * gB + C * C * gC);
+        const double hb = -0.5 * (2.0 * A * B * gA + (A * C + B * B) * gB + 2.0 * B * C * gC);
         // dL/dcov3d += T^T Gs T
-        G3[0] += ga * T0[0] * T0[0] + hb * 2.0f * T0[0] * T1[0] + gc * T1[0] * T1[0];
+        G3[0] += ga * T0[0] * T0[0] + 2.0 * hb * T0[0] * T1[0] + gc * T1[0] * T1[0];
         G3[1] += ga * T0[0] * T0[1] + hb * (T0[0] * T1[1] + T1[0] * T0[1]) + gc * T1[0] * T1[1];
         G3[2] += ga * T0[0] * T0[2] + hb * (T0[0] * T1[2] + T1[0] * T0[2]) + gc * T1[0] * T1[2];
-        G3[3] += ga * T0[1] * T0[1] + hb * 2.0f * T0[1] * T1[1] + gc * T1[1] * T1[1];
+        G3[3] += ga * T0[1] * T0[1] + 2.0 * hb * T0[1] * T1[1] + gc * T1[1] * T1[1];
         G3[4] += ga * T0[1] * T0[2] + hb * (T0[1] * T1[2] + T1[1] * T0[2]) + gc * T1[1] * T1[2];
-        G3[5] += ga * T0[2] * T0[2] + hb * 2.0f * T0[2] * T1[2] + gc * T1[2] * T1[2];
+        G3[5] += ga * T0[2] * T0[2] + 2.0 * hb * T0[2] * T1[2] + gc * T1[2] * T1[2];
         // dL/dT = 2 Gs T Sigma -> Jacobian entries -> camera-space mean
-        float dT0[3], dT1[3];
+        double dT0[3], dT1[3];
 #pragma unroll
         for (int k = 0; k < 3; ++k) {
-            dT0[k] = 2.0f * (ga * TC0[k] + hb * TC1[k]);
-            dT1[k] = 2.0f * (hb * TC0[k] + gc * TC1[k]);
+            dT0[k] = 2.0 * (ga * TC0[k] + hb * TC1[k]);
+            dT1[k] = 2.0 * (hb * TC0[k] + gc * TC1[k]);
         }
-        const float gj00 = dT0[0] * R[0] + dT0[1] * R[1] + dT0[2] * R[2];
-        const float gj02 = dT0[0] * R[6] + dT0[1] * R[7] + dT0[2] * R[8];
-        const float gj11 = dT1[0] * R[3] + dT1[1] * R[4] + dT1[2] * R[5];
-        const float gj12 = dT1[0] * R[6] + dT1[1] * R[7] + dT1[2] * R[8];
-        const float fx = cam.fx, fy = cam.fy;
-        const float gx = gmx * fx * iz - gj02 * fx * iz2;
-        const float gy = gmy * fy * iz - gj12 * fy * iz2;
-        const float gz = -(gmx * fx * x + gmy * fy * y + gj00 * fx + gj11 * fy) * iz2 +
-                         2.0f * (gj02 * fx * x + gj12 * fy * y) * iz2 * iz;
+        const double gj00 = dT0[0] * R[0] + dT0[1] * R[1] + dT0[2] * R[2];
+        const double gj02 = dT0[0] * R[6] + dT0[1] * R[7] + dT0[2] * R[8];
+        const double gj11 = dT1[0] * R[3] + dT1[1] * R[4] + dT1[2] * R[5];
+        const double gj12 = dT1[0] * R[6] + dT1[1] * R[7] + dT1[2] * R[8];
+        const double gx = gmx * fx * iz - gj02 * fx * iz2;
+        const double gy = gmy * fy * iz - gj12 * fy * iz2;
+        const double gz = -(gmx * fx * x + gmy * fy * y + gj00 * fx + gj11 * fy) * iz2 +
+                          2.0 * (gj02 * fx * x + gj12 * fy * y) * iz2 * iz;
         gm[0] += R[0] * gx + R[3] * gy + R[6] * gz;
         gm[1] += R[1] * gx + R[4] * gy + R[7] * gz;
         gm[2] += R[2] * gx + R[5] * gy + R[8] * gz;
         gop += gb4.y;
         // SH colour backward (colour = max(raw, 0)) and the view-direction term.
-        const float d0 = m0 - cam.cc[0], d1 = m1 - cam.cc[1], d2 = m2 - cam.cc[2];
-        const float dn = sqrtf(d0 * d0 + d1 * d1 + d2 * d2);
-        const float idn = 1.0f / dn;
-        const float dx = d0 * idn, dy = d1 * idn, dz = d2 * idn;
+        const double d0 = m0 - (double)cam.cc[0], d1 = m1 - (double)cam.cc[1], d2 = m2 - (double)cam.cc[2];
+        const double idn = 1.0 / sqrt(d0 * d0 + d1 * d1 + d2 * d2);
+        const float dx = (float)(d0 * idn), dy = (float)(d1 * idn), dz = (float)(d2 * idn);
         float basis[16], db[16][3];
         sh_basis_and_grad(DEG, dx, dy, dz, basis, db);
         const float gcol_in[3] = {gb4.z, gb4.w, gbl};
@@ -675,48 +681,48 @@ k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCf
             gdir[2] += db[k][2] * gbk;
         }
         if (K > 1) {
-            const float pd = dx * gdir[0] + dy * gdir[1] + dz * gdir[2];
-            gm[0] += (gdir[0] - dx * pd) * idn;
-            gm[1] += (gdir[1] - dy * pd) * idn;
-            gm[2] += (gdir[2] - dz * pd) * idn;
+            const double pd = (double)dx * gdir[0] + (double)dy * gdir[1] + (double)dz * gdir[2];
+            gm[0] += ((double)gdir[0] - dx * pd) * idn;
+            gm[1] += ((double)gdir[1] - dy * pd) * idn;
+            gm[2] += ((double)gdir[2] - dz * pd) * idn;
         }
     }
     // cov3d = M M^T: dM = 2 G3 M, M = Rq diag(s).
-    const float Gf[3][3] = {{G3[0], G3[1], G3[2]}, {G3[1], G3[3], G3[4]}, {G3[2], G3[4], G3[5]}};
-    float dM[9];
+    const double Gf[3][3] = {{G3[0], G3[1], G3[2]}, {G3[1], G3[3], G3[4]}, {G3[2], G3[4], G3[5]}};
+    double dM[9];
 #pragma unroll
     for (int i = 0; i < 3; ++i)
 #pragma unroll
         for (int j = 0; j < 3; ++j)
-            dM[3 * i + j] = 2.0f * (Gf[i][0] * M[j] + Gf[i][1] * M[3 + j] + Gf[i][2] * M[6 + j]);
-    float gls[3];
+            dM[3 * i + j] = 2.0 * (Gf[i][0] * M[j] + Gf[i][1] * M[3 + j] + Gf[i][2] * M[6 + j]);
+    double gls[3];
 #pragma unroll
     for (int j = 0; j < 3; ++j) gls[j] = (dM[j] * Rq[j] + dM[3 + j] * Rq[3 + j] + dM[6 + j] * Rq[6 + j]) * s[j];
-    float gR[9];
+    double gR[9];
 #pragma unroll
     for (int i = 0; i < 3; ++i)
 #pragma unroll
         for (int j = 0; j < 3; ++j) gR[3 * i + j] = dM[3 * i + j] * s[j];
-    const float g00 = gR[0], g01 = gR[1], g02 = gR[2], g10 = gR[3], g11 = gR[4], g12 = gR[5];
-    const float g20 = gR[6], g21 = gR[7], g22 = gR[8];
-    const float gqn0 = 2.0f * (-qz * g01 + qy * g02 + qz * g10 - qx * g12 - qy * g20 + qx * g21);
-    const float gqn1 = 2.0f * (qy * g01 + qz * g02 + qy * g10 - 2.0f * qx * g11 - qw * g12 + qz * g20 +
-                               qw * g21 - 2.0f * qx * g22);
-    const float gqn2 = 2.0f * (-2.0f * qy * g00 + qx * g01 + qw * g02 + qx * g10 + qz * g12 - qw * g20 +
-                               qz * g21 - 2.0f * qy * g22);
-    const float gqn3 = 2.0f * (-2.0f * qz * g00 - qw * g01 + qx * g02 + qw * g10 - 2.0f * qz * g11 +
+    const double g00 = gR[0], g01 = gR[1], g02 = gR[2], g10 = gR[3], g11 = gR[4], g12 = gR[5];
+    const double g20 = gR[6], g21 = gR[7], g22 = gR[8];
+    const double gqn0 = 2.0 * (-qz * g01 + qy * g02 + qz * g10 - qx * g12 - qy * g20 + qx * g21);
+    const double gqn1 = 2.0 * (qy * g01 + qz * g02 + qy * g10 - 2.0 * qx * g11 - qw * g12 + qz * g20 +
+                               qw * g21 - 2.0 * qx * g22);
+    const double gqn2 = 2.0 * (-2.0 * qy * g00 + qx * g01 + qw * g02 + qx * g10 + qz * g12 - qw * g20 +
+                               qz * g21 - 2.0 * qy * g22);
+    const double gqn3 = 2.0 * (-2.0 * qz * g00 - qw * g01 + qx * g02 + qw * g10 - 2.0 * qz * g11 +
                                qy * g12 + qx * g20 + qy * g21);
-    const float dot = qw * gqn0 + qx * gqn1 + qy * gqn2 + qz * gqn3;
+    const double dot = qw * gqn0 + qx * gqn1 + qy * gqn2 + qz * gqn3;
     const float op = 1.0f / (1.0f + __expf(-P.ol[g]));
-    G.means[3 * g] = gm[0];
-    G.means[3 * g + 1] = gm[1];
-    G.means[3 * g + 2] = gm[2];
-    G.ls[3 * g] = gls[0];
-    G.ls[3 * g + 1] = gls[1];
-    G.ls[3 * g + 2] = gls[2];
+    G.means[3 * g] = (float)gm[0];
+    G.means[3 * g + 1] = (float)gm[1];
+    G.means[3 * g + 2] = (float)gm[2];
+    G.ls[3 * g] = (float)gls[0];
+    G.ls[3 * g + 1] = (float)gls[1];
+    G.ls[3 * g + 2] = (float)gls[2];
     reinterpret_cast<float4*>(G.q)[g] =
-        make_float4((gqn0 - qw * dot) * qinv, (gqn1 - qx * dot) * qinv, (gqn2 - qy * dot) * qinv,
-                    (gqn3 - qz * dot) * qinv);
+        make_float4((float)((gqn0 - qw * dot) * qinv), (float)((gqn1 - qx * dot) * qinv),
+                    (float)((gqn2 - qy * dot) * qinv), (float)((gqn3 - qz * dot) * qinv));
     G.ol[g] = gop * op * (1.0f - op);
     float* gshg = G.sh + (size_t)g * K * 3;
 #pragma unroll
@@ -790,9 +796,11 @@ struct TrainWs {
     int64_t* blk;
     int64_t* pairs;
     ProjView pv;
-    uint64_t* keys;
+    int64_t* blk2;
+    uint32_t* order;   // Gaussian ids sorted by depth
+    uint32_t* keys;    // tile id of each pair (depth order)
     uint32_t* vals;
-    uint64_t* skeys;
+    uint32_t* skeys;   // sorted by tile id
     uint32_t* svals;
     char* radix;
     size_t radix_bytes;
@@ -811,7 +819,7 @@ template <typename WS>
 static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int W, int tile,
                          int64_t cap) {
     const int tiles = ((W + tile - 1) / tile) * ((H + tile - 1) / tile);
-    const int key_bits = 32 + bits_for(tiles > 1 ? tiles - 1 : 1);
+    const int tile_bits = bits_for(tiles > 1 ? tiles - 1 : 1);
     const int64_t nb = div_up(n, kProjThreads) + 1;
     const int64_t px = (int64_t)H * W;
     L.err = ws.template take<unsigned int>(1);
@@ -824,13 +832,17 @@ static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int 
     L.pv.p1 = ws.template take<float4>(n);
     L.pv.p2 = ws.template take<float>(n);
     L.pv.dkey = ws.template take<uint32_t>(n);
+    L.pv.dsort = ws.template take<uint32_t>(n);
     L.pv.rect = ws.template take<ushort4>(n);
     L.pv.cnt = ws.template take<uint32_t>(n);
-    L.keys = ws.template take<uint64_t>(cap);
+    L.blk2 = ws.template take<int64_t>(nb);
+    L.order = ws.template take<uint32_t>(n);
+    L.keys = ws.template take<uint32_t>(cap);
     L.vals = ws.template take<uint32_t>(cap);
-    L.skeys = ws.template take<uint64_t>(cap);
+    L.skeys = ws.template take<uint32_t>(cap);
     L.svals = ws.template take<uint32_t>(cap);
-    L.radix_bytes = radix_workspace_bytes(cap, key_bits);
+    // one scratch region serves the depth sort (N, 32 bits) and the tile sort (P, tile bits)
+    L.radix_bytes = std::max(radix_workspace_bytes(n, 32, 4), radix_workspace_bytes(cap, tile_bits, 4));
     L.radix = ws.template take<char>(L.radix_bytes);
     L.ranges = ws.template take<int2>(tiles);
     L.image = ws.template take<float>(px * 3);
@@ -893,16 +905,24 @@ static gs_status project_and_sort_view(const GConst& P, int64_t n, const TCam& c
     }
     scan_block_totals<int64_t><<<1, 1024, 0, st>>>(L.blk, nb, L.pairs + view);
     GS_CHECK_LAUNCH();
+    // Gaussians in (depth bits, id) order; those without pairs sort last.
+    unsigned int* rerr = nullptr;
+    gs_status s = radix_sort_pairs32(L.pv.dsort, nullptr, nullptr, n, 32, nullptr, L.order, L.radix,
+                                     L.radix_bytes, st, &rerr, L.err);
+    if (s != GS_OK) return s;
+    launch_sorted_count(L.pv, L.order, n, L.blk2, st);
+    GS_CHECK_LAUNCH();
+    scan_block_totals<int64_t><<<1, 1024, 0, st>>>(L.blk2, nb, nullptr);
+    GS_CHECK_LAUNCH();
     {
         KernelTimer kt("train_emit", st);
-        launch_emit(L.pv, n, cfg, L.blk, cap, L.keys, L.vals, L.err, st);
+        launch_emit(L.pv, L.order, n, cfg, L.blk2, cap, L.keys, L.vals, L.err, st);
         GS_CHECK_LAUNCH();
     }
     const int tiles = cfg.tiles_x * cfg.tiles_y;
-    const int key_bits = 32 + bits_for(tiles > 1 ? tiles - 1 : 1);
-    unsigned int* rerr = nullptr;
-    gs_status s = radix_sort_pairs(L.keys, L.vals, L.pairs + view, cap, key_bits, L.skeys, L.svals,
-                                   L.radix, L.radix_bytes, st, &rerr, L.err);
+    const int tile_bits = bits_for(tiles > 1 ? tiles - 1 : 1);
+    s = radix_sort_pairs32(L.keys, L.vals, L.pairs + view, cap, tile_bits, L.skeys, L.svals, L.radix,
+                           L.radix_bytes, st, &rerr, L.err);
     if (s != GS_OK) return s;
     k_train_ranges<<<div_up(tiles, 256), 256, 0, st>>>(L.skeys, L.pairs + view, cap, tiles, L.ranges);
     GS_CHECK_LAUNCH();

@@ -35,6 +35,7 @@ struct ProjView {
     float4* p1;
     float* p2;
     uint32_t* dkey;   // bits of the camera-space depth
+    uint32_t* dsort;  // depth-sort key: dkey, or 0xffffffff for a Gaussian without pairs
     ushort4* rect;    // inclusive tile rectangle x0, x1, y0, y1
     uint32_t* cnt;    // tiles in the rectangle (0 = no pairs)
 };
@@ -48,9 +49,11 @@ TCfg make_tcfg(const gs_train_config& c, int H, int W);
 void launch_project(const GConst& P, int64_t n, const TCam& cam, const TCfg& cfg, int view,
                     const ProjView& pv, int64_t* blk, uint64_t* touch, float* vis_counts,
                     float* grad2d, cudaStream_t st);
-void launch_emit(const ProjView& pv, int64_t n, const TCfg& cfg, const int64_t* blk_offsets,
-                 int64_t capacity, uint64_t* keys, uint32_t* vals, unsigned int* err,
-                 cudaStream_t st);
+void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int64_t* blk,
+                         cudaStream_t st);
+void launch_emit(const ProjView& pv, const uint32_t* order, int64_t n, const TCfg& cfg,
+                 const int64_t* blk_offsets, int64_t capacity, uint32_t* keys, uint32_t* vals,
+                 unsigned int* err, cudaStream_t st);
 constexpr int kProjThreads = 256;
 
 }  // namespace gs

@@ -152,6 +152,7 @@ k_train_project(GConst P, int64_t n, TCam cam, TCfg cfg, int view, ProjView pv,
         pv.p1[g] = make_float4(C, op, col[0], col[1]);
         pv.p2[g] = col[2];
         pv.dkey[g] = __float_as_uint(z);
+        pv.dsort[g] = count > 0 ? __float_as_uint(z) : 0xffffffffu;
         pv.rect[g] = rc;
         pv.cnt[g] = count;
         if (vis_counts != nullptr && visible) vis_counts[g] += 1.0f;
@@ -168,15 +169,31 @@ k_train_project(GConst P, int64_t n, TCam cam, TCfg cfg, int view, ProjView pv,
     if (threadIdx.x == 0) blk[blockIdx.x] = total;
 }
 
-// Keys tile << 32 | depth bits for every tile of a Gaussian's rectangle, Gaussian-major
-// and row-major within the rectangle; values are Gaussian ids.
+// Pair counts of the Gaussians in depth order (`order` = Gaussian ids sorted by depth
+// bits, stable), one total per block for the offset scan.
 __global__ void __launch_bounds__(kProjThreads)
-k_train_emit(ProjView pv, int64_t n, int tiles_x, const int64_t* __restrict__ blk_offsets,
-             int64_t capacity, uint64_t* __restrict__ keys, uint32_t* __restrict__ vals,
+k_sorted_count(const uint32_t* __restrict__ cnt, const uint32_t* __restrict__ order, int64_t n,
+               int64_t* __restrict__ blk) {
+    __shared__ int64_t smem[33];
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t c = (i < n) ? cnt[order[i]] : 0u;
+    int64_t total;
+    block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
+    if (threadIdx.x == 0) blk[blockIdx.x] = total;
+}
+
+// Pairs of the Gaussians in depth order, each Gaussian's tiles row-major: key = tile id,
+// value = Gaussian id. A stable sort on the tile id then yields the reference's
+// (tile, depth bits, Gaussian id) order (src/gsplat_cpu/sort.cpp:24-27).
+__global__ void __launch_bounds__(kProjThreads)
+k_train_emit(ProjView pv, const uint32_t* __restrict__ order, int64_t n, int tiles_x,
+             const int64_t* __restrict__ blk_offsets, int64_t capacity,
+             uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
              unsigned int* __restrict__ err) {
     __shared__ int64_t smem[33];
-    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const uint32_t c = (g < n) ? pv.cnt[g] : 0u;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const uint32_t g = (i < n) ? order[i] : 0u;
+    const uint32_t c = (i < n) ? pv.cnt[g] : 0u;
     int64_t total;
     const int64_t off = blk_offsets[blockIdx.x] + block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
     if (c == 0) return;
@@ -185,12 +202,11 @@ k_train_emit(ProjView pv, int64_t n, int tiles_x, const int64_t* __restrict__ bl
         return;
     }
     const ushort4 r = pv.rect[g];
-    const uint64_t lo = pv.dkey[g];
     int64_t pos = off;
     for (int ty = r.z; ty <= r.w; ++ty)
         for (int tx = r.x; tx <= r.y; ++tx) {
-            keys[pos] = ((uint64_t)(ty * tiles_x + tx) << 32) | lo;
-            vals[pos] = (uint32_t)g;
+            keys[pos] = (uint32_t)(ty * tiles_x + tx);
+            vals[pos] = g;
             ++pos;
         }
 }
@@ -202,11 +218,17 @@ void launch_project(const GConst& P, int64_t n, const TCam& cam, const TCfg& cfg
                                                                       touch, vis_counts, grad2d);
 }
 
-void launch_emit(const ProjView& pv, int64_t n, const TCfg& cfg, const int64_t* blk_offsets,
-                 int64_t capacity, uint64_t* keys, uint32_t* vals, unsigned int* err,
-                 cudaStream_t st) {
-    k_train_emit<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv, n, cfg.tiles_x, blk_offsets,
-                                                                   capacity, keys, vals, err);
+void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int64_t* blk,
+                         cudaStream_t st) {
+    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, order, n, blk);
+}
+
+void launch_emit(const ProjView& pv, const uint32_t* order, int64_t n, const TCfg& cfg,
+                 const int64_t* blk_offsets, int64_t capacity, uint32_t* keys, uint32_t* vals,
+                 unsigned int* err, cudaStream_t st) {
+    k_train_emit<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv, order, n, cfg.tiles_x,
+                                                                   blk_offsets, capacity, keys,
+                                                                   vals, err);
 }
 
 }  // namespace gs

@@ -159,7 +159,7 @@ def run(args, rank: int, world: int, local: int) -> dict:
                    "parallelism": f"dp{world} over views + NCCL allreduce",
                    "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},
         "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
-                "h2d_bytes_per_step": int(sum(t.numel() * 4 for t in targets_host)),
+                "h2d_bytes_per_step": int(sum(t.size * 4 for t in targets_host)),
                 "d2h_bytes_per_step": 4},
         "gpu_launches": int(sum(v["launches_per_step"] for v in per_kernel.values())),
         "pairs_per_view": pairs, "loss": loss_now,
