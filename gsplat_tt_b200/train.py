@@ -21,6 +21,7 @@ import torch
 
 from . import _lib
 from ._lib import check, lib
+from .dist import reduce_step_buffer
 
 PARAM_NAMES = ("means", "log_scales", "quats", "opacity_logits", "sh")
 DEFAULT_LR = {"means": 1.6e-4, "log_scales": 5e-3, "quats": 1e-3, "opacity_logits": 0.05,
@@ -267,14 +268,11 @@ class Trainer:
         return self.losses
 
     def _allreduce_and_adam(self, st) -> None:
-        import torch.distributed as dist
         # error word of this rank's step (first 4 bytes at the workspace's first 256-byte
         # boundary) rides along in the reduced buffer so every rank agrees on skipping Adam
         off = (-self.ws.data_ptr()) % 256
         errw = self.ws[off:off + 4].view(torch.int32)
-        self.err_slot.copy_((errw != 0).to(torch.float32))
-        dist.all_reduce(self.grads.flat, group=self.pg)
-        self._err_i32.copy_((self.err_slot > 0).to(torch.int32))
+        reduce_step_buffer(self.grads.flat, self.err_slot, errw, self._err_i32, self.pg)
         p, m, v, g = (b.c_struct() for b in (self.params, self.m, self.v, self.grads))
         check(lib.gs_sparse_adam(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
                                  self.vis_counts.data_ptr(), self.n, self.step_count,

@@ -6,7 +6,8 @@ radius 5 looking at the origin; loss 0.8 L1 + 0.2 (1 - SSIM); sparse Adam with b
 (0.9, 0.999), eps 1e-15 and the per-group learning rates of configs[3]. The views are split
 evenly over the ranks (strong scaling: the step's total work is fixed); gradients are summed
 with one NCCL allreduce. ``GS_BENCH_CONFIG=c4`` selects configs[3] (3M Gaussians, 8 views of
-1600x1056, f = 1300, radius 4) instead.
+1600x1056, f = 1300, radius 4) instead; ``GS_BENCH_VIEWS=k`` keeps only the first k views (for
+small ncu captures; the benchmark line then names the reduced workload).
 """
 from __future__ import annotations
 
@@ -18,6 +19,7 @@ import torch
 
 from . import scenes
 from ._lib import check, lib, timing_report
+from .dist import view_slice
 from .train import TrainConfig, Trainer
 
 LR_BASELINE = {"means": 1.6e-4, "log_scales": 5e-3, "quats": 1e-3, "opacity_logits": 5e-2,
@@ -61,12 +63,11 @@ def run(args, rank: int, world: int, local: int) -> dict:
     name = config_name()
     c = scenes.CONFIGS[name]
     dev = torch.device("cuda", local)
-    V = c["views"]
-    if V % world != 0:
-        raise SystemExit(f"{V} views do not split evenly over {world} GPUs")
-    per = V // world
+    V = int(os.environ.get("GS_BENCH_VIEWS", c["views"]))  # fewer views: profiling runs only
+    lo, hi = view_slice(V, world, rank)
+    per = hi - lo
     cams_all = scenes.training_cameras(name)
-    mine = cams_all[rank * per:(rank + 1) * per]
+    mine = cams_all[lo:hi]
     H, W = c["height"], c["width"]
     params = scenes.cluster_scene(c["n"], sh_degree=3, seed=0)
     targets_host = view_targets(mine, rank * per)
