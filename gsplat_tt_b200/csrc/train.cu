@@ -107,64 +107,94 @@ __device__ __forceinline__ float centred_power(const RPair& q, float du, float d
     return __fmaf_rn(dv, t3, __fmaf_rn(du, t2, q.P0));
 }
 
-template <int TILE>
-__global__ void __launch_bounds__(TILE * TILE)
+// Pixel layout of the rasterisers: a TILE x TILE tile is covered by TILE*TILE/PPT threads;
+// thread t owns column t % TILE and rows t / TILE + i * (TILE / PPT), i < PPT. One pair read
+// from shared memory then serves PPT pixels.
+template <int TILE, int PPT>
+struct PixLayout {
+    static constexpr int kThreads = TILE * TILE / PPT;
+    static constexpr int kRowStep = TILE / PPT;
+};
+
+constexpr int kRasterBatch = 128;  // pairs staged per batch
+
+template <int TILE, int PPT>
+__global__ void __launch_bounds__(TILE * TILE / PPT)
 k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals, ProjView pv,
             TCfg cfg, int H, int W, float* __restrict__ image, float* __restrict__ final_T,
             int32_t* __restrict__ n_contrib) {
-    constexpr int NB = 256;  // pairs staged per batch
+    using LY = PixLayout<TILE, PPT>;
+    constexpr int NB = kRasterBatch;
     __shared__ RPair sp[NB];
     const int tile = blockIdx.x;
     const int tx = tile % cfg.tiles_x, ty = tile / cfg.tiles_x;
-    const int lx = threadIdx.x % TILE, ly = threadIdx.x / TILE;
-    const int x = tx * TILE + lx, y = ty * TILE + ly;
-    const bool inside = (x < W) && (y < H);
+    const int lx = threadIdx.x % TILE, ly0 = threadIdx.x / TILE;
+    const int x = tx * TILE + lx;
     const float centre = 0.5f * TILE;
-    const float du = ((float)lx + 0.5f) - centre, dv = ((float)ly + 0.5f) - centre;
+    const float du = ((float)lx + 0.5f) - centre;
     const float ox = (float)(tx * TILE), oy = (float)(ty * TILE);
     const int2 rg = ranges[tile];
     const float amax = cfg.amax, amin = cfg.amin, tmin = cfg.tmin;
-    float T = 1.0f, c0 = 0.0f, c1 = 0.0f, c2 = 0.0f;
-    bool done = !inside;
-    int last = 0;
+    float dv[PPT], T[PPT], c0[PPT], c1[PPT], c2[PPT];
+    int last[PPT];
+    unsigned live_mask = 0;  // pixels still blending
+#pragma unroll
+    for (int i = 0; i < PPT; ++i) {
+        const int ly = ly0 + i * LY::kRowStep;
+        dv[i] = ((float)ly + 0.5f) - centre;
+        T[i] = 1.0f;
+        c0[i] = c1[i] = c2[i] = 0.0f;
+        last[i] = 0;
+        if (x < W && ty * TILE + ly < H) live_mask |= 1u << i;
+    }
     for (int b0 = rg.x; b0 < rg.y; b0 += NB) {
         __syncthreads();
-        const int i = b0 + threadIdx.x;
-        if (threadIdx.x < NB && i < rg.y) {
-            const uint32_t g = svals[i];
+        for (int s = threadIdx.x; s < NB && b0 + s < rg.y; s += LY::kThreads) {
+            const uint32_t g = svals[b0 + s];
             float mxl, myl;
-            sp[threadIdx.x] = stage_pair(pv.p0[g], pv.p1[g], pv.p2[g], ox, oy, centre, mxl, myl);
+            sp[s] = stage_pair(pv.p0[g], pv.p1[g], pv.p2[g], ox, oy, centre, mxl, myl);
         }
         __syncthreads();
         const int nb = min(NB, rg.y - b0);
-        for (int j = 0; j < nb && !done; ++j) {
+        for (int j = 0; j < nb && live_mask; ++j) {
             const RPair q = sp[j];
-            const float power = centred_power(q, du, dv);
-            const float w = __expf(fminf(power, 0.0f));
-            const float alpha = fminf(q.op * w, amax);
-            if (alpha >= amin) {
-                const float Tn = T * (1.0f - alpha);
-                if (Tn < tmin) {
-                    done = true;
-                } else {
-                    const float at = alpha * T;
-                    c0 = __fmaf_rn(at, q.r, c0);
-                    c1 = __fmaf_rn(at, q.g, c1);
-                    c2 = __fmaf_rn(at, q.b, c2);
-                    T = Tn;
-                    last = b0 - rg.x + j + 1;
+            const float t1 = __fmaf_rn(q.Af, du, q.Lx);  // shared by the thread's pixels
+#pragma unroll
+            for (int i = 0; i < PPT; ++i) {
+                if (!((live_mask >> i) & 1u)) continue;
+                const float t2 = __fmaf_rn(q.Bf, dv[i], t1);
+                const float t3 = __fmaf_rn(q.Cf, dv[i], q.Ly);
+                const float power = __fmaf_rn(dv[i], t3, __fmaf_rn(du, t2, q.P0));
+                const float w = __expf(fminf(power, 0.0f));
+                const float alpha = fminf(q.op * w, amax);
+                if (alpha >= amin) {
+                    const float Tn = T[i] * (1.0f - alpha);
+                    if (Tn < tmin) {
+                        live_mask &= ~(1u << i);
+                    } else {
+                        const float at = alpha * T[i];
+                        c0[i] = __fmaf_rn(at, q.r, c0[i]);
+                        c1[i] = __fmaf_rn(at, q.g, c1[i]);
+                        c2[i] = __fmaf_rn(at, q.b, c2[i]);
+                        T[i] = Tn;
+                        last[i] = b0 - rg.x + j + 1;
+                    }
                 }
             }
         }
-        if (__syncthreads_count(!done) == 0) break;
+        if (__syncthreads_count(live_mask != 0) == 0) break;
     }
-    if (!inside) return;
-    const size_t o = (size_t)y * W + x;
-    image[3 * o] = c0 + T * cfg.bg[0];
-    image[3 * o + 1] = c1 + T * cfg.bg[1];
-    image[3 * o + 2] = c2 + T * cfg.bg[2];
-    final_T[o] = T;
-    n_contrib[o] = last;
+#pragma unroll
+    for (int i = 0; i < PPT; ++i) {
+        const int y = ty * TILE + ly0 + i * LY::kRowStep;
+        if (x >= W || y >= H) continue;
+        const size_t o = (size_t)y * W + x;
+        image[3 * o] = c0[i] + T[i] * cfg.bg[0];
+        image[3 * o + 1] = c1[i] + T[i] * cfg.bg[1];
+        image[3 * o + 2] = c2[i] + T[i] * cfg.bg[2];
+        final_T[o] = T[i];
+        n_contrib[o] = last[i];
+    }
 }
 
 struct BPair {
@@ -177,52 +207,65 @@ struct BPair {
 // stored final T and count of processed pairs): per pixel and live pair
 //   T_i = T_{i+1} / (1 - a_i),  da = T_i (c.g) - behind / (1 - a_i),  behind += a T_i (c.g)
 // with behind starting at T_final (bg.g). The nine per-pixel terms (dopacity, dcolour,
-// G u^2, G uv, G v^2, G u, G v with G = dL/dpower) are reduced per warp with shuffles,
-// per tile in shared memory, and added once per pair into the view's per-Gaussian rows.
-template <int TILE>
-__global__ void __launch_bounds__(TILE * TILE)
+// G u^2, G uv, G v^2, G u, G v with G = dL/dpower) are summed over the thread's PPT pixels
+// in registers, over the warp with shuffles, over the tile in shared memory, and added once
+// per pair into the view's per-Gaussian rows with float4 atomics.
+template <int TILE, int PPT>
+__global__ void __launch_bounds__(TILE * TILE / PPT)
 k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals, ProjView pv,
             TCfg cfg, int H, int W, const float* __restrict__ dimg,
             const float* __restrict__ final_T, const int32_t* __restrict__ n_contrib,
             float* __restrict__ grad2d) {
-    constexpr int NB = 256;  // pairs staged per batch
+    using LY = PixLayout<TILE, PPT>;
+    constexpr int NB = kRasterBatch;
     __shared__ BPair sp[NB];
     __shared__ float acc[9][NB];
     __shared__ int s_max;
     const int tile = blockIdx.x;
     const int tx = tile % cfg.tiles_x, ty = tile / cfg.tiles_x;
-    const int lx = threadIdx.x % TILE, ly = threadIdx.x / TILE;
-    const int x = tx * TILE + lx, y = ty * TILE + ly;
-    const bool inside = (x < W) && (y < H);
+    const int lx = threadIdx.x % TILE, ly0 = threadIdx.x / TILE;
+    const int x = tx * TILE + lx;
     const float centre = 0.5f * TILE;
-    const float du = ((float)lx + 0.5f) - centre, dv = ((float)ly + 0.5f) - centre;
-    const float xx = (float)lx + 0.5f, yy = (float)ly + 0.5f;
+    const float du = ((float)lx + 0.5f) - centre;
+    const float xx = (float)lx + 0.5f;
     const float ox = (float)(tx * TILE), oy = (float)(ty * TILE);
     const int2 rg = ranges[tile];
     const int lane = threadIdx.x & 31;
     const float amax = cfg.amax, amin = cfg.amin;
-    float T = 1.0f, g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, behind = 0.0f;
-    int last = 0;
-    if (inside) {
-        const size_t o = (size_t)y * W + x;
-        T = final_T[o];
-        last = n_contrib[o];
-        g0 = dimg[3 * o];
-        g1 = dimg[3 * o + 1];
-        g2 = dimg[3 * o + 2];
-        behind = T * (cfg.bg[0] * g0 + cfg.bg[1] * g1 + cfg.bg[2] * g2);
+    float dv[PPT], yy[PPT], T[PPT], g0[PPT], g1[PPT], g2[PPT], behind[PPT];
+    int last[PPT];
+    int my_max = 0;
+#pragma unroll
+    for (int i = 0; i < PPT; ++i) {
+        const int ly = ly0 + i * LY::kRowStep;
+        const int y = ty * TILE + ly;
+        dv[i] = ((float)ly + 0.5f) - centre;
+        yy[i] = (float)ly + 0.5f;
+        T[i] = 1.0f;
+        g0[i] = g1[i] = g2[i] = behind[i] = 0.0f;
+        last[i] = 0;
+        if (x < W && y < H) {
+            const size_t o = (size_t)y * W + x;
+            T[i] = final_T[o];
+            last[i] = n_contrib[o];
+            g0[i] = dimg[3 * o];
+            g1[i] = dimg[3 * o + 1];
+            g2[i] = dimg[3 * o + 2];
+            behind[i] = T[i] * (cfg.bg[0] * g0[i] + cfg.bg[1] * g1[i] + cfg.bg[2] * g2[i]);
+            my_max = max(my_max, last[i]);
+        }
     }
     if (threadIdx.x == 0) s_max = 0;
     __syncthreads();
-    if (last > 0) atomicMax(&s_max, last);
+    if (my_max > 0) atomicMax(&s_max, my_max);
     __syncthreads();
     const int maxl = s_max;
     for (int hi = maxl; hi > 0; hi -= NB) {
         const int lo = max(0, hi - NB);
         const int nb = hi - lo;
         __syncthreads();
-        if (threadIdx.x < nb) {
-            const uint32_t g = svals[rg.x + lo + threadIdx.x];
+        for (int s = threadIdx.x; s < nb; s += LY::kThreads) {
+            const uint32_t g = svals[rg.x + lo + s];
             const float4 p0 = pv.p0[g], p1 = pv.p1[g];
             BPair bp;
             bp.q = stage_pair(p0, p1, pv.p2[g], ox, oy, centre, bp.mxl, bp.myl);
@@ -230,45 +273,56 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             bp.B = p0.w;
             bp.C = p1.x;
             bp.gid = g;
-            sp[threadIdx.x] = bp;
+            sp[s] = bp;
 #pragma unroll
-            for (int k = 0; k < 9; ++k) acc[k][threadIdx.x] = 0.0f;
+            for (int k = 0; k < 9; ++k) acc[k][s] = 0.0f;
         }
         __syncthreads();
         for (int j = nb - 1; j >= 0; --j) {
+            const int idx = lo + j;
             float v[9];
 #pragma unroll
             for (int k = 0; k < 9; ++k) v[k] = 0.0f;
-            bool live = false;
-            if (lo + j < last) {
+            bool live_any = false;
+            if (idx < my_max) {
                 const BPair& bp = sp[j];
-                const float power = centred_power(bp.q, du, dv);
-                const float w = __expf(fminf(power, 0.0f));
-                const float raw = bp.q.op * w;
-                const bool clamp = raw > amax;
-                const float alpha = fminf(raw, amax);
-                if (alpha >= amin) {
-                    live = true;
-                    const float one_m = 1.0f - alpha;
-                    T = T / one_m;
-                    const float cg = bp.q.r * g0 + bp.q.g * g1 + bp.q.b * g2;
-                    const float dalpha = T * cg - behind / one_m;
-                    const float at = alpha * T;
-                    behind = __fmaf_rn(at, cg, behind);
+                const RPair q = bp.q;
+                const float t1 = __fmaf_rn(q.Af, du, q.Lx);
+                const float u = xx - bp.mxl;
+#pragma unroll
+                for (int i = 0; i < PPT; ++i) {
+                    if (idx >= last[i]) continue;
+                    const float t2 = __fmaf_rn(q.Bf, dv[i], t1);
+                    const float t3 = __fmaf_rn(q.Cf, dv[i], q.Ly);
+                    const float power = __fmaf_rn(dv[i], t3, __fmaf_rn(du, t2, q.P0));
+                    const float w = __expf(fminf(power, 0.0f));
+                    const float raw = q.op * w;
+                    const bool clamp = raw > amax;
+                    const float alpha = fminf(raw, amax);
+                    if (alpha < amin) continue;
+                    live_any = true;
+                    const float r = __fdividef(1.0f, 1.0f - alpha);
+                    const float Ti = T[i] * r;
+                    const float cg = q.r * g0[i] + q.g * g1[i] + q.b * g2[i];
+                    const float dalpha = Ti * cg - behind[i] * r;
+                    const float at = alpha * Ti;
+                    behind[i] = __fmaf_rn(at, cg, behind[i]);
+                    T[i] = Ti;
                     const float G = (!clamp && power <= 0.0f) ? dalpha * alpha : 0.0f;
-                    const float u = xx - bp.mxl, vv = yy - bp.myl;
-                    v[0] = clamp ? 0.0f : dalpha * w;
-                    v[1] = at * g0;
-                    v[2] = at * g1;
-                    v[3] = at * g2;
-                    v[4] = G * u * u;
-                    v[5] = G * u * vv;
-                    v[6] = G * vv * vv;
-                    v[7] = G * u;
-                    v[8] = G * vv;
+                    const float vv = yy[i] - bp.myl;
+                    const float Gu = G * u, Gv = G * vv;
+                    v[0] += clamp ? 0.0f : dalpha * w;
+                    v[1] = __fmaf_rn(at, g0[i], v[1]);
+                    v[2] = __fmaf_rn(at, g1[i], v[2]);
+                    v[3] = __fmaf_rn(at, g2[i], v[3]);
+                    v[4] = __fmaf_rn(Gu, u, v[4]);
+                    v[5] = __fmaf_rn(Gu, vv, v[5]);
+                    v[6] = __fmaf_rn(Gv, vv, v[6]);
+                    v[7] += Gu;
+                    v[8] += Gv;
                 }
             }
-            if (__any_sync(0xffffffffu, live)) {
+            if (__any_sync(0xffffffffu, live_any)) {
 #pragma unroll
                 for (int k = 0; k < 9; ++k) {
 #pragma unroll
@@ -281,11 +335,11 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             }
         }
         __syncthreads();
-        if (threadIdx.x < nb) {
-            const BPair& bp = sp[threadIdx.x];
-            const float s0 = acc[0][threadIdx.x], s1 = acc[1][threadIdx.x], s2 = acc[2][threadIdx.x];
-            const float s3 = acc[3][threadIdx.x], Suu = acc[4][threadIdx.x], Suv = acc[5][threadIdx.x];
-            const float Svv = acc[6][threadIdx.x], Su = acc[7][threadIdx.x], Sv = acc[8][threadIdx.x];
+        for (int s = threadIdx.x; s < nb; s += LY::kThreads) {
+            const BPair& bp = sp[s];
+            const float s0 = acc[0][s], s1 = acc[1][s], s2 = acc[2][s], s3 = acc[3][s];
+            const float Suu = acc[4][s], Suv = acc[5][s], Svv = acc[6][s], Su = acc[7][s];
+            const float Sv = acc[8][s];
             if (s0 != 0.0f || s1 != 0.0f || s2 != 0.0f || s3 != 0.0f || Su != 0.0f || Sv != 0.0f ||
                 Suu != 0.0f || Suv != 0.0f || Svv != 0.0f) {
                 float4* gr = reinterpret_cast<float4*>(grad2d + (size_t)bp.gid * kGradStride);
@@ -1171,9 +1225,9 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
         {
             KernelTimer kt("raster_fwd", st);
             if (c.tile == 16)
-                k_train_fwd<16><<<tiles, 256, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
+                k_train_fwd<16, 4><<<tiles, 64, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
             else
-                k_train_fwd<32><<<tiles, 1024, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
+                k_train_fwd<32, 4><<<tiles, 256, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
             GS_CHECK_LAUNCH();
         }
         LC.H = vh;
@@ -1201,11 +1255,11 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
             KernelTimer kt("raster_bwd", st);
             float* g2 = L.grad2d + (size_t)v * n * kGradStride;
             if (c.tile == 16)
-                k_train_bwd<16><<<tiles, 256, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
-                                                       L.final_T, L.ncon, g2);
+                k_train_bwd<16, 4><<<tiles, 64, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
+                                                         L.final_T, L.ncon, g2);
             else
-                k_train_bwd<32><<<tiles, 1024, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
-                                                        L.final_T, L.ncon, g2);
+                k_train_bwd<32, 4><<<tiles, 256, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
+                                                          L.final_T, L.ncon, g2);
             GS_CHECK_LAUNCH();
         }
         if (grad2d_out) {
