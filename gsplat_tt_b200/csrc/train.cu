@@ -76,44 +76,98 @@ __global__ void k_train_ranges(const uint32_t* __restrict__ skeys, const int64_t
 // (gsplat/blend_backward_ref.py:68-92), opacity and colour.
 struct RPair {
     float Af, Bf, Cf, P0, Lx, Ly, op, r, g, b;
+    uint32_t rows, cols;  // tile rows / columns with a pixel centre that can reach alpha_min
 };
 
+// Rows and columns of a TILE x TILE tile whose pixel centres can reach alpha >= amin for
+// this pair: alpha <= op exp(-m2 / 2), so a pixel can be live only if
+// m2 <= 2 ln(op / amin). Per row (column) the minimum of the quadratic form over the
+// row's (column's) centres is taken exactly; the test keeps a slack far above the fp32
+// error of both this bound and the per-pixel power (1e-4 of the form's magnitude plus
+// 0.02), so a skipped pixel is one the per-pixel test would skip too: results do not change.
+template <int TILE>
+__device__ __forceinline__ void reach_masks(float A, float B, float C, float op, float mxl,
+                                            float myl, float amin, uint32_t& rows,
+                                            uint32_t& cols) {
+    rows = 0u;
+    cols = 0u;
+    if (!(op >= amin)) return;
+    if (!(A > 0.0f) || !(C > 0.0f) || !(A * C - B * B > 0.0f)) {
+        rows = cols = (TILE == 32) ? 0xffffffffu : ((1u << TILE) - 1u);
+        return;
+    }
+    const float th = 2.0f * __logf(op / amin) + 0.02f;
+    const float ulo = 0.5f - mxl, uhi = (float)TILE - 0.5f - mxl;
+    const float vlo = 0.5f - myl, vhi = (float)TILE - 0.5f - myl;
+    const float iA = 1.0f / A, iC = 1.0f / C;
+#pragma unroll 4
+    for (int k = 0; k < TILE; ++k) {
+        {   // row k: v fixed, minimise over u
+            const float v = ((float)k + 0.5f) - myl;
+            const float us = fminf(fmaxf(-B * v * iA, ulo), uhi);
+            const float m2 = A * us * us + 2.0f * B * us * v + C * v * v;
+            const float mag = A * us * us + 2.0f * fabsf(B * us * v) + C * v * v;
+            if (m2 - 1e-4f * mag <= th) rows |= 1u << k;
+        }
+        {   // column k: u fixed, minimise over v
+            const float u = ((float)k + 0.5f) - mxl;
+            const float vs = fminf(fmaxf(-B * u * iC, vlo), vhi);
+            const float m2 = A * u * u + 2.0f * B * u * vs + C * vs * vs;
+            const float mag = A * u * u + 2.0f * fabsf(B * u * vs) + C * vs * vs;
+            if (m2 - 1e-4f * mag <= th) cols |= 1u << k;
+        }
+    }
+}
+
 // Coefficients in float64 from the fp32 conic and tile-local mean, rounded once.
+template <int TILE>
 __device__ __forceinline__ RPair stage_pair(float4 p0, float4 p1, float p2, float ox, float oy,
-                                            float centre, float& mxl, float& myl) {
+                                            float centre, float amin, float& mxl, float& myl) {
     RPair q;
-    mxl = p0.x - ox;
-    myl = p0.y - oy;
-    q.Af = -0.5f * p0.z;
+    mxl = __fsub_rn(p0.x, ox);
+    myl = __fsub_rn(p0.y, oy);
+    q.Af = __fmul_rn(-0.5f, p0.z);
     q.Bf = -p0.w;
-    q.Cf = -0.5f * p1.x;
+    q.Cf = __fmul_rn(-0.5f, p1.x);
+    // float64 without contraction, in the reference's operation order
+    // (gsplat/blend_backward_ref.py:79-84), rounded once to fp32.
     const double a = q.Af, b = q.Bf, c = q.Cf;
-    const double U0 = (double)centre - (double)mxl, V0 = (double)centre - (double)myl;
-    q.P0 = (float)(a * U0 * U0 + b * U0 * V0 + c * V0 * V0);
-    q.Lx = (float)(2.0 * a * U0 + b * V0);
-    q.Ly = (float)(b * U0 + 2.0 * c * V0);
+    const double U0 = __dsub_rn((double)centre, (double)mxl);
+    const double V0 = __dsub_rn((double)centre, (double)myl);
+    q.P0 = (float)__dadd_rn(__dadd_rn(__dmul_rn(__dmul_rn(a, U0), U0), __dmul_rn(__dmul_rn(b, U0), V0)),
+                            __dmul_rn(__dmul_rn(c, V0), V0));
+    q.Lx = (float)__dadd_rn(__dmul_rn(__dmul_rn(2.0, a), U0), __dmul_rn(b, V0));
+    q.Ly = (float)__dadd_rn(__dmul_rn(b, U0), __dmul_rn(__dmul_rn(2.0, c), V0));
     q.op = p1.y;
     q.r = p1.z;
     q.g = p1.w;
     q.b = p2;
+    reach_masks<TILE>(p0.z, p0.w, p1.x, p1.y, mxl, myl, amin, q.rows, q.cols);
     return q;
 }
 
-// power = P0 + du (Lx + Af du + Bf dv) + dv (Ly + Cf dv), with explicit FMAs so the forward
-// and backward kernels evaluate bit-identical alphas and hence identical decisions.
-__device__ __forceinline__ float centred_power(const RPair& q, float du, float dv) {
-    const float t2 = __fmaf_rn(q.Bf, dv, __fmaf_rn(q.Af, du, q.Lx));
-    const float t3 = __fmaf_rn(q.Cf, dv, q.Ly);
-    return __fmaf_rn(dv, t3, __fmaf_rn(du, t2, q.P0));
+// power = P0 + du (Lx + Af du + Bf dv) + dv (Ly + Cf dv), every product and sum rounded
+// separately in the reference's order (gsplat/blend_backward_ref.py:88-92): the forward and
+// backward kernels and the oracle evaluate bit-identical powers, so only exp can move a
+// forward decision. `lx_af` = Lx + Af du is shared by the pixels of one column.
+__device__ __forceinline__ float centred_power(const RPair& q, float lx_af, float du, float dv) {
+    const float inner = __fadd_rn(lx_af, __fmul_rn(q.Bf, dv));
+    const float e6 = __fadd_rn(q.P0, __fmul_rn(du, inner));
+    const float e8 = __fadd_rn(q.Ly, __fmul_rn(q.Cf, dv));
+    return __fadd_rn(e6, __fmul_rn(dv, e8));
+}
+__device__ __forceinline__ float lx_plus_af_du(const RPair& q, float du) {
+    return __fadd_rn(q.Lx, __fmul_rn(q.Af, du));
 }
 
 // Pixel layout of the rasterisers: a TILE x TILE tile is covered by TILE*TILE/PPT threads;
-// thread t owns column t % TILE and rows t / TILE + i * (TILE / PPT), i < PPT. One pair read
-// from shared memory then serves PPT pixels.
+// thread t owns column t % TILE and the PPT consecutive rows (t / TILE) * PPT + i. One pair
+// read from shared memory then serves PPT pixels, and the pair's row/column reach masks
+// decide per thread (and per warp) whether any of them needs evaluating.
 template <int TILE, int PPT>
 struct PixLayout {
     static constexpr int kThreads = TILE * TILE / PPT;
-    static constexpr int kRowStep = TILE / PPT;
+    static constexpr uint32_t kBandMask = (1u << PPT) - 1u;
 };
 
 constexpr int kRasterBatch = 128;  // pairs staged per batch
@@ -128,7 +182,7 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     __shared__ RPair sp[NB];
     const int tile = blockIdx.x;
     const int tx = tile % cfg.tiles_x, ty = tile / cfg.tiles_x;
-    const int lx = threadIdx.x % TILE, ly0 = threadIdx.x / TILE;
+    const int lx = threadIdx.x % TILE, ly0 = (threadIdx.x / TILE) * PPT;
     const int x = tx * TILE + lx;
     const float centre = 0.5f * TILE;
     const float du = ((float)lx + 0.5f) - centre;
@@ -140,7 +194,7 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     unsigned live_mask = 0;  // pixels still blending
 #pragma unroll
     for (int i = 0; i < PPT; ++i) {
-        const int ly = ly0 + i * LY::kRowStep;
+        const int ly = ly0 + i;
         dv[i] = ((float)ly + 0.5f) - centre;
         T[i] = 1.0f;
         c0[i] = c1[i] = c2[i] = 0.0f;
@@ -152,23 +206,24 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
         for (int s = threadIdx.x; s < NB && b0 + s < rg.y; s += LY::kThreads) {
             const uint32_t g = svals[b0 + s];
             float mxl, myl;
-            sp[s] = stage_pair(pv.p0[g], pv.p1[g], pv.p2[g], ox, oy, centre, mxl, myl);
+            sp[s] = stage_pair<TILE>(pv.p0[g], pv.p1[g], pv.p2[g], ox, oy, centre, amin, mxl, myl);
         }
         __syncthreads();
         const int nb = min(NB, rg.y - b0);
         for (int j = 0; j < nb && live_mask; ++j) {
             const RPair q = sp[j];
-            const float t1 = __fmaf_rn(q.Af, du, q.Lx);  // shared by the thread's pixels
+            const uint32_t reach = ((q.cols >> lx) & 1u) ? (q.rows >> ly0) & LY::kBandMask : 0u;
+            const uint32_t todo = reach & live_mask;
+            if (!todo) continue;
+            const float t1 = lx_plus_af_du(q, du);  // shared by the thread's pixels
 #pragma unroll
             for (int i = 0; i < PPT; ++i) {
-                if (!((live_mask >> i) & 1u)) continue;
-                const float t2 = __fmaf_rn(q.Bf, dv[i], t1);
-                const float t3 = __fmaf_rn(q.Cf, dv[i], q.Ly);
-                const float power = __fmaf_rn(dv[i], t3, __fmaf_rn(du, t2, q.P0));
+                if (!((todo >> i) & 1u)) continue;
+                const float power = centred_power(q, t1, du, dv[i]);
                 const float w = __expf(fminf(power, 0.0f));
-                const float alpha = fminf(q.op * w, amax);
+                const float alpha = fminf(__fmul_rn(q.op, w), amax);
                 if (alpha >= amin) {
-                    const float Tn = T[i] * (1.0f - alpha);
+                    const float Tn = __fmul_rn(T[i], __fsub_rn(1.0f, alpha));
                     if (Tn < tmin) {
                         live_mask &= ~(1u << i);
                     } else {
@@ -186,7 +241,7 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     }
 #pragma unroll
     for (int i = 0; i < PPT; ++i) {
-        const int y = ty * TILE + ly0 + i * LY::kRowStep;
+        const int y = ty * TILE + ly0 + i;
         if (x >= W || y >= H) continue;
         const size_t o = (size_t)y * W + x;
         image[3 * o] = c0[i] + T[i] * cfg.bg[0];
@@ -223,7 +278,7 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     __shared__ int s_max;
     const int tile = blockIdx.x;
     const int tx = tile % cfg.tiles_x, ty = tile / cfg.tiles_x;
-    const int lx = threadIdx.x % TILE, ly0 = threadIdx.x / TILE;
+    const int lx = threadIdx.x % TILE, ly0 = (threadIdx.x / TILE) * PPT;
     const int x = tx * TILE + lx;
     const float centre = 0.5f * TILE;
     const float du = ((float)lx + 0.5f) - centre;
@@ -237,7 +292,7 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     int my_max = 0;
 #pragma unroll
     for (int i = 0; i < PPT; ++i) {
-        const int ly = ly0 + i * LY::kRowStep;
+        const int ly = ly0 + i;
         const int y = ty * TILE + ly;
         dv[i] = ((float)ly + 0.5f) - centre;
         yy[i] = (float)ly + 0.5f;
@@ -268,7 +323,7 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             const uint32_t g = svals[rg.x + lo + s];
             const float4 p0 = pv.p0[g], p1 = pv.p1[g];
             BPair bp;
-            bp.q = stage_pair(p0, p1, pv.p2[g], ox, oy, centre, bp.mxl, bp.myl);
+            bp.q = stage_pair<TILE>(p0, p1, pv.p2[g], ox, oy, centre, amin, bp.mxl, bp.myl);
             bp.A = p0.z;
             bp.B = p0.w;
             bp.C = p1.x;
@@ -284,19 +339,19 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
 #pragma unroll
             for (int k = 0; k < 9; ++k) v[k] = 0.0f;
             bool live_any = false;
-            if (idx < my_max) {
-                const BPair& bp = sp[j];
+            const BPair& bp = sp[j];
+            const uint32_t reach = (idx < my_max && ((bp.q.cols >> lx) & 1u))
+                                       ? (bp.q.rows >> ly0) & LY::kBandMask : 0u;
+            if (reach) {
                 const RPair q = bp.q;
-                const float t1 = __fmaf_rn(q.Af, du, q.Lx);
+                const float t1 = lx_plus_af_du(q, du);
                 const float u = xx - bp.mxl;
 #pragma unroll
                 for (int i = 0; i < PPT; ++i) {
-                    if (idx >= last[i]) continue;
-                    const float t2 = __fmaf_rn(q.Bf, dv[i], t1);
-                    const float t3 = __fmaf_rn(q.Cf, dv[i], q.Ly);
-                    const float power = __fmaf_rn(dv[i], t3, __fmaf_rn(du, t2, q.P0));
+                    if (!((reach >> i) & 1u) || idx >= last[i]) continue;
+                    const float power = centred_power(q, t1, du, dv[i]);
                     const float w = __expf(fminf(power, 0.0f));
-                    const float raw = q.op * w;
+                    const float raw = __fmul_rn(q.op, w);
                     const bool clamp = raw > amax;
                     const float alpha = fminf(raw, amax);
                     if (alpha < amin) continue;

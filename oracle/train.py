@@ -374,6 +374,83 @@ def backward_2d(proj, image, dL_dimage, H, W, cfg: Cfg, ties: bool = False):
     return (out, tie_g) if ties else out
 
 
+def backward_2d_exact(proj, dL_dimage, H, W, cfg: Cfg, ties: bool = False):
+    """The same per-Gaussian 2D gradients as backward_2d, with the forward decisions
+    (alphas, clamps, live masks, stops) taken in fp32 exactly as the forward makes them and
+    every gradient term evaluated in float64. In exact arithmetic the reference's
+    front-to-back formula, dalpha_i = T_i c.g - (I.g - C_acc(<=i).g) / (1 - a_i), equals a
+    back-to-front accumulation of the colour behind each pair; evaluated in fp32 the
+    former cancels (I.g and C_acc.g are both O(1) while their difference is small behind
+    opaque layers) and loses up to a few 1e-3 relative on opaque scenes. This function
+    accumulates back to front in float64: the exact gradient of the fp32 forward."""
+    tile = cfg.tile
+    m2, con = np.asarray(proj["means2d"], f32), np.asarray(proj["conic"], f32)
+    op, col = np.asarray(proj["opacity"], f32), np.asarray(proj["colors"], f32)
+    N = m2.shape[0]
+    pl, utid, start, cnt, ox, oy, xx, yy, tx, ty, inside = _sweep(proj, H, W, tile)
+    nt = utid.size
+    centre = f32(tile / 2)
+
+    def tiles_of(a):
+        pad = np.zeros((ty * tile, tx * tile) + a.shape[2:], f32)
+        pad[:H, :W] = a
+        t = pad.reshape((ty, tile, tx, tile) + a.shape[2:]).swapaxes(1, 2)
+        return t.reshape((ty * tx, tile, tile) + a.shape[2:])[utid]
+    Gp = tiles_of(np.asarray(dL_dimage, f32)).astype(np.float64)
+    amax, amin, tmin, one = f32(cfg.alpha_max), f32(cfg.alpha_min), f32(cfg.t_min), f32(1)
+    near = lambda q, th: np.abs(q / th - 1.0) < TIE_RTOL  # noqa: E731
+    alive = inside.copy()
+    T = np.ones((nt, tile, tile), f32)
+    taint = np.zeros((nt, tile, tile), bool)
+    tie_g = np.zeros(N, bool)
+    recs = []
+    for k in range(int(cnt.max()) if nt else 0):   # fp32 forward: the decisions
+        n = int(np.searchsorted(-cnt, -k, side="left"))
+        g = pl["g"][start[:n] + k]
+        mxl, myl = m2[g, 0][:, None, None] - ox[:n], m2[g, 1][:, None, None] - oy[:n]
+        Af, Bf, Cf, P0, Lx, Ly = _centred(*(con[g, i][:, None, None] for i in range(3)),
+                                          mxl, myl, centre)
+        du, dv = xx - centre, yy - centre
+        power = (P0 + du * (Lx + Af * du + Bf * dv) + dv * (Ly + Cf * dv)).astype(f32)
+        wgt = np.exp(np.minimum(power, f32(0))).astype(f32)
+        raw = op[g][:, None, None] * wgt
+        clamp = raw > amax
+        alpha = np.where(clamp, amax, raw).astype(f32)
+        live = alive[:n] & (alpha >= amin)
+        if ties:
+            taint[:n] |= alive[:n] & (near(alpha, amin) | near(raw, amax)
+                                      | (live & near(T[:n] * (one - alpha), tmin)))
+            tie_g[g[(taint[:n] & (alpha >= amin * (one - f32(TIE_RTOL)))).any((1, 2))]] = True
+        stop = live & (T[:n] * (one - alpha) < tmin)
+        live &= ~stop
+        alive[:n] &= ~stop
+        T[:n] = np.where(live, T[:n] * (one - alpha), T[:n])
+        recs.append((n, g, mxl, myl, power, wgt, clamp, alpha, live))
+    Tc = T.astype(np.float64)
+    behind = Tc * (Gp * np.asarray(cfg.background, np.float64)).sum(-1)
+    grads = np.zeros((N, 9), np.float64)
+    for (n, g, mxl, myl, power, wgt, clamp, alpha, live) in reversed(recs):
+        a, w = alpha.astype(np.float64), wgt.astype(np.float64)
+        Gk = Gp[:n]
+        cg = (col[g][:, None, None, :].astype(np.float64) * Gk).sum(-1)
+        Ti = np.where(live, Tc[:n] / (1.0 - a), Tc[:n])
+        dal = Ti * cg - behind[:n] / (1.0 - a)
+        at = np.where(live, a * Ti, 0.0)
+        behind[:n] += at * cg
+        Tc[:n] = Ti
+        u = (xx - mxl).astype(np.float64)
+        v = (yy - myl).astype(np.float64)
+        G = np.where(live & ~clamp & (power <= 0), dal * a, 0.0)
+        terms = np.stack([np.where(live & ~clamp, dal * w, 0.0), at * Gk[..., 0], at * Gk[..., 1],
+                          at * Gk[..., 2], G * u * u, G * u * v, G * v * v, G * u, G * v], -1)
+        s = terms.reshape(n, -1, 9).sum(1)
+        Ac, Bc, Cc_ = (con[g, i].astype(np.float64) for i in range(3))
+        pair = np.stack([Ac * s[:, 7] + Bc * s[:, 8], Bc * s[:, 7] + Cc_ * s[:, 8], -0.5 * s[:, 4],
+                         -s[:, 5], -0.5 * s[:, 6], s[:, 0], s[:, 1], s[:, 2], s[:, 3]], 1)
+        np.add.at(grads, g, pair)
+    return (grads, tie_g) if ties else grads
+
+
 # ------------------------------------------------------------------ loss
 
 WIN, SIGMA = 11, 1.5

@@ -143,3 +143,14 @@ def test_blend_backward_vs_dense_fp64_oracle():
         ref = np.concatenate([d["dL_dmeans2d"], d["dL_dconic"], d["dL_dopacity"][:, None],
                               d["dL_dcolors"]], 1)
         assert ot.rel_error(g2d[vis], ref[vis]) <= 1e-2
+
+
+def test_exact_backward_agrees_with_reference_formula(tiled):
+    """float64 back-to-front (backward_2d_exact) vs the reference's fp32 front-to-back slots
+    on the reference-pinned tiled case: the same gradient up to the fp32 formula's error."""
+    params, w2c, K, H, W = tiled_inputs(tiled)
+    cfg = ot.Cfg(sh_degree=0, tile=32)
+    pr = ot.project(params, w2c, K, H, W, cfg)
+    g64 = ot.backward_2d_exact(pr, tiled["dL_dimage"], H, W, cfg)
+    ok = ~tiled["tie_g"]
+    assert ot.rel_error(g64[ok], tiled["g2d"][ok]) <= 2e-3
