@@ -57,6 +57,8 @@ _sig("gs_compute_cov3d", status, vp, vp, i64, vp, vp)
 _sig("gs_project", status, vp, vp, vp, vp, vp, vp, f32, i64, i32, i32, i32, f32, f32, i32,
      vp, vp, vp, vp, vp, vp, vp, vp, vp, vp, sz, vp)
 _sig("gs_project_workspace_size", sz, i64)
+_sig("gs_project_noalloc", status, vp, vp, vp, vp, vp, vp, f32, i64, i32, i32, i32, f32, f32, i32,
+     vp, vp, vp, vp, vp, vp, vp, vp, vp, vp)
 _sig("gs_tile_assign", status, vp, vp, i64, i32, i32, i32, vp, vp, f32, vp, vp, i64, vp, vp,
      vp, vp, sz, vp)
 _sig("gs_tile_assign_workspace_size", sz, i64, i64)

@@ -8,6 +8,7 @@
 // precondition for bit-exact pair counts, sorted orders and tile ranges.
 #include <cstdarg>
 #include <cstring>
+#include <mutex>
 
 #include "common.cuh"
 #include "scan.cuh"
@@ -687,6 +688,108 @@ extern "C" gs_status gs_tile_assign(const float* means_2d, const float* radii, i
     GS_CHECK_LAUNCH();
     if (num_pairs_host) {
         GS_CUDA_CHECK(cudaMemcpyAsync(num_pairs_host, num_pairs_dev, sizeof(int64_t),
+                                      cudaMemcpyDeviceToHost, st));
+        GS_CUDA_CHECK(cudaStreamSynchronize(st));
+    }
+    return GS_OK;
+}
+
+// ================================================================== allocation-free projection
+//
+// A second entry to the projection for callers that cannot allocate device memory, whose
+// only scratch (one int64 visible count per 256-Gaussian block) lives in the array below.
+// The array is ordinary module memory: every device that loads the library holds it
+// (512 KB) until the process exits.
+
+static constexpr int64_t kNoAllocMaxGaussians = 1ll << 24;
+static constexpr int64_t kNoAllocScratch = (kNoAllocMaxGaussians + kProjBlock - 1) / kProjBlock + 1;
+static __device__ __align__(256) int64_t g_project_scratch[kNoAllocScratch];
+
+static constexpr int kNoAllocMaxDevices = 64;
+static std::mutex g_project_scratch_mu;
+static int64_t* g_project_scratch_addr[kNoAllocMaxDevices] = {};
+
+// Device address of g_project_scratch on the current device. In host code the array's
+// name is only a host-side stand-in, so the address is looked up once per device (with
+// that device current) and cached.
+static gs_status project_scratch_address(int64_t** out) {
+    int dev = 0;
+    GS_CUDA_CHECK(cudaGetDevice(&dev));
+    GS_ARG_CHECK(dev >= 0 && dev < kNoAllocMaxDevices,
+                 "gs_project_noalloc: device %d is beyond the %d devices it supports", dev,
+                 kNoAllocMaxDevices);
+    std::lock_guard<std::mutex> lock(g_project_scratch_mu);
+    if (g_project_scratch_addr[dev] == nullptr) {
+        int64_t* ptr = nullptr;
+        const cudaError_t err = cudaGetSymbolAddress((void**)&ptr, g_project_scratch);
+        if (err != cudaSuccess || ptr == nullptr) {
+            set_error("gs_project_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                      cudaGetErrorString(err));
+            return GS_ERR_CUDA;
+        }
+        g_project_scratch_addr[dev] = ptr;
+    }
+    *out = g_project_scratch_addr[dev];
+    return GS_OK;
+}
+
+extern "C" gs_status gs_project_noalloc(const float* means, const float* cov3d, const float* e,
+                                        const float* K, const float* colors,
+                                        const float* opacities, float min_opacity, int64_t n,
+                                        int32_t height, int32_t width, int32_t max_radius,
+                                        float contrib_floor, float k_cap, int32_t use_isoellipse,
+                                        float* means_2d, float* covs_2d, float* depths,
+                                        float* radii, uint8_t* valid_mask, float* colors_out,
+                                        float* opacities_out, int64_t* num_visible_dev,
+                                        int64_t* num_visible_host, void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    GS_ARG_CHECK(n >= 0 && n <= kNoAllocMaxGaussians,
+                 "gs_project_noalloc: n = %lld, but at most %lld Gaussians fit its fixed "
+                 "scratch; use gs_project with a workspace for more",
+                 (long long)n, (long long)kNoAllocMaxGaussians);
+    if (use_isoellipse) {
+        set_error("gs_project_noalloc: use_isoellipse is not supported");
+        return GS_ERR_UNSUPPORTED;
+    }
+    GS_ARG_CHECK(height > 0 && width > 0, "gs_project_noalloc: bad sizes");
+    GS_ARG_CHECK(e && K, "gs_project_noalloc: extrinsics/intrinsics (host) required");
+    GS_ARG_CHECK(num_visible_dev, "gs_project_noalloc: num_visible_dev required");
+    if (n > 0)
+        GS_ARG_CHECK(means && cov3d && means_2d && covs_2d && depths && radii && valid_mask,
+                     "gs_project_noalloc: null pointer");
+    GS_ARG_CHECK(contrib_floor > 0.0f, "gs_project_noalloc: contrib_floor must be > 0");
+    int64_t* blocks = nullptr;
+    gs_status s = project_scratch_address(&blocks);
+    if (s != GS_OK) return s;
+    ProjCam P;
+    const float r[9] = {e[0], e[1], e[2], e[4], e[5], e[6], e[8], e[9], e[10]};
+    memcpy(P.r, r, sizeof(r));
+    P.t[0] = e[3]; P.t[1] = e[7]; P.t[2] = e[11];
+    P.fx = K[0]; P.fy = K[4]; P.cx = K[2]; P.cy = K[5];
+    P.height = height; P.width = width;
+    const int mr = max_radius < 0 ? 0x7fffffff
+                                   : (max_radius > 0 ? max_radius : (height < width ? height : width) / 2);
+    P.max_r = (float)mr;
+    P.min_opacity = min_opacity; P.contrib_floor = contrib_floor; P.k_cap = k_cap;
+    if (n == 0) {
+        GS_CUDA_CHECK(cudaMemsetAsync(num_visible_dev, 0, sizeof(int64_t), st));
+        if (num_visible_host) *num_visible_host = 0;
+        return GS_OK;
+    }
+    // Every scratch entry this call reads is written earlier in the same call (one count
+    // per block, then the in-place scan), so nothing needs clearing between calls.
+    const unsigned int nb = div_up(n, kProjBlock);
+    k_project_count<<<nb, kProjBlock, 0, st>>>(P, means, cov3d, opacities, n, valid_mask, blocks);
+    GS_CHECK_LAUNCH();
+    scan_block_totals<int64_t><<<1, 1024, 0, st>>>(blocks, nb, num_visible_dev);
+    GS_CHECK_LAUNCH();
+    k_project_emit<<<nb, kProjBlock, 0, st>>>(P, means, cov3d, opacities, colors, n, valid_mask,
+                                              blocks, means_2d, covs_2d, depths, radii, colors_out,
+                                              opacities_out);
+    GS_CHECK_LAUNCH();
+    if (num_visible_host) {
+        GS_CUDA_CHECK(cudaMemcpyAsync(num_visible_host, num_visible_dev, sizeof(int64_t),
                                       cudaMemcpyDeviceToHost, st));
         GS_CUDA_CHECK(cudaStreamSynchronize(st));
     }

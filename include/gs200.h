@@ -101,6 +101,28 @@ gs_status gs_project(const float* means, const float* cov3d, const float* extrin
                      void* stream);
 size_t gs_project_workspace_size(int64_t n);
 
+/* gs_project without a workspace, for callers that cannot allocate device memory -- a
+ * plug-in running inside a host application that owns every device buffer, or a real-time
+ * loop where the synchronising cudaMalloc is not allowed. No counterpart in the reference
+ * (its CPU stages allocate std::vectors freely).
+ *   Same arguments, results and errors as gs_project, minus the workspace. Its scratch is a
+ *   fixed 512 KB array inside libgs200.so, present on every device that loads the library
+ *   until the process exits; it bounds n to at most 16,777,216 (2^24) Gaussians, and a
+ *   larger n returns GS_ERR_ARG. It calls no allocator.
+ *   The first call on a device looks up that array's device address (cudaGetSymbolAddress)
+ *   and caches it; make that first call before any stream capture.
+ *   All calls share the one array: calls that may overlap on the GPU (different streams or
+ *   host threads without ordering between them) race and corrupt each other's results.
+ *   Nothing is left over between calls that a later call depends on. */
+gs_status gs_project_noalloc(const float* means, const float* cov3d, const float* extrinsics,
+                             const float* intrinsics, const float* colors, const float* opacities,
+                             float min_opacity, int64_t n, int32_t height, int32_t width,
+                             int32_t max_radius, float contrib_floor, float k_cap,
+                             int32_t use_isoellipse, float* means_2d, float* covs_2d,
+                             float* depths, float* radii, uint8_t* valid_mask,
+                             float* colors_out, float* opacities_out, int64_t* num_visible_dev,
+                             int64_t* num_visible_host, void* stream);
+
 /* tile_assign (src/gsplat_cpu/tile_assign.cpp:26-368; pybind tile_assign,
  * backends/cpu_cpp/pybind_module.cpp:318-392).
  *   means_2d M*2, radii M*2; covs_2d M*4 and opacities M are both NULL (no pair cull)
