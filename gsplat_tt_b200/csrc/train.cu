@@ -171,6 +171,7 @@ struct PixLayout {
 };
 
 constexpr int kRasterBatch = 128;  // pairs staged per batch
+constexpr int kRasterPPT = 4;      // pixels per thread: 64 threads per 16x16 tile
 
 template <int TILE, int PPT>
 __global__ void __launch_bounds__(TILE * TILE / PPT)
@@ -1280,9 +1281,9 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
         {
             KernelTimer kt("raster_fwd", st);
             if (c.tile == 16)
-                k_train_fwd<16, 4><<<tiles, 64, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
+                k_train_fwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
             else
-                k_train_fwd<32, 4><<<tiles, 256, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
+                k_train_fwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
             GS_CHECK_LAUNCH();
         }
         LC.H = vh;
@@ -1310,10 +1311,10 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
             KernelTimer kt("raster_bwd", st);
             float* g2 = L.grad2d + (size_t)v * n * kGradStride;
             if (c.tile == 16)
-                k_train_bwd<16, 4><<<tiles, 64, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
+                k_train_bwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
                                                          L.final_T, L.ncon, g2);
             else
-                k_train_bwd<32, 4><<<tiles, 256, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
+                k_train_bwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
                                                           L.final_T, L.ncon, g2);
             GS_CHECK_LAUNCH();
         }

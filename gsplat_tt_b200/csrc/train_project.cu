@@ -185,30 +185,47 @@ k_sorted_count(const uint32_t* __restrict__ cnt, const uint32_t* __restrict__ or
 // Pairs of the Gaussians in depth order, each Gaussian's tiles row-major: key = tile id,
 // value = Gaussian id. A stable sort on the tile id then yields the reference's
 // (tile, depth bits, Gaussian id) order (src/gsplat_cpu/sort.cpp:24-27).
+// Warp-cooperative: the warp's 32 Gaussians own one contiguous run of pairs, and lane l
+// writes pairs l, l + 32, ... of that run (finding its Gaussian by a binary search over
+// the warp's offsets), so consecutive lanes store to consecutive addresses.
 __global__ void __launch_bounds__(kProjThreads)
 k_train_emit(ProjView pv, const uint32_t* __restrict__ order, int64_t n, int tiles_x,
              const int64_t* __restrict__ blk_offsets, int64_t capacity,
              uint32_t* __restrict__ keys, uint32_t* __restrict__ vals,
              unsigned int* __restrict__ err) {
     __shared__ int64_t smem[33];
+    __shared__ int64_t s_off[kProjThreads];   // first pair of each thread's Gaussian
+    __shared__ uint32_t s_gid[kProjThreads];
+    __shared__ ushort4 s_rect[kProjThreads];
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t g = (i < n) ? order[i] : 0u;
     const uint32_t c = (i < n) ? pv.cnt[g] : 0u;
     int64_t total;
     const int64_t off = blk_offsets[blockIdx.x] + block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
-    if (c == 0) return;
-    if (off + c > capacity) {
-        atomicOr(err, DEV_OVERFLOW);
+    s_off[threadIdx.x] = off;
+    s_gid[threadIdx.x] = g;
+    s_rect[threadIdx.x] = (c > 0) ? pv.rect[g] : make_ushort4(0, 0, 0, 0);
+    __syncwarp();
+    const int lane = threadIdx.x & 31, wbase = threadIdx.x & ~31;
+    const int64_t run0 = __shfl_sync(0xffffffffu, off, 0);
+    const int64_t run1 = __shfl_sync(0xffffffffu, off + (int64_t)c, 31);
+    if (run1 > capacity) {
+        if (c > 0 && off + (int64_t)c > capacity) atomicOr(err, DEV_OVERFLOW);
         return;
     }
-    const ushort4 r = pv.rect[g];
-    int64_t pos = off;
-    for (int ty = r.z; ty <= r.w; ++ty)
-        for (int tx = r.x; tx <= r.y; ++tx) {
-            keys[pos] = (uint32_t)(ty * tiles_x + tx);
-            vals[pos] = g;
-            ++pos;
+    for (int64_t p = run0 + lane; p < run1; p += 32) {
+        int lo = 0, hi = 31;  // last lane of the warp whose first pair is <= p
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s_off[wbase + mid] <= p) lo = mid; else hi = mid - 1;
         }
+        const ushort4 r = s_rect[wbase + lo];
+        const int w = r.y - r.x + 1;
+        const int j = (int)(p - s_off[wbase + lo]);
+        const int ty = r.z + j / w, tx = r.x + j % w;
+        keys[p] = (uint32_t)(ty * tiles_x + tx);
+        vals[p] = s_gid[wbase + lo];
+    }
 }
 
 void launch_project(const GConst& P, int64_t n, const TCam& cam, const TCfg& cfg, int view,
