@@ -12,12 +12,34 @@ namespace gs {
 
 __device__ __forceinline__ float exp_rounded(float x) { return (float)exp((double)x); }
 
+// SH coefficients of a block's Gaussians are staged in shared memory with coalesced 16-byte
+// loads (the block's rows are one contiguous run of 3 K floats each); each thread then
+// reads its own row from shared memory.
+template <int DEG>
 __global__ void __launch_bounds__(kProjThreads)
 k_train_project(GConst P, int64_t n, TCam cam, TCfg cfg, int view, ProjView pv,
                 int64_t* __restrict__ blk, uint64_t* __restrict__ touch,
                 float* __restrict__ vis_counts, float* __restrict__ grad2d) {
+    constexpr int K = (DEG + 1) * (DEG + 1);
+    constexpr int ROW = 3 * K;  // floats of SH per Gaussian
+    extern __shared__ __align__(16) float s_sh[];
     __shared__ int64_t smem[33];
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    {
+        const int64_t g0 = (int64_t)blockIdx.x * blockDim.x;
+        const int rows = (int)min((int64_t)blockDim.x, n - g0);
+        const float* src = P.sh + (size_t)g0 * ROW;
+        const int total = rows * ROW;
+        if (((uintptr_t)src & 15u) == 0) {
+            const int nv = total >> 2;
+            for (int i = threadIdx.x; i < nv; i += blockDim.x)
+                reinterpret_cast<float4*>(s_sh)[i] = reinterpret_cast<const float4*>(src)[i];
+            for (int i = (nv << 2) + threadIdx.x; i < total; i += blockDim.x) s_sh[i] = src[i];
+        } else {
+            for (int i = threadIdx.x; i < total; i += blockDim.x) s_sh[i] = src[i];
+        }
+        __syncthreads();
+    }
     uint32_t count = 0;
     if (g < n) {
         const float m0 = P.means[3 * g], m1 = P.means[3 * g + 1], m2 = P.means[3 * g + 2];
@@ -96,19 +118,19 @@ k_train_project(GConst P, int64_t n, TCam cam, TCfg cfg, int view, ProjView pv,
             const float dx = d0 / dn, dy = d1 / dn, dz = d2 / dn;
             float basis[16];
             basis[0] = 0.28209479177387814f;
-            if (cfg.sh_degree >= 1) {
+            if (DEG >= 1) {
                 basis[1] = -0.4886025119029199f * dy;
                 basis[2] = 0.4886025119029199f * dz;
                 basis[3] = -0.4886025119029199f * dx;
             }
-            if (cfg.sh_degree >= 2) {
+            if (DEG >= 2) {
                 const float xx = dx * dx, yy = dy * dy, zz = dz * dz;
                 basis[4] = 1.0925484305920792f * (dx * dy);
                 basis[5] = -1.0925484305920792f * (dy * dz);
                 basis[6] = 0.31539156525252005f * (2.0f * zz - xx - yy);
                 basis[7] = -1.0925484305920792f * (dx * dz);
                 basis[8] = 0.5462742152960396f * (xx - yy);
-                if (cfg.sh_degree >= 3) {
+                if (DEG >= 3) {
                     basis[9] = -0.5900435899266435f * dy * (3.0f * xx - yy);
                     basis[10] = 2.890611442640554f * (dx * dy) * dz;
                     basis[11] = -0.4570457994644658f * dy * (4.0f * zz - xx - yy);
@@ -118,11 +140,12 @@ k_train_project(GConst P, int64_t n, TCam cam, TCfg cfg, int view, ProjView pv,
                     basis[15] = -0.5900435899266435f * dx * (xx - 3.0f * yy);
                 }
             }
-            const float* sh = P.sh + (size_t)g * cfg.K * 3;
+            const float* sh = s_sh + threadIdx.x * ROW;
 #pragma unroll
             for (int ch = 0; ch < 3; ++ch) {
                 float r = basis[0] * sh[ch];
-                for (int k = 1; k < cfg.K; ++k) r = r + basis[k] * sh[3 * k + ch];
+#pragma unroll
+                for (int k = 1; k < K; ++k) r = r + basis[k] * sh[3 * k + ch];
                 r = r + 0.5f;
                 col[ch] = fmaxf(r, 0.0f);
             }
@@ -231,8 +254,23 @@ k_train_emit(ProjView pv, const uint32_t* __restrict__ order, int64_t n, int til
 void launch_project(const GConst& P, int64_t n, const TCam& cam, const TCfg& cfg, int view,
                     const ProjView& pv, int64_t* blk, uint64_t* touch, float* vis_counts,
                     float* grad2d, cudaStream_t st) {
-    k_train_project<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(P, n, cam, cfg, view, pv, blk,
-                                                                      touch, vis_counts, grad2d);
+    const unsigned int nb = div_up(n, kProjThreads);
+    const size_t smem = (size_t)kProjThreads * 3 * cfg.K * sizeof(float);
+    switch (cfg.sh_degree) {
+        case 0:
+            k_train_project<0><<<nb, kProjThreads, smem, st>>>(P, n, cam, cfg, view, pv, blk, touch, vis_counts, grad2d);
+            break;
+        case 1:
+            k_train_project<1><<<nb, kProjThreads, smem, st>>>(P, n, cam, cfg, view, pv, blk, touch, vis_counts, grad2d);
+            break;
+        case 2:
+            k_train_project<2><<<nb, kProjThreads, smem, st>>>(P, n, cam, cfg, view, pv, blk, touch, vis_counts, grad2d);
+            break;
+        default:
+            cudaFuncSetAttribute(k_train_project<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+            k_train_project<3><<<nb, kProjThreads, smem, st>>>(P, n, cam, cfg, view, pv, blk, touch, vis_counts, grad2d);
+            break;
+    }
 }
 
 void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int64_t* blk,
