@@ -1,56 +1,32 @@
-// radix_sort.cu -- stable LSD radix sort of (uint64 key, uint32 value) pairs.
+// radix_sort.cu -- stable LSD radix sort of (key, uint32 value) pairs, 64- or 32-bit keys.
 //
-// Onesweep structure: one up-front kernel reads every key once and builds the digit
-// histograms of all passes; each pass is then a single kernel that ranks a 4096-item
-// tile in shared memory (warp-level multisplit with __match_any_sync), publishes the
-// tile's per-digit counts, resolves its global digit offsets with a decoupled
-// look-back over earlier tiles, and writes the tile out in digit-sorted runs so the
-// global stores are coalesced. Only the low `key_bits` bits are sorted: passes above
-// the tile-id bit width are skipped (45 bits for 8,160 tiles -> 6 passes).
-//
-// Every look-back wait is bounded; on timeout the kernel raises DEV_TIMEOUT in the
-// error word and continues with the offsets it has, so the host reports
-// GS_ERR_TIMEOUT instead of the GPU hanging.
+// One up-front kernel reads every key once and builds the digit histograms of all passes;
+// each pass is then one onesweep kernel (onesweep.cuh). Only the low `key_bits` bits are
+// sorted: passes above the key's bit width are skipped (45 bits for 8,160 display tiles
+// -> 6 passes).
 #include "common.cuh"
+#include "onesweep.cuh"
 #include "radix_sort.cuh"
+#include "rect_pairs.cuh"
 
 namespace gs {
 
-constexpr int kRadixBits = 8;
-constexpr int kRadix = 1 << kRadixBits;
-constexpr int kSortThreads = 256;
-constexpr int kSortWarps = kSortThreads / 32;
-constexpr int kSortItems = 16;
-constexpr int kTileItems = kSortThreads * kSortItems;  // 4096
-constexpr unsigned int kFlagAgg = 1u << 30;
-constexpr unsigned int kFlagInc = 2u << 30;
-constexpr unsigned int kValueMask = (1u << 30) - 1;
-constexpr int kSpinLimit = 1 << 22;
-
-static_assert(kSortThreads == kRadix, "one thread per digit in the look-back");
-
-template <typename KeyT>
-struct SortSmem {
-    KeyT keys[kTileItems];
-    uint32_t vals[kTileItems];
-    uint32_t warp_hist[kSortWarps][kRadix];
-    uint32_t local_off[kRadix];
-    uint32_t gbase[kRadix];
-    uint32_t tile;
-};
-
-// Digit histograms of every pass in one read of the keys.
+// Digit histograms of every pass in one read of the keys (only the low key_bits bits).
 template <typename KeyT>
 __global__ void k_radix_hist(const KeyT* __restrict__ keys, const int64_t* __restrict__ n_dev,
-                             int64_t n_host, int npass, uint32_t* __restrict__ hist) {
+                             int64_t n_host, int npass, int key_bits, uint32_t* __restrict__ hist) {
     __shared__ uint32_t sh[8][kRadix];
-    const int64_t n = n_dev ? min(*n_dev, n_host) : n_host;  // device count, capped
+    const int64_t nd = n_dev ? *n_dev : n_host;
+    const int64_t n = nd <= n_host ? nd : 0;  // over capacity: nothing (see k_onesweep_pass)
     for (int i = threadIdx.x; i < 8 * kRadix; i += blockDim.x) (&sh[0][0])[i] = 0;
     __syncthreads();
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
          i += (int64_t)gridDim.x * blockDim.x) {
         const KeyT k = keys[i];
-        for (int p = 0; p < npass; ++p) atomicAdd(&sh[p][(uint32_t)(k >> (p * kRadixBits)) & (kRadix - 1)], 1u);
+        for (int p = 0; p < npass; ++p) {
+            const uint32_t mask = (1u << min(kRadixBits, key_bits - p * kRadixBits)) - 1u;
+            atomicAdd(&sh[p][(uint32_t)(k >> (p * kRadixBits)) & mask], 1u);
+        }
     }
     __syncthreads();
     for (int i = threadIdx.x; i < npass * kRadix; i += blockDim.x) {
@@ -75,150 +51,6 @@ __global__ void k_radix_hist_scan(uint32_t* __restrict__ hist, int npass) {
         hist[p * kRadix + threadIdx.x] = s[threadIdx.x] - v;
         __syncthreads();
     }
-}
-
-__device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
-    return *(const volatile uint32_t*)p;
-}
-__device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) { *(volatile uint32_t*)p = v; }
-
-// One onesweep pass over digit `shift`.
-template <typename KeyT>
-__global__ void __launch_bounds__(kSortThreads, 3)
-k_radix_pass(const KeyT* __restrict__ keys_in, const uint32_t* __restrict__ vals_in,
-             KeyT* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
-             const int64_t* __restrict__ n_dev, int64_t n_host, int shift,
-             const uint32_t* __restrict__ digit_offsets, uint32_t* __restrict__ lookback,
-             uint32_t* __restrict__ tile_counter, unsigned int* __restrict__ err) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    SortSmem<KeyT>& S = *reinterpret_cast<SortSmem<KeyT>*>(smem_raw);
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t n = n_dev ? min(*n_dev, n_host) : n_host;  // device count, capped
-
-    if (tid == 0) S.tile = atomicAdd(tile_counter, 1u);
-    for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads) (&S.warp_hist[0][0])[i] = 0;
-    __syncthreads();
-    const uint32_t tile = S.tile;
-    const int64_t base = (int64_t)tile * kTileItems;
-    if (base >= n) return;
-    const int valid = (int)min((int64_t)kTileItems, n - base);
-
-    // Load (warp-striped: warp w owns items [512 w, 512 w + 512) of the tile). Pads
-    // past the end get an all-ones digit so they rank after every real item.
-    KeyT key[kSortItems];
-    uint32_t val[kSortItems];
-#pragma unroll
-    for (int j = 0; j < kSortItems; ++j) {
-        const int li = warp * (kSortItems * 32) + j * 32 + lane;
-        if (li < valid) {
-            key[j] = keys_in[base + li];
-            val[j] = vals_in ? vals_in[base + li] : (uint32_t)(base + li);  // null: iota
-        } else {
-            key[j] = (KeyT)(kRadix - 1) << shift;
-            val[j] = 0;
-        }
-    }
-#define GS_DIGIT(k) ((uint32_t)((k) >> shift) & (uint32_t)(kRadix - 1))
-
-    // Warp-level multisplit: rank of each item among the warp's items of its digit.
-    // Peers are found with one ballot per digit bit (pure ALU, pipelines across items);
-    // each peer group's leader claims the group's slots with one shared atomic, kept in
-    // item order by __syncwarp.
-    uint32_t rank[kSortItems];
-    const uint32_t lt_mask = (1u << lane) - 1u;
-#pragma unroll
-    for (int j = 0; j < kSortItems; ++j) {
-        const uint32_t d = GS_DIGIT(key[j]);
-        uint32_t peers = 0xffffffffu;
-#pragma unroll
-        for (int b = 0; b < kRadixBits; ++b) {
-            const uint32_t bit = (d >> b) & 1u;
-            const uint32_t m = __ballot_sync(0xffffffffu, bit);
-            peers &= bit ? m : ~m;
-        }
-        const int leader = 31 - __clz(peers);
-        uint32_t old = 0;
-        if (lane == leader) old = atomicAdd(&S.warp_hist[warp][d], (uint32_t)__popc(peers));
-        rank[j] = __shfl_sync(0xffffffffu, old, leader) + __popc(peers & lt_mask);
-        __syncwarp();
-    }
-    __syncthreads();
-
-    // Per digit (thread = digit): warp prefix, tile count, then the tile's offset.
-    const int d = tid;
-    uint32_t count = 0;
-#pragma unroll
-    for (int w = 0; w < kSortWarps; ++w) {
-        const uint32_t c = S.warp_hist[w][d];
-        S.warp_hist[w][d] = count;
-        count += c;
-    }
-    if (d == kRadix - 1) count -= (uint32_t)(kTileItems - valid);
-
-    // Decoupled look-back over earlier tiles of this pass.
-    uint32_t* my = lookback + (size_t)tile * kRadix + d;
-    uint32_t excl = 0;
-    if (tile == 0) {
-        st_volatile(my, kFlagInc | count);
-    } else {
-        st_volatile(my, kFlagAgg | count);
-        int64_t k = (int64_t)tile - 1;
-        int spins = 0;
-        while (k >= 0) {
-            const uint32_t v = ld_volatile(lookback + (size_t)k * kRadix + d);
-            const uint32_t flag = v & ~kValueMask;
-            if (flag == 0u) {
-                if (++spins > kSpinLimit) {
-                    atomicOr(err, DEV_TIMEOUT);
-                    break;
-                }
-                __nanosleep(32);
-                continue;
-            }
-            excl += v & kValueMask;
-            if (flag == kFlagInc) break;
-            --k;
-        }
-        st_volatile(my, kFlagInc | (excl + count));
-    }
-    S.gbase[d] = digit_offsets[d] + excl;
-
-    // Block-local exclusive offsets of the digits (tile-sorted order).
-    {
-        __shared__ uint32_t scan_s[kRadix];
-        scan_s[d] = count + (d == kRadix - 1 ? (uint32_t)(kTileItems - valid) : 0u);
-        __syncthreads();
-        for (int o = 1; o < kRadix; o <<= 1) {
-            const uint32_t t = (d >= o) ? scan_s[d - o] : 0u;
-            __syncthreads();
-            scan_s[d] += t;
-            __syncthreads();
-        }
-        const uint32_t tot = count + (d == kRadix - 1 ? (uint32_t)(kTileItems - valid) : 0u);
-        S.local_off[d] = scan_s[d] - tot;
-    }
-    __syncthreads();
-
-    // Scatter into shared memory in digit-sorted order.
-#pragma unroll
-    for (int j = 0; j < kSortItems; ++j) {
-        const uint32_t d = GS_DIGIT(key[j]);
-        const uint32_t pos = S.local_off[d] + S.warp_hist[warp][d] + rank[j];
-        S.keys[pos] = key[j];
-        S.vals[pos] = val[j];
-    }
-    __syncthreads();
-
-    // Coalesced write-out: consecutive threads write consecutive items of a digit run.
-#pragma unroll 4
-    for (int i = tid; i < valid; i += kSortThreads) {
-        const KeyT k = S.keys[i];
-        const uint32_t dd = GS_DIGIT(k);
-        const uint32_t out = S.gbase[dd] + ((uint32_t)i - S.local_off[dd]);
-        if (keys_out) keys_out[out] = k;
-        vals_out[out] = S.vals[i];
-    }
-#undef GS_DIGIT
 }
 
 size_t radix_workspace_bytes(int64_t n, int key_bits, int key_bytes) {
@@ -265,13 +97,14 @@ gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64
     const int hist_blocks = (int)std::min<int64_t>(kNumSMs * 4, std::max<int64_t>(1, (n_cap + 4095) / 4096));
     {
         KernelTimer kt("radix_hist", st);
-        k_radix_hist<KeyT><<<hist_blocks, 512, 0, st>>>(keys, n_dev, n_cap, npass, hist);
+        k_radix_hist<KeyT><<<hist_blocks, 512, 0, st>>>(keys, n_dev, n_cap, npass, key_bits, hist);
         GS_CHECK_LAUNCH();
         k_radix_hist_scan<<<1, kRadix, 0, st>>>(hist, npass);
         GS_CHECK_LAUNCH();
     }
     const size_t smem = sizeof(SortSmem<KeyT>);
-    GS_CUDA_CHECK(cudaFuncSetAttribute(k_radix_pass<KeyT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<KeyT, GlobalSource<KeyT>>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const KeyT* kin = keys;
     const uint32_t* vin = vals;
     for (int p = 0; p < npass; ++p) {
@@ -279,8 +112,9 @@ gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64
         KeyT* kout = last ? keys_out : ((p & 1) ? kb : ka);
         uint32_t* vout = last ? vals_out : ((p & 1) ? vb : va);
         KernelTimer kt(sizeof(KeyT) == 8 ? "radix_pass" : "radix_pass32", st);
-        k_radix_pass<KeyT><<<(unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1), kSortThreads, smem, st>>>(
-            kin, vin, kout, vout, n_dev, n_cap, p * kRadixBits, hist + p * kRadix,
+        k_onesweep_pass<KeyT><<<(unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1), kSortThreads, smem, st>>>(
+            GlobalSource<KeyT>{kin, vin}, kout, vout, n_dev, n_cap, p * kRadixBits,
+            std::min(kRadixBits, key_bits - p * kRadixBits), hist + p * kRadix,
             look + (size_t)p * ntiles * kRadix, counters + p, err);
         GS_CHECK_LAUNCH();
         kin = kout;
@@ -303,6 +137,64 @@ gs_status radix_sort_pairs32(const uint32_t* keys, const uint32_t* vals, const i
                              unsigned int** err_out, unsigned int* err_ext) {
     return radix_sort_pairs_t<uint32_t>(keys, vals, n_dev, n_cap, key_bits, keys_out, vals_out,
                                         workspace, workspace_bytes, st, err_out, err_ext);
+}
+
+// Training tile sort: the first pass draws its items from the Gaussians' tile rectangles
+// (pair emission fused into the pass); later passes read the previous pass's output. The
+// caller supplies every pass's exclusive digit offsets (npass x 256), derived from the
+// per-tile pair counts, so no histogram pass over the pairs is needed; only values are
+// written by the last pass.
+gs_status radix_sort_rect_pairs(const RectPairSource& src, const int64_t* n_dev, int64_t n_cap,
+                                int key_bits, const uint32_t* digit_offsets, uint32_t* vals_out,
+                                void* workspace, size_t workspace_bytes, cudaStream_t st,
+                                unsigned int* err_ext) {
+    const int npass = radix_num_passes(key_bits);
+    const int64_t ntiles = (n_cap + kTileItems - 1) / kTileItems + 1;
+    Workspace ws(workspace, workspace_bytes);
+    unsigned int* err = ws.take<unsigned int>(1);
+    ws.take<uint32_t>((size_t)npass * kRadix);
+    uint32_t* look = ws.take<uint32_t>((size_t)npass * ntiles * kRadix);
+    uint32_t* counters = ws.take<uint32_t>(npass);
+    uint32_t* ka = (uint32_t*)ws.take<char>((size_t)n_cap * sizeof(uint32_t));
+    uint32_t* va = ws.take<uint32_t>(n_cap);
+    uint32_t* kb = (uint32_t*)ws.take<char>((size_t)n_cap * sizeof(uint32_t));
+    uint32_t* vb = ws.take<uint32_t>(n_cap);
+    if (!ws.ok()) {
+        set_error("tile sort: workspace too small (%zu < %zu)", workspace_bytes,
+                  radix_workspace_bytes(n_cap, key_bits, 4));
+        return GS_ERR_ARG;
+    }
+    GS_CUDA_CHECK(cudaMemsetAsync(err, 0, (char*)(counters + npass) - (char*)err, st));
+    if (err_ext) err = err_ext;
+    const size_t smem = sizeof(SortSmem<uint32_t>);
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, RectPairSource>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, GlobalSource<uint32_t>>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    const unsigned int grid = (unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1);
+    {
+        KernelTimer kt("tile_sort_emit", st);
+        k_onesweep_pass<uint32_t, RectPairSource><<<grid, kSortThreads, smem, st>>>(
+            src, npass == 1 ? nullptr : ka, npass == 1 ? vals_out : va, n_dev, n_cap, 0,
+            std::min(kRadixBits, key_bits), digit_offsets, look, counters, err);
+        GS_CHECK_LAUNCH();
+    }
+    const uint32_t* kin = ka;
+    const uint32_t* vin = va;
+    for (int p = 1; p < npass; ++p) {
+        const bool lastp = (p == npass - 1);
+        uint32_t* kout = lastp ? nullptr : ((p & 1) ? kb : ka);
+        uint32_t* vout = lastp ? vals_out : ((p & 1) ? vb : va);
+        KernelTimer kt("tile_sort_pass", st);
+        k_onesweep_pass<uint32_t, GlobalSource<uint32_t>><<<grid, kSortThreads, smem, st>>>(
+            GlobalSource<uint32_t>{kin, vin}, kout, vout, n_dev, n_cap, p * kRadixBits,
+            std::min(kRadixBits, key_bits - p * kRadixBits), digit_offsets + p * kRadix,
+            look + (size_t)p * ntiles * kRadix, counters + p, err);
+        GS_CHECK_LAUNCH();
+        kin = kout;
+        vin = vout;
+    }
+    return GS_OK;
 }
 
 // ------------------------------------------------------------------ sort_and_bin

@@ -1,0 +1,104 @@
+// rect_pairs.cuh -- (Gaussian, tile) pairs generated from tile rectangles, as a onesweep
+// item source: the first pass of the training tile sort emits its items itself.
+//
+// Pair order before the sort (the order the stable sort must preserve within a tile):
+// Gaussians in depth order, each Gaussian's tiles row-major inside its rectangle;
+// key = tile id (ty * tiles_x + tx), value = Gaussian id. Sorting that stably by tile id
+// gives the reference's (tile, depth bits, Gaussian id) order (src/gsplat_cpu/sort.cpp:24-27).
+#pragma once
+
+#include "onesweep.cuh"
+
+namespace gs {
+
+struct RectPairSource {
+    const uint32_t* order;   // Gaussian ids in depth order
+    const uint32_t* goff;    // first pair of each depth-ordered Gaussian; n + 1 entries
+    const uint32_t* tfirst;  // per 4096-pair tile: depth index of the Gaussian holding its first pair
+    const uint32_t* last;    // [0]: depth index of the last Gaussian with pairs
+    const ushort4* rect;     // per depth-ordered Gaussian: tile columns x0..x1, rows y0..y1
+    int tiles_x;
+
+    // The tile's pairs come from depth-ordered Gaussians gf..gl (at most `valid` of them,
+    // each has at least one pair), taken in chunks of 256, one per thread. A thread writes
+    // the pairs of its Gaussian that fall in the tile into the tile's shared key / value
+    // arrays itself, walking the rectangle row-major, when there are at most kOwnPairs of
+    // them; longer runs are queued and written by whole warps (lanes striding over the
+    // run), so one large Gaussian does not serialise its warp. The thread then takes its
+    // warp-striped items from shared memory.
+    static constexpr uint32_t kOwnPairs = 32;
+
+    __device__ __forceinline__ void load(SortSmem<uint32_t>& S, uint32_t tile, int64_t base,
+                                         int valid, int64_t n, uint32_t pad,
+                                         uint32_t (&key)[kSortItems],
+                                         uint32_t (&val)[kSortItems]) const {
+        // Queue of long runs, double-buffered by chunk parity: chunk k writes buffer k & 1
+        // before its first barrier, and chunk k + 2 (the next writer of that buffer) starts
+        // only after every warp has passed chunk k + 1's first barrier. Each counter is
+        // read by all threads between chunk k's two barriers and cleared after the second.
+        __shared__ uint32_t s_big[2][kSortThreads];
+        __shared__ uint32_t s_nbig[2];
+        const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+        const uint32_t lo_p = (uint32_t)base, hi_p = (uint32_t)(base + valid);
+        const uint32_t gf = tfirst[tile];
+        const uint32_t gnext = (base + kTileItems < n) ? tfirst[tile + 1] : last[0];
+        const uint32_t gl = min(gnext, gf + (uint32_t)valid - 1u);
+        const uint32_t tx_n = (uint32_t)tiles_x;
+        if (tid < 2) s_nbig[tid] = 0u;
+        __syncthreads();
+        int par = 0;
+        for (uint32_t c0 = gf; c0 <= gl; c0 += kSortThreads, par ^= 1) {
+            const uint32_t i = c0 + (uint32_t)tid;
+            if (i <= gl) {
+                const uint32_t off = goff[i], end = goff[i + 1], gid = order[i];
+                const ushort4 r = rect[i];
+                const uint32_t p0 = max(off, lo_p), p1 = min(end, hi_p);
+                if (p1 > p0 && p1 - p0 <= kOwnPairs) {
+                    const uint32_t w = (uint32_t)r.y - (uint32_t)r.x + 1u;
+                    const uint32_t j0 = p0 - off;
+                    uint32_t ty = r.z + j0 / w, tx = r.x + j0 % w;
+                    for (uint32_t p = p0; p < p1; ++p) {
+                        S.keys[p - lo_p] = ty * tx_n + tx;
+                        S.vals[p - lo_p] = gid;
+                        if (++tx > r.y) {
+                            tx = r.x;
+                            ++ty;
+                        }
+                    }
+                } else if (p1 > p0) {
+                    s_big[par][atomicAdd(&s_nbig[par], 1u)] = i;
+                }
+            }
+            __syncthreads();
+            const uint32_t nbig = s_nbig[par];
+            __syncthreads();
+            if (tid == 0) s_nbig[par] = 0u;
+            for (uint32_t q = (uint32_t)warp; q < nbig; q += kSortWarps) {
+                const uint32_t bi = s_big[par][q];
+                const uint32_t off = goff[bi], end = goff[bi + 1], gid = order[bi];
+                const ushort4 r = rect[bi];
+                const uint32_t p0 = max(off, lo_p), p1 = min(end, hi_p);
+                const uint32_t w = (uint32_t)r.y - (uint32_t)r.x + 1u;
+                for (uint32_t p = p0 + (uint32_t)lane; p < p1; p += 32u) {
+                    const uint32_t j = p - off;
+                    S.keys[p - lo_p] = (r.z + j / w) * tx_n + r.x + j % w;
+                    S.vals[p - lo_p] = gid;
+                }
+            }
+        }
+        __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kSortItems; ++j) {
+            const int li = warp * (kSortItems * 32) + j * 32 + lane;
+            if (li < valid) {
+                key[j] = S.keys[li];
+                val[j] = S.vals[li];
+            } else {  // pads get the largest digit so they rank after every real item
+                key[j] = pad;
+                val[j] = 0u;
+            }
+        }
+    }
+};
+
+}  // namespace gs

@@ -60,4 +60,22 @@ __global__ void scan_block_totals(T* totals, int64_t n, T* grand) {
     if (threadIdx.x == 0 && grand != nullptr) *grand = carry;
 }
 
+// scan_block_totals over gridDim.x independent segments, one block each: segment s is
+// totals[s * stride, s * stride + n), its grand total goes to grand[s].
+template <typename T>
+__global__ void scan_block_totals_segments(T* totals, int64_t n, int64_t stride, T* grand) {
+    __shared__ T smem[33];
+    T* seg = totals + (int64_t)blockIdx.x * stride;
+    T carry = 0;
+    for (int64_t base = 0; base < n; base += blockDim.x) {
+        const int64_t i = base + threadIdx.x;
+        T v = (i < n) ? seg[i] : T(0);
+        T tot;
+        T ex = block_exclusive_scan<T>(v, smem, &tot);
+        if (i < n) seg[i] = carry + ex;
+        carry += tot;
+    }
+    if (threadIdx.x == 0) grand[blockIdx.x] = carry;
+}
+
 }  // namespace gs

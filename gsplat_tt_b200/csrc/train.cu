@@ -5,6 +5,7 @@
 #include <vector>
 
 #include "radix_sort.cuh"
+#include "rect_pairs.cuh"
 #include "scan.cuh"
 #include "train.cuh"
 
@@ -50,31 +51,11 @@ TCfg make_tcfg(const gs_train_config& c, int H, int W) {
     return t;
 }
 
-// ------------------------------------------------------------------ tile ranges
-
-// [start, end) of each tile in the sorted keys (binary search), (0, 0) when empty.
-__global__ void k_train_ranges(const uint32_t* __restrict__ skeys, const int64_t* __restrict__ p_dev,
-                               int64_t cap, int ntiles, int2* __restrict__ ranges) {
-    const int t = blockIdx.x * blockDim.x + threadIdx.x;
-    if (t >= ntiles) return;
-    const int64_t p = min(*p_dev, cap);
-    auto lower = [&](uint32_t target) {
-        int64_t lo = 0, hi = p;
-        while (lo < hi) {
-            const int64_t mid = (lo + hi) >> 1;
-            if (skeys[mid] < target) lo = mid + 1; else hi = mid;
-        }
-        return lo;
-    };
-    const int64_t s = lower((uint32_t)t), e = lower((uint32_t)t + 1u);
-    ranges[t] = (e > s) ? make_int2((int)s, (int)e) : make_int2(0, 0);
-}
-
 // ------------------------------------------------------------------ rasterisers
 
 // One pair staged in shared memory: the tile-centred power polynomial
 // (gsplat/blend_backward_ref.py:68-92), opacity and colour.
-struct RPair {
+struct __align__(16) RPair {
     float Af, Bf, Cf, P0, Lx, Ly, op, r, g, b;
     uint32_t rows, cols;  // tile rows / columns with a pixel centre that can reach alpha_min
 };
@@ -253,10 +234,42 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     }
 }
 
-struct BPair {
+// Warp sums of nine per-lane values in 14 shuffles instead of 45: a halving transpose
+// for values 0-7 (at each step a lane keeps half of its partial sums and sends the other
+// half to its partner), a butterfly for value 8. On return lane l with (l & 3) == 0 holds
+// the sum of value l >> 2 in s8, and every lane holds the sum of value 8 in s1.
+__device__ __forceinline__ void warp_sum9(const float (&v)[9], int lane, float& s8, float& s1) {
+    constexpr unsigned kAll = 0xffffffffu;
+    const bool b4 = (lane & 16) != 0, b3 = (lane & 8) != 0, b2 = (lane & 4) != 0;
+    float a[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const float send = b4 ? v[k] : v[k + 4];
+        const float keep = b4 ? v[k + 4] : v[k];
+        a[k] = keep + __shfl_xor_sync(kAll, send, 16);
+    }
+    float b[2];
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+        const float send = b3 ? a[k] : a[k + 2];
+        const float keep = b3 ? a[k + 2] : a[k];
+        b[k] = keep + __shfl_xor_sync(kAll, send, 8);
+    }
+    float c = (b2 ? b[1] : b[0]) + __shfl_xor_sync(kAll, b2 ? b[0] : b[1], 4);
+    c += __shfl_xor_sync(kAll, c, 2);
+    c += __shfl_xor_sync(kAll, c, 1);
+    s8 = c;
+    float d = v[8];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) d += __shfl_xor_sync(kAll, d, o);
+    s1 = d;
+}
+
+struct __align__(16) BPair {  // 80 bytes: five 16-byte shared-memory loads
     RPair q;
     float mxl, myl, A, B, C;
     uint32_t gid;
+    float pad[2];
 };
 
 // Back-to-front replay (gsplat/blend_backward_ref.py:134-249 terms, recomputed from the
@@ -275,7 +288,7 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     using LY = PixLayout<TILE, PPT>;
     constexpr int NB = kRasterBatch;
     __shared__ BPair sp[NB];
-    __shared__ float acc[9][NB];
+    __shared__ float acc[9][NB + 1];  // rows one bank apart: the 8-lane atomics hit 8 banks
     __shared__ int s_max;
     const int tile = blockIdx.x;
     const int tx = tile % cfg.tiles_x, ty = tile / cfg.tiles_x;
@@ -379,15 +392,10 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
                 }
             }
             if (__any_sync(0xffffffffu, live_any)) {
-#pragma unroll
-                for (int k = 0; k < 9; ++k) {
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) v[k] += __shfl_xor_sync(0xffffffffu, v[k], o);
-                }
-                if (lane == 0) {
-#pragma unroll
-                    for (int k = 0; k < 9; ++k) atomicAdd(&acc[k][j], v[k]);
-                }
+                float s8, s1;
+                warp_sum9(v, lane, s8, s1);
+                if ((lane & 3) == 0) atomicAdd(&acc[lane >> 2][j], s8);
+                if (lane == 1) atomicAdd(&acc[8][j], s1);
             }
         }
         __syncthreads();
@@ -410,9 +418,7 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
 
 // ------------------------------------------------------------------ loss
 
-constexpr int kLossTile = 16;
-constexpr int kHalo = 5;
-constexpr int kSpan = kLossTile + 2 * kHalo;  // 26
+constexpr int kHalo = 5;  // half-width of the 11-tap SSIM window
 
 struct LossCfg {
     float taps[11];
@@ -443,86 +449,127 @@ __global__ void k_loss_l1(const float* __restrict__ img, const float* __restrict
     }
 }
 
-// Separable 11-tap Gaussian of one 16x16 output tile of one channel from a
-// (26 x 26) shared patch; `hbuf` holds the 26 x 16 horizontal pass.
-__device__ __forceinline__ float filt_v(const float (*hbuf)[kLossTile], const float* taps, int ly, int lx) {
-    float s = 0.0f;
-#pragma unroll
-    for (int k = 0; k < 11; ++k) s = __fmaf_rn(taps[k], hbuf[ly + k][lx], s);
-    return s;
-}
+// SSIM tiles: 32 x 32 outputs per block of 256 threads, from a (42 x 42) patch (halo 5
+// for the 11-tap window). Horizontal pass: a thread filters 4 adjacent outputs of a patch
+// row from 14 values held in registers; vertical pass: a thread filters 4 adjacent rows
+// of an output column from 14 values. Shared rows are padded to 45 floats, which keeps the
+// horizontal pass's four rows per warp on distinct banks.
+constexpr int kSsimT = 32;                    // output tile edge
+constexpr int kSsimP = kSsimT + 2 * kHalo;    // 42
+constexpr int kSsimS = 45;                    // padded patch row stride
+constexpr int kSsimHItems = kSsimP * (kSsimT / 4);  // 336 horizontal items of 4 outputs
+
+struct SsimFwdSmem {
+    float px[3][kSsimP][kSsimS];
+    float py[3][kSsimP][kSsimS];
+    float h[5][kSsimP][kSsimT];
+};
+struct SsimBwdSmem {
+    float p[3][kSsimP][kSsimS];
+    float h[3][kSsimP][kSsimT];
+};
 
 // SSIM forward + its partial derivatives (gsplat/train_loss.py:126-165): per pixel and
 // channel mu_x, mu_y, E_xx, E_yy, E_xy (zero padding), S, and the maps d_mu, d_xx, d_xy
-// (scaled by -lambda / n) that the second pass filters. Sums |x - y| and S.
-__global__ void __launch_bounds__(kLossTile * kLossTile)
+// (scaled by -lambda / n; planar [3][H][W]) that the second pass filters. Sums |x - y|
+// and S. The image patch is read once for all three channels, row segments contiguous.
+__global__ void __launch_bounds__(256)
 k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg L,
            float* __restrict__ dmu, float* __restrict__ dxx, float* __restrict__ dxy,
            double* __restrict__ acc) {
-    __shared__ float px[kSpan][kSpan], py[kSpan][kSpan];
-    __shared__ float h[5][kSpan][kLossTile];
+    extern __shared__ __align__(16) unsigned char ssim_raw[];
+    SsimFwdSmem& S = *reinterpret_cast<SsimFwdSmem*>(ssim_raw);
     __shared__ double red[2][8];
-    const int lx = threadIdx.x % kLossTile, ly = threadIdx.x / kLossTile;
-    const int x0 = blockIdx.x * kLossTile, y0 = blockIdx.y * kLossTile;
-    const int x = x0 + lx, y = y0 + ly;
-    const bool inside = x < L.W && y < L.H;
+    const int tid = threadIdx.x;
+    const int x0 = blockIdx.x * kSsimT, y0 = blockIdx.y * kSsimT;
+    for (int i = tid; i < kSsimP * kSsimP * 3; i += 256) {
+        const int r = i / (kSsimP * 3), rem = i - r * (kSsimP * 3);
+        const int c = rem / 3, ch = rem - c * 3;
+        const int yy = y0 - kHalo + r, xx = x0 - kHalo + c;
+        const bool in = yy >= 0 && yy < L.H && xx >= 0 && xx < L.W;
+        const size_t o = ((size_t)yy * L.W + xx) * 3 + ch;
+        S.px[ch][r][c] = in ? img[o] : 0.0f;
+        S.py[ch][r][c] = in ? tgt[o] : 0.0f;
+    }
+    __syncthreads();
     double s_l1 = 0.0, s_ssim = 0.0;
     const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
     const float w = -L.lambda * L.inv_n;
+    const int vc = tid & 31, vr0 = (tid >> 5) * 4;  // vertical item: column, first of 4 rows
     for (int ch = 0; ch < 3; ++ch) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < kSpan * kSpan; i += blockDim.x) {
-            const int yy = y0 - kHalo + i / kSpan, xx = x0 - kHalo + i % kSpan;
-            const bool in = yy >= 0 && yy < L.H && xx >= 0 && xx < L.W;
-            const size_t o = ((size_t)yy * L.W + xx) * 3 + ch;
-            px[i / kSpan][i % kSpan] = in ? img[o] : 0.0f;
-            py[i / kSpan][i % kSpan] = in ? tgt[o] : 0.0f;
-        }
-        __syncthreads();
-        for (int i = threadIdx.x; i < kSpan * kLossTile; i += blockDim.x) {
-            const int r = i / kLossTile, c = i % kLossTile;
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+        for (int it = tid; it < kSsimHItems; it += 256) {
+            const int r = it >> 3, c0 = (it & 7) * 4;
+            float xv[14], yv[14];
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float xv = px[r][c + k], yv = py[r][c + k], t = L.taps[k];
-                a0 = __fmaf_rn(t, xv, a0);
-                a1 = __fmaf_rn(t, yv, a1);
-                a2 = __fmaf_rn(t, xv * xv, a2);
-                a3 = __fmaf_rn(t, yv * yv, a3);
-                a4 = __fmaf_rn(t, xv * yv, a4);
+            for (int k = 0; k < 14; ++k) {
+                xv[k] = S.px[ch][r][c0 + k];
+                yv[k] = S.py[ch][r][c0 + k];
             }
-            h[0][r][c] = a0; h[1][r][c] = a1; h[2][r][c] = a2; h[3][r][c] = a3; h[4][r][c] = a4;
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+#pragma unroll
+                for (int k = 0; k < 11; ++k) {
+                    const float xk = xv[o + k], yk = yv[o + k], t = L.taps[k];
+                    a0 = __fmaf_rn(t, xk, a0);
+                    a1 = __fmaf_rn(t, yk, a1);
+                    a2 = __fmaf_rn(t, xk * xk, a2);
+                    a3 = __fmaf_rn(t, yk * yk, a3);
+                    a4 = __fmaf_rn(t, xk * yk, a4);
+                }
+                S.h[0][r][c0 + o] = a0;
+                S.h[1][r][c0 + o] = a1;
+                S.h[2][r][c0 + o] = a2;
+                S.h[3][r][c0 + o] = a3;
+                S.h[4][r][c0 + o] = a4;
+            }
         }
         __syncthreads();
-        if (inside) {
-            const float mx = filt_v(h[0], L.taps, ly, lx), my = filt_v(h[1], L.taps, ly, lx);
-            const float exx = filt_v(h[2], L.taps, ly, lx), eyy = filt_v(h[3], L.taps, ly, lx);
-            const float exy = filt_v(h[4], L.taps, ly, lx);
+        float m[5][4];
+#pragma unroll
+        for (int q = 0; q < 5; ++q) {
+            float v[14];
+#pragma unroll
+            for (int k = 0; k < 14; ++k) v[k] = S.h[q][vr0 + k][vc];
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                float a = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 11; ++k) a = __fmaf_rn(L.taps[k], v[o + k], a);
+                m[q][o] = a;
+            }
+        }
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+            const int x = x0 + vc, y = y0 + vr0 + o;
+            if (x >= L.W || y >= L.H) continue;
+            const float mx = m[0][o], my = m[1][o], exx = m[2][o], eyy = m[3][o], exy = m[4][o];
             const float mxy = mx * my;
             const float A = 2.0f * mxy + C1;
             const float B = 2.0f * (exy - mxy) + C2;
             const float C = mx * mx + my * my + C1;
             const float D = (exx - mx * mx) + (eyy - my * my) + C2;
-            const float S = (A * B) / (C * D);
-            const float Sw = S * w;
-            const size_t o = ((size_t)y * L.W + x) * 3 + ch;
-            dmu[o] = Sw * (2.0f * my / A - 2.0f * my / B - 2.0f * mx / C + 2.0f * mx / D);
-            dxx[o] = -Sw / D;
-            dxy[o] = 2.0f * Sw / B;
-            s_ssim += S;
-            s_l1 += fabsf(px[ly + kHalo][lx + kHalo] - py[ly + kHalo][lx + kHalo]);
+            const float Sv = (A * B) / (C * D);
+            const float Sw = Sv * w;
+            const size_t po = ((size_t)ch * L.H + y) * L.W + x;
+            dmu[po] = Sw * (2.0f * my / A - 2.0f * my / B - 2.0f * mx / C + 2.0f * mx / D);
+            dxx[po] = -Sw / D;
+            dxy[po] = 2.0f * Sw / B;
+            s_ssim += Sv;
+            s_l1 += fabsf(S.px[ch][vr0 + o + kHalo][vc + kHalo] - S.py[ch][vr0 + o + kHalo][vc + kHalo]);
         }
+        __syncthreads();
     }
     for (int o = 16; o > 0; o >>= 1) {
         s_l1 += __shfl_xor_sync(0xffffffffu, s_l1, o);
         s_ssim += __shfl_xor_sync(0xffffffffu, s_ssim, o);
     }
-    if ((threadIdx.x & 31) == 0) {
-        red[0][threadIdx.x >> 5] = s_l1;
-        red[1][threadIdx.x >> 5] = s_ssim;
+    if ((tid & 31) == 0) {
+        red[0][tid >> 5] = s_l1;
+        red[1][tid >> 5] = s_ssim;
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
+    if (tid == 0) {
         double a = 0.0, b = 0.0;
         for (int k = 0; k < 8; ++k) { a += red[0][k]; b += red[1][k]; }
         atomicAdd(&acc[0], a);
@@ -530,50 +577,72 @@ k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg
     }
 }
 
-// dL/dx = G*d_mu + 2 x G*d_xx + y G*d_xy + (1 - lambda)/n sign(x - y).
-__global__ void __launch_bounds__(kLossTile * kLossTile)
+// dL/dx = G*d_mu + 2 x G*d_xx + y G*d_xy + (1 - lambda)/n sign(x - y), per channel from
+// (42 x 42) patches of the planar maps; written interleaved (H, W, 3) like the image.
+__global__ void __launch_bounds__(256)
 k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt,
            const float* __restrict__ dmu, const float* __restrict__ dxx,
            const float* __restrict__ dxy, LossCfg L, float* __restrict__ dimg) {
-    __shared__ float p[3][kSpan][kSpan];
-    __shared__ float h[3][kSpan][kLossTile];
-    const int lx = threadIdx.x % kLossTile, ly = threadIdx.x / kLossTile;
-    const int x0 = blockIdx.x * kLossTile, y0 = blockIdx.y * kLossTile;
-    const int x = x0 + lx, y = y0 + ly;
-    const bool inside = x < L.W && y < L.H;
+    extern __shared__ __align__(16) unsigned char ssim_raw[];
+    SsimBwdSmem& S = *reinterpret_cast<SsimBwdSmem*>(ssim_raw);
+    const int tid = threadIdx.x;
+    const int x0 = blockIdx.x * kSsimT, y0 = blockIdx.y * kSsimT;
     const float wl1 = (1.0f - L.lambda) * L.inv_n;
+    const int vc = tid & 31, vr0 = (tid >> 5) * 4;
     for (int ch = 0; ch < 3; ++ch) {
-        __syncthreads();
-        for (int i = threadIdx.x; i < kSpan * kSpan; i += blockDim.x) {
-            const int yy = y0 - kHalo + i / kSpan, xx = x0 - kHalo + i % kSpan;
+        const size_t plane = (size_t)ch * L.H * L.W;
+        for (int i = tid; i < kSsimP * kSsimP; i += 256) {
+            const int r = i / kSsimP, c = i - r * kSsimP;
+            const int yy = y0 - kHalo + r, xx = x0 - kHalo + c;
             const bool in = yy >= 0 && yy < L.H && xx >= 0 && xx < L.W;
-            const size_t o = ((size_t)yy * L.W + xx) * 3 + ch;
-            p[0][i / kSpan][i % kSpan] = in ? dmu[o] : 0.0f;
-            p[1][i / kSpan][i % kSpan] = in ? dxx[o] : 0.0f;
-            p[2][i / kSpan][i % kSpan] = in ? dxy[o] : 0.0f;
+            const size_t o = plane + (size_t)yy * L.W + xx;
+            S.p[0][r][c] = in ? dmu[o] : 0.0f;
+            S.p[1][r][c] = in ? dxx[o] : 0.0f;
+            S.p[2][r][c] = in ? dxy[o] : 0.0f;
         }
         __syncthreads();
-        for (int i = threadIdx.x; i < kSpan * kLossTile; i += blockDim.x) {
-            const int r = i / kLossTile, c = i % kLossTile;
-            float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+        for (int it = tid; it < kSsimHItems; it += 256) {
+            const int r = it >> 3, c0 = (it & 7) * 4;
 #pragma unroll
-            for (int k = 0; k < 11; ++k) {
-                const float t = L.taps[k];
-                a0 = __fmaf_rn(t, p[0][r][c + k], a0);
-                a1 = __fmaf_rn(t, p[1][r][c + k], a1);
-                a2 = __fmaf_rn(t, p[2][r][c + k], a2);
+            for (int q = 0; q < 3; ++q) {
+                float v[14];
+#pragma unroll
+                for (int k = 0; k < 14; ++k) v[k] = S.p[q][r][c0 + k];
+#pragma unroll
+                for (int o = 0; o < 4; ++o) {
+                    float a = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 11; ++k) a = __fmaf_rn(L.taps[k], v[o + k], a);
+                    S.h[q][r][c0 + o] = a;
+                }
             }
-            h[0][r][c] = a0; h[1][r][c] = a1; h[2][r][c] = a2;
         }
         __syncthreads();
-        if (inside) {
-            const size_t o = ((size_t)y * L.W + x) * 3 + ch;
-            const float P = filt_v(h[0], L.taps, ly, lx), Q = filt_v(h[1], L.taps, ly, lx);
-            const float Rr = filt_v(h[2], L.taps, ly, lx);
-            const float xv = img[o], yv = tgt[o];
-            const float d = xv - yv;
-            dimg[o] = P + 2.0f * xv * Q + yv * Rr + wl1 * (float)((d > 0.0f) - (d < 0.0f));
+        float m[3][4];
+#pragma unroll
+        for (int q = 0; q < 3; ++q) {
+            float v[14];
+#pragma unroll
+            for (int k = 0; k < 14; ++k) v[k] = S.h[q][vr0 + k][vc];
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                float a = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 11; ++k) a = __fmaf_rn(L.taps[k], v[o + k], a);
+                m[q][o] = a;
+            }
         }
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+            const int x = x0 + vc, y = y0 + vr0 + o;
+            if (x >= L.W || y >= L.H) continue;
+            const size_t io = ((size_t)y * L.W + x) * 3 + ch;
+            const float xv = img[io], yv = tgt[io];
+            const float d = xv - yv;
+            dimg[io] = m[0][o] + 2.0f * xv * m[1][o] + yv * m[2][o] +
+                       wl1 * (float)((d > 0.0f) - (d < 0.0f));
+        }
+        __syncthreads();
     }
 }
 
@@ -903,15 +972,20 @@ struct TrainWs {
     uint64_t* touch;
     TCam* cams;
     float* grad2d;
-    int64_t* blk;
+    int64_t* blk;      // per-view block pair totals, view v at v * blk_stride
+    int64_t blk_stride;
     int64_t* pairs;
-    ProjView pv;
+    ProjView pv;       // every view's projected records, [view][n]
     int64_t* blk2;
     uint32_t* order;   // Gaussian ids sorted by depth
-    uint32_t* keys;    // tile id of each pair (depth order)
-    uint32_t* vals;
-    uint32_t* skeys;   // sorted by tile id
-    uint32_t* svals;
+    uint32_t* goff;    // first pair of each depth-ordered Gaussian (n + 1)
+    ushort4* rect_d;   // tile rectangle of each depth-ordered Gaussian with pairs
+    uint32_t* tfirst;  // per 4096-pair sort tile: depth index of its first pair's Gaussian
+    int64_t tfirst_len;
+    uint32_t* tlast;   // depth index of the last Gaussian with pairs
+    int* tdiff;        // row-wise difference array of the per-tile pair counts
+    uint32_t* tdig;    // tile-sort digit offsets, 4 passes x 256
+    uint32_t* svals;   // Gaussian ids sorted by (tile, depth bits, id)
     char* radix;
     size_t radix_bytes;
     int2* ranges;
@@ -936,20 +1010,26 @@ static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int 
     L.touch = ws.template take<uint64_t>(n);
     L.cams = ws.template take<TCam>(n_views);
     L.grad2d = ws.template take<float>((size_t)n_views * n * kGradStride);
-    L.blk = ws.template take<int64_t>(nb);
+    L.blk_stride = nb;
+    L.blk = ws.template take<int64_t>((size_t)n_views * nb);
     L.pairs = ws.template take<int64_t>(n_views);
-    L.pv.p0 = ws.template take<float4>(n);
-    L.pv.p1 = ws.template take<float4>(n);
-    L.pv.p2 = ws.template take<float>(n);
-    L.pv.dkey = ws.template take<uint32_t>(n);
-    L.pv.dsort = ws.template take<uint32_t>(n);
-    L.pv.rect = ws.template take<ushort4>(n);
-    L.pv.cnt = ws.template take<uint32_t>(n);
+    const size_t nv = (size_t)n_views * n;  // projected records of every view, [view][n]
+    L.pv.p0 = ws.template take<float4>(nv);
+    L.pv.p1 = ws.template take<float4>(nv);
+    L.pv.p2 = ws.template take<float>(nv);
+    L.pv.dkey = ws.template take<uint32_t>(nv);
+    L.pv.dsort = ws.template take<uint32_t>(nv);
+    L.pv.rect = ws.template take<ushort4>(nv);
+    L.pv.cnt = ws.template take<uint32_t>(nv);
     L.blk2 = ws.template take<int64_t>(nb);
     L.order = ws.template take<uint32_t>(n);
-    L.keys = ws.template take<uint32_t>(cap);
-    L.vals = ws.template take<uint32_t>(cap);
-    L.skeys = ws.template take<uint32_t>(cap);
+    L.goff = ws.template take<uint32_t>(n + 1);
+    L.rect_d = ws.template take<ushort4>(n);
+    L.tfirst_len = div_up(cap, kTileItems) + 1;
+    L.tfirst = ws.template take<uint32_t>(L.tfirst_len);
+    L.tlast = ws.template take<uint32_t>(1);
+    L.tdiff = ws.template take<int>((size_t)(W / tile + 2) * (H / tile + 1));
+    L.tdig = ws.template take<uint32_t>(4 * 256);
     L.svals = ws.template take<uint32_t>(cap);
     // one scratch region serves the depth sort (N, 32 bits) and the tile sort (P, tile bits)
     L.radix_bytes = std::max(radix_workspace_bytes(n, 32, 4), radix_workspace_bytes(cap, tile_bits, 4));
@@ -981,6 +1061,11 @@ static gs_status check_cfg(const gs_train_config* cfg) {
     return GS_OK;
 }
 
+// Tile rows are bounded by the tile-count kernel, tile columns by the 16-bit rectangles.
+static bool image_fits(int32_t h, int32_t w, int tile) {
+    return h > 0 && w > 0 && (h + tile - 1) / tile <= kMaxTileRows && (w + tile - 1) / tile <= 65535;
+}
+
 static GConst gconst(const gs_gaussians* p) {
     return GConst{p->means, p->log_scales, p->quats, p->opacity_logits, p->sh};
 }
@@ -1003,39 +1088,56 @@ extern "C" size_t gs_train_workspace_size(int64_t n, int32_t sh_degree, int32_t 
     return s.s.bytes();
 }
 
-static gs_status project_and_sort_view(const GConst& P, int64_t n, const TCam& cam, const TCfg& cfg,
-                                       int view, TrainWs& L, int64_t cap, float* vis_counts,
-                                       bool with_grad, cudaStream_t st) {
-    const unsigned int nb = div_up(n, kProjThreads);
+// Every view's projection in one pass over the parameters (cameras already in L.cams),
+// then each view's pair total in L.pairs[v].
+static gs_status project_views(const GConst& P, int64_t n, int n_views, const TCfg& cfg,
+                               TrainWs& L, float* vis_counts, bool with_grad, cudaStream_t st) {
     {
         KernelTimer kt("train_project", st);
-        launch_project(P, n, cam, cfg, view, L.pv, L.blk, L.touch, vis_counts,
-                       with_grad ? L.grad2d + (size_t)view * n * kGradStride : nullptr, st);
+        launch_project(P, n, L.cams, n_views, cfg, L.pv, L.blk, L.blk_stride, L.touch, vis_counts,
+                       with_grad ? L.grad2d : nullptr, st);
         GS_CHECK_LAUNCH();
     }
-    scan_block_totals<int64_t><<<1, 1024, 0, st>>>(L.blk, nb, L.pairs + view);
+    scan_block_totals_segments<int64_t><<<n_views, 1024, 0, st>>>(L.blk, div_up(n, kProjThreads),
+                                                                  L.blk_stride, L.pairs);
     GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
+// Depth order, pair offsets, tile counts / ranges and the tile sort of one projected view.
+static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, int64_t cap,
+                           cudaStream_t st) {
+    const unsigned int nb = div_up(n, kProjThreads);
+    const ProjView pv = L.pv.view(view, n);
     // Gaussians in (depth bits, id) order; those without pairs sort last.
     unsigned int* rerr = nullptr;
-    gs_status s = radix_sort_pairs32(L.pv.dsort, nullptr, nullptr, n, 32, nullptr, L.order, L.radix,
+    gs_status s = radix_sort_pairs32(pv.dsort, nullptr, nullptr, n, 32, nullptr, L.order, L.radix,
                                      L.radix_bytes, st, &rerr, L.err);
     if (s != GS_OK) return s;
-    launch_sorted_count(L.pv, L.order, n, L.blk2, st);
+    launch_sorted_count(pv, L.order, n, L.blk2, st);
     GS_CHECK_LAUNCH();
     scan_block_totals<int64_t><<<1, 1024, 0, st>>>(L.blk2, nb, nullptr);
     GS_CHECK_LAUNCH();
-    {
-        KernelTimer kt("train_emit", st);
-        launch_emit(L.pv, L.order, n, cfg, L.blk2, cap, L.keys, L.vals, L.err, st);
-        GS_CHECK_LAUNCH();
-    }
     const int tiles = cfg.tiles_x * cfg.tiles_y;
     const int tile_bits = bits_for(tiles > 1 ? tiles - 1 : 1);
-    s = radix_sort_pairs32(L.keys, L.vals, L.pairs + view, cap, tile_bits, L.skeys, L.svals, L.radix,
-                           L.radix_bytes, st, &rerr, L.err);
+    const int npass = radix_num_passes(tile_bits);
+    {
+        KernelTimer kt("pair_offsets", st);
+        GS_CUDA_CHECK(cudaMemsetAsync(L.tlast, 0, sizeof(uint32_t), st));
+        launch_pair_offsets(pv, L.order, n, L.blk2, cap, L.goff, L.rect_d, L.tfirst, L.tfirst_len,
+                            L.tlast, L.err, st);
+        GS_CHECK_LAUNCH();
+    }
+    {
+        KernelTimer kt("tile_counts", st);
+        s = launch_tile_counts(pv, n, cfg.tiles_x, cfg.tiles_y, npass, L.pairs + view, cap, L.tdiff,
+                               L.ranges, L.tdig, st);
+        if (s != GS_OK) return s;
+    }
+    const RectPairSource src{L.order, L.goff, L.tfirst, L.tlast, L.rect_d, cfg.tiles_x};
+    s = radix_sort_rect_pairs(src, L.pairs + view, cap, tile_bits, L.tdig, L.svals, L.radix,
+                              L.radix_bytes, st, L.err);
     if (s != GS_OK) return s;
-    k_train_ranges<<<div_up(tiles, 256), 256, 0, st>>>(L.skeys, L.pairs + view, cap, tiles, L.ranges);
-    GS_CHECK_LAUNCH();
     return GS_OK;
 }
 
@@ -1058,16 +1160,11 @@ extern "C" gs_status gs_train_count_pairs(const gs_gaussians* params, int64_t n,
     TrainWs L;
     train_layout(ws, L, n, n_views, H, W, cfg->tile_size, 1);
     GS_ARG_CHECK(ws.ok(), "gs_train_count_pairs: workspace too small");
-    const GConst P = gconst(params);
-    const unsigned int nb = div_up(n, kProjThreads);
-    for (int v = 0; v < n_views; ++v) {
-        const TCam cam = make_tcam(cams[v]);
-        const TCfg c = make_tcfg(*cfg, cams[v].height, cams[v].width);
-        launch_project(P, n, cam, c, v, L.pv, L.blk, L.touch, nullptr, nullptr, st);
-        GS_CHECK_LAUNCH();
-        scan_block_totals<int64_t><<<1, 1024, 0, st>>>(L.blk, nb, L.pairs + v);
-        GS_CHECK_LAUNCH();
-    }
+    std::vector<TCam> hc(n_views);
+    for (int v = 0; v < n_views; ++v) hc[v] = make_tcam(cams[v]);
+    GS_CUDA_CHECK(cudaMemcpyAsync(L.cams, hc.data(), n_views * sizeof(TCam), cudaMemcpyHostToDevice, st));
+    gs_status s = project_views(gconst(params), n, n_views, make_tcfg(*cfg, H, W), L, nullptr, false, st);
+    if (s != GS_OK) return s;
     GS_CUDA_CHECK(cudaMemcpyAsync(pairs_host, L.pairs, n_views * sizeof(int64_t),
                                   cudaMemcpyDeviceToHost, st));
     GS_CUDA_CHECK(cudaStreamSynchronize(st));
@@ -1116,6 +1213,10 @@ extern "C" gs_status gs_train_project_view(const gs_gaussians* params, int64_t n
                  "gs_train_project_view: bad arguments");
     GS_ARG_CHECK(pair_capacity >= 1 && pair_capacity < (1ll << 30),
                  "gs_train_project_view: bad pair_capacity");
+    GS_ARG_CHECK(n < (1ll << 32), "gs_train_project_view: n must be below 2^32");
+    GS_ARG_CHECK(image_fits(cam->height, cam->width, cfg->tile_size),
+                 "gs_train_project_view: image must be 1..%d tile rows and 1..65535 tile columns",
+                 kMaxTileRows);
     Workspace ws(workspace, workspace_bytes);
     TrainWs L;
     train_layout(ws, L, n, 1, cam->height, cam->width, cfg->tile_size, pair_capacity);
@@ -1125,8 +1226,10 @@ extern "C" gs_status gs_train_project_view(const gs_gaussians* params, int64_t n
     GS_CUDA_CHECK(cudaMemsetAsync(vis_counts, 0, n * sizeof(float), st));
     const TCam tc = make_tcam(*cam);
     const TCfg c = make_tcfg(*cfg, cam->height, cam->width);
-    gs_status s = project_and_sort_view(gconst(params), n, tc, c, 0, L, pair_capacity, vis_counts,
-                                        false, st);
+    GS_CUDA_CHECK(cudaMemcpyAsync(L.cams, &tc, sizeof(TCam), cudaMemcpyHostToDevice, st));
+    gs_status s = project_views(gconst(params), n, 1, c, L, vis_counts, false, st);
+    if (s != GS_OK) return s;
+    s = sort_view(n, c, 0, L, pair_capacity, st);
     if (s != GS_OK) return s;
     k_export_projection<<<div_up(n, 256), 256, 0, st>>>(L.pv, n, means2d, conic, opacity, colors,
                                                         depth, rects);
@@ -1236,7 +1339,9 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
                  "gs_train_step: quats must be 16-byte aligned");
     int H = 0, W = 0;
     for (int v = 0; v < n_views; ++v) {
-        GS_ARG_CHECK(cams[v].height > 0 && cams[v].width > 0, "gs_train_step: bad image size");
+        GS_ARG_CHECK(image_fits(cams[v].height, cams[v].width, cfg->tile_size),
+                     "gs_train_step: image must be 1..%d tile rows and 1..65535 tile columns",
+                     kMaxTileRows);
         GS_ARG_CHECK(targets[v] != nullptr, "gs_train_step: null target");
         H = std::max(H, (int)cams[v].height);
         W = std::max(W, (int)cams[v].width);
@@ -1271,19 +1376,30 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
         LC.lambda = cfg->lambda_dssim;
     }
 
+    if (cfg->use_ssim) {
+        GS_CUDA_CHECK(cudaFuncSetAttribute(k_ssim_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)sizeof(SsimFwdSmem)));
+        GS_CUDA_CHECK(cudaFuncSetAttribute(k_ssim_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)sizeof(SsimBwdSmem)));
+    }
+    {
+        gs_status s = project_views(P, n, n_views, make_tcfg(*cfg, H, W), L, vis_counts, true, st);
+        if (s != GS_OK) return s;
+    }
     for (int v = 0; v < n_views; ++v) {
         const int vh = cams[v].height, vw = cams[v].width;
         const TCfg c = make_tcfg(*cfg, vh, vw);
-        gs_status s = project_and_sort_view(P, n, hc[v], c, v, L, pair_capacity, vis_counts, true, st);
+        gs_status s = sort_view(n, c, v, L, pair_capacity, st);
         if (s != GS_OK) return s;
+        const ProjView pvv = L.pv.view(v, n);
         float* img = images ? images + (size_t)v * vh * vw * 3 : L.image;
         const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
         {
             KernelTimer kt("raster_fwd", st);
             if (c.tile == 16)
-                k_train_fwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
+                k_train_fwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(L.ranges, L.svals, pvv, c, vh, vw, img, L.final_T, L.ncon);
             else
-                k_train_fwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, img, L.final_T, L.ncon);
+                k_train_fwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(L.ranges, L.svals, pvv, c, vh, vw, img, L.final_T, L.ncon);
             GS_CHECK_LAUNCH();
         }
         LC.H = vh;
@@ -1293,11 +1409,11 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
             KernelTimer kt("loss", st);
             const int64_t n3 = (int64_t)vh * vw * 3;
             if (cfg->use_ssim) {
-                dim3 grid(div_up(vw, kLossTile), div_up(vh, kLossTile));
-                k_ssim_fwd<<<grid, kLossTile * kLossTile, 0, st>>>(img, targets[v], LC, L.dmu, L.dxx,
+                dim3 grid(div_up(vw, kSsimT), div_up(vh, kSsimT));
+                k_ssim_fwd<<<grid, 256, sizeof(SsimFwdSmem), st>>>(img, targets[v], LC, L.dmu, L.dxx,
                                                                    L.dxy, L.loss_acc + 2 * v);
                 GS_CHECK_LAUNCH();
-                k_ssim_bwd<<<grid, kLossTile * kLossTile, 0, st>>>(img, targets[v], L.dmu, L.dxx, L.dxy,
+                k_ssim_bwd<<<grid, 256, sizeof(SsimBwdSmem), st>>>(img, targets[v], L.dmu, L.dxx, L.dxy,
                                                                    LC, L.dimg);
             } else {
                 k_loss_l1<<<(unsigned int)std::min<int64_t>(div_up(n3, 256), kNumSMs * 8), 256, 0, st>>>(
@@ -1311,10 +1427,10 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
             KernelTimer kt("raster_bwd", st);
             float* g2 = L.grad2d + (size_t)v * n * kGradStride;
             if (c.tile == 16)
-                k_train_bwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
+                k_train_bwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(L.ranges, L.svals, pvv, c, vh, vw, L.dimg,
                                                          L.final_T, L.ncon, g2);
             else
-                k_train_bwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(L.ranges, L.svals, L.pv, c, vh, vw, L.dimg,
+                k_train_bwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(L.ranges, L.svals, pvv, c, vh, vw, L.dimg,
                                                           L.final_T, L.ncon, g2);
             GS_CHECK_LAUNCH();
         }

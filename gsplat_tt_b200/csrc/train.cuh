@@ -28,7 +28,8 @@ struct GConst {
     const float* sh;
 };
 
-// Projected record of one Gaussian for one view, as the rasterisers read it:
+// Projected records of the Gaussians for one view (or, for the projection kernel, all of a
+// step's views back to back, [view][n]), as the rasterisers read them:
 // p0 = (mean x, mean y, conic A, conic B), p1 = (conic C, opacity, r, g), p2 = b.
 struct ProjView {
     float4* p0;
@@ -38,6 +39,13 @@ struct ProjView {
     uint32_t* dsort;  // depth-sort key: dkey, or 0xffffffff for a Gaussian without pairs
     ushort4* rect;    // inclusive tile rectangle x0, x1, y0, y1
     uint32_t* cnt;    // tiles in the rectangle (0 = no pairs)
+
+    // View v's records inside the [view][n] arrays.
+    ProjView view(int v, int64_t n) const {
+        const size_t o = (size_t)v * n;
+        return ProjView{p0 + o, p1 + o, p2 + o, dkey ? dkey + o : nullptr, dsort + o, rect + o,
+                        cnt + o};
+    }
 };
 
 constexpr int kGradStride = 12;  // floats per Gaussian in a view's 2D-gradient rows
@@ -46,14 +54,22 @@ TCam make_tcam(const gs_camera& c);
 TCfg make_tcfg(const gs_train_config& c, int H, int W);
 
 // train_project.cu (compiled without FMA contraction)
-void launch_project(const GConst& P, int64_t n, const TCam& cam, const TCfg& cfg, int view,
-                    const ProjView& pv, int64_t* blk, uint64_t* touch, float* vis_counts,
-                    float* grad2d, cudaStream_t st);
+// Projects every view (cams: device array of n_views cameras) in one pass; pv arrays are
+// [n_views][n], blk holds each view's per-block pair totals at v * blk_stride.
+void launch_project(const GConst& P, int64_t n, const TCam* cams, int n_views, const TCfg& cfg,
+                    const ProjView& pv, int64_t* blk, int64_t blk_stride, uint64_t* touch,
+                    float* vis_counts, float* grad2d, cudaStream_t st);
 void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int64_t* blk,
                          cudaStream_t st);
-void launch_emit(const ProjView& pv, const uint32_t* order, int64_t n, const TCfg& cfg,
-                 const int64_t* blk_offsets, int64_t capacity, uint32_t* keys, uint32_t* vals,
-                 unsigned int* err, cudaStream_t st);
+void launch_pair_offsets(const ProjView& pv, const uint32_t* order, int64_t n,
+                         const int64_t* blk_offsets, int64_t capacity, uint32_t* goff,
+                         ushort4* rect_d, uint32_t* tfirst, int64_t tfirst_len, uint32_t* last,
+                         unsigned int* err, cudaStream_t st);
+gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y, int npass,
+                             const int64_t* pairs, int64_t capacity, int* diff, int2* ranges,
+                             uint32_t* digit_offsets, cudaStream_t st);
 constexpr int kProjThreads = 256;
+constexpr int kMaxViews = 64;  // views per training step (one bit each in the touched mask)
+constexpr int kMaxTileRows = 4096;  // tile rows the tile-count kernel handles
 
 }  // namespace gs

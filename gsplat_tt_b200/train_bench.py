@@ -47,14 +47,15 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, px: int) -> float
     """Algorithmic DRAM bytes of one launch of the HBM-bound kernels (per view unless
     noted): projection reads the SH3 params (236 B) and writes the 2D record, key and rect
     (48 + 16 B) per Gaussian; the sparse Adam (one launch per parameter group, averaged)
-    reads p, m, v, g and writes p, m, v for the 59 values of each row; the emission writes
-    12 B per pair."""
+    reads p, m, v, g and writes p, m, v for the 59 values of each row; the fused emission +
+    first tile-sort pass reads 16 B per Gaussian (depth order, pair offset, rectangle) and
+    writes 8 B per pair (tile key and Gaussian id)."""
     if name == "train_project":
         return n * (236.0 + 64.0)
     if name == "sparse_adam":
         return n * 59 * 28.0
-    if name == "train_emit":
-        return pairs * 12.0 + n * 16.0
+    if name == "tile_sort_emit":
+        return pairs * 8.0 + n * 16.0
     return None
 
 

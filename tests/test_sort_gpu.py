@@ -55,6 +55,21 @@ def test_key_widths_and_duplicates(gd, bits):
     np.testing.assert_array_equal(vg, vo)
 
 
+@pytest.mark.parametrize("bits", [5, 12, 21, 40])
+def test_bits_above_key_bits_are_ignored(gd, bits):
+    """Keys with set bits above key_bits sort stably on their low key_bits bits only
+    (the last pass's digit is narrower than a byte here)."""
+    rng = np.random.default_rng(100 + bits)
+    n = 200_000
+    keys = rng.integers(0, 1 << 62, n, dtype=np.uint64)
+    vals = np.arange(n, dtype=np.uint32)
+    low = keys & np.uint64((1 << bits) - 1)
+    order = np.argsort(low, kind="stable")
+    kg, vg = run(gd, keys, vals, bits)
+    np.testing.assert_array_equal(vg, vals[order])
+    np.testing.assert_array_equal(kg, keys[order])
+
+
 def test_c2_full_matches_reference_golden(gd):
     G = np.load(os.path.join(GOLDEN, "sort.npz"))
     keys, vals = scenes.c2_pairs()
