@@ -141,6 +141,16 @@ __device__ __forceinline__ float lx_plus_af_du(const RPair& q, float du) {
     return __fadd_rn(q.Lx, __fmul_rn(q.Af, du));
 }
 
+// centred_power for two pixels of one column at once with Blackwell's packed fp32x2
+// operations: each lane rounds exactly as the scalar version does.
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
+__device__ __forceinline__ float2 centred_power2(const RPair& q, float lx_af, float du, float2 dv) {
+    const float2 inner = __fadd2_rn(f2(lx_af), __fmul2_rn(f2(q.Bf), dv));
+    const float2 e6 = __fadd2_rn(f2(q.P0), __fmul2_rn(f2(du), inner));
+    const float2 e8 = __fadd2_rn(f2(q.Ly), __fmul2_rn(f2(q.Cf), dv));
+    return __fadd2_rn(e6, __fmul2_rn(dv, e8));
+}
+
 // Pixel layout of the rasterisers: a TILE x TILE tile is covered by TILE*TILE/PPT threads;
 // thread t owns column t % TILE and the PPT consecutive rows (t / TILE) * PPT + i. One pair
 // read from shared memory then serves PPT pixels, and the pair's row/column reach masks
@@ -161,6 +171,8 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             int32_t* __restrict__ n_contrib) {
     using LY = PixLayout<TILE, PPT>;
     constexpr int NB = kRasterBatch;
+    constexpr int NP = PPT / 2;  // pixel pairs per thread, each blended with packed fp32x2 math
+    static_assert(PPT % 2 == 0, "pixels are processed in pairs");
     __shared__ RPair sp[NB];
     const int tile = blockIdx.x;
     const int tx = tile % cfg.tiles_x, ty = tile / cfg.tiles_x;
@@ -171,17 +183,20 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     const float ox = (float)(tx * TILE), oy = (float)(ty * TILE);
     const int2 rg = ranges[tile];
     const float amax = cfg.amax, amin = cfg.amin, tmin = cfg.tmin;
-    float dv[PPT], T[PPT], c0[PPT], c1[PPT], c2[PPT];
+    float2 dv[NP], T[NP], cr[NP], cg[NP], cb[NP];
     int last[PPT];
     unsigned live_mask = 0;  // pixels still blending
 #pragma unroll
+    for (int h = 0; h < NP; ++h) {
+        dv[h] = make_float2(((float)(ly0 + 2 * h) + 0.5f) - centre,
+                            ((float)(ly0 + 2 * h + 1) + 0.5f) - centre);
+        T[h] = f2(1.0f);
+        cr[h] = cg[h] = cb[h] = f2(0.0f);
+    }
+#pragma unroll
     for (int i = 0; i < PPT; ++i) {
-        const int ly = ly0 + i;
-        dv[i] = ((float)ly + 0.5f) - centre;
-        T[i] = 1.0f;
-        c0[i] = c1[i] = c2[i] = 0.0f;
         last[i] = 0;
-        if (x < W && ty * TILE + ly < H) live_mask |= 1u << i;
+        if (x < W && ty * TILE + ly0 + i < H) live_mask |= 1u << i;
     }
     for (int b0 = rg.x; b0 < rg.y; b0 += NB) {
         __syncthreads();
@@ -199,24 +214,29 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             if (!todo) continue;
             const float t1 = lx_plus_af_du(q, du);  // shared by the thread's pixels
 #pragma unroll
-            for (int i = 0; i < PPT; ++i) {
-                if (!((todo >> i) & 1u)) continue;
-                const float power = centred_power(q, t1, du, dv[i]);
-                const float w = __expf(fminf(power, 0.0f));
-                const float alpha = fminf(__fmul_rn(q.op, w), amax);
-                if (alpha >= amin) {
-                    const float Tn = __fmul_rn(T[i], __fsub_rn(1.0f, alpha));
-                    if (Tn < tmin) {
-                        live_mask &= ~(1u << i);
-                    } else {
-                        const float at = alpha * T[i];
-                        c0[i] = __fmaf_rn(at, q.r, c0[i]);
-                        c1[i] = __fmaf_rn(at, q.g, c1[i]);
-                        c2[i] = __fmaf_rn(at, q.b, c2[i]);
-                        T[i] = Tn;
-                        last[i] = b0 - rg.x + j + 1;
-                    }
-                }
+            for (int h = 0; h < NP; ++h) {
+                const uint32_t tb = (todo >> (2 * h)) & 3u;
+                if (!tb) continue;
+                const float2 power = centred_power2(q, t1, du, dv[h]);
+                const float2 w = make_float2(__expf(fminf(power.x, 0.0f)), __expf(fminf(power.y, 0.0f)));
+                const float2 ow = __fmul2_rn(f2(q.op), w);
+                const float2 alpha = make_float2(fminf(ow.x, amax), fminf(ow.y, amax));
+                const float2 Tn = __fmul2_rn(T[h], __fadd2_rn(f2(1.0f), make_float2(-alpha.x, -alpha.y)));
+                const bool h0 = (tb & 1u) && alpha.x >= amin, h1 = (tb & 2u) && alpha.y >= amin;
+                const bool s0 = h0 && Tn.x < tmin, s1 = h1 && Tn.y < tmin;  // pixel stops
+                const bool u0 = h0 && !s0, u1 = h1 && !s1;                  // pixel blends
+                if (s0) live_mask &= ~(1u << (2 * h));
+                if (s1) live_mask &= ~(1u << (2 * h + 1));
+                if (!(u0 || u1)) continue;
+                const float2 at0 = __fmul2_rn(alpha, T[h]);
+                const float2 at = make_float2(u0 ? at0.x : 0.0f, u1 ? at0.y : 0.0f);
+                cr[h] = __ffma2_rn(at, f2(q.r), cr[h]);
+                cg[h] = __ffma2_rn(at, f2(q.g), cg[h]);
+                cb[h] = __ffma2_rn(at, f2(q.b), cb[h]);
+                T[h] = make_float2(u0 ? Tn.x : T[h].x, u1 ? Tn.y : T[h].y);
+                const int idx = b0 - rg.x + j + 1;
+                if (u0) last[2 * h] = idx;
+                if (u1) last[2 * h + 1] = idx;
             }
         }
         if (__syncthreads_count(live_mask != 0) == 0) break;
@@ -225,11 +245,14 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     for (int i = 0; i < PPT; ++i) {
         const int y = ty * TILE + ly0 + i;
         if (x >= W || y >= H) continue;
+        const int h = i >> 1;
+        const bool hi = i & 1;
+        const float Ti = hi ? T[h].y : T[h].x;
         const size_t o = (size_t)y * W + x;
-        image[3 * o] = c0[i] + T[i] * cfg.bg[0];
-        image[3 * o + 1] = c1[i] + T[i] * cfg.bg[1];
-        image[3 * o + 2] = c2[i] + T[i] * cfg.bg[2];
-        final_T[o] = T[i];
+        image[3 * o] = (hi ? cr[h].y : cr[h].x) + Ti * cfg.bg[0];
+        image[3 * o + 1] = (hi ? cg[h].y : cg[h].x) + Ti * cfg.bg[1];
+        image[3 * o + 2] = (hi ? cb[h].y : cb[h].x) + Ti * cfg.bg[2];
+        final_T[o] = Ti;
         n_contrib[o] = last[i];
     }
 }
@@ -287,6 +310,8 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             float* __restrict__ grad2d) {
     using LY = PixLayout<TILE, PPT>;
     constexpr int NB = kRasterBatch;
+    constexpr int NP = PPT / 2;  // pixel pairs per thread (packed fp32x2 math)
+    static_assert(PPT % 2 == 0, "pixels are processed in pairs");
     __shared__ BPair sp[NB];
     __shared__ float acc[9][NB + 1];  // rows one bank apart: the 8-lane atomics hit 8 banks
     __shared__ int s_max;
@@ -301,27 +326,38 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     const int2 rg = ranges[tile];
     const int lane = threadIdx.x & 31;
     const float amax = cfg.amax, amin = cfg.amin;
-    float dv[PPT], yy[PPT], T[PPT], g0[PPT], g1[PPT], g2[PPT], behind[PPT];
+    float2 dv[NP], yy[NP], T[NP], g0[NP], g1[NP], g2[NP], behind[NP];
     int last[PPT];
     int my_max = 0;
 #pragma unroll
     for (int i = 0; i < PPT; ++i) {
         const int ly = ly0 + i;
         const int y = ty * TILE + ly;
-        dv[i] = ((float)ly + 0.5f) - centre;
-        yy[i] = (float)ly + 0.5f;
-        T[i] = 1.0f;
-        g0[i] = g1[i] = g2[i] = behind[i] = 0.0f;
+        float Ti = 1.0f, a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, bh = 0.0f;
         last[i] = 0;
         if (x < W && y < H) {
             const size_t o = (size_t)y * W + x;
-            T[i] = final_T[o];
+            Ti = final_T[o];
             last[i] = n_contrib[o];
-            g0[i] = dimg[3 * o];
-            g1[i] = dimg[3 * o + 1];
-            g2[i] = dimg[3 * o + 2];
-            behind[i] = T[i] * (cfg.bg[0] * g0[i] + cfg.bg[1] * g1[i] + cfg.bg[2] * g2[i]);
+            a0 = dimg[3 * o];
+            a1 = dimg[3 * o + 1];
+            a2 = dimg[3 * o + 2];
+            bh = Ti * (cfg.bg[0] * a0 + cfg.bg[1] * a1 + cfg.bg[2] * a2);
             my_max = max(my_max, last[i]);
+        }
+        float2& d2 = dv[i >> 1];
+        float2& y2 = yy[i >> 1];
+        float2& t2 = T[i >> 1];
+        float2& e0 = g0[i >> 1];
+        float2& e1 = g1[i >> 1];
+        float2& e2 = g2[i >> 1];
+        float2& b2 = behind[i >> 1];
+        if (i & 1) {
+            d2.y = ((float)ly + 0.5f) - centre; y2.y = (float)ly + 0.5f; t2.y = Ti;
+            e0.y = a0; e1.y = a1; e2.y = a2; b2.y = bh;
+        } else {
+            d2.x = ((float)ly + 0.5f) - centre; y2.x = (float)ly + 0.5f; t2.x = Ti;
+            e0.x = a0; e1.x = a1; e2.x = a2; b2.x = bh;
         }
     }
     if (threadIdx.x == 0) s_max = 0;
@@ -349,9 +385,9 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
         __syncthreads();
         for (int j = nb - 1; j >= 0; --j) {
             const int idx = lo + j;
-            float v[9];
+            float2 v[9];
 #pragma unroll
-            for (int k = 0; k < 9; ++k) v[k] = 0.0f;
+            for (int k = 0; k < 9; ++k) v[k] = f2(0.0f);
             bool live_any = false;
             const BPair& bp = sp[j];
             const uint32_t reach = (idx < my_max && ((bp.q.cols >> lx) & 1u))
@@ -361,39 +397,50 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
                 const float t1 = lx_plus_af_du(q, du);
                 const float u = xx - bp.mxl;
 #pragma unroll
-                for (int i = 0; i < PPT; ++i) {
-                    if (!((reach >> i) & 1u) || idx >= last[i]) continue;
-                    const float power = centred_power(q, t1, du, dv[i]);
-                    const float w = __expf(fminf(power, 0.0f));
-                    const float raw = __fmul_rn(q.op, w);
-                    const bool clamp = raw > amax;
-                    const float alpha = fminf(raw, amax);
-                    if (alpha < amin) continue;
+                for (int h = 0; h < NP; ++h) {
+                    const bool r0 = ((reach >> (2 * h)) & 1u) && idx < last[2 * h];
+                    const bool r1 = ((reach >> (2 * h + 1)) & 1u) && idx < last[2 * h + 1];
+                    if (!(r0 || r1)) continue;
+                    const float2 power = centred_power2(q, t1, du, dv[h]);
+                    const float2 w = make_float2(__expf(fminf(power.x, 0.0f)), __expf(fminf(power.y, 0.0f)));
+                    const float2 raw = __fmul2_rn(f2(q.op), w);
+                    const float2 alpha = make_float2(fminf(raw.x, amax), fminf(raw.y, amax));
+                    const bool l0 = r0 && alpha.x >= amin, l1 = r1 && alpha.y >= amin;
+                    if (!(l0 || l1)) continue;
                     live_any = true;
-                    const float r = __fdividef(1.0f, 1.0f - alpha);
-                    const float Ti = T[i] * r;
-                    const float cg = q.r * g0[i] + q.g * g1[i] + q.b * g2[i];
-                    const float dalpha = Ti * cg - behind[i] * r;
-                    const float at = alpha * Ti;
-                    behind[i] = __fmaf_rn(at, cg, behind[i]);
-                    T[i] = Ti;
-                    const float G = (!clamp && power <= 0.0f) ? dalpha * alpha : 0.0f;
-                    const float vv = yy[i] - bp.myl;
-                    const float Gu = G * u, Gv = G * vv;
-                    v[0] += clamp ? 0.0f : dalpha * w;
-                    v[1] = __fmaf_rn(at, g0[i], v[1]);
-                    v[2] = __fmaf_rn(at, g1[i], v[2]);
-                    v[3] = __fmaf_rn(at, g2[i], v[3]);
-                    v[4] = __fmaf_rn(Gu, u, v[4]);
-                    v[5] = __fmaf_rn(Gu, vv, v[5]);
-                    v[6] = __fmaf_rn(Gv, vv, v[6]);
-                    v[7] += Gu;
-                    v[8] += Gv;
+                    // d alpha / d power and d alpha / d opacity vanish where alpha is clamped
+                    const bool c0 = l0 && !(raw.x > amax), c1 = l1 && !(raw.y > amax);
+                    const float2 rr = make_float2(__fdividef(1.0f, 1.0f - alpha.x),
+                                                  __fdividef(1.0f, 1.0f - alpha.y));
+                    const float2 Ti = __fmul2_rn(T[h], rr);
+                    const float2 cgv = __ffma2_rn(f2(q.b), g2[h], __ffma2_rn(f2(q.g), g1[h], __fmul2_rn(f2(q.r), g0[h])));
+                    const float2 dalpha = __ffma2_rn(Ti, cgv, make_float2(-behind[h].x * rr.x, -behind[h].y * rr.y));
+                    const float2 at0 = __fmul2_rn(alpha, Ti);
+                    const float2 at = make_float2(l0 ? at0.x : 0.0f, l1 ? at0.y : 0.0f);
+                    behind[h] = __ffma2_rn(at, cgv, behind[h]);
+                    T[h] = make_float2(l0 ? Ti.x : T[h].x, l1 ? Ti.y : T[h].y);
+                    const float2 dd = make_float2(c0 ? dalpha.x : 0.0f, c1 ? dalpha.y : 0.0f);
+                    const float2 G = make_float2(power.x <= 0.0f ? dd.x * alpha.x : 0.0f,
+                                                 power.y <= 0.0f ? dd.y * alpha.y : 0.0f);
+                    const float2 vv = __fadd2_rn(yy[h], f2(-bp.myl));
+                    const float2 Gu = __fmul2_rn(G, f2(u)), Gv = __fmul2_rn(G, vv);
+                    v[0] = __ffma2_rn(dd, w, v[0]);
+                    v[1] = __ffma2_rn(at, g0[h], v[1]);
+                    v[2] = __ffma2_rn(at, g1[h], v[2]);
+                    v[3] = __ffma2_rn(at, g2[h], v[3]);
+                    v[4] = __ffma2_rn(Gu, f2(u), v[4]);
+                    v[5] = __ffma2_rn(Gu, vv, v[5]);
+                    v[6] = __ffma2_rn(Gv, vv, v[6]);
+                    v[7] = __fadd2_rn(v[7], Gu);
+                    v[8] = __fadd2_rn(v[8], Gv);
                 }
             }
             if (__any_sync(0xffffffffu, live_any)) {
+                float vs[9];
+#pragma unroll
+                for (int k = 0; k < 9; ++k) vs[k] = v[k].x + v[k].y;
                 float s8, s1;
-                warp_sum9(v, lane, s8, s1);
+                warp_sum9(vs, lane, s8, s1);
                 if ((lane & 3) == 0) atomicAdd(&acc[lane >> 2][j], s8);
                 if (lane == 1) atomicAdd(&acc[8][j], s1);
             }
@@ -499,44 +546,59 @@ k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg
     for (int ch = 0; ch < 3; ++ch) {
         for (int it = tid; it < kSsimHItems; it += 256) {
             const int r = it >> 3, c0 = (it & 7) * 4;
-            float xv[14], yv[14];
+            // (x, y) and (x^2, y^2) filtered as packed fp32x2 pairs, x y on its own
+            float2 xy[14], sq[14];
+            float pr[14];
 #pragma unroll
             for (int k = 0; k < 14; ++k) {
-                xv[k] = S.px[ch][r][c0 + k];
-                yv[k] = S.py[ch][r][c0 + k];
+                xy[k] = make_float2(S.px[ch][r][c0 + k], S.py[ch][r][c0 + k]);
+                sq[k] = __fmul2_rn(xy[k], xy[k]);
+                pr[k] = __fmul_rn(xy[k].x, xy[k].y);
             }
 #pragma unroll
             for (int o = 0; o < 4; ++o) {
-                float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f, a4 = 0.f;
+                float2 a01 = f2(0.0f), a23 = f2(0.0f);
+                float a4 = 0.0f;
 #pragma unroll
                 for (int k = 0; k < 11; ++k) {
-                    const float xk = xv[o + k], yk = yv[o + k], t = L.taps[k];
-                    a0 = __fmaf_rn(t, xk, a0);
-                    a1 = __fmaf_rn(t, yk, a1);
-                    a2 = __fmaf_rn(t, xk * xk, a2);
-                    a3 = __fmaf_rn(t, yk * yk, a3);
-                    a4 = __fmaf_rn(t, xk * yk, a4);
+                    const float t = L.taps[k];
+                    a01 = __ffma2_rn(f2(t), xy[o + k], a01);
+                    a23 = __ffma2_rn(f2(t), sq[o + k], a23);
+                    a4 = __fmaf_rn(t, pr[o + k], a4);
                 }
-                S.h[0][r][c0 + o] = a0;
-                S.h[1][r][c0 + o] = a1;
-                S.h[2][r][c0 + o] = a2;
-                S.h[3][r][c0 + o] = a3;
+                S.h[0][r][c0 + o] = a01.x;
+                S.h[1][r][c0 + o] = a01.y;
+                S.h[2][r][c0 + o] = a23.x;
+                S.h[3][r][c0 + o] = a23.y;
                 S.h[4][r][c0 + o] = a4;
             }
         }
         __syncthreads();
         float m[5][4];
 #pragma unroll
-        for (int q = 0; q < 5; ++q) {
+        for (int q = 0; q < 4; q += 2) {  // quantities (0, 1) and (2, 3) packed
+            float2 v[14];
+#pragma unroll
+            for (int k = 0; k < 14; ++k) v[k] = make_float2(S.h[q][vr0 + k][vc], S.h[q + 1][vr0 + k][vc]);
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                float2 a = f2(0.0f);
+#pragma unroll
+                for (int k = 0; k < 11; ++k) a = __ffma2_rn(f2(L.taps[k]), v[o + k], a);
+                m[q][o] = a.x;
+                m[q + 1][o] = a.y;
+            }
+        }
+        {
             float v[14];
 #pragma unroll
-            for (int k = 0; k < 14; ++k) v[k] = S.h[q][vr0 + k][vc];
+            for (int k = 0; k < 14; ++k) v[k] = S.h[4][vr0 + k][vc];
 #pragma unroll
             for (int o = 0; o < 4; ++o) {
                 float a = 0.0f;
 #pragma unroll
                 for (int k = 0; k < 11; ++k) a = __fmaf_rn(L.taps[k], v[o + k], a);
-                m[q][o] = a;
+                m[4][o] = a;
             }
         }
 #pragma unroll
@@ -603,33 +665,57 @@ k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt,
         __syncthreads();
         for (int it = tid; it < kSsimHItems; it += 256) {
             const int r = it >> 3, c0 = (it & 7) * 4;
+            {   // maps 0 and 1 packed
+                float2 v[14];
 #pragma unroll
-            for (int q = 0; q < 3; ++q) {
+                for (int k = 0; k < 14; ++k) v[k] = make_float2(S.p[0][r][c0 + k], S.p[1][r][c0 + k]);
+#pragma unroll
+                for (int o = 0; o < 4; ++o) {
+                    float2 a = f2(0.0f);
+#pragma unroll
+                    for (int k = 0; k < 11; ++k) a = __ffma2_rn(f2(L.taps[k]), v[o + k], a);
+                    S.h[0][r][c0 + o] = a.x;
+                    S.h[1][r][c0 + o] = a.y;
+                }
+            }
+            {
                 float v[14];
 #pragma unroll
-                for (int k = 0; k < 14; ++k) v[k] = S.p[q][r][c0 + k];
+                for (int k = 0; k < 14; ++k) v[k] = S.p[2][r][c0 + k];
 #pragma unroll
                 for (int o = 0; o < 4; ++o) {
                     float a = 0.0f;
 #pragma unroll
                     for (int k = 0; k < 11; ++k) a = __fmaf_rn(L.taps[k], v[o + k], a);
-                    S.h[q][r][c0 + o] = a;
+                    S.h[2][r][c0 + o] = a;
                 }
             }
         }
         __syncthreads();
         float m[3][4];
+        {
+            float2 v[14];
 #pragma unroll
-        for (int q = 0; q < 3; ++q) {
+            for (int k = 0; k < 14; ++k) v[k] = make_float2(S.h[0][vr0 + k][vc], S.h[1][vr0 + k][vc]);
+#pragma unroll
+            for (int o = 0; o < 4; ++o) {
+                float2 a = f2(0.0f);
+#pragma unroll
+                for (int k = 0; k < 11; ++k) a = __ffma2_rn(f2(L.taps[k]), v[o + k], a);
+                m[0][o] = a.x;
+                m[1][o] = a.y;
+            }
+        }
+        {
             float v[14];
 #pragma unroll
-            for (int k = 0; k < 14; ++k) v[k] = S.h[q][vr0 + k][vc];
+            for (int k = 0; k < 14; ++k) v[k] = S.h[2][vr0 + k][vc];
 #pragma unroll
             for (int o = 0; o < 4; ++o) {
                 float a = 0.0f;
 #pragma unroll
                 for (int k = 0; k < 11; ++k) a = __fmaf_rn(L.taps[k], v[o + k], a);
-                m[q][o] = a;
+                m[2][o] = a;
             }
         }
 #pragma unroll
@@ -664,42 +750,61 @@ __constant__ float c_C3[7] = {-0.5900435899266435f, 2.890611442640554f, -0.45704
                               0.3731763325901154f, -0.4570457994644658f, 1.445305721320277f,
                               -0.5900435899266435f};
 
-__device__ __forceinline__ void sh_basis_and_grad(int deg, float x, float y, float z, float* b,
-                                                  float (*db)[3]) {
+// Real SH basis up to degree `deg` at unit direction (x, y, z) (gsplat/train_oracle.py:99-122).
+__device__ __forceinline__ void sh_basis(int deg, float x, float y, float z, float* b) {
     b[0] = kC0;
-    db[0][0] = db[0][1] = db[0][2] = 0.0f;
     if (deg < 1) return;
-    b[1] = -kC1 * y; db[1][0] = 0.f; db[1][1] = -kC1; db[1][2] = 0.f;
-    b[2] = kC1 * z; db[2][0] = 0.f; db[2][1] = 0.f; db[2][2] = kC1;
-    b[3] = -kC1 * x; db[3][0] = -kC1; db[3][1] = 0.f; db[3][2] = 0.f;
+    b[1] = -kC1 * y;
+    b[2] = kC1 * z;
+    b[3] = -kC1 * x;
     if (deg < 2) return;
     const float xx = x * x, yy = y * y, zz = z * z;
     const float* c = c_C2;
-    b[4] = c[0] * (x * y); db[4][0] = c[0] * y; db[4][1] = c[0] * x; db[4][2] = 0.f;
-    b[5] = c[1] * (y * z); db[5][0] = 0.f; db[5][1] = c[1] * z; db[5][2] = c[1] * y;
+    b[4] = c[0] * (x * y);
+    b[5] = c[1] * (y * z);
     b[6] = c[2] * (2.0f * zz - xx - yy);
-    db[6][0] = -2.0f * c[2] * x; db[6][1] = -2.0f * c[2] * y; db[6][2] = 4.0f * c[2] * z;
-    b[7] = c[3] * (x * z); db[7][0] = c[3] * z; db[7][1] = 0.f; db[7][2] = c[3] * x;
-    b[8] = c[4] * (xx - yy); db[8][0] = 2.0f * c[4] * x; db[8][1] = -2.0f * c[4] * y; db[8][2] = 0.f;
+    b[7] = c[3] * (x * z);
+    b[8] = c[4] * (xx - yy);
     if (deg < 3) return;
     const float* e = c_C3;
     b[9] = e[0] * y * (3.0f * xx - yy);
-    db[9][0] = e[0] * 6.0f * x * y; db[9][1] = e[0] * (3.0f * xx - 3.0f * yy); db[9][2] = 0.f;
     b[10] = e[1] * (x * y) * z;
-    db[10][0] = e[1] * y * z; db[10][1] = e[1] * x * z; db[10][2] = e[1] * x * y;
     b[11] = e[2] * y * (4.0f * zz - xx - yy);
-    db[11][0] = -2.0f * e[2] * x * y; db[11][1] = e[2] * (4.0f * zz - xx - 3.0f * yy);
-    db[11][2] = 8.0f * e[2] * y * z;
     b[12] = e[3] * z * (2.0f * zz - 3.0f * xx - 3.0f * yy);
-    db[12][0] = -6.0f * e[3] * x * z; db[12][1] = -6.0f * e[3] * y * z;
-    db[12][2] = e[3] * (6.0f * zz - 3.0f * xx - 3.0f * yy);
     b[13] = e[4] * x * (4.0f * zz - xx - yy);
-    db[13][0] = e[4] * (4.0f * zz - 3.0f * xx - yy); db[13][1] = -2.0f * e[4] * x * y;
-    db[13][2] = 8.0f * e[4] * x * z;
     b[14] = e[5] * z * (xx - yy);
-    db[14][0] = 2.0f * e[5] * x * z; db[14][1] = -2.0f * e[5] * y * z; db[14][2] = e[5] * (xx - yy);
     b[15] = e[6] * x * (xx - 3.0f * yy);
-    db[15][0] = e[6] * (3.0f * xx - 3.0f * yy); db[15][1] = -6.0f * e[6] * x * y; db[15][2] = 0.f;
+}
+
+// Gradient with respect to the direction of sum_k w[k] basis_k(x, y, z), term by term.
+__device__ __forceinline__ void sh_dir_grad(int deg, float x, float y, float z, const float* w,
+                                            float* g) {
+    g[0] = g[1] = g[2] = 0.0f;
+    if (deg < 1) return;
+    g[1] += -kC1 * w[1];
+    g[2] += kC1 * w[2];
+    g[0] += -kC1 * w[3];
+    if (deg < 2) return;
+    const float xx = x * x, yy = y * y, zz = z * z;
+    const float* c = c_C2;
+    g[0] += c[0] * y * w[4]; g[1] += c[0] * x * w[4];
+    g[1] += c[1] * z * w[5]; g[2] += c[1] * y * w[5];
+    g[0] += -2.0f * c[2] * x * w[6]; g[1] += -2.0f * c[2] * y * w[6]; g[2] += 4.0f * c[2] * z * w[6];
+    g[0] += c[3] * z * w[7]; g[2] += c[3] * x * w[7];
+    g[0] += 2.0f * c[4] * x * w[8]; g[1] += -2.0f * c[4] * y * w[8];
+    if (deg < 3) return;
+    const float* e = c_C3;
+    g[0] += e[0] * 6.0f * x * y * w[9]; g[1] += e[0] * (3.0f * xx - 3.0f * yy) * w[9];
+    g[0] += e[1] * y * z * w[10]; g[1] += e[1] * x * z * w[10]; g[2] += e[1] * x * y * w[10];
+    g[0] += -2.0f * e[2] * x * y * w[11]; g[1] += e[2] * (4.0f * zz - xx - 3.0f * yy) * w[11];
+    g[2] += 8.0f * e[2] * y * z * w[11];
+    g[0] += -6.0f * e[3] * x * z * w[12]; g[1] += -6.0f * e[3] * y * z * w[12];
+    g[2] += e[3] * (6.0f * zz - 3.0f * xx - 3.0f * yy) * w[12];
+    g[0] += e[4] * (4.0f * zz - 3.0f * xx - yy) * w[13]; g[1] += -2.0f * e[4] * x * y * w[13];
+    g[2] += 8.0f * e[4] * x * z * w[13];
+    g[0] += 2.0f * e[5] * x * z * w[14]; g[1] += -2.0f * e[5] * y * z * w[14];
+    g[2] += e[5] * (xx - yy) * w[14];
+    g[0] += e[6] * (3.0f * xx - 3.0f * yy) * w[15]; g[1] += -6.0f * e[6] * x * y * w[15];
 }
 
 struct GMut {
@@ -716,196 +821,213 @@ struct GMut {
 // accumulate across views; the log-scale, quaternion and logit gradients are formed once.
 // The geometric part runs in fp64: the covariance gradient cancels strongly along the
 // viewing direction (the part of cov3d a view cannot see), and fp32 there leaves errors
-// of ~1e-2 relative to the group's largest gradient. SH terms stay fp32.
+// of ~1e-2 relative to the group's largest gradient. SH terms stay fp32. The block's SH
+// rows and SH-gradient accumulators live in shared memory (coefficient-major, one padded
+// row per coefficient), which keeps the per-thread register state to the fp64 geometry.
+constexpr int kParamThreads = 128;
+constexpr int kParamStride = kParamThreads + 1;  // shared row stride: consecutive rows one bank apart
+
 template <int DEG>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(kParamThreads, 4)
 k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCfg cfg,
             const float* __restrict__ grad2d, const uint64_t* __restrict__ touch, GMut G) {
-    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (g >= n) return;
     constexpr int K = (DEG + 1) * (DEG + 1);
-    const uint64_t mask = touch[g];
-    double gm[3] = {0.0, 0.0, 0.0};
-    double G3[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // 00 01 02 11 12 22
-    float gop = 0.0f;
-    float gsh[3 * K];
-#pragma unroll
-    for (int k = 0; k < 3 * K; ++k) gsh[k] = 0.0f;
-    const double m0 = P.means[3 * g], m1 = P.means[3 * g + 1], m2 = P.means[3 * g + 2];
-    const float4 q = reinterpret_cast<const float4*>(P.q)[g];
-    const double qinv = 1.0 / sqrt((double)q.x * q.x + (double)q.y * q.y + (double)q.z * q.z +
-                                   (double)q.w * q.w);
-    const double qw = q.x * qinv, qx = q.y * qinv, qy = q.z * qinv, qz = q.w * qinv;
-    double Rq[9];
-    Rq[0] = 1.0 - 2.0 * (qy * qy + qz * qz);
-    Rq[1] = 2.0 * (qx * qy - qw * qz);
-    Rq[2] = 2.0 * (qx * qz + qw * qy);
-    Rq[3] = 2.0 * (qx * qy + qw * qz);
-    Rq[4] = 1.0 - 2.0 * (qx * qx + qz * qz);
-    Rq[5] = 2.0 * (qy * qz - qw * qx);
-    Rq[6] = 2.0 * (qx * qz - qw * qy);
-    Rq[7] = 2.0 * (qy * qz + qw * qx);
-    Rq[8] = 1.0 - 2.0 * (qx * qx + qy * qy);
-    const double s[3] = {exp((double)P.ls[3 * g]), exp((double)P.ls[3 * g + 1]),
-                         exp((double)P.ls[3 * g + 2])};
-    double M[9];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j) M[3 * i + j] = Rq[3 * i + j] * s[j];
-    double S[3][3];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int k = i; k < 3; ++k) {
-            S[i][k] = M[3 * i] * M[3 * k] + M[3 * i + 1] * M[3 * k + 1] + M[3 * i + 2] * M[3 * k + 2];
-            S[k][i] = S[i][k];
-        }
-    const float* shg = P.sh + (size_t)g * K * 3;
-    for (int v = 0; v < n_views; ++v) {
-        if (!((mask >> v) & 1ull)) continue;
-        const float* gr = grad2d + ((size_t)v * n + g) * kGradStride;
-        const float4 ga4 = reinterpret_cast<const float4*>(gr)[0];
-        const float4 gb4 = reinterpret_cast<const float4*>(gr)[1];
-        const float gbl = gr[8];
-        if (ga4.x == 0.f && ga4.y == 0.f && ga4.z == 0.f && ga4.w == 0.f && gb4.x == 0.f &&
-            gb4.y == 0.f && gb4.z == 0.f && gb4.w == 0.f && gbl == 0.f)
-            continue;
-        const double gmx = ga4.x, gmy = ga4.y, gA = ga4.z, gB = ga4.w, gC = gb4.x;
-        const TCam& cam = cams[v];
-        double R[9];
-#pragma unroll
-        for (int k = 0; k < 9; ++k) R[k] = cam.R[k];
-        const double x = R[0] * m0 + R[1] * m1 + R[2] * m2 + (double)cam.t[0];
-        const double y = R[3] * m0 + R[4] * m1 + R[5] * m2 + (double)cam.t[1];
-        const double z = R[6] * m0 + R[7] * m1 + R[8] * m2 + (double)cam.t[2];
-        if (!(z > (double)cfg.near_plane)) continue;
-        const double fx = cam.fx, fy = cam.fy;
-        const double iz = 1.0 / z, iz2 = iz * iz;
-        const double j00 = fx * iz, j02 = -fx * x * iz2;
-        const double j11 = fy * iz, j12 = -fy * y * iz2;
-        double T0[3], T1[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            T0[k] = j00 * R[k] + j02 * R[6 + k];
-            T1[k] = j11 * R[3 + k] + j12 * R[6 + k];
-        }
-        double TC0[3], TC1[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            TC0[k] = T0[0] * S[0][k] + T0[1] * S[1][k] + T0[2] * S[2][k];
-            TC1[k] = T1[0] * S[0][k] + T1[1] * S[1][k] + T1[2] * S[2][k];
-        }
-        const double lp = cfg.lowpass;
-        const double a = T0[0] * TC0[0] + T0[1] * TC0[1] + T0[2] * TC0[2] + lp;
-        const double b = T1[0] * TC0[0] + T1[1] * TC0[1] + T1[2] * TC0[2];
-        const double c = T1[0] * TC1[0] + T1[1] * TC1[1] + T1[2] * TC1[2] + lp;
-        const double idet = 1.0 / (a * c - b * b);
-        const double A = c * idet, B = -b * idet, C = a * idet;
-        // conic -> 2D covariance
-        const double ga = -(A * A * gA + A * B * gB + B * B * gC);
-        const double gc = -(B * B * gA + B * C * gB + C * C * gC);
-        const double hb = -0.5 * (2.0 * A * B * gA + (A * C + B * B) * gB + 2.0 * B * C * gC);
-        // dL/dcov3d += T^T Gs T
-        G3[0] += ga * T0[0] * T0[0] + 2.0 * hb * T0[0] * T1[0] + gc * T1[0] * T1[0];
-        G3[1] += ga * T0[0] * T0[1] + hb * (T0[0] * T1[1] + T1[0] * T0[1]) + gc * T1[0] * T1[1];
-        G3[2] += ga * T0[0] * T0[2] + hb * (T0[0] * T1[2] + T1[0] * T0[2]) + gc * T1[0] * T1[2];
-        G3[3] += ga * T0[1] * T0[1] + 2.0 * hb * T0[1] * T1[1] + gc * T1[1] * T1[1];
-        G3[4] += ga * T0[1] * T0[2] + hb * (T0[1] * T1[2] + T1[1] * T0[2]) + gc * T1[1] * T1[2];
-        G3[5] += ga * T0[2] * T0[2] + 2.0 * hb * T0[2] * T1[2] + gc * T1[2] * T1[2];
-        // dL/dT = 2 Gs T Sigma -> Jacobian entries -> camera-space mean
-        double dT0[3], dT1[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            dT0[k] = 2.0 * (ga * TC0[k] + hb * TC1[k]);
-            dT1[k] = 2.0 * (hb * TC0[k] + gc * TC1[k]);
-        }
-        const double gj00 = dT0[0] * R[0] + dT0[1] * R[1] + dT0[2] * R[2];
-        const double gj02 = dT0[0] * R[6] + dT0[1] * R[7] + dT0[2] * R[8];
-        const double gj11 = dT1[0] * R[3] + dT1[1] * R[4] + dT1[2] * R[5];
-        const double gj12 = dT1[0] * R[6] + dT1[1] * R[7] + dT1[2] * R[8];
-        const double gx = gmx * fx * iz - gj02 * fx * iz2;
-        const double gy = gmy * fy * iz - gj12 * fy * iz2;
-        const double gz = -(gmx * fx * x + gmy * fy * y + gj00 * fx + gj11 * fy) * iz2 +
-                          2.0 * (gj02 * fx * x + gj12 * fy * y) * iz2 * iz;
-        gm[0] += R[0] * gx + R[3] * gy + R[6] * gz;
-        gm[1] += R[1] * gx + R[4] * gy + R[7] * gz;
-        gm[2] += R[2] * gx + R[5] * gy + R[8] * gz;
-        gop += gb4.y;
-        // SH colour backward (colour = max(raw, 0)) and the view-direction term.
-        const double d0 = m0 - (double)cam.cc[0], d1 = m1 - (double)cam.cc[1], d2 = m2 - (double)cam.cc[2];
-        const double idn = 1.0 / sqrt(d0 * d0 + d1 * d1 + d2 * d2);
-        const float dx = (float)(d0 * idn), dy = (float)(d1 * idn), dz = (float)(d2 * idn);
-        float basis[16], db[16][3];
-        sh_basis_and_grad(DEG, dx, dy, dz, basis, db);
-        const float gcol_in[3] = {gb4.z, gb4.w, gbl};
-        float gcol[3];
-#pragma unroll
-        for (int ch = 0; ch < 3; ++ch) {
-            float raw = 0.5f;
-#pragma unroll
-            for (int k = 0; k < K; ++k) raw += basis[k] * shg[3 * k + ch];
-            gcol[ch] = (raw >= 0.0f) ? gcol_in[ch] : 0.0f;
-        }
-        float gdir[3] = {0.f, 0.f, 0.f};
-#pragma unroll
-        for (int k = 0; k < K; ++k) {
-            const float s0 = shg[3 * k], s1 = shg[3 * k + 1], s2 = shg[3 * k + 2];
-            gsh[3 * k] += basis[k] * gcol[0];
-            gsh[3 * k + 1] += basis[k] * gcol[1];
-            gsh[3 * k + 2] += basis[k] * gcol[2];
-            const float gbk = s0 * gcol[0] + s1 * gcol[1] + s2 * gcol[2];
-            gdir[0] += db[k][0] * gbk;
-            gdir[1] += db[k][1] * gbk;
-            gdir[2] += db[k][2] * gbk;
-        }
-        if (K > 1) {
-            const double pd = (double)dx * gdir[0] + (double)dy * gdir[1] + (double)dz * gdir[2];
-            gm[0] += ((double)gdir[0] - dx * pd) * idn;
-            gm[1] += ((double)gdir[1] - dy * pd) * idn;
-            gm[2] += ((double)gdir[2] - dz * pd) * idn;
-        }
+    constexpr int ROW = 3 * K;
+    extern __shared__ float s_param[];
+    float* s_sh = s_param;                          // [ROW][kParamStride]
+    float* s_gsh = s_param + ROW * kParamStride;    // [ROW][kParamStride]
+    const int tid = threadIdx.x;
+    const int64_t g0 = (int64_t)blockIdx.x * kParamThreads;
+    const int rows = (int)min((int64_t)kParamThreads, n - g0);
+    for (int i = tid; i < rows * ROW; i += kParamThreads) {
+        const int t = i / ROW, c = i - t * ROW;
+        s_sh[c * kParamStride + t] = P.sh[g0 * ROW + i];
     }
-    // cov3d = M M^T: dM = 2 G3 M, M = Rq diag(s).
-    const double Gf[3][3] = {{G3[0], G3[1], G3[2]}, {G3[1], G3[3], G3[4]}, {G3[2], G3[4], G3[5]}};
-    double dM[9];
+    for (int c = 0; c < ROW; ++c) s_gsh[c * kParamStride + tid] = 0.0f;
+    __syncthreads();
+    const int64_t g = g0 + tid;
+    if (g < n) {
+        const uint64_t mask = touch[g];
+        double gm[3] = {0.0, 0.0, 0.0};
+        double G3[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // 00 01 02 11 12 22
+        float gop = 0.0f;
+        const double m0 = P.means[3 * g], m1 = P.means[3 * g + 1], m2 = P.means[3 * g + 2];
+        const float4 q = reinterpret_cast<const float4*>(P.q)[g];
+        const double qinv = 1.0 / sqrt((double)q.x * q.x + (double)q.y * q.y + (double)q.z * q.z +
+                                       (double)q.w * q.w);
+        const double qw = q.x * qinv, qx = q.y * qinv, qy = q.z * qinv, qz = q.w * qinv;
+        double Rq[9];
+        Rq[0] = 1.0 - 2.0 * (qy * qy + qz * qz);
+        Rq[1] = 2.0 * (qx * qy - qw * qz);
+        Rq[2] = 2.0 * (qx * qz + qw * qy);
+        Rq[3] = 2.0 * (qx * qy + qw * qz);
+        Rq[4] = 1.0 - 2.0 * (qx * qx + qz * qz);
+        Rq[5] = 2.0 * (qy * qz - qw * qx);
+        Rq[6] = 2.0 * (qx * qz - qw * qy);
+        Rq[7] = 2.0 * (qy * qz + qw * qx);
+        Rq[8] = 1.0 - 2.0 * (qx * qx + qy * qy);
+        const double s[3] = {exp((double)P.ls[3 * g]), exp((double)P.ls[3 * g + 1]),
+                             exp((double)P.ls[3 * g + 2])};
+        double M[9];
 #pragma unroll
-    for (int i = 0; i < 3; ++i)
+        for (int i = 0; i < 3; ++i)
 #pragma unroll
-        for (int j = 0; j < 3; ++j)
-            dM[3 * i + j] = 2.0 * (Gf[i][0] * M[j] + Gf[i][1] * M[3 + j] + Gf[i][2] * M[6 + j]);
-    double gls[3];
+            for (int j = 0; j < 3; ++j) M[3 * i + j] = Rq[3 * i + j] * s[j];
+        double S[6];  // 00 01 02 11 12 22
+        S[0] = M[0] * M[0] + M[1] * M[1] + M[2] * M[2];
+        S[1] = M[0] * M[3] + M[1] * M[4] + M[2] * M[5];
+        S[2] = M[0] * M[6] + M[1] * M[7] + M[2] * M[8];
+        S[3] = M[3] * M[3] + M[4] * M[4] + M[5] * M[5];
+        S[4] = M[3] * M[6] + M[4] * M[7] + M[5] * M[8];
+        S[5] = M[6] * M[6] + M[7] * M[7] + M[8] * M[8];
+        for (int v = 0; v < n_views; ++v) {
+            if (!((mask >> v) & 1ull)) continue;
+            const float* gr = grad2d + ((size_t)v * n + g) * kGradStride;
+            const float4 ga4 = reinterpret_cast<const float4*>(gr)[0];
+            const float4 gb4 = reinterpret_cast<const float4*>(gr)[1];
+            const float gbl = gr[8];
+            if (ga4.x == 0.f && ga4.y == 0.f && ga4.z == 0.f && ga4.w == 0.f && gb4.x == 0.f &&
+                gb4.y == 0.f && gb4.z == 0.f && gb4.w == 0.f && gbl == 0.f)
+                continue;
+            const double gmx = ga4.x, gmy = ga4.y, gA = ga4.z, gB = ga4.w, gC = gb4.x;
+            const TCam& cam = cams[v];
+            double R[9];
 #pragma unroll
-    for (int j = 0; j < 3; ++j) gls[j] = (dM[j] * Rq[j] + dM[3 + j] * Rq[3 + j] + dM[6 + j] * Rq[6 + j]) * s[j];
-    double gR[9];
+            for (int k = 0; k < 9; ++k) R[k] = cam.R[k];
+            const double x = R[0] * m0 + R[1] * m1 + R[2] * m2 + (double)cam.t[0];
+            const double y = R[3] * m0 + R[4] * m1 + R[5] * m2 + (double)cam.t[1];
+            const double z = R[6] * m0 + R[7] * m1 + R[8] * m2 + (double)cam.t[2];
+            if (!(z > (double)cfg.near_plane)) continue;
+            const double fx = cam.fx, fy = cam.fy;
+            const double iz = 1.0 / z, iz2 = iz * iz;
+            const double j00 = fx * iz, j02 = -fx * x * iz2;
+            const double j11 = fy * iz, j12 = -fy * y * iz2;
+            double T0[3], T1[3];
 #pragma unroll
-    for (int i = 0; i < 3; ++i)
+            for (int k = 0; k < 3; ++k) {
+                T0[k] = j00 * R[k] + j02 * R[6 + k];
+                T1[k] = j11 * R[3 + k] + j12 * R[6 + k];
+            }
+            double TC0[3], TC1[3];
+            TC0[0] = T0[0] * S[0] + T0[1] * S[1] + T0[2] * S[2];
+            TC0[1] = T0[0] * S[1] + T0[1] * S[3] + T0[2] * S[4];
+            TC0[2] = T0[0] * S[2] + T0[1] * S[4] + T0[2] * S[5];
+            TC1[0] = T1[0] * S[0] + T1[1] * S[1] + T1[2] * S[2];
+            TC1[1] = T1[0] * S[1] + T1[1] * S[3] + T1[2] * S[4];
+            TC1[2] = T1[0] * S[2] + T1[1] * S[4] + T1[2] * S[5];
+            const double lp = cfg.lowpass;
+            const double a = T0[0] * TC0[0] + T0[1] * TC0[1] + T0[2] * TC0[2] + lp;
+            const double b = T1[0] * TC0[0] + T1[1] * TC0[1] + T1[2] * TC0[2];
+            const double c = T1[0] * TC1[0] + T1[1] * TC1[1] + T1[2] * TC1[2] + lp;
+            const double idet = 1.0 / (a * c - b * b);
+            const double A = c * idet, B = -b * idet, C = a * idet;
+            // conic -> 2D covariance
+            const double ga = -(A * A * gA + A * B * gB + B * B * gC);
+            const double gc = -(B * B * gA + B * C * gB + C * C * gC);
+            const double hb = -0.5 * (2.0 * A * B * gA + (A * C + B * B) * gB + 2.0 * B * C * gC);
+            // dL/dcov3d += T^T Gs T
+            G3[0] += ga * T0[0] * T0[0] + 2.0 * hb * T0[0] * T1[0] + gc * T1[0] * T1[0];
+            G3[1] += ga * T0[0] * T0[1] + hb * (T0[0] * T1[1] + T1[0] * T0[1]) + gc * T1[0] * T1[1];
+            G3[2] += ga * T0[0] * T0[2] + hb * (T0[0] * T1[2] + T1[0] * T0[2]) + gc * T1[0] * T1[2];
+            G3[3] += ga * T0[1] * T0[1] + 2.0 * hb * T0[1] * T1[1] + gc * T1[1] * T1[1];
+            G3[4] += ga * T0[1] * T0[2] + hb * (T0[1] * T1[2] + T1[1] * T0[2]) + gc * T1[1] * T1[2];
+            G3[5] += ga * T0[2] * T0[2] + 2.0 * hb * T0[2] * T1[2] + gc * T1[2] * T1[2];
+            // dL/dT = 2 Gs T Sigma -> Jacobian entries -> camera-space mean
+            double dT0[3], dT1[3];
 #pragma unroll
-        for (int j = 0; j < 3; ++j) gR[3 * i + j] = dM[3 * i + j] * s[j];
-    const double g00 = gR[0], g01 = gR[1], g02 = gR[2], g10 = gR[3], g11 = gR[4], g12 = gR[5];
-    const double g20 = gR[6], g21 = gR[7], g22 = gR[8];
-    const double gqn0 = 2.0 * (-qz * g01 + qy * g02 + qz * g10 - qx * g12 - qy * g20 + qx * g21);
-    const double gqn1 = 2.0 * (qy * g01 + qz * g02 + qy * g10 - 2.0 * qx * g11 - qw * g12 + qz * g20 +
-                               qw * g21 - 2.0 * qx * g22);
-    const double gqn2 = 2.0 * (-2.0 * qy * g00 + qx * g01 + qw * g02 + qx * g10 + qz * g12 - qw * g20 +
-                               qz * g21 - 2.0 * qy * g22);
-    const double gqn3 = 2.0 * (-2.0 * qz * g00 - qw * g01 + qx * g02 + qw * g10 - 2.0 * qz * g11 +
-                               qy * g12 + qx * g20 + qy * g21);
-    const double dot = qw * gqn0 + qx * gqn1 + qy * gqn2 + qz * gqn3;
-    const float op = 1.0f / (1.0f + __expf(-P.ol[g]));
-    G.means[3 * g] = (float)gm[0];
-    G.means[3 * g + 1] = (float)gm[1];
-    G.means[3 * g + 2] = (float)gm[2];
-    G.ls[3 * g] = (float)gls[0];
-    G.ls[3 * g + 1] = (float)gls[1];
-    G.ls[3 * g + 2] = (float)gls[2];
-    reinterpret_cast<float4*>(G.q)[g] =
-        make_float4((float)((gqn0 - qw * dot) * qinv), (float)((gqn1 - qx * dot) * qinv),
-                    (float)((gqn2 - qy * dot) * qinv), (float)((gqn3 - qz * dot) * qinv));
-    G.ol[g] = gop * op * (1.0f - op);
-    float* gshg = G.sh + (size_t)g * K * 3;
+            for (int k = 0; k < 3; ++k) {
+                dT0[k] = 2.0 * (ga * TC0[k] + hb * TC1[k]);
+                dT1[k] = 2.0 * (hb * TC0[k] + gc * TC1[k]);
+            }
+            const double gj00 = dT0[0] * R[0] + dT0[1] * R[1] + dT0[2] * R[2];
+            const double gj02 = dT0[0] * R[6] + dT0[1] * R[7] + dT0[2] * R[8];
+            const double gj11 = dT1[0] * R[3] + dT1[1] * R[4] + dT1[2] * R[5];
+            const double gj12 = dT1[0] * R[6] + dT1[1] * R[7] + dT1[2] * R[8];
+            const double gx = gmx * fx * iz - gj02 * fx * iz2;
+            const double gy = gmy * fy * iz - gj12 * fy * iz2;
+            const double gz = -(gmx * fx * x + gmy * fy * y + gj00 * fx + gj11 * fy) * iz2 +
+                              2.0 * (gj02 * fx * x + gj12 * fy * y) * iz2 * iz;
+            gm[0] += R[0] * gx + R[3] * gy + R[6] * gz;
+            gm[1] += R[1] * gx + R[4] * gy + R[7] * gz;
+            gm[2] += R[2] * gx + R[5] * gy + R[8] * gz;
+            gop += gb4.y;
+            // SH colour backward (colour = max(raw, 0)) and the view-direction term.
+            const double d0 = m0 - (double)cam.cc[0], d1 = m1 - (double)cam.cc[1], d2 = m2 - (double)cam.cc[2];
+            const double idn = 1.0 / sqrt(d0 * d0 + d1 * d1 + d2 * d2);
+            const float dx = (float)(d0 * idn), dy = (float)(d1 * idn), dz = (float)(d2 * idn);
+            float basis[16];
+            sh_basis(DEG, dx, dy, dz, basis);
+            const float gcol_in[3] = {gb4.z, gb4.w, gbl};
+            float gcol[3];
 #pragma unroll
-    for (int k = 0; k < 3 * K; ++k) gshg[k] = gsh[k];
+            for (int ch = 0; ch < 3; ++ch) {
+                float raw = 0.5f;
+#pragma unroll
+                for (int k = 0; k < K; ++k) raw += basis[k] * s_sh[(3 * k + ch) * kParamStride + tid];
+                gcol[ch] = (raw >= 0.0f) ? gcol_in[ch] : 0.0f;
+            }
+            float gbk[16];
+#pragma unroll
+            for (int k = 0; k < K; ++k) {
+                float* acc = s_gsh + 3 * k * kParamStride + tid;
+                acc[0] += basis[k] * gcol[0];
+                acc[kParamStride] += basis[k] * gcol[1];
+                acc[2 * kParamStride] += basis[k] * gcol[2];
+                const float* sk = s_sh + 3 * k * kParamStride + tid;
+                gbk[k] = sk[0] * gcol[0] + sk[kParamStride] * gcol[1] + sk[2 * kParamStride] * gcol[2];
+            }
+            if (K > 1) {
+                float gdir[3];
+                sh_dir_grad(DEG, dx, dy, dz, gbk, gdir);
+                const double pd = (double)dx * gdir[0] + (double)dy * gdir[1] + (double)dz * gdir[2];
+                gm[0] += ((double)gdir[0] - dx * pd) * idn;
+                gm[1] += ((double)gdir[1] - dy * pd) * idn;
+                gm[2] += ((double)gdir[2] - dz * pd) * idn;
+            }
+        }
+        // cov3d = M M^T: dM = 2 G3 M, M = Rq diag(s).
+        const double Gf[3][3] = {{G3[0], G3[1], G3[2]}, {G3[1], G3[3], G3[4]}, {G3[2], G3[4], G3[5]}};
+        double dM[9];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j)
+                dM[3 * i + j] = 2.0 * (Gf[i][0] * M[j] + Gf[i][1] * M[3 + j] + Gf[i][2] * M[6 + j]);
+        double gls[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) gls[j] = (dM[j] * Rq[j] + dM[3 + j] * Rq[3 + j] + dM[6 + j] * Rq[6 + j]) * s[j];
+        double gR[9];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) gR[3 * i + j] = dM[3 * i + j] * s[j];
+        const double g00 = gR[0], g01 = gR[1], g02 = gR[2], g10 = gR[3], g11 = gR[4], g12 = gR[5];
+        const double g20 = gR[6], g21 = gR[7], g22 = gR[8];
+        const double gqn0 = 2.0 * (-qz * g01 + qy * g02 + qz * g10 - qx * g12 - qy * g20 + qx * g21);
+        const double gqn1 = 2.0 * (qy * g01 + qz * g02 + qy * g10 - 2.0 * qx * g11 - qw * g12 + qz * g20 +
+                                   qw * g21 - 2.0 * qx * g22);
+        const double gqn2 = 2.0 * (-2.0 * qy * g00 + qx * g01 + qw * g02 + qx * g10 + qz * g12 - qw * g20 +
+                                   qz * g21 - 2.0 * qy * g22);
+        const double gqn3 = 2.0 * (-2.0 * qz * g00 - qw * g01 + qx * g02 + qw * g10 - 2.0 * qz * g11 +
+                                   qy * g12 + qx * g20 + qy * g21);
+        const double dot = qw * gqn0 + qx * gqn1 + qy * gqn2 + qz * gqn3;
+        const float op = 1.0f / (1.0f + __expf(-P.ol[g]));
+        G.means[3 * g] = (float)gm[0];
+        G.means[3 * g + 1] = (float)gm[1];
+        G.means[3 * g + 2] = (float)gm[2];
+        G.ls[3 * g] = (float)gls[0];
+        G.ls[3 * g + 1] = (float)gls[1];
+        G.ls[3 * g + 2] = (float)gls[2];
+        reinterpret_cast<float4*>(G.q)[g] =
+            make_float4((float)((gqn0 - qw * dot) * qinv), (float)((gqn1 - qx * dot) * qinv),
+                        (float)((gqn2 - qy * dot) * qinv), (float)((gqn3 - qz * dot) * qinv));
+        G.ol[g] = gop * op * (1.0f - op);
+    }
+    __syncthreads();
+    for (int i = tid; i < rows * ROW; i += kParamThreads) {
+        const int t = i / ROW, c = i - t * ROW;
+        G.sh[g0 * ROW + i] = s_gsh[c * kParamStride + t];
+    }
 }
 
 // View v's 2D gradient rows in the reference's (N, 9) layout (zero where untouched).
@@ -945,23 +1067,68 @@ __device__ __forceinline__ float bf16_round(float x) {
     return __uint_as_float(u);
 }
 
-__global__ void k_sparse_adam(AdamParams A, const float* __restrict__ vis,
-                              const unsigned int* __restrict__ err, int group) {
+// One Adam update of element e (column col of its row) when its row is visible.
+__device__ __forceinline__ void adam_update(const AdamParams& A, const AdamGroup& G, int col,
+                                            float g, float& p, float& m, float& v) {
+    const float m1 = A.b1 * m + (1.0f - A.b1) * g;
+    const float v1 = A.b2 * v + (1.0f - A.b2) * g * g;
+    const float den = sqrtf(v1) * A.isq_bc2 + A.eps;
+    const float ss = (G.sh_band_split && col >= 3) ? G.step_size_rest : G.step_size;
+    p = p - ss * (m1 / den);
+    m = A.bf16 ? bf16_round(m1) : m1;
+    v = A.bf16 ? bf16_round(v1) : v1;
+}
+
+// Rows with a visibility count > 0 (gsplat/t2_param_backward.py:195-223), W elements per row
+// (a compile-time width turns the row / column split into a multiply-shift). With VEC, four
+// consecutive elements per thread through 16-byte loads and stores (the group's arrays are
+// 16-byte aligned); the count's remainder modulo 4 is done element by element.
+template <int W, bool VEC>
+__global__ void __launch_bounds__(256)
+k_sparse_adam(AdamParams A, const float* __restrict__ vis, const unsigned int* __restrict__ err,
+              int group) {
     if (err != nullptr && *err != 0u) return;
     const AdamGroup& G = A.grp[group];
-    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < G.count;
-         e += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t row = e / G.width;
+    const uint32_t count = (uint32_t)G.count;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    const uint32_t t0 = blockIdx.x * blockDim.x + threadIdx.x;
+    uint32_t done = 0;
+    if (VEC) {
+        const uint32_t n4 = count / 4u;
+        for (uint32_t i = t0; i < n4; i += stride) {
+            const uint32_t e = 4u * i;
+            const uint32_t r0 = e / W, r3 = (e + 3u) / W;
+            bool any = false;
+            for (uint32_t r = r0; r <= r3; ++r) any |= vis[r] > 0.0f;
+            if (!any) continue;
+            const float4 g4 = reinterpret_cast<const float4*>(G.g)[i];
+            float4 p4 = reinterpret_cast<const float4*>(G.p)[i];
+            float4 m4 = reinterpret_cast<const float4*>(G.m)[i];
+            float4 v4 = reinterpret_cast<const float4*>(G.v)[i];
+            float* pp = &p4.x;
+            float* mm = &m4.x;
+            float* vv = &v4.x;
+            const float* gg = &g4.x;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t ek = e + (uint32_t)k;
+                const uint32_t row = ek / W;
+                if (vis[row] > 0.0f) adam_update(A, G, (int)(ek - row * W), gg[k], pp[k], mm[k], vv[k]);
+            }
+            reinterpret_cast<float4*>(G.p)[i] = p4;
+            reinterpret_cast<float4*>(G.m)[i] = m4;
+            reinterpret_cast<float4*>(G.v)[i] = v4;
+        }
+        done = n4 * 4u;
+    }
+    for (uint32_t e = done + t0; e < count; e += stride) {
+        const uint32_t row = e / W;
         if (!(vis[row] > 0.0f)) continue;
-        const float g = G.g[e];
-        const float m1 = A.b1 * G.m[e] + (1.0f - A.b1) * g;
-        const float v1 = A.b2 * G.v[e] + (1.0f - A.b2) * g * g;
-        const float den = sqrtf(v1) * A.isq_bc2 + A.eps;
-        float ss = G.step_size;
-        if (G.sh_band_split && (e % G.width) >= 3) ss = G.step_size_rest;
-        G.p[e] = G.p[e] - ss * (m1 / den);
-        G.m[e] = A.bf16 ? bf16_round(m1) : m1;
-        G.v[e] = A.bf16 ? bf16_round(v1) : v1;
+        float p = G.p[e], m = G.m[e], v = G.v[e];
+        adam_update(A, G, (int)(e - row * W), G.g[e], p, m, v);
+        G.p[e] = p;
+        G.m[e] = m;
+        G.v[e] = v;
     }
 }
 
@@ -1293,9 +1460,25 @@ static gs_status launch_adam(const AdamParams& A, const float* vis, const unsign
                              cudaStream_t st) {
     KernelTimer kt("sparse_adam", st);
     for (int i = 0; i < 5; ++i) {
-        const int64_t cnt = A.grp[i].count;
-        const unsigned int blocks = (unsigned int)std::min<int64_t>(div_up(cnt, 256), kNumSMs * 16);
-        k_sparse_adam<<<blocks, 256, 0, st>>>(A, vis, err, i);
+        const AdamGroup& G = A.grp[i];
+        const int64_t cnt = G.count;
+        GS_ARG_CHECK(cnt < (1ll << 32), "sparse Adam: a parameter group exceeds 2^32 elements");
+        const bool vec = (((uintptr_t)G.p | (uintptr_t)G.m | (uintptr_t)G.v | (uintptr_t)G.g) & 15u) == 0;
+        const unsigned int blocks =
+            (unsigned int)std::min<int64_t>(div_up(vec ? div_up(cnt, 4) : cnt, 256), kNumSMs * 16);
+#define GS_ADAM(W_)                                                                             \
+    (vec ? k_sparse_adam<W_, true><<<blocks, 256, 0, st>>>(A, vis, err, i)                     \
+         : k_sparse_adam<W_, false><<<blocks, 256, 0, st>>>(A, vis, err, i))
+        switch (G.width) {
+            case 1: GS_ADAM(1); break;
+            case 3: GS_ADAM(3); break;
+            case 4: GS_ADAM(4); break;
+            case 12: GS_ADAM(12); break;
+            case 27: GS_ADAM(27); break;
+            case 48: GS_ADAM(48); break;
+            default: set_error("sparse Adam: unsupported row width %d", G.width); return GS_ERR_ARG;
+        }
+#undef GS_ADAM
         GS_CHECK_LAUNCH();
     }
     return GS_OK;
@@ -1448,12 +1631,17 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
         KernelTimer kt("param_bwd", st);
         TCfg c = make_tcfg(*cfg, H, W);
         GMut G{grads->means, grads->log_scales, grads->quats, grads->opacity_logits, grads->sh};
-        const unsigned int nb = div_up(n, 128);
+        const unsigned int nb = div_up(n, kParamThreads);
+        const int K = (cfg->sh_degree + 1) * (cfg->sh_degree + 1);
+        const size_t smem = 2 * (size_t)3 * K * kParamStride * sizeof(float);
         switch (cfg->sh_degree) {
-            case 0: k_param_bwd<0><<<nb, 128, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
-            case 1: k_param_bwd<1><<<nb, 128, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
-            case 2: k_param_bwd<2><<<nb, 128, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
-            default: k_param_bwd<3><<<nb, 128, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            case 0: k_param_bwd<0><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            case 1: k_param_bwd<1><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            case 2: k_param_bwd<2><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            default:
+                GS_CUDA_CHECK(cudaFuncSetAttribute(k_param_bwd<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+                k_param_bwd<3><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G);
+                break;
         }
         GS_CHECK_LAUNCH();
     }

@@ -29,10 +29,11 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
     constexpr int K = (DEG + 1) * (DEG + 1);
     constexpr int ROW = 3 * K;  // floats of SH per Gaussian
     extern __shared__ __align__(16) float s_sh[];
-    __shared__ int64_t smem[33];
+    __shared__ unsigned long long s_tot[kMaxViews];  // the block's pairs per view
     __shared__ TCam s_cam[kMaxViews];
     for (int i = threadIdx.x; i < n_views * (int)(sizeof(TCam) / 4); i += blockDim.x)
         reinterpret_cast<uint32_t*>(s_cam)[i] = reinterpret_cast<const uint32_t*>(cams)[i];
+    for (int i = threadIdx.x; i < n_views; i += blockDim.x) s_tot[i] = 0ull;
     const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     {
         const int64_t g0 = (int64_t)blockIdx.x * blockDim.x;
@@ -218,14 +219,18 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
                 }
             }
         }
-        int64_t total;
-        block_exclusive_scan<int64_t>((int64_t)count, smem, &total);
-        if (threadIdx.x == 0) blk[v * blk_stride + blockIdx.x] = total;
+        uint32_t wsum = count;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) wsum += __shfl_xor_sync(0xffffffffu, wsum, o);
+        if ((threadIdx.x & 31) == 0 && wsum != 0u) atomicAdd(&s_tot[v], (unsigned long long)wsum);
     }
     if (live) {
         if (touch != nullptr) touch[g] = touched;
         if (vis_counts != nullptr && nvis > 0.0f) vis_counts[g] += nvis;
     }
+    __syncthreads();
+    for (int v = threadIdx.x; v < n_views; v += blockDim.x)
+        blk[v * blk_stride + blockIdx.x] = (int64_t)s_tot[v];
 }
 
 // Pair counts of the Gaussians in depth order (`order` = Gaussian ids sorted by depth
