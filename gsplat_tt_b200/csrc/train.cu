@@ -2,6 +2,7 @@
 // the gs_train_step orchestration (one stream, no host synchronisation inside a step).
 #include <cmath>
 #include <cstring>
+#include <mutex>
 #include <vector>
 
 #include "radix_sort.cuh"
@@ -1134,15 +1135,15 @@ k_sparse_adam(AdamParams A, const float* __restrict__ vis, const unsigned int* _
 
 // ------------------------------------------------------------------ workspace layout
 
-struct TrainWs {
-    unsigned int* err;
-    uint64_t* touch;
-    TCam* cams;
-    float* grad2d;
-    int64_t* blk;      // per-view block pair totals, view v at v * blk_stride
-    int64_t blk_stride;
-    int64_t* pairs;
-    ProjView pv;       // every view's projected records, [view][n]
+// Per-view scratch. A step's views are spread over kLanes lanes, each with its own stream
+// (the caller's stream for lane 0) and its own copy of these buffers, so one view's
+// rasterisers run while the next view sorts.
+#ifndef GS_TRAIN_LANES
+#define GS_TRAIN_LANES 2
+#endif
+constexpr int kLanes = GS_TRAIN_LANES;
+
+struct ViewLane {
     int64_t* blk2;
     uint32_t* order;   // Gaussian ids sorted by depth
     uint32_t* goff;    // first pair of each depth-ordered Gaussian (n + 1)
@@ -1163,7 +1164,20 @@ struct TrainWs {
     float* dmu;
     float* dxx;
     float* dxy;
+};
+
+struct TrainWs {
+    unsigned int* err;
+    uint64_t* touch;
+    TCam* cams;
+    float* grad2d;
+    int64_t* blk;      // per-view block pair totals, view v at v * blk_stride
+    int64_t blk_stride;
+    int64_t* pairs;
+    ProjView pv;       // every view's projected records, [view][n]
     double* loss_acc;
+    int nlanes;
+    ViewLane lane[kLanes];
 };
 
 template <typename WS>
@@ -1188,27 +1202,31 @@ static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int 
     L.pv.dsort = ws.template take<uint32_t>(nv);
     L.pv.rect = ws.template take<ushort4>(nv);
     L.pv.cnt = ws.template take<uint32_t>(nv);
-    L.blk2 = ws.template take<int64_t>(nb);
-    L.order = ws.template take<uint32_t>(n);
-    L.goff = ws.template take<uint32_t>(n + 1);
-    L.rect_d = ws.template take<ushort4>(n);
-    L.tfirst_len = div_up(cap, kTileItems) + 1;
-    L.tfirst = ws.template take<uint32_t>(L.tfirst_len);
-    L.tlast = ws.template take<uint32_t>(1);
-    L.tdiff = ws.template take<int>((size_t)(W / tile + 2) * (H / tile + 1));
-    L.tdig = ws.template take<uint32_t>(4 * 256);
-    L.svals = ws.template take<uint32_t>(cap);
-    // one scratch region serves the depth sort (N, 32 bits) and the tile sort (P, tile bits)
-    L.radix_bytes = std::max(radix_workspace_bytes(n, 32, 4), radix_workspace_bytes(cap, tile_bits, 4));
-    L.radix = ws.template take<char>(L.radix_bytes);
-    L.ranges = ws.template take<int2>(tiles);
-    L.image = ws.template take<float>(px * 3);
-    L.final_T = ws.template take<float>(px);
-    L.ncon = ws.template take<int32_t>(px);
-    L.dimg = ws.template take<float>(px * 3);
-    L.dmu = ws.template take<float>(px * 3);
-    L.dxx = ws.template take<float>(px * 3);
-    L.dxy = ws.template take<float>(px * 3);
+    L.nlanes = std::min(kLanes, n_views);
+    for (int l = 0; l < L.nlanes; ++l) {
+        ViewLane& V = L.lane[l];
+        V.blk2 = ws.template take<int64_t>(nb);
+        V.order = ws.template take<uint32_t>(n);
+        V.goff = ws.template take<uint32_t>(n + 1);
+        V.rect_d = ws.template take<ushort4>(n);
+        V.tfirst_len = div_up(cap, kTileItems) + 1;
+        V.tfirst = ws.template take<uint32_t>(V.tfirst_len);
+        V.tlast = ws.template take<uint32_t>(1);
+        V.tdiff = ws.template take<int>((size_t)(W / tile + 2) * (H / tile + 1));
+        V.tdig = ws.template take<uint32_t>(4 * 256);
+        V.svals = ws.template take<uint32_t>(cap);
+        // one scratch region serves the depth sort (N, 32 bits) and the tile sort (P, tile bits)
+        V.radix_bytes = std::max(radix_workspace_bytes(n, 32, 4), radix_workspace_bytes(cap, tile_bits, 4));
+        V.radix = ws.template take<char>(V.radix_bytes);
+        V.ranges = ws.template take<int2>(tiles);
+        V.image = ws.template take<float>(px * 3);
+        V.final_T = ws.template take<float>(px);
+        V.ncon = ws.template take<int32_t>(px);
+        V.dimg = ws.template take<float>(px * 3);
+        V.dmu = ws.template take<float>(px * 3);
+        V.dxx = ws.template take<float>(px * 3);
+        V.dxy = ws.template take<float>(px * 3);
+    }
     L.loss_acc = ws.template take<double>(2 * (size_t)n_views);
 }
 
@@ -1220,6 +1238,35 @@ struct SizerAdapter {
         return nullptr;
     }
 };
+
+// Auxiliary streams of lanes 1.. (non-blocking, created once per device) and the events
+// that fork them from and join them to the caller's stream.
+struct LaneStreams {
+    cudaStream_t s[kLanes];
+    cudaEvent_t fork;
+    cudaEvent_t join[kLanes];
+};
+
+static gs_status lane_streams(LaneStreams** out) {
+    static std::mutex mu;
+    static LaneStreams* per_dev[64] = {};
+    int dev = 0;
+    GS_CUDA_CHECK(cudaGetDevice(&dev));
+    GS_ARG_CHECK(dev >= 0 && dev < 64, "train: device index %d out of range", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (per_dev[dev] == nullptr) {
+        LaneStreams* ls = new LaneStreams();
+        ls->s[0] = nullptr;
+        for (int l = 1; l < kLanes; ++l)
+            GS_CUDA_CHECK(cudaStreamCreateWithFlags(&ls->s[l], cudaStreamNonBlocking));
+        GS_CUDA_CHECK(cudaEventCreateWithFlags(&ls->fork, cudaEventDisableTiming));
+        for (int l = 0; l < kLanes; ++l)
+            GS_CUDA_CHECK(cudaEventCreateWithFlags(&ls->join[l], cudaEventDisableTiming));
+        per_dev[dev] = ls;
+    }
+    *out = per_dev[dev];
+    return GS_OK;
+}
 
 static gs_status check_cfg(const gs_train_config* cfg) {
     GS_ARG_CHECK(cfg != nullptr, "train: null config");
@@ -1272,39 +1319,100 @@ static gs_status project_views(const GConst& P, int64_t n, int n_views, const TC
 }
 
 // Depth order, pair offsets, tile counts / ranges and the tile sort of one projected view.
-static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, int64_t cap,
-                           cudaStream_t st) {
+static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, ViewLane& V,
+                           int64_t cap, cudaStream_t st) {
     const unsigned int nb = div_up(n, kProjThreads);
     const ProjView pv = L.pv.view(view, n);
     // Gaussians in (depth bits, id) order; those without pairs sort last.
     unsigned int* rerr = nullptr;
-    gs_status s = radix_sort_pairs32(pv.dsort, nullptr, nullptr, n, 32, nullptr, L.order, L.radix,
-                                     L.radix_bytes, st, &rerr, L.err);
+    gs_status s = radix_sort_pairs32(pv.dsort, nullptr, nullptr, n, 32, nullptr, V.order, V.radix,
+                                     V.radix_bytes, st, &rerr, L.err);
     if (s != GS_OK) return s;
-    launch_sorted_count(pv, L.order, n, L.blk2, st);
+    launch_sorted_count(pv, V.order, n, V.blk2, st);
     GS_CHECK_LAUNCH();
-    scan_block_totals<int64_t><<<1, 1024, 0, st>>>(L.blk2, nb, nullptr);
+    scan_block_totals<int64_t><<<1, 1024, 0, st>>>(V.blk2, nb, nullptr);
     GS_CHECK_LAUNCH();
     const int tiles = cfg.tiles_x * cfg.tiles_y;
     const int tile_bits = bits_for(tiles > 1 ? tiles - 1 : 1);
     const int npass = radix_num_passes(tile_bits);
     {
         KernelTimer kt("pair_offsets", st);
-        GS_CUDA_CHECK(cudaMemsetAsync(L.tlast, 0, sizeof(uint32_t), st));
-        launch_pair_offsets(pv, L.order, n, L.blk2, cap, L.goff, L.rect_d, L.tfirst, L.tfirst_len,
-                            L.tlast, L.err, st);
+        GS_CUDA_CHECK(cudaMemsetAsync(V.tlast, 0, sizeof(uint32_t), st));
+        launch_pair_offsets(pv, V.order, n, V.blk2, cap, V.goff, V.rect_d, V.tfirst, V.tfirst_len,
+                            V.tlast, L.err, st);
         GS_CHECK_LAUNCH();
     }
     {
         KernelTimer kt("tile_counts", st);
-        s = launch_tile_counts(pv, n, cfg.tiles_x, cfg.tiles_y, npass, L.pairs + view, cap, L.tdiff,
-                               L.ranges, L.tdig, st);
+        s = launch_tile_counts(pv, n, cfg.tiles_x, cfg.tiles_y, npass, L.pairs + view, cap, V.tdiff,
+                               V.ranges, V.tdig, st);
         if (s != GS_OK) return s;
     }
-    const RectPairSource src{L.order, L.goff, L.tfirst, L.tlast, L.rect_d, cfg.tiles_x};
-    s = radix_sort_rect_pairs(src, L.pairs + view, cap, tile_bits, L.tdig, L.svals, L.radix,
-                              L.radix_bytes, st, L.err);
+    const RectPairSource src{V.order, V.goff, V.tfirst, V.tlast, V.rect_d, cfg.tiles_x};
+    s = radix_sort_rect_pairs(src, L.pairs + view, cap, tile_bits, V.tdig, V.svals, V.radix,
+                              V.radix_bytes, st, L.err);
     if (s != GS_OK) return s;
+    return GS_OK;
+}
+
+// One view after the projection: sort, forward, loss, backward into the view's 2D-gradient
+// rows (and the optional exports), all on stream st with lane V's scratch.
+static gs_status run_view(int64_t n, int v, const gs_camera& cam, const gs_train_config& cfg,
+                          LossCfg LC, const float* target, float* images, float* grad2d_out,
+                          float* view_losses, TrainWs& L, ViewLane& V, int64_t cap,
+                          cudaStream_t st) {
+    const int vh = cam.height, vw = cam.width;
+    const TCfg c = make_tcfg(cfg, vh, vw);
+    gs_status s = sort_view(n, c, v, L, V, cap, st);
+    if (s != GS_OK) return s;
+    const ProjView pvv = L.pv.view(v, n);
+    float* img = images ? images + (size_t)v * vh * vw * 3 : V.image;
+    const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
+    {
+        KernelTimer kt("raster_fwd", st);
+        if (c.tile == 16)
+            k_train_fwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
+        else
+            k_train_fwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
+        GS_CHECK_LAUNCH();
+    }
+    LC.H = vh;
+    LC.W = vw;
+    LC.inv_n = (float)(1.0 / (3.0 * vh * vw));
+    {
+        KernelTimer kt("loss", st);
+        const int64_t n3 = (int64_t)vh * vw * 3;
+        if (cfg.use_ssim) {
+            dim3 grid(div_up(vw, kSsimT), div_up(vh, kSsimT));
+            k_ssim_fwd<<<grid, 256, sizeof(SsimFwdSmem), st>>>(img, target, LC, V.dmu, V.dxx,
+                                                               V.dxy, L.loss_acc + 2 * v);
+            GS_CHECK_LAUNCH();
+            k_ssim_bwd<<<grid, 256, sizeof(SsimBwdSmem), st>>>(img, target, V.dmu, V.dxx, V.dxy,
+                                                               LC, V.dimg);
+        } else {
+            k_loss_l1<<<(unsigned int)std::min<int64_t>(div_up(n3, 256), kNumSMs * 8), 256, 0, st>>>(
+                img, target, n3, LC, V.dimg, L.loss_acc + 2 * v);
+        }
+        GS_CHECK_LAUNCH();
+        k_loss_finalize<<<1, 1, 0, st>>>(L.loss_acc + 2 * v, LC, cfg.use_ssim, view_losses + v);
+        GS_CHECK_LAUNCH();
+    }
+    {
+        KernelTimer kt("raster_bwd", st);
+        float* g2 = L.grad2d + (size_t)v * n * kGradStride;
+        if (c.tile == 16)
+            k_train_bwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, V.dimg,
+                                                     V.final_T, V.ncon, g2);
+        else
+            k_train_bwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, V.dimg,
+                                                      V.final_T, V.ncon, g2);
+        GS_CHECK_LAUNCH();
+    }
+    if (grad2d_out) {
+        k_export_grad2d<<<div_up(n, 256), 256, 0, st>>>(L.grad2d, L.touch, n, v,
+                                                        grad2d_out + (size_t)v * n * 9);
+        GS_CHECK_LAUNCH();
+    }
     return GS_OK;
 }
 
@@ -1396,13 +1504,14 @@ extern "C" gs_status gs_train_project_view(const gs_gaussians* params, int64_t n
     GS_CUDA_CHECK(cudaMemcpyAsync(L.cams, &tc, sizeof(TCam), cudaMemcpyHostToDevice, st));
     gs_status s = project_views(gconst(params), n, 1, c, L, vis_counts, false, st);
     if (s != GS_OK) return s;
-    s = sort_view(n, c, 0, L, pair_capacity, st);
+    ViewLane& V = L.lane[0];
+    s = sort_view(n, c, 0, L, V, pair_capacity, st);
     if (s != GS_OK) return s;
     k_export_projection<<<div_up(n, 256), 256, 0, st>>>(L.pv, n, means2d, conic, opacity, colors,
                                                         depth, rects);
     GS_CHECK_LAUNCH();
     const int tiles = c.tiles_x * c.tiles_y;
-    GS_CUDA_CHECK(cudaMemcpyAsync(tile_ranges, L.ranges, tiles * sizeof(int2), cudaMemcpyDeviceToDevice, st));
+    GS_CUDA_CHECK(cudaMemcpyAsync(tile_ranges, V.ranges, tiles * sizeof(int2), cudaMemcpyDeviceToDevice, st));
     unsigned int herr = 0;
     GS_CUDA_CHECK(cudaMemcpyAsync(pairs_host, L.pairs, sizeof(int64_t), cudaMemcpyDeviceToHost, st));
     GS_CUDA_CHECK(cudaMemcpyAsync(&herr, L.err, sizeof(unsigned int), cudaMemcpyDeviceToHost, st));
@@ -1417,7 +1526,7 @@ extern "C" gs_status gs_train_project_view(const gs_gaussians* params, int64_t n
         return GS_ERR_TIMEOUT;
     }
     if (*pairs_host > 0)
-        GS_CUDA_CHECK(cudaMemcpyAsync(sorted_ids, L.svals, *pairs_host * sizeof(uint32_t),
+        GS_CUDA_CHECK(cudaMemcpyAsync(sorted_ids, V.svals, *pairs_host * sizeof(uint32_t),
                                       cudaMemcpyDeviceToDevice, st));
     return GS_OK;
 }
@@ -1569,60 +1678,33 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
         gs_status s = project_views(P, n, n_views, make_tcfg(*cfg, H, W), L, vis_counts, true, st);
         if (s != GS_OK) return s;
     }
-    for (int v = 0; v < n_views; ++v) {
-        const int vh = cams[v].height, vw = cams[v].width;
-        const TCfg c = make_tcfg(*cfg, vh, vw);
-        gs_status s = sort_view(n, c, v, L, pair_capacity, st);
-        if (s != GS_OK) return s;
-        const ProjView pvv = L.pv.view(v, n);
-        float* img = images ? images + (size_t)v * vh * vw * 3 : L.image;
-        const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
-        {
-            KernelTimer kt("raster_fwd", st);
-            if (c.tile == 16)
-                k_train_fwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(L.ranges, L.svals, pvv, c, vh, vw, img, L.final_T, L.ncon);
-            else
-                k_train_fwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(L.ranges, L.svals, pvv, c, vh, vw, img, L.final_T, L.ncon);
-            GS_CHECK_LAUNCH();
-        }
-        LC.H = vh;
-        LC.W = vw;
-        LC.inv_n = (float)(1.0 / (3.0 * vh * vw));
-        {
-            KernelTimer kt("loss", st);
-            const int64_t n3 = (int64_t)vh * vw * 3;
-            if (cfg->use_ssim) {
-                dim3 grid(div_up(vw, kSsimT), div_up(vh, kSsimT));
-                k_ssim_fwd<<<grid, 256, sizeof(SsimFwdSmem), st>>>(img, targets[v], LC, L.dmu, L.dxx,
-                                                                   L.dxy, L.loss_acc + 2 * v);
-                GS_CHECK_LAUNCH();
-                k_ssim_bwd<<<grid, 256, sizeof(SsimBwdSmem), st>>>(img, targets[v], L.dmu, L.dxx, L.dxy,
-                                                                   LC, L.dimg);
-            } else {
-                k_loss_l1<<<(unsigned int)std::min<int64_t>(div_up(n3, 256), kNumSMs * 8), 256, 0, st>>>(
-                    img, targets[v], n3, LC, L.dimg, L.loss_acc + 2 * v);
-            }
-            GS_CHECK_LAUNCH();
-            k_loss_finalize<<<1, 1, 0, st>>>(L.loss_acc + 2 * v, LC, cfg->use_ssim, view_losses + v);
-            GS_CHECK_LAUNCH();
-        }
-        {
-            KernelTimer kt("raster_bwd", st);
-            float* g2 = L.grad2d + (size_t)v * n * kGradStride;
-            if (c.tile == 16)
-                k_train_bwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(L.ranges, L.svals, pvv, c, vh, vw, L.dimg,
-                                                         L.final_T, L.ncon, g2);
-            else
-                k_train_bwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(L.ranges, L.svals, pvv, c, vh, vw, L.dimg,
-                                                          L.final_T, L.ncon, g2);
-            GS_CHECK_LAUNCH();
-        }
-        if (grad2d_out) {
-            k_export_grad2d<<<div_up(n, 256), 256, 0, st>>>(L.grad2d, L.touch, n, v,
-                                                            grad2d_out + (size_t)v * n * 9);
-            GS_CHECK_LAUNCH();
+    // Views round-robin over the lanes; lanes 1.. run on auxiliary streams forked from the
+    // caller's stream after the projection and joined back before the parameter backward.
+    LaneStreams* LS = nullptr;
+    cudaStream_t lst[kLanes] = {st};
+    if (L.nlanes > 1) {
+        gs_status ls = lane_streams(&LS);
+        if (ls != GS_OK) return ls;
+        GS_CUDA_CHECK(cudaEventRecord(LS->fork, st));
+        for (int l = 1; l < L.nlanes; ++l) {
+            lst[l] = LS->s[l];
+            GS_CUDA_CHECK(cudaStreamWaitEvent(lst[l], LS->fork, 0));
         }
     }
+    gs_status vs = GS_OK;
+    for (int v = 0; v < n_views && vs == GS_OK; ++v) {
+        ViewLane& V = L.lane[v % L.nlanes];
+        const cudaStream_t vst = lst[v % L.nlanes];
+        vs = run_view(n, v, cams[v], *cfg, LC, targets[v], images, grad2d_out, view_losses, L, V,
+                      pair_capacity, vst);
+    }
+    if (L.nlanes > 1) {  // join every lane, also after an error, before anything else runs on st
+        for (int l = 1; l < L.nlanes; ++l) {
+            GS_CUDA_CHECK(cudaEventRecord(LS->join[l], lst[l]));
+            GS_CUDA_CHECK(cudaStreamWaitEvent(st, LS->join[l], 0));
+        }
+    }
+    if (vs != GS_OK) return vs;
     if (pairs) {
         GS_CUDA_CHECK(cudaMemcpyAsync(pairs, L.pairs, n_views * sizeof(int64_t),
                                       cudaMemcpyDeviceToDevice, st));

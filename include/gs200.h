@@ -232,6 +232,10 @@ typedef struct gs_train_config {
  *   pair_capacity bounds the (Gaussian, tile) pairs of one view; if a view needs more,
  *   the step leaves params and moments untouched and gs_workspace_error() reports
  *   GS_ERR_OVERFLOW (grow the capacity with gs_train_count_pairs and retry).
+ *   All work is ordered on `stream`: with two or more views, views alternate between
+ *   `stream` and an internal stream of the library (created once per device) that is
+ *   forked from `stream` after the projection and joined back to it before the parameter
+ *   backward, so the call stays capturable into a CUDA graph.
  * No counterpart in one reference call: it chains gsplat/blend_backward_dev.py:404
  * forward_fast, gsplat/train_loss.py:126 loss_and_grad_device, blend_backward_dev.py:444
  * ref_slots_fast, gsplat/t2_param_backward.py:244 t2_step (extended to SH1-3 and
