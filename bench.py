@@ -193,6 +193,9 @@ def cpu_sort_baseline(keys, vals, budget_s: float = 15.0) -> dict:
             "sample": f"{iters} full C2 sorts of {n} pairs"}
 
 
+C2_PASS_DRAM_BYTES = 204.86e6 + 156.46e6
+
+
 def run_sort(args, rank, world, local) -> dict:
     import torch
     from gsplat_tt_b200 import scenes
@@ -283,9 +286,12 @@ def run_sort(args, rank, world, local) -> dict:
         "e2e": {"value": sum_over_ranks(float(n), world) / (e2e_ms / 1e3), "unit": "pairs/s",
                 "h2d_bytes_per_step": 12 * n, "d2h_bytes_per_step": 4 * n},
         "gpu_launches": int(args.steps * (2 + (SORT_KEY_BITS + 7) // 8)),
-        "roofline": {"bound": "hbm", "kernel": "k_radix_pass", "achieved": achieved,
+        "roofline": {"bound": "hbm", "kernel": "k_onesweep_pass<u64>", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / peaks["hbm_gbs"], "traffic": None,
+                     "frac": achieved / peaks["hbm_gbs"],
+                     # dram__bytes_read.sum + dram__bytes_write.sum of one middle pass of this
+                     # workload under ncu (profiles/k_onesweep_pass_c2.md)
+                     "traffic": C2_PASS_DRAM_BYTES,
                      "peak_source": peaks["source"], "avg_launch_ms": avg_ms,
                      "algorithmic_bytes_per_launch": per_launch_bytes},
         "kernel_ms": {k: v[0] / v[1] for k, v in rep.items()},

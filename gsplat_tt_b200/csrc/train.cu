@@ -816,26 +816,22 @@ struct GMut {
     float* sh;
 };
 
-// The projection backward runs as two kernels over the Gaussians, each looping over the
-// views that gave the Gaussian 2D gradients (the touch mask): k_param_bwd_sh forms the SH
-// gradient and the view-direction part of the mean gradient (fp32 SH terms, the
-// direction in fp64, as the colour path of gsplat/t2_param_backward.py extended to SH1-3),
-// and k_param_bwd_geo adds the analytic projection backward of
-// gsplat/t2_param_backward.py:123-192 for means, log-scales, quaternions and opacity
-// logits. The geometric part runs in fp64: the covariance gradient cancels strongly along
-// the viewing direction (the part of cov3d a view cannot see), and fp32 there leaves
-// errors of ~1e-2 relative to the group's largest gradient. Splitting keeps each kernel's
-// register state small enough for several blocks per SM.
+// Per Gaussian, over every view that gave it 2D gradients: the analytic projection
+// backward of gsplat/t2_param_backward.py:123-192 extended with SH bands 1-3 and the
+// view-direction term, summed over views. dL/dcov3d, dL/dopacity and the SH gradient
+// accumulate across views; the log-scale, quaternion and logit gradients are formed once.
+// The geometric part runs in fp64: the covariance gradient cancels strongly along the
+// viewing direction (the part of cov3d a view cannot see), and fp32 there leaves errors
+// of ~1e-2 relative to the group's largest gradient. SH terms stay fp32. The block's SH
+// rows and SH-gradient accumulators live in shared memory (coefficient-major, one padded
+// row per coefficient), which keeps the per-thread register state to the fp64 geometry.
 constexpr int kParamThreads = 128;
 constexpr int kParamStride = kParamThreads + 1;  // shared row stride: consecutive rows one bank apart
 
-// SH gradients (rows staged coefficient-major in shared memory with their accumulators)
-// and the view-direction mean gradient, which it writes to G.means for the geometric
-// kernel to add to.
 template <int DEG>
-__global__ void __launch_bounds__(kParamThreads)
-k_param_bwd_sh(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, float near_plane,
-               const float* __restrict__ grad2d, const uint64_t* __restrict__ touch, GMut G) {
+__global__ void __launch_bounds__(kParamThreads, 4)
+k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCfg cfg,
+            const float* __restrict__ grad2d, const uint64_t* __restrict__ touch, GMut G) {
     constexpr int K = (DEG + 1) * (DEG + 1);
     constexpr int ROW = 3 * K;
     extern __shared__ float s_param[];
@@ -854,22 +850,115 @@ k_param_bwd_sh(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, 
     if (g < n) {
         const uint64_t mask = touch[g];
         double gm[3] = {0.0, 0.0, 0.0};
+        double G3[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // 00 01 02 11 12 22
+        float gop = 0.0f;
         const double m0 = P.means[3 * g], m1 = P.means[3 * g + 1], m2 = P.means[3 * g + 2];
+        const float4 q = reinterpret_cast<const float4*>(P.q)[g];
+        const double qinv = 1.0 / sqrt((double)q.x * q.x + (double)q.y * q.y + (double)q.z * q.z +
+                                       (double)q.w * q.w);
+        const double qw = q.x * qinv, qx = q.y * qinv, qy = q.z * qinv, qz = q.w * qinv;
+        double Rq[9];
+        Rq[0] = 1.0 - 2.0 * (qy * qy + qz * qz);
+        Rq[1] = 2.0 * (qx * qy - qw * qz);
+        Rq[2] = 2.0 * (qx * qz + qw * qy);
+        Rq[3] = 2.0 * (qx * qy + qw * qz);
+        Rq[4] = 1.0 - 2.0 * (qx * qx + qz * qz);
+        Rq[5] = 2.0 * (qy * qz - qw * qx);
+        Rq[6] = 2.0 * (qx * qz - qw * qy);
+        Rq[7] = 2.0 * (qy * qz + qw * qx);
+        Rq[8] = 1.0 - 2.0 * (qx * qx + qy * qy);
+        const double s[3] = {exp((double)P.ls[3 * g]), exp((double)P.ls[3 * g + 1]),
+                             exp((double)P.ls[3 * g + 2])};
+        double M[9];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) M[3 * i + j] = Rq[3 * i + j] * s[j];
+        double S[6];  // 00 01 02 11 12 22
+        S[0] = M[0] * M[0] + M[1] * M[1] + M[2] * M[2];
+        S[1] = M[0] * M[3] + M[1] * M[4] + M[2] * M[5];
+        S[2] = M[0] * M[6] + M[1] * M[7] + M[2] * M[8];
+        S[3] = M[3] * M[3] + M[4] * M[4] + M[5] * M[5];
+        S[4] = M[3] * M[6] + M[4] * M[7] + M[5] * M[8];
+        S[5] = M[6] * M[6] + M[7] * M[7] + M[8] * M[8];
         for (int v = 0; v < n_views; ++v) {
             if (!((mask >> v) & 1ull)) continue;
             const float* gr = grad2d + ((size_t)v * n + g) * kGradStride;
-            const float gc0 = gr[6], gc1 = gr[7], gc2 = gr[8];
-            if (gc0 == 0.f && gc1 == 0.f && gc2 == 0.f) continue;
+            const float4 ga4 = reinterpret_cast<const float4*>(gr)[0];
+            const float4 gb4 = reinterpret_cast<const float4*>(gr)[1];
+            const float gbl = gr[8];
+            if (ga4.x == 0.f && ga4.y == 0.f && ga4.z == 0.f && ga4.w == 0.f && gb4.x == 0.f &&
+                gb4.y == 0.f && gb4.z == 0.f && gb4.w == 0.f && gbl == 0.f)
+                continue;
+            const double gmx = ga4.x, gmy = ga4.y, gA = ga4.z, gB = ga4.w, gC = gb4.x;
             const TCam& cam = cams[v];
-            const double z = (double)cam.R[6] * m0 + (double)cam.R[7] * m1 + (double)cam.R[8] * m2 +
-                             (double)cam.t[2];
-            if (!(z > (double)near_plane)) continue;
+            double R[9];
+#pragma unroll
+            for (int k = 0; k < 9; ++k) R[k] = cam.R[k];
+            const double x = R[0] * m0 + R[1] * m1 + R[2] * m2 + (double)cam.t[0];
+            const double y = R[3] * m0 + R[4] * m1 + R[5] * m2 + (double)cam.t[1];
+            const double z = R[6] * m0 + R[7] * m1 + R[8] * m2 + (double)cam.t[2];
+            if (!(z > (double)cfg.near_plane)) continue;
+            const double fx = cam.fx, fy = cam.fy;
+            const double iz = 1.0 / z, iz2 = iz * iz;
+            const double j00 = fx * iz, j02 = -fx * x * iz2;
+            const double j11 = fy * iz, j12 = -fy * y * iz2;
+            double T0[3], T1[3];
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                T0[k] = j00 * R[k] + j02 * R[6 + k];
+                T1[k] = j11 * R[3 + k] + j12 * R[6 + k];
+            }
+            double TC0[3], TC1[3];
+            TC0[0] = T0[0] * S[0] + T0[1] * S[1] + T0[2] * S[2];
+            TC0[1] = T0[0] * S[1] + T0[1] * S[3] + T0[2] * S[4];
+            TC0[2] = T0[0] * S[2] + T0[1] * S[4] + T0[2] * S[5];
+            TC1[0] = T1[0] * S[0] + T1[1] * S[1] + T1[2] * S[2];
+            TC1[1] = T1[0] * S[1] + T1[1] * S[3] + T1[2] * S[4];
+            TC1[2] = T1[0] * S[2] + T1[1] * S[4] + T1[2] * S[5];
+            const double lp = cfg.lowpass;
+            const double a = T0[0] * TC0[0] + T0[1] * TC0[1] + T0[2] * TC0[2] + lp;
+            const double b = T1[0] * TC0[0] + T1[1] * TC0[1] + T1[2] * TC0[2];
+            const double c = T1[0] * TC1[0] + T1[1] * TC1[1] + T1[2] * TC1[2] + lp;
+            const double idet = 1.0 / (a * c - b * b);
+            const double A = c * idet, B = -b * idet, C = a * idet;
+            // conic -> 2D covariance
+            const double ga = -(A * A * gA + A * B * gB + B * B * gC);
+            const double gc = -(B * B * gA + B * C * gB + C * C * gC);
+            const double hb = -0.5 * (2.0 * A * B * gA + (A * C + B * B) * gB + 2.0 * B * C * gC);
+            // dL/dcov3d += T^T Gs T
+            G3[0] += ga * T0[0] * T0[0] + 2.0 * hb * T0[0] * T1[0] + gc * T1[0] * T1[0];
+            G3[1] += ga * T0[0] * T0[1] + hb * (T0[0] * T1[1] + T1[0] * T0[1]) + gc * T1[0] * T1[1];
+            G3[2] += ga * T0[0] * T0[2] + hb * (T0[0] * T1[2] + T1[0] * T0[2]) + gc * T1[0] * T1[2];
+            G3[3] += ga * T0[1] * T0[1] + 2.0 * hb * T0[1] * T1[1] + gc * T1[1] * T1[1];
+            G3[4] += ga * T0[1] * T0[2] + hb * (T0[1] * T1[2] + T1[1] * T0[2]) + gc * T1[1] * T1[2];
+            G3[5] += ga * T0[2] * T0[2] + 2.0 * hb * T0[2] * T1[2] + gc * T1[2] * T1[2];
+            // dL/dT = 2 Gs T Sigma -> Jacobian entries -> camera-space mean
+            double dT0[3], dT1[3];
+#pragma unroll
+            for (int k = 0; k < 3; ++k) {
+                dT0[k] = 2.0 * (ga * TC0[k] + hb * TC1[k]);
+                dT1[k] = 2.0 * (hb * TC0[k] + gc * TC1[k]);
+            }
+            const double gj00 = dT0[0] * R[0] + dT0[1] * R[1] + dT0[2] * R[2];
+            const double gj02 = dT0[0] * R[6] + dT0[1] * R[7] + dT0[2] * R[8];
+            const double gj11 = dT1[0] * R[3] + dT1[1] * R[4] + dT1[2] * R[5];
+            const double gj12 = dT1[0] * R[6] + dT1[1] * R[7] + dT1[2] * R[8];
+            const double gx = gmx * fx * iz - gj02 * fx * iz2;
+            const double gy = gmy * fy * iz - gj12 * fy * iz2;
+            const double gz = -(gmx * fx * x + gmy * fy * y + gj00 * fx + gj11 * fy) * iz2 +
+                              2.0 * (gj02 * fx * x + gj12 * fy * y) * iz2 * iz;
+            gm[0] += R[0] * gx + R[3] * gy + R[6] * gz;
+            gm[1] += R[1] * gx + R[4] * gy + R[7] * gz;
+            gm[2] += R[2] * gx + R[5] * gy + R[8] * gz;
+            gop += gb4.y;
+            // SH colour backward (colour = max(raw, 0)) and the view-direction term.
             const double d0 = m0 - (double)cam.cc[0], d1 = m1 - (double)cam.cc[1], d2 = m2 - (double)cam.cc[2];
             const double idn = 1.0 / sqrt(d0 * d0 + d1 * d1 + d2 * d2);
             const float dx = (float)(d0 * idn), dy = (float)(d1 * idn), dz = (float)(d2 * idn);
             float basis[16];
             sh_basis(DEG, dx, dy, dz, basis);
-            const float gcol_in[3] = {gc0, gc1, gc2};
+            const float gcol_in[3] = {gb4.z, gb4.w, gbl};
             float gcol[3];
 #pragma unroll
             for (int ch = 0; ch < 3; ++ch) {
@@ -897,173 +986,49 @@ k_param_bwd_sh(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, 
                 gm[2] += ((double)gdir[2] - dz * pd) * idn;
             }
         }
+        // cov3d = M M^T: dM = 2 G3 M, M = Rq diag(s).
+        const double Gf[3][3] = {{G3[0], G3[1], G3[2]}, {G3[1], G3[3], G3[4]}, {G3[2], G3[4], G3[5]}};
+        double dM[9];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j)
+                dM[3 * i + j] = 2.0 * (Gf[i][0] * M[j] + Gf[i][1] * M[3 + j] + Gf[i][2] * M[6 + j]);
+        double gls[3];
+#pragma unroll
+        for (int j = 0; j < 3; ++j) gls[j] = (dM[j] * Rq[j] + dM[3 + j] * Rq[3 + j] + dM[6 + j] * Rq[6 + j]) * s[j];
+        double gR[9];
+#pragma unroll
+        for (int i = 0; i < 3; ++i)
+#pragma unroll
+            for (int j = 0; j < 3; ++j) gR[3 * i + j] = dM[3 * i + j] * s[j];
+        const double g00 = gR[0], g01 = gR[1], g02 = gR[2], g10 = gR[3], g11 = gR[4], g12 = gR[5];
+        const double g20 = gR[6], g21 = gR[7], g22 = gR[8];
+        const double gqn0 = 2.0 * (-qz * g01 + qy * g02 + qz * g10 - qx * g12 - qy * g20 + qx * g21);
+        const double gqn1 = 2.0 * (qy * g01 + qz * g02 + qy * g10 - 2.0 * qx * g11 - qw * g12 + qz * g20 +
+                                   qw * g21 - 2.0 * qx * g22);
+        const double gqn2 = 2.0 * (-2.0 * qy * g00 + qx * g01 + qw * g02 + qx * g10 + qz * g12 - qw * g20 +
+                                   qz * g21 - 2.0 * qy * g22);
+        const double gqn3 = 2.0 * (-2.0 * qz * g00 - qw * g01 + qx * g02 + qw * g10 - 2.0 * qz * g11 +
+                                   qy * g12 + qx * g20 + qy * g21);
+        const double dot = qw * gqn0 + qx * gqn1 + qy * gqn2 + qz * gqn3;
+        const float op = 1.0f / (1.0f + __expf(-P.ol[g]));
         G.means[3 * g] = (float)gm[0];
         G.means[3 * g + 1] = (float)gm[1];
         G.means[3 * g + 2] = (float)gm[2];
+        G.ls[3 * g] = (float)gls[0];
+        G.ls[3 * g + 1] = (float)gls[1];
+        G.ls[3 * g + 2] = (float)gls[2];
+        reinterpret_cast<float4*>(G.q)[g] =
+            make_float4((float)((gqn0 - qw * dot) * qinv), (float)((gqn1 - qx * dot) * qinv),
+                        (float)((gqn2 - qy * dot) * qinv), (float)((gqn3 - qz * dot) * qinv));
+        G.ol[g] = gop * op * (1.0f - op);
     }
     __syncthreads();
     for (int i = tid; i < rows * ROW; i += kParamThreads) {
         const int t = i / ROW, c = i - t * ROW;
         G.sh[g0 * ROW + i] = s_gsh[c * kParamStride + t];
     }
-}
-
-// Means (added to the view-direction part already in G.means), log-scales, quaternions
-// and opacity logits.
-__global__ void __launch_bounds__(kParamThreads, 4)
-k_param_bwd_geo(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCfg cfg,
-                const float* __restrict__ grad2d, const uint64_t* __restrict__ touch, GMut G) {
-    const int64_t g = (int64_t)blockIdx.x * kParamThreads + threadIdx.x;
-    if (g >= n) return;
-    const uint64_t mask = touch[g];
-    double gm[3] = {0.0, 0.0, 0.0};
-    double G3[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // 00 01 02 11 12 22
-    float gop = 0.0f;
-    const double m0 = P.means[3 * g], m1 = P.means[3 * g + 1], m2 = P.means[3 * g + 2];
-    const float4 q = reinterpret_cast<const float4*>(P.q)[g];
-    const double qinv = 1.0 / sqrt((double)q.x * q.x + (double)q.y * q.y + (double)q.z * q.z +
-                                   (double)q.w * q.w);
-    const double qw = q.x * qinv, qx = q.y * qinv, qy = q.z * qinv, qz = q.w * qinv;
-    double Rq[9];
-    Rq[0] = 1.0 - 2.0 * (qy * qy + qz * qz);
-    Rq[1] = 2.0 * (qx * qy - qw * qz);
-    Rq[2] = 2.0 * (qx * qz + qw * qy);
-    Rq[3] = 2.0 * (qx * qy + qw * qz);
-    Rq[4] = 1.0 - 2.0 * (qx * qx + qz * qz);
-    Rq[5] = 2.0 * (qy * qz - qw * qx);
-    Rq[6] = 2.0 * (qx * qz - qw * qy);
-    Rq[7] = 2.0 * (qy * qz + qw * qx);
-    Rq[8] = 1.0 - 2.0 * (qx * qx + qy * qy);
-    const double s[3] = {exp((double)P.ls[3 * g]), exp((double)P.ls[3 * g + 1]),
-                         exp((double)P.ls[3 * g + 2])};
-    double S[6];  // cov3d = M M^T with M = Rq diag(s): 00 01 02 11 12 22
-    {
-        double M[9];
-#pragma unroll
-        for (int i = 0; i < 3; ++i)
-#pragma unroll
-            for (int j = 0; j < 3; ++j) M[3 * i + j] = Rq[3 * i + j] * s[j];
-        S[0] = M[0] * M[0] + M[1] * M[1] + M[2] * M[2];
-        S[1] = M[0] * M[3] + M[1] * M[4] + M[2] * M[5];
-        S[2] = M[0] * M[6] + M[1] * M[7] + M[2] * M[8];
-        S[3] = M[3] * M[3] + M[4] * M[4] + M[5] * M[5];
-        S[4] = M[3] * M[6] + M[4] * M[7] + M[5] * M[8];
-        S[5] = M[6] * M[6] + M[7] * M[7] + M[8] * M[8];
-    }
-    for (int v = 0; v < n_views; ++v) {
-        if (!((mask >> v) & 1ull)) continue;
-        const float* gr = grad2d + ((size_t)v * n + g) * kGradStride;
-        const float4 ga4 = reinterpret_cast<const float4*>(gr)[0];
-        const float2 gb2 = reinterpret_cast<const float2*>(gr)[2];  // dC, dopacity
-        if (ga4.x == 0.f && ga4.y == 0.f && ga4.z == 0.f && ga4.w == 0.f && gb2.x == 0.f &&
-            gb2.y == 0.f)
-            continue;
-        const double gmx = ga4.x, gmy = ga4.y, gA = ga4.z, gB = ga4.w, gC = gb2.x;
-        const TCam& cam = cams[v];
-        double R[9];
-#pragma unroll
-        for (int k = 0; k < 9; ++k) R[k] = cam.R[k];
-        const double x = R[0] * m0 + R[1] * m1 + R[2] * m2 + (double)cam.t[0];
-        const double y = R[3] * m0 + R[4] * m1 + R[5] * m2 + (double)cam.t[1];
-        const double z = R[6] * m0 + R[7] * m1 + R[8] * m2 + (double)cam.t[2];
-        if (!(z > (double)cfg.near_plane)) continue;
-        const double fx = cam.fx, fy = cam.fy;
-        const double iz = 1.0 / z, iz2 = iz * iz;
-        const double j00 = fx * iz, j02 = -fx * x * iz2;
-        const double j11 = fy * iz, j12 = -fy * y * iz2;
-        double T0[3], T1[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            T0[k] = j00 * R[k] + j02 * R[6 + k];
-            T1[k] = j11 * R[3 + k] + j12 * R[6 + k];
-        }
-        double TC0[3], TC1[3];
-        TC0[0] = T0[0] * S[0] + T0[1] * S[1] + T0[2] * S[2];
-        TC0[1] = T0[0] * S[1] + T0[1] * S[3] + T0[2] * S[4];
-        TC0[2] = T0[0] * S[2] + T0[1] * S[4] + T0[2] * S[5];
-        TC1[0] = T1[0] * S[0] + T1[1] * S[1] + T1[2] * S[2];
-        TC1[1] = T1[0] * S[1] + T1[1] * S[3] + T1[2] * S[4];
-        TC1[2] = T1[0] * S[2] + T1[1] * S[4] + T1[2] * S[5];
-        const double lp = cfg.lowpass;
-        const double a = T0[0] * TC0[0] + T0[1] * TC0[1] + T0[2] * TC0[2] + lp;
-        const double b = T1[0] * TC0[0] + T1[1] * TC0[1] + T1[2] * TC0[2];
-        const double c = T1[0] * TC1[0] + T1[1] * TC1[1] + T1[2] * TC1[2] + lp;
-        const double idet = 1.0 / (a * c - b * b);
-        const double A = c * idet, B = -b * idet, C = a * idet;
-        // conic -> 2D covariance
-        const double ga = -(A * A * gA + A * B * gB + B * B * gC);
-        const double gc = -(B * B * gA + B * C * gB + C * C * gC);
-        const double hb = -0.5 * (2.0 * A * B * gA + (A * C + B * B) * gB + 2.0 * B * C * gC);
-        // dL/dcov3d += T^T Gs T
-        G3[0] += ga * T0[0] * T0[0] + 2.0 * hb * T0[0] * T1[0] + gc * T1[0] * T1[0];
-        G3[1] += ga * T0[0] * T0[1] + hb * (T0[0] * T1[1] + T1[0] * T0[1]) + gc * T1[0] * T1[1];
-        G3[2] += ga * T0[0] * T0[2] + hb * (T0[0] * T1[2] + T1[0] * T0[2]) + gc * T1[0] * T1[2];
-        G3[3] += ga * T0[1] * T0[1] + 2.0 * hb * T0[1] * T1[1] + gc * T1[1] * T1[1];
-        G3[4] += ga * T0[1] * T0[2] + hb * (T0[1] * T1[2] + T1[1] * T0[2]) + gc * T1[1] * T1[2];
-        G3[5] += ga * T0[2] * T0[2] + 2.0 * hb * T0[2] * T1[2] + gc * T1[2] * T1[2];
-        // dL/dT = 2 Gs T Sigma -> Jacobian entries -> camera-space mean
-        double dT0[3], dT1[3];
-#pragma unroll
-        for (int k = 0; k < 3; ++k) {
-            dT0[k] = 2.0 * (ga * TC0[k] + hb * TC1[k]);
-            dT1[k] = 2.0 * (hb * TC0[k] + gc * TC1[k]);
-        }
-        const double gj00 = dT0[0] * R[0] + dT0[1] * R[1] + dT0[2] * R[2];
-        const double gj02 = dT0[0] * R[6] + dT0[1] * R[7] + dT0[2] * R[8];
-        const double gj11 = dT1[0] * R[3] + dT1[1] * R[4] + dT1[2] * R[5];
-        const double gj12 = dT1[0] * R[6] + dT1[1] * R[7] + dT1[2] * R[8];
-        const double gx = gmx * fx * iz - gj02 * fx * iz2;
-        const double gy = gmy * fy * iz - gj12 * fy * iz2;
-        const double gz = -(gmx * fx * x + gmy * fy * y + gj00 * fx + gj11 * fy) * iz2 +
-                          2.0 * (gj02 * fx * x + gj12 * fy * y) * iz2 * iz;
-        gm[0] += R[0] * gx + R[3] * gy + R[6] * gz;
-        gm[1] += R[1] * gx + R[4] * gy + R[7] * gz;
-        gm[2] += R[2] * gx + R[5] * gy + R[8] * gz;
-        gop += gb2.y;
-    }
-    // cov3d = M M^T: dM = 2 G3 M, M = Rq diag(s).
-    double M[9];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j) M[3 * i + j] = Rq[3 * i + j] * s[j];
-    const double Gf[3][3] = {{G3[0], G3[1], G3[2]}, {G3[1], G3[3], G3[4]}, {G3[2], G3[4], G3[5]}};
-    double dM[9];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j)
-            dM[3 * i + j] = 2.0 * (Gf[i][0] * M[j] + Gf[i][1] * M[3 + j] + Gf[i][2] * M[6 + j]);
-    double gls[3];
-#pragma unroll
-    for (int j = 0; j < 3; ++j) gls[j] = (dM[j] * Rq[j] + dM[3 + j] * Rq[3 + j] + dM[6 + j] * Rq[6 + j]) * s[j];
-    double gR[9];
-#pragma unroll
-    for (int i = 0; i < 3; ++i)
-#pragma unroll
-        for (int j = 0; j < 3; ++j) gR[3 * i + j] = dM[3 * i + j] * s[j];
-    const double g00 = gR[0], g01 = gR[1], g02 = gR[2], g10 = gR[3], g11 = gR[4], g12 = gR[5];
-    const double g20 = gR[6], g21 = gR[7], g22 = gR[8];
-    const double gqn0 = 2.0 * (-qz * g01 + qy * g02 + qz * g10 - qx * g12 - qy * g20 + qx * g21);
-    const double gqn1 = 2.0 * (qy * g01 + qz * g02 + qy * g10 - 2.0 * qx * g11 - qw * g12 + qz * g20 +
-                               qw * g21 - 2.0 * qx * g22);
-    const double gqn2 = 2.0 * (-2.0 * qy * g00 + qx * g01 + qw * g02 + qx * g10 + qz * g12 - qw * g20 +
-                               qz * g21 - 2.0 * qy * g22);
-    const double gqn3 = 2.0 * (-2.0 * qz * g00 - qw * g01 + qx * g02 + qw * g10 - 2.0 * qz * g11 +
-                               qy * g12 + qx * g20 + qy * g21);
-    const double dot = qw * gqn0 + qx * gqn1 + qy * gqn2 + qz * gqn3;
-    const float op = 1.0f / (1.0f + __expf(-P.ol[g]));
-    // the SH kernel left the view-direction part of the mean gradient here (fp32 rounded)
-    G.means[3 * g] = (float)(gm[0] + (double)G.means[3 * g]);
-    G.means[3 * g + 1] = (float)(gm[1] + (double)G.means[3 * g + 1]);
-    G.means[3 * g + 2] = (float)(gm[2] + (double)G.means[3 * g + 2]);
-    G.ls[3 * g] = (float)gls[0];
-    G.ls[3 * g + 1] = (float)gls[1];
-    G.ls[3 * g + 2] = (float)gls[2];
-    reinterpret_cast<float4*>(G.q)[g] =
-        make_float4((float)((gqn0 - qw * dot) * qinv), (float)((gqn1 - qx * dot) * qinv),
-                    (float)((gqn2 - qy * dot) * qinv), (float)((gqn3 - qz * dot) * qinv));
-    G.ol[g] = gop * op * (1.0f - op);
 }
 
 // View v's 2D gradient rows in the reference's (N, 9) layout (zero where untouched).
@@ -1756,18 +1721,15 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
         const unsigned int nb = div_up(n, kParamThreads);
         const int K = (cfg->sh_degree + 1) * (cfg->sh_degree + 1);
         const size_t smem = 2 * (size_t)3 * K * kParamStride * sizeof(float);
-        const float nearp = c.near_plane;
         switch (cfg->sh_degree) {
-            case 0: k_param_bwd_sh<0><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, nearp, L.grad2d, L.touch, G); break;
-            case 1: k_param_bwd_sh<1><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, nearp, L.grad2d, L.touch, G); break;
-            case 2: k_param_bwd_sh<2><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, nearp, L.grad2d, L.touch, G); break;
+            case 0: k_param_bwd<0><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            case 1: k_param_bwd<1><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
+            case 2: k_param_bwd<2><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
             default:
-                GS_CUDA_CHECK(cudaFuncSetAttribute(k_param_bwd_sh<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-                k_param_bwd_sh<3><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, nearp, L.grad2d, L.touch, G);
+                GS_CUDA_CHECK(cudaFuncSetAttribute(k_param_bwd<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+                k_param_bwd<3><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G);
                 break;
         }
-        GS_CHECK_LAUNCH();
-        k_param_bwd_geo<<<nb, kParamThreads, 0, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G);
         GS_CHECK_LAUNCH();
     }
     if (apply_adam) {

@@ -44,19 +44,51 @@ def train_cfg() -> TrainConfig:
 
 
 def _kernel_bytes(name: str, n: int, views: int, pairs: float, px: int) -> float | None:
-    """Algorithmic DRAM bytes of one launch of the HBM-bound kernels (per view unless
-    noted): projection reads the SH3 params (236 B) and writes the 2D record, key and rect
-    (48 + 16 B) per Gaussian; the sparse Adam (one launch per parameter group, averaged)
-    reads p, m, v, g and writes p, m, v for the 59 values of each row; the fused emission +
-    first tile-sort pass reads 16 B per Gaussian (depth order, pair offset, rectangle) and
-    writes 8 B per pair (tile key and Gaussian id)."""
+    """Algorithmic DRAM bytes of one timed launch of the HBM-bound kernels (the minimum the
+    algorithm moves, not what the implementation happens to move):
+
+    * train_project (one launch for all of the rank's views): the SH3 parameters once
+      (236 B per Gaussian) and per view the 52 B record (mean 8, conic 12, colour 12,
+      opacity 4, depth key 4, rectangle 8, pair count 4);
+    * radix_pass32 (one pass of the depth sort over N): 4 B key + 4 B value read and written;
+    * tile_sort_emit (pair emission fused into the first tile-sort pass): 16 B per Gaussian
+      read (depth order, first-pair offset, rectangle), 8 B per pair written;
+    * tile_sort_pass (the second tile-sort pass): 8 B per pair read, 4 B per pair written;
+    * sparse_adam (the five group launches under one timer): 28 B per parameter value
+      (p, m, v, g read; p, m, v written) for the 59 values of each row;
+    * param_bwd: the parameters read and their gradients written (236 B each per Gaussian)
+      and the 2D-gradient rows (36 B) of every view.
+    The rasterisers and the loss filters are SM-issue bound and have no entry."""
     if name == "train_project":
-        return n * (236.0 + 64.0)
-    if name == "sparse_adam":
-        return n * 59 * 28.0
+        return n * 236.0 + views * n * 52.0
+    if name == "radix_pass32":
+        return n * 16.0
     if name == "tile_sort_emit":
         return pairs * 8.0 + n * 16.0
+    if name == "tile_sort_pass":
+        return pairs * 12.0
+    if name == "sparse_adam":
+        return n * 59 * 28.0
+    if name == "param_bwd":
+        return n * 472.0 + views * n * 36.0
     return None
+
+
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch measured by ncu on
+# the C4 scene with one view (3M Gaussians, 21,898,068 pairs), and the unit the traffic
+# scales with when the bench's workload is larger (profiles/train_kernels_c4_1view.md).
+NCU_TRAFFIC_C4_1VIEW = {
+    "tile_sort_emit": (172.1e6, "pairs"),
+    "tile_sort_pass": (247.2e6, "pairs"),
+}
+C4_1VIEW_PAIRS = 21898068.0
+
+
+def _traffic(name: str, pairs: float) -> float | None:
+    t = NCU_TRAFFIC_C4_1VIEW.get(name)
+    if t is None:
+        return None
+    return t[0] * pairs / C4_1VIEW_PAIRS
 
 
 def run(args, rank: int, world: int, local: int) -> dict:
@@ -150,43 +182,20 @@ def run(args, rank: int, world: int, local: int) -> dict:
             entry.update({"algorithmic_bytes": b, "achieved_gbs": gbs,
                           "frac_hbm": gbs / peaks["hbm_gbs"]})
         per_kernel[k] = entry
-    dom = max(per_kernel.items(), key=lambda kv: kv[1]["ms_per_step"])
-    out = {
-        "metric": "train-step Mpix/s (fwd+bwd+Adam)",
-        "value": value, "unit": "Mpix/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"{name.upper()} train step: {c['n']} Gaussians SH3, {V} views "
-                               f"{W}x{H} ({per} per GPU), L1+SSIM, sparse Adam",
-                   "gaussians": c["n"], "views": V, "width": W, "height": H, "tile": 16,
-                   "parallelism": f"dp{world} over views + NCCL allreduce",
-                   "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},
-        "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
-                "h2d_bytes_per_step": int(sum(t.size * 4 for t in targets_host)),
-                "d2h_bytes_per_step": 4},
-        "gpu_launches": int(sum(v["launches_per_step"] for v in per_kernel.values())),
-        "pairs_per_view": pairs, "loss": loss_now,
-        "kernels": per_kernel,
-        "clocks": clk.summary(),
-    }
+    # the dominant kernel with an HBM byte model (the rasterisers, which take more time, are
+    # SM-issue bound: about 72 % issue-active at 1-2 % of DRAM bandwidth per ncu)
+    hbm = {k: v for k, v in per_kernel.items() if "achieved_gbs" in v}
+    dom = max(hbm.items(), key=lambda kv: kv[1]["ms_per_step"])
     dom_name, d = dom
-    if "achieved_gbs" in d:
-        out["roofline"] = {"bound": "hbm", "kernel": dom_name, "achieved": d["achieved_gbs"],
-                           "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": d["frac_hbm"],
-                           "traffic": None, "peak_source": peaks["source"]}
-    else:
-        # The rasterisers are not DRAM-bound (their pair records and pixel state stay in
-        # L2 / shared memory); report the dominant kernel's DRAM fraction honestly from
-        # its own algorithmic bytes: per pair 36 B of record reads, per pixel 48 B (fwd:
-        # image, T, count writes; bwd: T, count, dL/dimage reads) and 48 B of atomics.
-        px = H * W
-        b = pairs * 36.0 + px * 48.0 + (pairs * 48.0 if "bwd" in dom_name else 0.0)
-        gbs = b / (d["ms_per_launch"] / 1e3) / 1e9
-        out["roofline"] = {"bound": "hbm", "kernel": dom_name, "achieved": gbs,
-                           "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                           "frac": gbs / peaks["hbm_gbs"], "traffic": None,
-                           "peak_source": peaks["source"],
-                           "note": "issue-bound rasteriser; DRAM fraction of its algorithmic bytes"}
+    raster = {k: per_kernel[k]["ms_per_step"] for k in ("raster_fwd", "raster_bwd") if k in per_kernel}
+    out["roofline"] = {"bound": "hbm", "kernel": dom_name, "achieved": d["achieved_gbs"],
+                       "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": d["frac_hbm"],
+                       "traffic": _traffic(dom_name, pairs),
+                       "traffic_source": "ncu dram bytes of one launch at C4 / 1 view, scaled by pairs",
+                       "peak_source": peaks["source"],
+                       "note": "largest HBM-bound kernel of the step; the rasterisers "
+                               f"({', '.join(f'{k} {v:.1f} ms' for k, v in raster.items())} per step) "
+                               "are SM-issue bound and have no HBM roofline"}
     sort_parts = {k: per_kernel[k] for k in ("radix_hist", "radix_pass32", "pair_offsets",
                                              "tile_counts", "tile_sort_emit", "tile_sort_pass")
                   if k in per_kernel}
