@@ -91,6 +91,45 @@ def _traffic(name: str, pairs: float) -> float | None:
     return t[0] * pairs / C4_1VIEW_PAIRS
 
 
+def summarize_kernels(rep: dict, ksteps: int, n: int, views: int, pairs: float, px: int,
+                      peaks: dict):
+    """Per-kernel figures from the library's timer report ({name: (total ms, launches)} over
+    ksteps steps), the roofline object for the largest kernel with an HBM byte model, and
+    the sort's share of the step."""
+    per_kernel = {}
+    for k, (tot, cnt) in rep.items():
+        avg = tot / cnt
+        entry = {"ms_per_launch": avg, "launches_per_step": cnt / ksteps,
+                 "ms_per_step": tot / ksteps}
+        b = _kernel_bytes(k, n, views, pairs, px)
+        if b is not None:
+            gbs = b / (avg / 1e3) / 1e9
+            entry.update({"algorithmic_bytes": b, "achieved_gbs": gbs,
+                          "frac_hbm": gbs / peaks["hbm_gbs"]})
+        per_kernel[k] = entry
+    # the largest kernel with an HBM byte model (the rasterisers, which take more time, are
+    # SM-issue bound: about 72 % issue-active at 1-2 % of DRAM bandwidth per ncu)
+    hbm = {k: v for k, v in per_kernel.items() if "achieved_gbs" in v}
+    dom_name, d = max(hbm.items(), key=lambda kv: kv[1]["ms_per_step"])
+    raster = {k: per_kernel[k]["ms_per_step"] for k in ("raster_fwd", "raster_bwd") if k in per_kernel}
+    roofline = {"bound": "hbm", "kernel": dom_name, "achieved": d["achieved_gbs"],
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": d["frac_hbm"],
+                "traffic": _traffic(dom_name, pairs),
+                "traffic_source": "ncu dram bytes of one launch at C4 / 1 view, scaled by pairs",
+                "peak_source": peaks["source"],
+                "note": "largest HBM-bound kernel of the step; the rasterisers "
+                        f"({', '.join(f'{k} {v:.1f} ms' for k, v in raster.items())} per step) "
+                        "are SM-issue bound and have no HBM roofline"}
+    sort_parts = {k: per_kernel[k] for k in ("radix_hist", "radix_pass32", "pair_offsets",
+                                             "tile_counts", "tile_sort_emit", "tile_sort_pass")
+                  if k in per_kernel}
+    sort_in_step = None
+    if sort_parts:
+        sort_in_step = {"ms_per_step": sum(v["ms_per_step"] for v in sort_parts.values()),
+                        "parts": sorted(sort_parts)}
+    return per_kernel, roofline, sort_in_step
+
+
 def run(args, rank: int, world: int, local: int) -> dict:
     from bench import ClockSampler, barrier, max_over_ranks, measured_peaks  # noqa: E402
     name = config_name()
@@ -169,39 +208,28 @@ def run(args, rank: int, world: int, local: int) -> dict:
     lib.gs_timing_reset()
     pairs = tr.pairs.float().mean().item()
     peaks = measured_peaks()
-    per_kernel = {}
-    for k, (tot, cnt) in rep.items():
-        avg = tot / cnt
-        entry = {"ms_per_launch": avg, "launches_per_step": cnt / ksteps,
-                 "ms_per_step": tot / ksteps}
-        b = _kernel_bytes(k, tr.n, per, pairs, H * W)
-        if k == "sparse_adam":
-            b = b / 1.0  # one timer covers the five group launches
-        if b is not None:
-            gbs = b / (avg / 1e3) / 1e9
-            entry.update({"algorithmic_bytes": b, "achieved_gbs": gbs,
-                          "frac_hbm": gbs / peaks["hbm_gbs"]})
-        per_kernel[k] = entry
-    # the dominant kernel with an HBM byte model (the rasterisers, which take more time, are
-    # SM-issue bound: about 72 % issue-active at 1-2 % of DRAM bandwidth per ncu)
-    hbm = {k: v for k, v in per_kernel.items() if "achieved_gbs" in v}
-    dom = max(hbm.items(), key=lambda kv: kv[1]["ms_per_step"])
-    dom_name, d = dom
-    raster = {k: per_kernel[k]["ms_per_step"] for k in ("raster_fwd", "raster_bwd") if k in per_kernel}
-    out["roofline"] = {"bound": "hbm", "kernel": dom_name, "achieved": d["achieved_gbs"],
-                       "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": d["frac_hbm"],
-                       "traffic": _traffic(dom_name, pairs),
-                       "traffic_source": "ncu dram bytes of one launch at C4 / 1 view, scaled by pairs",
-                       "peak_source": peaks["source"],
-                       "note": "largest HBM-bound kernel of the step; the rasterisers "
-                               f"({', '.join(f'{k} {v:.1f} ms' for k, v in raster.items())} per step) "
-                               "are SM-issue bound and have no HBM roofline"}
-    sort_parts = {k: per_kernel[k] for k in ("radix_hist", "radix_pass32", "pair_offsets",
-                                             "tile_counts", "tile_sort_emit", "tile_sort_pass")
-                  if k in per_kernel}
-    if sort_parts:
-        out["sort_in_step"] = {"ms_per_step": sum(v["ms_per_step"] for v in sort_parts.values()),
-                               "parts": sorted(sort_parts)}
+    per_kernel, roofline, sort_in_step = summarize_kernels(rep, ksteps, tr.n, per, pairs, H * W, peaks)
+    out = {
+        "metric": "train-step Mpix/s (fwd+bwd+Adam)",
+        "value": value, "unit": "Mpix/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{name.upper()} train step: {c['n']} Gaussians SH3, {V} views "
+                               f"{W}x{H} ({per} per GPU), L1+SSIM, sparse Adam",
+                   "gaussians": c["n"], "views": V, "width": W, "height": H, "tile": 16,
+                   "parallelism": f"dp{world} over views + NCCL allreduce",
+                   "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},
+        "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
+                "h2d_bytes_per_step": int(sum(t.size * 4 for t in targets_host)),
+                "d2h_bytes_per_step": 4},
+        "gpu_launches": int(sum(v["launches_per_step"] for v in per_kernel.values())),
+        "pairs_per_view": pairs, "loss": loss_now,
+        "kernels": per_kernel,
+        "clocks": clk.summary(),
+    }
+    out["roofline"] = roofline
+    if sort_in_step is not None:
+        out["sort_in_step"] = sort_in_step
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(name)
     return out

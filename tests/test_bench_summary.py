@@ -1,0 +1,42 @@
+"""bench.py's training summary on a synthetic kernel-timer report (host only): per-kernel
+HBM fractions, the roofline object on the largest HBM-bound kernel, the ncu traffic
+scaling, and the sort's share of the step."""
+import pytest
+
+from gsplat_tt_b200 import train_bench as tb
+
+PEAKS = {"hbm_gbs": 6541.5, "source": "measured"}
+
+
+def test_summary_picks_largest_hbm_kernel_and_scales_traffic():
+    n, views, pairs, px = 6_000_000, 32, 46_000_000.0, 1920 * 1080
+    ksteps = 2
+    rep = {  # name: (total ms over ksteps steps, launches)
+        "train_project": (12.4, 2),
+        "radix_pass32": (14.8, 256),
+        "tile_sort_emit": (26.0, 64),
+        "tile_sort_pass": (18.8, 64),
+        "raster_fwd": (33.2, 64),
+        "raster_bwd": (74.2, 64),
+        "loss": (11.7, 64),
+        "param_bwd": (11.7, 2),
+        "sparse_adam": (3.4, 2),
+    }
+    per_kernel, roof, sort = tb.summarize_kernels(rep, ksteps, n, views, pairs, px, PEAKS)
+    assert roof["kernel"] == "tile_sort_emit"          # raster_bwd is larger but issue-bound
+    assert "achieved_gbs" not in per_kernel["raster_bwd"]
+    e = per_kernel["tile_sort_emit"]
+    assert e["ms_per_step"] == pytest.approx(13.0)
+    assert e["algorithmic_bytes"] == pytest.approx(pairs * 8 + n * 16)
+    assert roof["achieved"] == pytest.approx(e["algorithmic_bytes"] / (26.0 / 64 / 1e3) / 1e9)
+    assert roof["frac"] == pytest.approx(roof["achieved"] / 6541.5)
+    assert roof["traffic"] == pytest.approx(172.1e6 * pairs / 21898068.0)
+    assert "raster_bwd 37.1 ms" in roof["note"]
+    assert sort["ms_per_step"] == pytest.approx((14.8 + 26.0 + 18.8) / 2)
+    assert per_kernel["train_project"]["algorithmic_bytes"] == pytest.approx(n * 236 + views * n * 52)
+
+
+def test_summary_without_traffic_entry():
+    rep = {"sparse_adam": (2.0, 1), "raster_bwd": (30.0, 1)}
+    per_kernel, roof, sort = tb.summarize_kernels(rep, 1, 1000, 1, 5000.0, 100, PEAKS)
+    assert roof["kernel"] == "sparse_adam" and roof["traffic"] is None and sort is None
