@@ -1164,6 +1164,7 @@ struct ViewLane {
     float* dmu;
     float* dxx;
     float* dxy;
+    float* target;     // staging copy of a view's target when the caller passes host memory
 };
 
 struct TrainWs {
@@ -1226,6 +1227,7 @@ static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int 
         V.dmu = ws.template take<float>(px * 3);
         V.dxx = ws.template take<float>(px * 3);
         V.dxy = ws.template take<float>(px * 3);
+        V.target = ws.template take<float>(px * 3);
     }
     L.loss_acc = ws.template take<double>(2 * (size_t)n_views);
 }
@@ -1245,6 +1247,11 @@ struct LaneStreams {
     cudaStream_t s[kLanes];
     cudaEvent_t fork;
     cudaEvent_t join[kLanes];
+    // host-target staging: copies run on their own stream; per lane, `staged` marks the
+    // copy done and `consumed` the loss kernels that read the lane's staging buffer
+    cudaStream_t copy;
+    cudaEvent_t staged[kLanes];
+    cudaEvent_t consumed[kLanes];
 };
 
 static gs_status lane_streams(LaneStreams** out) {
@@ -1260,8 +1267,12 @@ static gs_status lane_streams(LaneStreams** out) {
         for (int l = 1; l < kLanes; ++l)
             GS_CUDA_CHECK(cudaStreamCreateWithFlags(&ls->s[l], cudaStreamNonBlocking));
         GS_CUDA_CHECK(cudaEventCreateWithFlags(&ls->fork, cudaEventDisableTiming));
-        for (int l = 0; l < kLanes; ++l)
+        for (int l = 0; l < kLanes; ++l) {
             GS_CUDA_CHECK(cudaEventCreateWithFlags(&ls->join[l], cudaEventDisableTiming));
+            GS_CUDA_CHECK(cudaEventCreateWithFlags(&ls->staged[l], cudaEventDisableTiming));
+            GS_CUDA_CHECK(cudaEventCreateWithFlags(&ls->consumed[l], cudaEventDisableTiming));
+        }
+        GS_CUDA_CHECK(cudaStreamCreateWithFlags(&ls->copy, cudaStreamNonBlocking));
         per_dev[dev] = ls;
     }
     *out = per_dev[dev];
@@ -1359,12 +1370,40 @@ static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, Vie
 
 // One view after the projection: sort, forward, loss, backward into the view's 2D-gradient
 // rows (and the optional exports), all on stream st with lane V's scratch.
+// True for host memory (pinned or pageable), which the step stages through the lane's
+// device buffer; device and managed memory are read in place.
+static bool is_host_pointer(const void* p) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return true;
+    }
+    return a.type == cudaMemoryTypeHost || a.type == cudaMemoryTypeUnregistered;
+}
+
 static gs_status run_view(int64_t n, int v, const gs_camera& cam, const gs_train_config& cfg,
                           LossCfg LC, const float* target, float* images, float* grad2d_out,
                           float* view_losses, TrainWs& L, ViewLane& V, int64_t cap,
-                          cudaStream_t st) {
+                          cudaStream_t st, LaneStreams* LS, int lane) {
     const int vh = cam.height, vw = cam.width;
     const TCfg c = make_tcfg(cfg, vh, vw);
+    // A host target is copied into the lane's staging buffer: with lanes, on the copy
+    // stream while this view sorts and blends (after the loss kernels of the lane's previous
+    // view have read the buffer); without, in order on st.
+    const bool host_target = is_host_pointer(target);
+    const size_t tbytes = (size_t)vh * vw * 3 * sizeof(float);
+    if (host_target) {
+        if (LS != nullptr) {
+            // a lane's first view in this call reuses the buffer after the fork, which already
+            // follows every earlier use (the previous call joined its lanes to st)
+            if (v != lane) GS_CUDA_CHECK(cudaStreamWaitEvent(LS->copy, LS->consumed[lane], 0));
+            GS_CUDA_CHECK(cudaMemcpyAsync(V.target, target, tbytes, cudaMemcpyHostToDevice, LS->copy));
+            GS_CUDA_CHECK(cudaEventRecord(LS->staged[lane], LS->copy));
+        } else {
+            GS_CUDA_CHECK(cudaMemcpyAsync(V.target, target, tbytes, cudaMemcpyHostToDevice, st));
+        }
+        target = V.target;
+    }
     gs_status s = sort_view(n, c, v, L, V, cap, st);
     if (s != GS_OK) return s;
     const ProjView pvv = L.pv.view(v, n);
@@ -1381,6 +1420,7 @@ static gs_status run_view(int64_t n, int v, const gs_camera& cam, const gs_train
     LC.H = vh;
     LC.W = vw;
     LC.inv_n = (float)(1.0 / (3.0 * vh * vw));
+    if (host_target && LS != nullptr) GS_CUDA_CHECK(cudaStreamWaitEvent(st, LS->staged[lane], 0));
     {
         KernelTimer kt("loss", st);
         const int64_t n3 = (int64_t)vh * vw * 3;
@@ -1399,6 +1439,7 @@ static gs_status run_view(int64_t n, int v, const gs_camera& cam, const gs_train
         k_loss_finalize<<<1, 1, 0, st>>>(L.loss_acc + 2 * v, LC, cfg.use_ssim, view_losses + v);
         GS_CHECK_LAUNCH();
     }
+    if (host_target && LS != nullptr) GS_CUDA_CHECK(cudaEventRecord(LS->consumed[lane], st));
     {
         KernelTimer kt("raster_bwd", st);
         float* g2 = L.grad2d + (size_t)v * n * kGradStride;
@@ -1695,13 +1736,14 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
             lst[l] = LS->s[l];
             GS_CUDA_CHECK(cudaStreamWaitEvent(lst[l], LS->fork, 0));
         }
+        GS_CUDA_CHECK(cudaStreamWaitEvent(LS->copy, LS->fork, 0));
     }
     gs_status vs = GS_OK;
     for (int v = 0; v < n_views && vs == GS_OK; ++v) {
         ViewLane& V = L.lane[v % nlanes];
         const cudaStream_t vst = lst[v % nlanes];
         vs = run_view(n, v, cams[v], *cfg, LC, targets[v], images, grad2d_out, view_losses, L, V,
-                      pair_capacity, vst);
+                      pair_capacity, vst, nlanes > 1 ? LS : nullptr, v % nlanes);
     }
     if (nlanes > 1) {  // join every lane, also after an error, before anything else runs on st
         for (int l = 1; l < nlanes; ++l) {

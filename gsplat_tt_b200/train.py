@@ -221,11 +221,18 @@ class Trainer:
             self._alloc(int(need * headroom) + 4096)
 
     def _targets(self, targets):
+        """Device tensors pass through; pinned host fp32 tensors also pass through (the
+        library copies each view's target on its own stream, overlapped with the other
+        views' work); numpy arrays and other host tensors are copied here."""
         ts = []
         for t in targets:
             if isinstance(t, np.ndarray):
                 t = torch.from_numpy(np.ascontiguousarray(t, np.float32))
-            ts.append(t.to(self.device, torch.float32).contiguous())
+            if (t.device.type == "cpu" and t.is_pinned() and t.dtype == torch.float32
+                    and t.is_contiguous()):
+                ts.append(t)
+            else:
+                ts.append(t.to(self.device, torch.float32).contiguous())
         return ts
 
     def step(self, cams, targets, check_errors: bool = False, images=None, grad2d=None):

@@ -200,3 +200,31 @@ def test_bf16_moments_round_to_bf16():
     for k in ot.PARAM_NAMES:
         m = tr.m.numpy()[k]
         np.testing.assert_array_equal(m, ot.bf16_round(m))
+
+
+def test_host_targets_match_device_targets():
+    """Pinned host targets (copied by the library on its own stream, overlapped with the
+    lanes) and pageable numpy targets give the same step as device targets over several
+    views: the same losses and gradients (up to the order of the backward's float atomics)."""
+    import torch
+    params = small_scene(6000, 3, seed=21)
+    H, W = 64, 96
+    cams = cams_for(5, H, W, 90.0)
+    targets = scenes.random_targets([scenes.Camera(c[0], c[1], H, W) for c in cams], seed=22)
+    results = []
+    for kind in ("device", "pinned", "numpy"):
+        tr, _ = trainer(params, 3, 16, len(cams), H, W)
+        tr.ensure_capacity(cams)
+        if kind == "device":
+            tg = [torch.from_numpy(t).cuda() for t in targets]
+        elif kind == "pinned":
+            tg = [torch.from_numpy(t).pin_memory() for t in targets]
+        else:
+            tg = targets
+        tr.step(cams, tg, check_errors=True)
+        torch.cuda.synchronize()
+        results.append((tr.losses.cpu().numpy(), tr.grads.numpy()))
+    for losses, g in results[1:]:
+        np.testing.assert_allclose(losses, results[0][0], rtol=1e-6)
+        for k in ot.PARAM_NAMES:
+            assert ot.rel_error(g[k], results[0][1][k]) <= 1e-5, k
