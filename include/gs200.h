@@ -224,7 +224,10 @@ typedef struct gs_train_config {
  *   vis_counts (N floats): number of views in which each Gaussian is visible. These two
  *   are the buffers a multi-GPU caller sums across ranks before calling gs_sparse_adam
  *   (apply_adam = 0 here).
- *   targets: n_views device pointers to H*W*3 fp32 target images (host array of pointers).
+ *   targets: n_views pointers to H*W*3 fp32 target images (host array of pointers), each
+ *   in device memory (read in place) or in host memory (copied into the workspace; from
+ *   pinned memory the copies run on an internal stream, overlapped with other views' work,
+ *   and the host buffers must stay unchanged until the step completes on `stream`).
  *   view_losses (device, n_views floats): per-view loss. images (nullable, device,
  *   n_views*H*W*3) and grad2d (nullable, device, n_views*N*9 of dmx, dmy, dA, dB, dC,
  *   dopacity, dr, dg, db) export intermediates for parity tests. pairs (nullable, device
