@@ -71,6 +71,9 @@ _sig("gs_timing_reset", None)
 _sig("gs_timing_report", i32, ctypes.c_char_p, sz, ctypes.POINTER(ctypes.c_double),
      ctypes.POINTER(i64), i32)
 _sig("gs_blend", status, vp, vp, vp, vp, vp, vp, i64, i32, i32, i32, vp, vp, vp)
+_sig("gs_cull_and_blend_workspace_size", sz, i64)
+_sig("gs_cull_and_blend", status, vp, vp, vp, vp, vp, vp, i64, i64, i32, i32, i32, i32, i32, f32,
+     i32, f32, vp, vp, vp, sz, vp)
 
 
 def check(code: int) -> None:

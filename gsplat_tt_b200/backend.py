@@ -139,10 +139,14 @@ class B200Backend(_BackendBase):
         cov3d = self._cached_cov3d(gaussians.scales, gaussians.rotations)
         floor_ = (self._mb_contrib_floor if self.contrib_floor_override is None
                   else float(self.contrib_floor_override))
+        # the reference's fused call renders with 32-pixel tiles whatever tile_size the
+        # staged path uses (backends/cpu_cpp/backend.py:364-381)
         return _d.render_full(gaussians.means, cov3d, gaussians.opacities, gaussians.colors,
                               extrinsics, intrinsics, image_height, image_width,
-                              tile_size=self.tile_size, min_opacity=self.min_opacity,
-                              contrib_floor=floor_, cull_disabled=self.cull_disabled,
+                              tile_size=32, min_opacity=self.min_opacity,
+                              contrib_floor=floor_, mb_contrib_floor=self._mb_contrib_floor,
+                              cull_disabled=self.cull_disabled,
+                              transmittance_threshold=self.transmittance_threshold,
                               max_radius=self.max_radius, k_cap=self.k_cap,
                               use_isoellipse=self.use_isoellipse)
 

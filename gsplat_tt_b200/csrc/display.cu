@@ -819,6 +819,249 @@ extern "C" gs_status gs_blend(const float* means_2d, const float* covs_2d, const
     return GS_OK;
 }
 
+// ------------------------------------------------------------------ microblock cull + blend
+
+// Per-Gaussian record of the cull (cull_and_blend.cpp:718-748): screen mean, inverse 2D
+// covariance (det clamped at 1e-6), log(floor / opacity) (>= 0: never kept), the
+// opacity-scaled bounding-box half extents, opacity and colour.
+struct CullRec {
+    float mx, my, ia, ib, ic, lt, xh, yh, op, cr, cg, cb;
+};
+static_assert(sizeof(CullRec) == 48, "CullRec is three 16-byte words");
+
+__global__ void k_cull_records(const float* __restrict__ means_2d, const float* __restrict__ covs_2d,
+                               const float* __restrict__ colors, const float* __restrict__ opacities,
+                               int64_t m, float floor_, CullRec* __restrict__ rec) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= m) return;
+    const float a = covs_2d[4 * i], b = covs_2d[4 * i + 1], c = covs_2d[4 * i + 3];
+    const float det = max_ref(a * c - b * b, 1e-6f);
+    CullRec r;
+    r.mx = means_2d[2 * i];
+    r.my = means_2d[2 * i + 1];
+    r.ia = c / det;
+    r.ib = -b / det;
+    r.ic = a / det;
+    r.op = opacities[i];
+    r.cr = colors[3 * i];
+    r.cg = colors[3 * i + 1];
+    r.cb = colors[3 * i + 2];
+    if (r.op <= floor_) {
+        r.lt = 0.0f;
+        r.xh = r.yh = 0.0f;
+    } else {
+        r.lt = logf_host(floor_ / r.op);
+        const float rd = sqrtf(-2.0f * r.lt);
+        r.xh = rd * sqrtf(max_ref(a, 0.0f));
+        r.yh = rd * sqrtf(max_ref(c, 0.0f));
+    }
+    rec[i] = r;
+}
+
+constexpr int kMbBatch = 128;  // Gaussians of the tile list staged per batch
+
+// cull_and_blend.cpp:316-675 (scalar build). One block of 32 warps per tile; warp w owns
+// microblock w = (my << 2) | mx (8 x 4 pixels, one per lane). Per batch of the tile's
+// sorted list, each warp keeps, in list order, the Gaussians whose exact minimum
+// Mahalanobis distance over its microblock reaches the floor (ballot compaction), then
+// blends them; a warp stops blending after the first Gaussian that leaves every pixel of
+// its microblock below transmittance_threshold, but keeps culling to the end of the list
+// so the kept / dropped statistics count every pair, as the reference's cull pass does.
+// Microblocks outside the tile or image (tiles narrower than 32) are culled for the
+// statistics and never blended.
+__global__ void __launch_bounds__(1024)
+k_cull_blend(const CullRec* __restrict__ rec, const int64_t* __restrict__ sorted_ids,
+             const int64_t* __restrict__ ranges, int tiles_x, int tile_size, int height, int width,
+             int cull_disabled, float tthresh, float* __restrict__ image,
+             unsigned long long* __restrict__ counts) {
+    __shared__ CullRec s_rec[kMbBatch];
+    __shared__ uint32_t s_rng[kMbBatch];  // mx_lo | mx_hi << 8 | my_lo << 16 | my_hi << 24; ~0: dropped
+    __shared__ int s_any[kMbBatch];
+    __shared__ uint8_t s_list[32][kMbBatch];
+    __shared__ unsigned long long s_kept, s_drop;
+    const int tile = blockIdx.x;
+    const int64_t start = ranges[2 * tile], end = ranges[2 * tile + 1];
+    if (start == end) return;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int ty = tile / tiles_x, tx = tile % tiles_x;
+    const float txt = (float)(tx * tile_size), tyt = (float)(ty * tile_size);
+    const int mbx = w & 3, mby = w >> 2;
+    const int py_tile = ty * tile_size, px_tile = tx * tile_size;
+    const int py_end = min(py_tile + tile_size, height), px_end = min(px_tile + tile_size, width);
+    const int py0 = py_tile + mby * 4, px0 = px_tile + mbx * 8;
+    const int py1 = min(py0 + 4, py_end), px1 = min(px0 + 8, px_end);
+    const bool mb_live = py0 < py1 && px0 < px1;
+    const int pi = lane >> 3, pj = lane & 7;
+    const bool pix = mb_live && pi < py1 - py0 && pj < px1 - px0;
+    const float py = (float)(py0 + pi) + 0.5f, px = (float)(px0 + pj) + 0.5f;
+    const float v_lo = (tyt + (float)(mby * 4));  // minus the mean per Gaussian
+    const float u_lo = (txt + (float)(mbx * 8));
+    float T = 1.0f, ar = 0.0f, ag = 0.0f, ab = 0.0f;
+    bool saturated = false;
+    int kept_total = 0;
+    if (tid == 0) s_kept = s_drop = 0ull;
+    for (int64_t b0 = start; b0 < end; b0 += kMbBatch) {
+        const int nb = (int)min((int64_t)kMbBatch, end - b0);
+        __syncthreads();
+        if (tid < nb) {
+            const CullRec r = rec[sorted_ids[b0 + tid]];
+            s_rec[tid] = r;
+            s_any[tid] = 0;
+            uint32_t rg = 0xffffffffu;
+            if (r.lt < 0.0f) {
+                const int mx_lo = max(0, (int)floorf(((r.mx - r.xh) - txt) / 8.0f));
+                const int mx_hi = min(3, (int)floorf(((r.mx + r.xh) - txt) / 8.0f));
+                const int my_lo = max(0, (int)floorf(((r.my - r.yh) - tyt) / 4.0f));
+                const int my_hi = min(7, (int)floorf(((r.my + r.yh) - tyt) / 4.0f));
+                if (mx_lo <= mx_hi && my_lo <= my_hi)
+                    rg = (uint32_t)mx_lo | (uint32_t)mx_hi << 8 | (uint32_t)my_lo << 16 |
+                         (uint32_t)my_hi << 24;
+            }
+            s_rng[tid] = rg;
+        }
+        __syncthreads();
+        // cull: this warp's microblock against the batch, list order kept by the ballot
+        int cnt = 0;
+        for (int c0 = 0; c0 < nb; c0 += 32) {
+            const int k = c0 + lane;
+            bool keep = false;
+            if (k < nb) {
+                const uint32_t rg = s_rng[k];
+                if (rg != 0xffffffffu && mbx >= (int)(rg & 0xff) && mbx <= (int)((rg >> 8) & 0xff) &&
+                    mby >= (int)((rg >> 16) & 0xff) && mby <= (int)(rg >> 24)) {
+                    const CullRec& r = s_rec[k];
+                    const float vl = v_lo - r.my, vh = vl + 4.0f;
+                    const bool y_in = (vl <= 0.0f) && (0.0f <= vh);
+                    const float v_fix = (vl > 0.0f) ? vl : vh;
+                    const float ul = u_lo - r.mx, uh = ul + 8.0f;
+                    const bool x_in = (ul <= 0.0f) && (0.0f <= uh);
+                    float m2;
+                    if (cull_disabled || (x_in && y_in)) {
+                        m2 = 0.0f;
+                    } else {
+                        float m2v = INFINITY, m2h = INFINITY;
+                        if (!x_in) {
+                            const float uf = (ul > 0.0f) ? ul : uh;
+                            float vs = -r.ib * uf / max_ref(r.ic, 1e-12f);
+                            vs = vs < vl ? vl : (vh < vs ? vh : vs);
+                            m2v = r.ia * uf * uf + 2.0f * r.ib * uf * vs + r.ic * vs * vs;
+                        }
+                        if (!y_in) {
+                            float us = -r.ib * v_fix / max_ref(r.ia, 1e-12f);
+                            us = us < ul ? ul : (uh < us ? uh : us);
+                            m2h = r.ia * us * us + 2.0f * r.ib * us * v_fix + r.ic * v_fix * v_fix;
+                        }
+                        m2 = min_ref(m2v, m2h);
+                    }
+                    keep = m2 <= -2.0f * r.lt;
+                }
+            }
+            const uint32_t bal = __ballot_sync(0xffffffffu, keep);
+            if (keep) {
+                s_list[w][cnt + __popc(bal & ((1u << lane) - 1u))] = (uint8_t)k;
+                s_any[k] = 1;
+            }
+            cnt += __popc(bal);
+        }
+        kept_total += cnt;
+        __syncwarp();
+        // blend this batch's kept list in order until the microblock saturates
+        if (mb_live && !saturated) {
+            for (int q = 0; q < cnt; ++q) {
+                const CullRec& r = s_rec[s_list[w][q]];
+                if (pix) {
+                    const float dx = px - r.mx, dy = py - r.my;
+                    const float power =
+                        -0.5f * (r.ia * dx * dx + 2.0f * r.ib * dx * dy + r.ic * dy * dy);
+                    const float gw = (float)exp((double)min_ref(power, 0.0f));
+                    const float alpha = min_ref(r.op * gw, 0.99f);
+                    const float at = alpha * T;
+                    ar += at * r.cr;
+                    ag += at * r.cg;
+                    ab += at * r.cb;
+                    T = T * (1.0f - alpha);
+                }
+                if (__all_sync(0xffffffffu, !pix || T < tthresh)) {
+                    saturated = true;
+                    break;
+                }
+            }
+        }
+        __syncthreads();
+        // statistics: Gaussians kept by no microblock (or dropped before the cull)
+        if (tid < nb && (s_rng[tid] == 0xffffffffu || s_any[tid] == 0)) atomicAdd(&s_drop, 1ull);
+    }
+    if (lane == 0 && kept_total > 0) atomicAdd(&s_kept, (unsigned long long)kept_total);
+    if (pix && kept_total > 0) {
+        const size_t o = ((size_t)(py0 + pi) * width + (px0 + pj)) * 3;
+        image[o] = ar;
+        image[o + 1] = ag;
+        image[o + 2] = ab;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        atomicAdd(&counts[0], s_drop);
+        atomicAdd(&counts[1], s_kept);
+    }
+}
+
+__global__ void k_cull_stats(const unsigned long long* __restrict__ counts, int64_t p,
+                             int64_t* __restrict__ stats) {
+    stats[0] = p;
+    stats[1] = (int64_t)counts[0];
+    stats[2] = (int64_t)counts[1];
+}
+
+extern "C" size_t gs_cull_and_blend_workspace_size(int64_t m) {
+    WorkspaceSizer s;
+    s.take<unsigned long long>(2);
+    s.take<CullRec>(m > 0 ? m : 1);
+    return s.bytes();
+}
+
+extern "C" gs_status gs_cull_and_blend(const float* means_2d, const float* covs_2d,
+                                       const float* colors, const float* opacities,
+                                       const int64_t* sorted_gaussian_ids,
+                                       const int64_t* tile_ranges, int64_t m, int64_t p,
+                                       int32_t tiles_x, int32_t tiles_y, int32_t tile_size,
+                                       int32_t height, int32_t width, float mb_contrib_floor,
+                                       int32_t cull_disabled, float transmittance_threshold,
+                                       float* image, int64_t* stats, void* workspace,
+                                       size_t workspace_bytes, void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    GS_ARG_CHECK(height > 0 && width > 0 && m >= 0 && p >= 0, "gs_cull_and_blend: bad sizes");
+    GS_ARG_CHECK(tile_size >= 1 && tile_size <= 32,
+                 "gs_cull_and_blend: tile_size must be in [1, 32] (8x4 microblocks of a 32x32 tile)");
+    GS_ARG_CHECK(tiles_x == (width + tile_size - 1) / tile_size &&
+                     tiles_y == (height + tile_size - 1) / tile_size,
+                 "gs_cull_and_blend: tile grid does not match the image");
+    GS_ARG_CHECK(image && tile_ranges && stats, "gs_cull_and_blend: null pointer");
+    if (m > 0 && p > 0)
+        GS_ARG_CHECK(means_2d && covs_2d && colors && opacities && sorted_gaussian_ids,
+                     "gs_cull_and_blend: null pointer");
+    Workspace ws(workspace, workspace_bytes);
+    unsigned long long* counts = ws.take<unsigned long long>(2);
+    CullRec* rec = ws.take<CullRec>(m > 0 ? m : 1);
+    GS_ARG_CHECK(ws.ok(), "gs_cull_and_blend: workspace too small (%zu < %zu)", workspace_bytes,
+                 gs_cull_and_blend_workspace_size(m));
+    GS_CUDA_CHECK(cudaMemsetAsync(image, 0, (size_t)height * width * 3 * sizeof(float), st));
+    GS_CUDA_CHECK(cudaMemsetAsync(counts, 0, 2 * sizeof(unsigned long long), st));
+    if (m > 0 && p > 0) {
+        k_cull_records<<<div_up(m, 256), 256, 0, st>>>(means_2d, covs_2d, colors, opacities, m,
+                                                       mb_contrib_floor, rec);
+        GS_CHECK_LAUNCH();
+        k_cull_blend<<<tiles_x * tiles_y, 1024, 0, st>>>(rec, sorted_gaussian_ids, tile_ranges,
+                                                         tiles_x, tile_size, height, width,
+                                                         cull_disabled, transmittance_threshold,
+                                                         image, counts);
+        GS_CHECK_LAUNCH();
+    }
+    k_cull_stats<<<1, 1, 0, st>>>(counts, p, stats);
+    GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
 // Device logf reproduction, exposed for the exhaustive parity test of the table.
 extern "C" gs_status gs_debug_logf_host(const float* x, float* y, int64_t n, void* stream) {
     clear_error();

@@ -222,18 +222,53 @@ def blend(means_2d, covs_2d, colors, opacities, sorted_gaussian_ids, tile_ranges
     return (img, alpha) if return_alpha else img
 
 
+def cull_and_blend(means_2d, covs_2d, colors, opacities, sorted_gaussian_ids, tile_ranges,
+                   tiles_x, tiles_y, tile_size, image_height, image_width,
+                   mb_contrib_floor=1.0 / 16384.0, cull_disabled=False,
+                   transmittance_threshold=1.0 / 255.0):
+    """Microblock cull + blend, the reference's default CPU display blend
+    (cull_and_blend.cpp:316-840; pybind cull_and_blend, pybind_module.cpp:764-820).
+    Returns ((H,W,3) fp32 CUDA image, stats dict with pairs_in, pairs_dropped,
+    pairs_kept_per_mb). cull_disabled / transmittance_threshold are the render_full
+    parameters the pybind entry fixes at False / 1/255."""
+    m2 = _t(means_2d, torch.float32, "means_2d", (2,))
+    M = m2.shape[0]
+    cv = _t(covs_2d, torch.float32, "covs_2d")
+    if cv.numel() != 4 * M:
+        raise ValueError("covs_2d must have shape (M, 4)")
+    col = _t(colors, torch.float32, "colors", (3,))
+    op = _t(opacities, torch.float32, "opacities").reshape(-1)
+    if col.shape[0] != M or op.shape[0] != M:
+        raise ValueError("means_2d, covs_2d, colors, opacities must share M")
+    sg = _t(sorted_gaussian_ids, torch.int64, "sorted_gaussian_ids").reshape(-1)
+    rng = _t(tile_ranges, torch.int64, "tile_ranges")
+    if rng.dim() != 2 or rng.shape[1] != 2 or rng.shape[0] != tiles_x * tiles_y:
+        raise ValueError("tile_ranges must have shape (tiles_x * tiles_y, 2)")
+    d = _dev()
+    img = torch.empty((image_height, image_width, 3), dtype=torch.float32, device=d)
+    st = torch.empty(3, dtype=torch.int64, device=d)
+    ws = _workspace(lib.gs_cull_and_blend_workspace_size(M))
+    check(lib.gs_cull_and_blend(_p(m2), _p(cv), _p(col), _p(op), _p(sg), _p(rng), M, sg.shape[0],
+                                int(tiles_x), int(tiles_y), int(tile_size), int(image_height),
+                                int(image_width), float(mb_contrib_floor), int(bool(cull_disabled)),
+                                float(transmittance_threshold), _p(img), _p(st), _p(ws), ws.numel(),
+                                _stream()))
+    s = st.cpu().tolist()
+    return img, {"pairs_in": s[0], "pairs_dropped": s[1], "pairs_kept_per_mb": s[2]}
+
+
 def render_full(means, cov3d, opacities, colors, extrinsics, intrinsics, image_height,
                 image_width, tile_size=32, min_opacity=1.0 / 255.0, contrib_floor=1.0 / 16384.0,
                 mb_contrib_floor=1.0 / 16384.0, cull_disabled=False,
                 transmittance_threshold=1.0 / 255.0, max_radius=0, k_cap=3.0,
                 use_isoellipse=False, blend_mode=0, return_alpha=False):
-    """One call for project -> tile_assign -> sort -> blend (pybind render_full,
-    pybind_module.cpp:1149-1575). Returns (image (H,W,3) float32 numpy, stats dict with
-    the reference's keys). The display blend is the plain per-tile blend
-    (blend.cpp); the microblock cull of the reference's default CPU path is not
-    applied, so pairs_dropped is 0 and mb_contrib_floor / transmittance_threshold are
-    accepted for signature compatibility only."""
-    del mb_contrib_floor, transmittance_threshold, blend_mode
+    """One call for project -> tile_assign -> sort -> microblock cull + blend (pybind
+    render_full, pybind_module.cpp:1149-1575, CPU path: cull_and_blend). Returns (image
+    (H,W,3) float32 numpy, stats dict with the reference's keys). blend_mode selects
+    Tenstorrent device blends in the reference and is ignored. With return_alpha the
+    plain per-tile blend (blend.cpp) also runs to give stats["alpha"] = 1 - final T,
+    which the reference's render_full does not output."""
+    del blend_mode
     t0 = time.perf_counter()
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
     ev[0].record()
@@ -250,17 +285,21 @@ def render_full(means, cov3d, opacities, colors, extrinsics, intrinsics, image_h
     tiles_y = (image_height + tile_size - 1) // tile_size
     sg, rng = sort(gids, tids, dp, tiles_x, tiles_y)
     ev[3].record()
-    out = blend(m2, cv.reshape(-1, 4), col, op, sg, rng, image_height, image_width, tile_size,
-                return_alpha=return_alpha)
+    img, cb = cull_and_blend(m2, cv.reshape(-1, 4), col, op, sg, rng, tiles_x, tiles_y, tile_size,
+                             image_height, image_width, mb_contrib_floor, cull_disabled,
+                             transmittance_threshold)
     ev[4].record()
-    img, alpha = out if return_alpha else (out, None)
+    alpha = None
+    if return_alpha:
+        _, alpha = blend(m2, cv.reshape(-1, 4), col, op, sg, rng, image_height, image_width,
+                         tile_size, return_alpha=True)
     img_np = img.cpu().numpy()
     stats = {
         "num_visible": int(m2.shape[0]),
         "num_entries": int(sg.shape[0]),
-        "pairs_in": int(sg.shape[0]),
-        "pairs_dropped": 0,
-        "pairs_kept_per_mb": 0,
+        "pairs_in": cb["pairs_in"],
+        "pairs_dropped": cb["pairs_dropped"],
+        "pairs_kept_per_mb": cb["pairs_kept_per_mb"],
         "project_ms": ev[0].elapsed_time(ev[1]),
         "tile_assign_ms": ev[1].elapsed_time(ev[2]),
         "sort_ms": ev[2].elapsed_time(ev[3]),

@@ -171,6 +171,25 @@ gs_status gs_blend(const float* means_2d, const float* covs_2d, const float* col
                    const int64_t* tile_ranges, int64_t m, int32_t height, int32_t width,
                    int32_t tile_size, float* image, float* alpha, void* stream);
 
+/* src/gsplat_cpu/cull_and_blend.cpp:678-840 cull_and_blend (the reference's default CPU
+ * display blend, pybind_module.cpp:764-820 and render_full's CPU path): each tile cut into
+ * 8x4-pixel microblocks; a Gaussian of the tile list is kept in each microblock where its
+ * exact minimum Mahalanobis distance over the microblock reaches mb_contrib_floor
+ * (cull_disabled: every microblock its bounding box overlaps); each microblock blends its
+ * list front to back, alpha = min(o * exp(min(power, 0)), 0.99), and stops after the first
+ * Gaussian that leaves every pixel's T below transmittance_threshold. image H*W*3 is
+ * zeroed first (pixels no Gaussian reaches stay 0). stats (device, 3 int64): pairs_in,
+ * pairs_dropped (pairs kept in no microblock), pairs_kept_per_mb. tile_size <= 32;
+ * workspace: gs_cull_and_blend_workspace_size(m) bytes. */
+size_t gs_cull_and_blend_workspace_size(int64_t m);
+gs_status gs_cull_and_blend(const float* means_2d, const float* covs_2d, const float* colors,
+                            const float* opacities, const int64_t* sorted_gaussian_ids,
+                            const int64_t* tile_ranges, int64_t m, int64_t p, int32_t tiles_x,
+                            int32_t tiles_y, int32_t tile_size, int32_t height, int32_t width,
+                            float mb_contrib_floor, int32_t cull_disabled,
+                            float transmittance_threshold, float* image, int64_t* stats,
+                            void* workspace, size_t workspace_bytes, void* stream);
+
 /* ------------------------------------------------------------------------------
  * Training path: per view project -> key emission -> sort -> ranges -> forward raster
  * -> loss -> backward raster; then one projection backward over all views and a

@@ -54,6 +54,10 @@ def lib():
         L.gso_logf_array.argtypes = [_f, _f, ctypes.c_int64]
         L.gso_blend.argtypes = [_f, _f, _f, _f, _i64, _i64, ctypes.c_int64, ctypes.c_int,
                                 ctypes.c_int, ctypes.c_int, _f, _f]
+        L.gso_cull_and_blend.argtypes = [_f, _f, _f, _f, _i64, _i64, ctypes.c_int64,
+                                         ctypes.c_int64, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                         ctypes.c_float, ctypes.c_int, ctypes.c_float, _f, _i64]
         _LIB = L
     return _LIB
 
@@ -149,6 +153,27 @@ def blend(means_2d, covs_2d, colors, opacities, sorted_gaussian_ids, tile_ranges
                     _p(rng, _i64), M, int(image_height), int(image_width), int(tile_size),
                     _p(img, _f), _p(alpha, _f))
     return (img, alpha) if return_alpha else img
+
+
+def cull_and_blend(means_2d, covs_2d, colors, opacities, sorted_gaussian_ids, tile_ranges,
+                   tiles_x, tiles_y, tile_size, image_height, image_width,
+                   mb_contrib_floor=1.0 / 16384.0, cull_disabled=False,
+                   transmittance_threshold=1.0 / 255.0):
+    """Microblock cull + blend (cull_and_blend.cpp, scalar build) -> (image, stats)."""
+    m2 = _c(means_2d, np.float32)
+    M = m2.shape[0]
+    cv = _c(covs_2d, np.float32).reshape(M, 4)
+    col, op = _c(colors, np.float32), _c(opacities, np.float32)
+    sg, rng = _c(sorted_gaussian_ids, np.int64), _c(tile_ranges, np.int64)
+    img = np.zeros((image_height, image_width, 3), np.float32)
+    st = np.zeros(3, np.int64)
+    lib().gso_cull_and_blend(_p(m2, _f), _p(cv, _f), _p(col, _f), _p(op, _f), _p(sg, _i64),
+                             _p(rng, _i64), M, sg.shape[0], int(tiles_x), int(tiles_y),
+                             int(tile_size), int(image_height), int(image_width),
+                             float(mb_contrib_floor), int(bool(cull_disabled)),
+                             float(transmittance_threshold), _p(img, _f), _p(st, _i64))
+    return img, {"pairs_in": int(st[0]), "pairs_dropped": int(st[1]),
+                 "pairs_kept_per_mb": int(st[2])}
 
 
 def logf_array(x):

@@ -357,6 +357,176 @@ void gso_blend(const float* means_2d, const float* covs_2d, const float* colors,
     free(inv);
 }
 
+/* ---------------------------------------------------------------- microblock cull + blend
+ * src/gsplat_cpu/cull_and_blend.cpp:316-840 cull_and_blend as the reference's scalar build
+ * runs it (no GSPLAT_SIMD_AVX2 / NEON: every microblock goes through the scalar blend loop).
+ * A tile is cut into 8x4-pixel microblocks, mb = (my << 2) | mx for mx 0..3, my 0..7;
+ * per Gaussian of the tile list (sorted order): drop if opacity <= mb_contrib_floor or
+ * its opacity-scaled bounding box misses every microblock; else keep it in each
+ * microblock whose exact minimum Mahalanobis distance over the microblock rectangle
+ * reaches the floor (cull.cpp:408-475). Each microblock then blends its kept list in order
+ * with alpha = min(op * exp(min(power, 0)), 0.99) and stops after the first Gaussian that
+ * leaves every pixel's T below transmittance_threshold (:599-640). */
+typedef struct {
+    float mx, my, ia, ib, ic, lt, xh, yh, op, r, g, b;
+} CullRec;
+
+static float clampf_ref(float v, float lo, float hi) { return v < lo ? lo : (hi < v ? hi : v); }
+
+void gso_cull_and_blend(const float* means_2d, const float* covs_2d, const float* colors,
+                        const float* opacities, const int64_t* sorted_ids,
+                        const int64_t* tile_ranges, int64_t m, int64_t p, int tiles_x,
+                        int tiles_y, int tile_size, int height, int width,
+                        float mb_contrib_floor, int cull_disabled,
+                        float transmittance_threshold, float* image, int64_t* stats) {
+    CullRec* rec = (CullRec*)malloc((size_t)(m > 0 ? m : 1) * sizeof(CullRec));
+    for (int64_t i = 0; i < m; ++i) {
+        const float a = covs_2d[4 * i], b = covs_2d[4 * i + 1], c = covs_2d[4 * i + 3];
+        const float det = fmaxf_ref(a * c - b * b, 1e-6f);
+        CullRec* r = &rec[i];
+        r->mx = means_2d[2 * i];
+        r->my = means_2d[2 * i + 1];
+        r->ia = c / det;
+        r->ib = -b / det;
+        r->ic = a / det;
+        r->op = opacities[i];
+        r->r = colors[3 * i];
+        r->g = colors[3 * i + 1];
+        r->b = colors[3 * i + 2];
+        if (r->op <= mb_contrib_floor) {
+            r->lt = 0.0f;
+            r->xh = r->yh = 0.0f;
+        } else {
+            r->lt = logf(mb_contrib_floor / r->op);
+            const float rd = sqrtf(-2.0f * r->lt);
+            r->xh = rd * sqrtf(fmaxf_ref(a, 0.0f));
+            r->yh = rd * sqrtf(fmaxf_ref(c, 0.0f));
+        }
+    }
+    int64_t dropped = 0, kept = 0;
+    int64_t lmax = 0;
+    for (int t = 0; t < tiles_x * tiles_y; ++t) {
+        const int64_t L = tile_ranges[2 * t + 1] - tile_ranges[2 * t];
+        if (L > lmax) lmax = L;
+    }
+    int64_t* lists = (int64_t*)malloc((size_t)(32 * (lmax > 0 ? lmax : 1)) * sizeof(int64_t));
+    for (int t = 0; t < tiles_x * tiles_y; ++t) {
+        const int64_t start = tile_ranges[2 * t], end = tile_ranges[2 * t + 1];
+        if (start == end) continue;
+        const int ty = t / tiles_x, tx = t % tiles_x;
+        const float txt = (float)(tx * tile_size), tyt = (float)(ty * tile_size);
+        const int py_tile = ty * tile_size, px_tile = tx * tile_size;
+        const int py_end_tile = py_tile + tile_size < height ? py_tile + tile_size : height;
+        const int px_end_tile = px_tile + tile_size < width ? px_tile + tile_size : width;
+        const int64_t L = end - start;
+        int64_t cnt[32];
+        for (int q = 0; q < 32; ++q) cnt[q] = 0;
+        for (int64_t l = 0; l < L; ++l) {
+            const int64_t g = sorted_ids[start + l];
+            const CullRec* r = &rec[g];
+            if (r->lt >= 0.0f) {
+                ++dropped;
+                continue;
+            }
+            const int mx_lo = clampi((int)floorf(((r->mx - r->xh) - txt) / 8.0f), 0, 1 << 30);
+            const int mx_hi_raw = (int)floorf(((r->mx + r->xh) - txt) / 8.0f);
+            const int my_lo = clampi((int)floorf(((r->my - r->yh) - tyt) / 4.0f), 0, 1 << 30);
+            const int my_hi_raw = (int)floorf(((r->my + r->yh) - tyt) / 4.0f);
+            const int mx_hi = mx_hi_raw < 3 ? mx_hi_raw : 3;
+            const int my_hi = my_hi_raw < 7 ? my_hi_raw : 7;
+            if (mx_lo > mx_hi || my_lo > my_hi) {
+                ++dropped;
+                continue;
+            }
+            const float thresh = -2.0f * r->lt;
+            const float ia_s = fmaxf_ref(r->ia, 1e-12f), ic_s = fmaxf_ref(r->ic, 1e-12f);
+            int any = 0;
+            for (int my = my_lo; my <= my_hi; ++my) {
+                const float v_lo = (tyt + (float)(my * 4)) - r->my;
+                const float v_hi = v_lo + 4.0f;
+                const int y_in = (v_lo <= 0.0f) && (0.0f <= v_hi);
+                const float v_fix = (v_lo > 0.0f) ? v_lo : v_hi;
+                for (int mx = mx_lo; mx <= mx_hi; ++mx) {
+                    const float u_lo = (txt + (float)(mx * 8)) - r->mx;
+                    const float u_hi = u_lo + 8.0f;
+                    const int x_in = (u_lo <= 0.0f) && (0.0f <= u_hi);
+                    float m2;
+                    if (cull_disabled || (x_in && y_in)) {
+                        m2 = 0.0f;
+                    } else {
+                        float m2v = INFINITY, m2h = INFINITY;
+                        if (!x_in) {
+                            const float uf = (u_lo > 0.0f) ? u_lo : u_hi;
+                            const float vs = clampf_ref(-r->ib * uf / ic_s, v_lo, v_hi);
+                            m2v = r->ia * uf * uf + 2.0f * r->ib * uf * vs + r->ic * vs * vs;
+                        }
+                        if (!y_in) {
+                            const float us = clampf_ref(-r->ib * v_fix / ia_s, u_lo, u_hi);
+                            m2h = r->ia * us * us + 2.0f * r->ib * us * v_fix + r->ic * v_fix * v_fix;
+                        }
+                        m2 = fminf_ref(m2v, m2h);
+                    }
+                    if (m2 <= thresh) {
+                        const int mb = (my << 2) | mx;
+                        lists[mb * lmax + cnt[mb]++] = g;
+                        any = 1;
+                        ++kept;
+                    }
+                }
+            }
+            if (!any) ++dropped;
+        }
+        for (int mb = 0; mb < 32; ++mb) {
+            if (cnt[mb] == 0) continue;
+            const int py0 = py_tile + (mb >> 2) * 4, px0 = px_tile + (mb & 3) * 8;
+            const int py1 = py0 + 4 < py_end_tile ? py0 + 4 : py_end_tile;
+            const int px1 = px0 + 8 < px_end_tile ? px0 + 8 : px_end_tile;
+            if (py0 >= py1 || px0 >= px1) continue;
+            const int h = py1 - py0, w = px1 - px0;
+            float T[32], acc[96];
+            for (int q = 0; q < h * w; ++q) T[q] = 1.0f;
+            for (int q = 0; q < 3 * h * w; ++q) acc[q] = 0.0f;
+            for (int64_t k = 0; k < cnt[mb]; ++k) {
+                const CullRec* r = &rec[lists[mb * lmax + k]];
+                for (int i = 0; i < h; ++i) {
+                    const float py = (float)(py0 + i) + 0.5f;
+                    for (int j = 0; j < w; ++j) {
+                        const float px = (float)(px0 + j) + 0.5f;
+                        const float dx = px - r->mx, dy = py - r->my;
+                        const float power =
+                            -0.5f * (r->ia * dx * dx + 2.0f * r->ib * dx * dy + r->ic * dy * dy);
+                        const float gw = expf(fminf_ref(power, 0.0f));
+                        const float alpha = fminf_ref(r->op * gw, 0.99f);
+                        const int q = i * w + j;
+                        const float tq = T[q];
+                        const float at = alpha * tq;
+                        acc[3 * q] += at * r->r;
+                        acc[3 * q + 1] += at * r->g;
+                        acc[3 * q + 2] += at * r->b;
+                        T[q] = tq * (1.0f - alpha);
+                    }
+                }
+                float tmax = 0.0f;
+                for (int q = 0; q < h * w; ++q) tmax = fmaxf_ref(tmax, T[q]);
+                if (tmax < transmittance_threshold) break;
+            }
+            for (int i = 0; i < h; ++i)
+                for (int j = 0; j < w; ++j) {
+                    const int q = i * w + j;
+                    const size_t o = (size_t)(py0 + i) * width + (px0 + j);
+                    image[3 * o] = acc[3 * q];
+                    image[3 * o + 1] = acc[3 * q + 1];
+                    image[3 * o + 2] = acc[3 * q + 2];
+                }
+        }
+    }
+    stats[0] = p;
+    stats[1] = dropped;
+    stats[2] = kept;
+    free(lists);
+    free(rec);
+}
+
 /* Host C library logf over an array (checker for the device reproduction). */
 void gso_logf_array(const float* x, float* y, int64_t n) {
     for (int64_t i = 0; i < n; ++i) y[i] = logf(x[i]);

@@ -67,6 +67,19 @@ void gso_blend(const float* means_2d, const float* covs_2d, const float* colors,
                const int64_t* tile_ranges, int64_t m, int height, int width, int tile_size,
                float* image, float* alpha_out);
 
+/*
+ * src/gsplat_cpu/cull_and_blend.cpp:316-840 cull_and_blend, scalar build (8x4-pixel
+ * microblocks, exact per-microblock cull, per-microblock stop at transmittance_threshold).
+ * image (H*W*3) must be zeroed by the caller (pixels of microblocks with no kept Gaussian
+ * are not written). stats[0..2] = pairs_in, pairs_dropped_all_mb, pairs_kept_per_mb.
+ */
+void gso_cull_and_blend(const float* means_2d, const float* covs_2d, const float* colors,
+                        const float* opacities, const int64_t* sorted_ids,
+                        const int64_t* tile_ranges, int64_t m, int64_t p, int tiles_x,
+                        int tiles_y, int tile_size, int height, int width,
+                        float mb_contrib_floor, int cull_disabled,
+                        float transmittance_threshold, float* image, int64_t* stats);
+
 /* y[i] = logf(x[i]) with the host C library (checks the device logf reproduction). */
 void gso_logf_array(const float* x, float* y, int64_t n);
 

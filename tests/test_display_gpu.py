@@ -171,8 +171,63 @@ def test_backend_plugin_stages(gd):
     gg = G()
     for k, val in T.items():
         setattr(gg, k, val)
-    be.cull_disabled = True
+    # the fused render is the reference's render_full: 32-pixel tiles, pair cull, microblock
+    # cull + blend -- checked against the oracle's chain of the same stages
     img2, stats = be.render_fused(gg, torch.from_numpy(cam.w2c), torch.from_numpy(cam.K), 256, 256)
-    assert np.abs(img2 - img).max() <= IMG_TOL
-    assert stats["num_visible"] == m2.shape[0] and stats["num_entries"] == s.shape[0]
+    cov3d = od.compute_cov3d(sc["scales"], sc["rotations"])
+    om2, ocv, od_, orad, ov = od.project_full_with_cov3d(sc["means"], cov3d, cam.w2c, cam.K, 256,
+                                                         256, sc["opacities"])
+    og, ot_, _ = od.tile_assign(om2, orad, 256, 256, 32, covs_2d=ocv, opacities=sc["opacities"][ov],
+                                contrib_floor=1.0 / 16384.0)
+    os_, org = od.sort(og, ot_, od_, 8, 8)
+    oimg, ost = od.cull_and_blend(om2, ocv, sc["colors"][ov], sc["opacities"][ov], os_, org, 8, 8,
+                                  32, 256, 256)
+    assert np.abs(img2 - oimg).max() <= IMG_TOL
+    assert stats["num_visible"] == om2.shape[0] and stats["num_entries"] == os_.shape[0]
+    for k in ("pairs_in", "pairs_dropped", "pairs_kept_per_mb"):
+        assert stats[k] == ost[k], k
     be.close()
+
+
+@pytest.mark.parametrize("H,W,tile,seed,n,floor,cull_off", [
+    (64, 48, 16, 11, 3000, 1.0 / 16384.0, False), (100, 37, 32, 12, 3000, 1.0 / 255.0, False),
+    (128, 128, 32, 13, 20000, 1.0 / 16384.0, False), (33, 65, 8, 14, 3000, 1.0 / 16384.0, True),
+    (720, 1280, 32, 15, 200000, 1.0 / 16384.0, False)])
+def test_cull_and_blend_vs_oracle(gd, H, W, tile, seed, n, floor, cull_off):
+    """Microblock cull + blend on the device against the oracle restatement (itself
+    bit-exact against the reference's compiled cull_and_blend): cull statistics exact,
+    image within 1e-4."""
+    means, scales, q, op, col, w2c, K = ragged_scene(n, H, W, seed)
+    c = od.compute_cov3d(scales, q)
+    m2, cv, d, rad, v = od.project_full_with_cov3d(means, c, w2c, K, H, W, op)
+    g, t, _ = od.tile_assign(m2, rad, H, W, tile, covs_2d=cv, opacities=op[v],
+                             contrib_floor=1.0 / 16384.0)
+    tx, ty = (W + tile - 1) // tile, (H + tile - 1) // tile
+    s, rg = od.sort(g, t, d, tx, ty)
+    for thr in (1.0 / 255.0, 1e-4):
+        io, so = od.cull_and_blend(m2, cv, col[v], op[v], s, rg, tx, ty, tile, H, W, floor,
+                                   cull_off, thr)
+        ig, sg = gd.cull_and_blend(m2, cv.reshape(-1, 4), col[v], op[v], s, rg, tx, ty, tile, H, W,
+                                   floor, cull_off, thr)
+        assert sg == so
+        assert np.abs(np_(ig) - io).max() <= IMG_TOL
+
+
+def test_render_full_matches_oracle_chain(gd):
+    """render_full (tile 32 default) = project -> pair cull -> sort -> microblock cull +
+    blend, against the same chain on the oracle, on C1."""
+    sc, cam = scenes.c1_scene(), scenes.c1_camera()
+    cov3d = od.compute_cov3d(sc["scales"], sc["rotations"])
+    img, st = gd.render_full(sc["means"], cov3d, sc["opacities"], sc["colors"], cam.w2c, cam.K,
+                             256, 256)
+    m2, cv, d, rad, v = od.project_full_with_cov3d(sc["means"], cov3d, cam.w2c, cam.K, 256, 256,
+                                                   sc["opacities"])
+    g, t, _ = od.tile_assign(m2, rad, 256, 256, 32, covs_2d=cv, opacities=sc["opacities"][v],
+                             contrib_floor=1.0 / 16384.0)
+    s, rg = od.sort(g, t, d, 8, 8)
+    io, so = od.cull_and_blend(m2, cv, sc["colors"][v], sc["opacities"][v], s, rg, 8, 8, 32, 256,
+                               256)
+    assert np.abs(img - io).max() <= IMG_TOL
+    assert st["num_visible"] == m2.shape[0] and st["num_entries"] == s.shape[0]
+    for k in ("pairs_in", "pairs_dropped", "pairs_kept_per_mb"):
+        assert st[k] == so[k], k

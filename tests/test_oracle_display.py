@@ -194,3 +194,50 @@ def test_oracle_vs_compiled_reference_ragged(H, W, tile, seed):
         io = od.blend(m2, cv, col[v], op[v], so[0], so[1], H, W, tile)
         ir = np.asarray(ref.blend(m2, cv.reshape(-1, 4), col[v], op[v], sr[0], sr[1], H, W, tile))
         assert np.array_equal(io, ir)
+
+
+@pytest.mark.parametrize("H,W,tile,seed", [(64, 48, 16, 5), (100, 37, 32, 6), (128, 128, 32, 7),
+                                           (256, 256, 16, 8)])
+def test_cull_and_blend_oracle_vs_compiled_reference(H, W, tile, seed):
+    """The microblock cull + blend restatement against the reference's compiled
+    cull_and_blend (scalar build): image and cull statistics bit-exact."""
+    ref = od.reference_module()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    means, scales, q, op, col, w2c, K = random_scene(4000, H, W, seed)
+    c = od.compute_cov3d(scales, q)
+    m2, cv, d, rad, v = od.project_full_with_cov3d(means, c, w2c, K, H, W, op)
+    g, t, _ = od.tile_assign(m2, rad, H, W, tile, covs_2d=cv, opacities=op[v],
+                             contrib_floor=1.0 / 16384.0)
+    tx, ty = (W + tile - 1) // tile, (H + tile - 1) // tile
+    s, rg = od.sort(g, t, d, tx, ty)
+    for floor in (1.0 / 16384.0, 1.0 / 255.0):
+        io, so = od.cull_and_blend(m2, cv, col[v], op[v], s, rg, tx, ty, tile, H, W, floor)
+        ir, sr = ref.cull_and_blend(m2, cv.reshape(-1, 4), col[v], op[v], s, rg, tx, ty, tile,
+                                    H, W, floor)
+        assert np.array_equal(io, np.asarray(ir))
+        assert so == {k: int(sr[k]) for k in ("pairs_in", "pairs_dropped", "pairs_kept_per_mb")}
+        assert so["pairs_kept_per_mb"] > 0
+
+
+def test_render_full_chain_matches_reference_render_full():
+    """The oracle's staged chain (project -> tile_assign with pair cull -> sort ->
+    microblock cull + blend) reproduces the reference's render_full on C1, tile 32."""
+    ref = od.reference_module()
+    if ref is None:
+        pytest.skip("oracle/_ref not built")
+    sc, cam = scenes.c1_scene(), scenes.c1_camera()
+    cov3d = od.compute_cov3d(sc["scales"], sc["rotations"])
+    img_r, st_r = ref.render_full(sc["means"], cov3d, sc["opacities"], sc["colors"], cam.w2c,
+                                  cam.K, 256, 256)
+    m2, cv, d, rad, v = od.project_full_with_cov3d(sc["means"], cov3d, cam.w2c, cam.K, 256, 256,
+                                                   sc["opacities"])
+    g, t, _ = od.tile_assign(m2, rad, 256, 256, 32, covs_2d=cv, opacities=sc["opacities"][v],
+                             contrib_floor=1.0 / 16384.0)
+    s, rg = od.sort(g, t, d, 8, 8)
+    img_o, st_o = od.cull_and_blend(m2, cv, sc["colors"][v], sc["opacities"][v], s, rg, 8, 8, 32,
+                                    256, 256)
+    assert np.array_equal(img_o, np.asarray(img_r))
+    assert int(st_r["num_visible"]) == m2.shape[0] and int(st_r["num_entries"]) == s.shape[0]
+    for k in ("pairs_in", "pairs_dropped", "pairs_kept_per_mb"):
+        assert st_o[k] == int(st_r[k]), k
