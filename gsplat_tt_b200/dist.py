@@ -3,8 +3,17 @@ in tests and on NCCL/CUDA in training).
 
 The reference has no multi-device trainer (its multi-chip mode is alternate-frame
 rendering over process pipes, render/afr.py:1-33); here every rank holds the full
-parameters, renders a contiguous share of the step's views, and one allreduce sums the
-per-Gaussian gradients, visibility counts and the ranks' error flags.
+parameters and renders a contiguous share of the step's views. The gradients are then
+combined in one of two ways:
+
+* `reduce_step_buffer`: one allreduce sums the per-Gaussian gradients, visibility counts
+  and the ranks' error flags, and every rank runs the identical sparse Adam on all rows;
+* `sharded_update` (the owner-sharded optimizer): each rank owns a contiguous range of
+  Gaussian rows; a reduce-scatter gives it the summed gradients and counts of its rows
+  only, it runs sparse Adam on those rows (its Adam moments are only ever touched there),
+  and an in-place all-gather of the parameters brings every rank's updated rows to all.
+  The same bytes cross the links as with the allreduce, but the Adam work and the moment
+  traffic are divided by the number of ranks.
 """
 from __future__ import annotations
 
@@ -31,3 +40,34 @@ def reduce_step_buffer(flat: torch.Tensor, err_slot: torch.Tensor, local_error: 
     err_slot.copy_((local_error != 0).to(err_slot.dtype).reshape(err_slot.shape))
     dist.all_reduce(flat, group=group)
     skip_out.copy_((err_slot.reshape(-1)[:1] > 0).to(torch.int32))
+
+
+def shard_rows(n: int, world: int) -> int:
+    """Rows per rank of the owner-sharded optimizer: rank r owns Gaussian rows
+    [r * rows, (r + 1) * rows); arrays are padded to world * rows rows (padding rows have
+    a zero visibility count, so Adam never updates them). A multiple of 4, so every rank's
+    first row of every group starts on a 16-byte boundary (vectorised Adam loads)."""
+    return max(4, -(-n // (4 * world)) * 4)
+
+
+def sharded_update(grad_groups, grad_shards, param_groups, local_error, err, skip_out, rank: int,
+                   world: int, adam_fn, group=None) -> None:
+    """One owner-sharded optimizer update, enqueued asynchronously on the current stream.
+
+    grad_groups / param_groups: per parameter group (and, last in grad_groups, the
+    visibility counts) a flat view of world * rows * width elements; grad_shards: the
+    matching rows * width buffers that receive this rank's reduced rows. `err` (1 float)
+    receives the number of ranks whose step failed (from `local_error`, non-zero = failed);
+    `skip_out` (int32) is 1 on every rank when any failed. adam_fn(skip_out) updates this
+    rank's parameter rows from grad_shards (and must honour skip_out). Every rank takes
+    the same collectives in the same order, also when the step is skipped."""
+    import torch.distributed as dist
+    err.copy_((local_error != 0).to(err.dtype).reshape(err.shape))
+    dist.all_reduce(err, group=group)
+    skip_out.copy_((err.reshape(-1)[:1] > 0).to(torch.int32))
+    for full, shard in zip(grad_groups, grad_shards):
+        dist.reduce_scatter_tensor(shard, full, group=group)
+    adam_fn(skip_out)
+    for full in param_groups:
+        chunk = full.numel() // world
+        dist.all_gather_into_tensor(full, full[rank * chunk:(rank + 1) * chunk], group=group)

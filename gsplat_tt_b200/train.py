@@ -7,9 +7,13 @@ rank, projection + SH -> key emission -> radix sort -> tile ranges -> forward ra
 loss -> backward raster, then one fused projection backward over all views and (on one
 GPU) the sparse Adam update, all on one CUDA stream through ``gs_train_step``.
 
-Multi-GPU (data parallel over views): each rank renders its own views; the per-Gaussian
-gradients and visibility counts -- one contiguous fp32 buffer -- are summed with an NCCL
-allreduce (torch.distributed), then every rank applies the identical sparse Adam step.
+Multi-GPU (data parallel over views): each rank renders its own views. By default the
+optimizer is owner-sharded (dist.sharded_update): the per-Gaussian gradients and
+visibility counts are reduce-scattered so each rank holds the sums of its own contiguous
+range of rows, each rank runs sparse Adam on those rows (holding Adam moments only there
+in use), and an in-place all-gather of the parameters brings every rank the updated
+rows. With ``sharded_optimizer=False`` one allreduce sums gradients + counts (one
+contiguous fp32 buffer) and every rank applies the identical sparse Adam step.
 """
 from __future__ import annotations
 
@@ -124,9 +128,13 @@ class GroupBuffer:
     the groups hold the visibility counts of a gradient buffer, so one allreduce covers
     gradients and counts."""
 
-    def __init__(self, n: int, sh_degree: int, device, extra: int = 0):
+    def __init__(self, n: int, sh_degree: int, device, extra: int = 0, rows: int | None = None):
+        """rows >= n: rows allocated per group (the owner-sharded optimizer pads every group
+        to world * rows-per-rank rows; the padding rows stay zero)."""
         self.n, self.K = n, (sh_degree + 1) ** 2
-        sizes = _group_sizes(n, self.K)
+        self.rows = n if rows is None else int(rows)
+        sizes = _group_sizes(self.rows, self.K)
+        self.widths = [s // self.rows for s in sizes]
         self.offsets = []
         off = 0
         for s in sizes:
@@ -135,15 +143,19 @@ class GroupBuffer:
         self.extra_offset = off
         self.flat = torch.zeros(off + extra, dtype=torch.float32, device=device)
         shapes = [(n, 3), (n, 3), (n, 4), (n,), (n, self.K, 3)]
-        self.views = {name: self.flat[o:o + s].view(*shape)
-                      for name, o, s, shape in zip(PARAM_NAMES, self.offsets, sizes, shapes)}
+        self.views = {name: self.flat[o:o + int(np.prod(shape))].view(*shape)
+                      for name, o, shape in zip(PARAM_NAMES, self.offsets, shapes)}
+        # every group's rows including padding, flat
+        self.padded = {name: self.flat[o:o + s] for name, o, s in zip(PARAM_NAMES, self.offsets, sizes)}
         self.extra = self.flat[off:off + extra]
 
     def __getitem__(self, k):
         return self.views[k]
 
-    def c_struct(self) -> GsGaussians:
-        return GsGaussians(*[self.views[k].data_ptr() for k in PARAM_NAMES])
+    def c_struct(self, row0: int = 0) -> GsGaussians:
+        """Group pointers, optionally starting at row `row0` of every group."""
+        return GsGaussians(*[self.views[k].data_ptr() + 4 * row0 * w
+                             for k, w in zip(PARAM_NAMES, self.widths)])
 
     def load(self, params: dict) -> None:
         for k in PARAM_NAMES:
@@ -165,7 +177,8 @@ class Trainer:
     """
 
     def __init__(self, params: dict, cfg: TrainConfig, n_views: int, height: int, width: int,
-                 pair_capacity: int | None = None, device=None, process_group=None):
+                 pair_capacity: int | None = None, device=None, process_group=None,
+                 sharded_optimizer: bool = True):
         if not torch.cuda.is_available():
             raise RuntimeError("Trainer needs a CUDA device")
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
@@ -174,19 +187,29 @@ class Trainer:
         self.n = int(np.asarray(params["means"]).shape[0]) if not isinstance(params["means"], torch.Tensor) \
             else int(params["means"].shape[0])
         self.n_views, self.H, self.W = int(n_views), int(height), int(width)
-        self.params = GroupBuffer(self.n, cfg.sh_degree, self.device)
+        self.pg = process_group
+        dist_on = torch.distributed.is_available() and torch.distributed.is_initialized()
+        self.world = torch.distributed.get_world_size(process_group) if dist_on else 1
+        self.rank = torch.distributed.get_rank(process_group) if dist_on else 0
+        self.sharded = bool(sharded_optimizer) and self.world > 1
+        from .dist import shard_rows
+        self.rows_per = shard_rows(self.n, self.world) if self.sharded else self.n
+        rows = self.rows_per * self.world if self.sharded else self.n
+        self.params = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows)
         self.params.load(params)
-        self.m = GroupBuffer(self.n, cfg.sh_degree, self.device)
-        self.v = GroupBuffer(self.n, cfg.sh_degree, self.device)
-        self.grads = GroupBuffer(self.n, cfg.sh_degree, self.device, extra=self.n + 1)
+        self.m = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows)
+        self.v = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows)
+        self.grads = GroupBuffer(self.n, cfg.sh_degree, self.device, extra=rows + 1, rows=rows)
         self.vis_counts = self.grads.extra[:self.n]
-        self.err_slot = self.grads.extra[self.n:]
+        self.err_slot = self.grads.extra[rows:]
+        if self.sharded:
+            # this rank's reduced rows of every gradient group and of the visibility counts
+            self._grad_shards = [torch.zeros(self.rows_per * w, dtype=torch.float32, device=self.device)
+                                 for w in self.grads.widths] + \
+                                [torch.zeros(self.rows_per, dtype=torch.float32, device=self.device)]
         self.losses = torch.zeros(self.n_views, dtype=torch.float32, device=self.device)
         self.pairs = torch.zeros(self.n_views, dtype=torch.int64, device=self.device)
         self.step_count = 0
-        self.pg = process_group
-        self.world = torch.distributed.get_world_size(process_group) \
-            if torch.distributed.is_available() and torch.distributed.is_initialized() else 1
         self._err_i32 = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.capacity = int(pair_capacity) if pair_capacity else 0
         self.ws = None
@@ -276,14 +299,37 @@ class Trainer:
 
     def _allreduce_and_adam(self, st) -> None:
         # error word of this rank's step (first 4 bytes at the workspace's first 256-byte
-        # boundary) rides along in the reduced buffer so every rank agrees on skipping Adam
+        # boundary) rides along so every rank agrees on skipping Adam
         off = (-self.ws.data_ptr()) % 256
         errw = self.ws[off:off + 4].view(torch.int32)
+        if self.sharded:
+            self._sharded_adam(errw, st)
+            return
         reduce_step_buffer(self.grads.flat, self.err_slot, errw, self._err_i32, self.pg)
         p, m, v, g = (b.c_struct() for b in (self.params, self.m, self.v, self.grads))
         check(lib.gs_sparse_adam(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
                                  self.vis_counts.data_ptr(), self.n, self.step_count,
                                  ctypes.byref(self.ccfg), self._err_i32.data_ptr(), st))
+
+    def _sharded_adam(self, errw, st) -> None:
+        """Owner-sharded update (dist.sharded_update): reduce-scatter gradients and counts,
+        sparse Adam on this rank's rows only, in-place all-gather of the parameters."""
+        from .dist import sharded_update
+        row0 = self.rank * self.rows_per
+        shards = self._grad_shards
+
+        def adam(skip):
+            p, m, v = (b.c_struct(row0) for b in (self.params, self.m, self.v))
+            g = GsGaussians(*[t.data_ptr() for t in shards[:5]])
+            check(lib.gs_sparse_adam(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v),
+                                     ctypes.byref(g), shards[5].data_ptr(), self.rows_per,
+                                     self.step_count, ctypes.byref(self.ccfg), skip.data_ptr(), st))
+
+        grad_groups = [self.grads.padded[k] for k in PARAM_NAMES] + \
+            [self.grads.extra[:self.rows_per * self.world]]
+        param_groups = [self.params.padded[k] for k in PARAM_NAMES]
+        sharded_update(grad_groups, shards, param_groups, errw, self.err_slot, self._err_i32,
+                       self.rank, self.world, adam, self.pg)
 
     def project_view(self, w2c, K, H, W) -> dict:
         """Projection, intersections, sorted pairs and tile ranges of one view (parity API)."""

@@ -4,8 +4,10 @@ Config ("C5"): 6,000,000 Gaussians, SH degree 3, 64-cl
 distributions of gsplat_tt_b200.scenes; 32 views of 1920x1080 (f = 1500) on a sphere of
 radius 5 looking at the origin; loss 0.8 L1 + 0.2 (1 - SSIM); sparse Adam with betas
 (0.9, 0.999), eps 1e-15 and the per-group learning rates of configs[3]. The views are split
-evenly over the ranks (strong scaling: the step's total work is fixed); gradients are summed
-with one NCCL allreduce. ``GS_BENCH_CONFIG=c4`` selects configs[3] (3M Gaussians, 8 views of
+evenly over the ranks (strong scaling: the step's total work is fixed); gradients are
+reduce-scattered to the rows' owners, each rank runs sparse Adam on its own rows and the
+parameters are all-gathered (``GS_BENCH_SHARDED=0``: one allreduce and replicated Adam
+instead). ``GS_BENCH_CONFIG=c4`` selects configs[3] (3M Gaussians, 8 views of
 1600x1056, f = 1300, radius 4) instead; ``GS_BENCH_VIEWS=k`` keeps only the first k views (for
 small ncu captures; the benchmark line then names the reduced workload).
 """
@@ -144,7 +146,9 @@ def run(args, rank: int, world: int, local: int) -> dict:
     params = scenes.cluster_scene(c["n"], sh_degree=3, seed=0)
     targets_host = view_targets(mine, rank * per)
     cfg = train_cfg()
-    tr = Trainer(params, cfg, per, H, W, device=dev)
+    # GS_BENCH_SHARDED=0: allreduce + replicated Adam instead of the owner-sharded optimizer
+    sharded = os.environ.get("GS_BENCH_SHARDED", "1") != "0"
+    tr = Trainer(params, cfg, per, H, W, device=dev, sharded_optimizer=sharded)
     del params
     cams = [(cm.w2c, cm.K, H, W) for cm in mine]
     pairs0 = tr.count_pairs(cams)
@@ -214,7 +218,10 @@ def run(args, rank: int, world: int, local: int) -> dict:
         "config": {"workload": f"{name.upper()} train step: {c['n']} Gaussians SH3, {V} views "
                                f"{W}x{H} ({per} per GPU), L1+SSIM, sparse Adam",
                    "gaussians": c["n"], "views": V, "width": W, "height": H, "tile": 16,
-                   "parallelism": f"dp{world} over views + NCCL allreduce",
+                   "parallelism": f"dp{world} over views" + (
+                       "" if world == 1 else
+                       " + NCCL reduce-scatter / all-gather, owner-sharded Adam" if tr.sharded
+                       else " + NCCL allreduce, replicated Adam"),
                    "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},
         "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
                 "h2d_bytes_per_step": int(sum(t.size * 4 for t in targets_host)),

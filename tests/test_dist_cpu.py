@@ -91,3 +91,94 @@ def test_view_slice():
     assert [view_slice(32, 4, r) for r in range(4)] == [(0, 8), (8, 16), (16, 24), (24, 32)]
     with pytest.raises(ValueError):
         view_slice(32, 3, 0)
+
+
+def _adam_rows(p, g, m, v, vis, skip, lr=0.1, b1=0.9, b2=0.999, eps=1e-8):
+    """Sparse Adam stand-in over rows (rows with a zero count are left alone)."""
+    if int(skip.item()):
+        return
+    w = p.numel() // vis.numel()
+    sel = (vis > 0).repeat_interleave(w)
+    m[sel] = b1 * m[sel] + (1 - b1) * g[sel]
+    v[sel] = b2 * v[sel] + (1 - b2) * g[sel] * g[sel]
+    p[sel] -= lr * m[sel] / (v[sel].sqrt() + eps)
+
+
+def _sharded_worker(rank, world, port, fail_rank, q):
+    from gsplat_tt_b200.dist import shard_rows, sharded_update
+    dist = _init(rank, world, port, 30)
+    n, widths = 7, (3, 4, 1)
+    rows = shard_rows(n, world)
+    total = rows * world
+    torch.manual_seed(0)
+    params0 = [torch.zeros(total * w) for w in widths]
+    for t, w in zip(params0, widths):
+        t[:n * w] = torch.randn(n * w)
+    gen = torch.Generator().manual_seed(100 + rank)
+    grads = [torch.zeros(total * w) for w in widths]
+    for t, w in zip(grads, widths):
+        t[:n * w] = torch.randn(n * w, generator=gen)
+    vis = torch.zeros(total)
+    vis[:n] = (torch.rand(n, generator=gen) > 0.3).float()
+    local_err = torch.tensor([1 if rank == fail_rank else 0], dtype=torch.int32)
+
+    # allreduce reference: every rank updates every row
+    ref_p = [t.clone() for t in params0]
+    ref_g = [t.clone() for t in grads]
+    ref_vis = vis.clone()
+    for t in ref_g + [ref_vis]:
+        dist.all_reduce(t)
+    ref_err = local_err.clone().float()
+    dist.all_reduce(ref_err)
+    ref_skip = (ref_err > 0).to(torch.int32)
+    for p, g, w in zip(ref_p, ref_g, widths):
+        _adam_rows(p, g, torch.zeros_like(p), torch.zeros_like(p), ref_vis, ref_skip)
+
+    # owner-sharded: reduce-scatter, Adam on this rank's rows, all-gather
+    params = [t.clone() for t in params0]
+    shards = [torch.zeros(rows * w) for w in widths] + [torch.zeros(rows)]
+    moments = [(torch.zeros(rows * w), torch.zeros(rows * w)) for w in widths]
+    err = torch.zeros(1)
+    skip = torch.zeros(1, dtype=torch.int32)
+
+    def adam(skip_flag):
+        for p, g, (m, v), w in zip(params, shards, moments, widths):
+            own = p[rank * rows * w:(rank + 1) * rows * w]
+            _adam_rows(own, g, m, v, shards[-1], skip_flag)
+
+    sharded_update(grads + [vis], shards, params, local_err, err, skip, rank, world, adam)
+    diff = max(float((a - b).abs().max()) for a, b in zip(params, ref_p))
+    pad_ok = all(float(p[n * w:].abs().max()) == 0.0 for p, w in zip(params, widths))
+    q.put((rank, diff, pad_ok, int(skip.item()), float(err.item()),
+           max(float((a - b).abs().max()) for a, b in zip(params, params0))))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_rank", [-1, 0])
+def test_sharded_update_matches_allreduce_update(fail_rank):
+    """Reduce-scatter + owner Adam + all-gather gives every rank the same parameters as the
+    allreduce + replicated Adam; a failed rank makes every rank skip the update."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_sharded_worker, args=(r, 2, port, fail_rank, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(2)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for rank, diff, pad_ok, skip, err, moved in res:
+        assert diff <= 1e-6, (rank, diff)
+        assert pad_ok
+        assert skip == (1 if fail_rank >= 0 else 0) and err == (1.0 if fail_rank >= 0 else 0.0)
+        assert (moved == 0.0) == (fail_rank >= 0)
+
+
+def test_shard_rows():
+    from gsplat_tt_b200.dist import shard_rows
+    assert shard_rows(7, 2) == 4 and shard_rows(8, 2) == 4 and shard_rows(9, 2) == 8
+    assert shard_rows(1, 8) == 4 and shard_rows(6_000_001, 8) % 4 == 0
+    for n in (1, 5, 1000, 12345):
+        for w in (1, 2, 4, 8):
+            assert shard_rows(n, w) * w >= n
