@@ -1133,6 +1133,89 @@ k_sparse_adam(AdamParams A, const float* __restrict__ vis, const unsigned int* _
     }
 }
 
+// ------------------------------------------------ owner-sharded Adam through NVSwitch multicast
+//
+// Multi-GPU update with the reduction and the broadcast inside the Adam kernel. Every GPU
+// holds its partial gradients (its own views) in a buffer bound to an NVLink multicast
+// object, and the parameters likewise. The GPU that owns a range of rows reads each
+// gradient element with multimem.ld_reduce -- the switch returns the sum over all GPUs --
+// updates the row with its own moments, and writes the new parameter with multimem.st,
+// which lands in every GPU's copy. The gradient sums cross the links once (to the owner)
+// and each updated parameter once (out of the owner); no gradient or parameter is staged.
+// The caller orders the kernel between two cross-GPU synchronisation points: all partial
+// gradients written before it starts, and every GPU's kernel finished before any GPU
+// reads parameters or overwrites gradients again.
+
+__device__ __forceinline__ float4 mc_ld_add_v4(const float* a) {
+    float4 r;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+                 : "l"(a)
+                 : "memory");
+    return r;
+}
+
+__device__ __forceinline__ void mc_st_v4(float* a, const float4& v) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(a),
+                 "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
+}
+
+// Stores through the multicast alias are made visible system-wide before the kernel ends.
+__device__ __forceinline__ void mc_release() {
+    asm volatile("fence.proxy.alias;" ::: "memory");
+    __threadfence_system();
+}
+
+// counts[i] = sum over GPUs of counts_mc[i] for this GPU's rows (rows4 float4s).
+__global__ void __launch_bounds__(256)
+k_mc_reduce_counts(const float* __restrict__ counts_mc, float* __restrict__ counts,
+                   uint32_t rows4, const unsigned int* __restrict__ skip) {
+    if (*skip != 0u) return;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < rows4; i += stride)
+        reinterpret_cast<float4*>(counts)[i] = mc_ld_add_v4(counts_mc + 4ull * i);
+}
+
+// One parameter group of this GPU's rows: G.p / G.m / G.v point at the rows' local copies,
+// g_mc / p_mc at the same rows through the gradient / parameter multicast mappings. The
+// group's element count is a multiple of 4 and every pointer 16-byte aligned. The update
+// arithmetic is adam_update's, element for element, as in k_sparse_adam.
+template <int W>
+__global__ void __launch_bounds__(256)
+k_sparse_adam_mc(AdamParams A, const float* __restrict__ vis, const unsigned int* __restrict__ skip,
+                 int group, const float* g_mc, float* p_mc) {
+    if (*skip != 0u) return;
+    const AdamGroup& G = A.grp[group];
+    const uint32_t n4 = (uint32_t)(G.count / 4);
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+        const uint32_t e = 4u * i;
+        const uint32_t r0 = e / W, r3 = (e + 3u) / W;
+        bool any = false;
+        for (uint32_t r = r0; r <= r3; ++r) any |= vis[r] > 0.0f;
+        if (!any) continue;
+        const float4 g4 = mc_ld_add_v4(g_mc + e);
+        float4 p4 = reinterpret_cast<const float4*>(G.p)[i];
+        float4 m4 = reinterpret_cast<const float4*>(G.m)[i];
+        float4 v4 = reinterpret_cast<const float4*>(G.v)[i];
+        float* pp = &p4.x;
+        float* mm = &m4.x;
+        float* vv = &v4.x;
+        const float* gg = &g4.x;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t ek = e + (uint32_t)k;
+            const uint32_t row = ek / W;
+            if (vis[row] > 0.0f) adam_update(A, G, (int)(ek - row * W), gg[k], pp[k], mm[k], vv[k]);
+        }
+        mc_st_v4(p_mc + e, p4);
+        reinterpret_cast<float4*>(G.m)[i] = m4;
+        reinterpret_cast<float4*>(G.v)[i] = v4;
+    }
+    mc_release();
+}
+
 // ------------------------------------------------------------------ workspace layout
 
 // Per-view scratch. A step's views are spread over kLanes lanes, each with its own stream
@@ -1649,6 +1732,60 @@ extern "C" gs_status gs_sparse_adam(const gs_gaussians* params, const gs_gaussia
     if (n == 0) return GS_OK;
     const AdamParams A = make_adam(params, exp_avg, exp_avg_sq, grads, n, step, cfg);
     return launch_adam(A, vis_counts, error_word, (cudaStream_t)stream);
+}
+
+extern "C" gs_status gs_sparse_adam_multicast(const gs_gaussians* params,
+                                              const gs_gaussians* params_mc,
+                                              const gs_gaussians* exp_avg,
+                                              const gs_gaussians* exp_avg_sq,
+                                              const gs_gaussians* grads_mc,
+                                              const float* vis_counts_mc, float* vis_scratch,
+                                              int64_t rows, int64_t step,
+                                              const gs_train_config* cfg,
+                                              const unsigned int* skip, void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(params && params_mc && exp_avg && exp_avg_sq && grads_mc && vis_counts_mc &&
+                 vis_scratch && skip && rows >= 0 && step >= 0,
+                 "gs_sparse_adam_multicast: bad arguments");
+    GS_ARG_CHECK(rows % 4 == 0 && rows < (1ll << 30),
+                 "gs_sparse_adam_multicast: rows must be a multiple of 4 below 2^30");
+    if (rows == 0) return GS_OK;
+    const AdamParams A = make_adam(params, exp_avg, exp_avg_sq, grads_mc, rows, step, cfg);
+    const float* Gm[5] = {grads_mc->means, grads_mc->log_scales, grads_mc->quats,
+                          grads_mc->opacity_logits, grads_mc->sh};
+    float* Pm[5] = {params_mc->means, params_mc->log_scales, params_mc->quats,
+                    params_mc->opacity_logits, params_mc->sh};
+    uintptr_t all = (uintptr_t)vis_counts_mc | (uintptr_t)vis_scratch;
+    for (int i = 0; i < 5; ++i)
+        all |= (uintptr_t)A.grp[i].p | (uintptr_t)A.grp[i].m | (uintptr_t)A.grp[i].v |
+               (uintptr_t)Gm[i] | (uintptr_t)Pm[i];
+    GS_ARG_CHECK((all & 15u) == 0, "gs_sparse_adam_multicast: every pointer must be 16-byte aligned");
+    KernelTimer kt("sparse_adam", st);
+    const uint32_t rows4 = (uint32_t)(rows / 4);
+    k_mc_reduce_counts<<<(unsigned)std::min<int64_t>(div_up(rows4, 256), kNumSMs * 8), 256, 0, st>>>(
+        vis_counts_mc, vis_scratch, rows4, skip);
+    GS_CHECK_LAUNCH();
+    for (int i = 0; i < 5; ++i) {
+        const AdamGroup& G = A.grp[i];
+        const unsigned int blocks =
+            (unsigned int)std::min<int64_t>(div_up(div_up(G.count, 4), 256), kNumSMs * 16);
+#define GS_ADAM_MC(W_) k_sparse_adam_mc<W_><<<blocks, 256, 0, st>>>(A, vis_scratch, skip, i, Gm[i], Pm[i])
+        switch (G.width) {
+            case 1: GS_ADAM_MC(1); break;
+            case 3: GS_ADAM_MC(3); break;
+            case 4: GS_ADAM_MC(4); break;
+            case 12: GS_ADAM_MC(12); break;
+            case 27: GS_ADAM_MC(27); break;
+            case 48: GS_ADAM_MC(48); break;
+            default: set_error("sparse Adam: unsupported row width %d", G.width); return GS_ERR_ARG;
+        }
+#undef GS_ADAM_MC
+        GS_CHECK_LAUNCH();
+    }
+    return GS_OK;
 }
 
 extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussians* exp_avg,

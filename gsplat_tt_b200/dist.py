@@ -62,12 +62,40 @@ def sharded_update(grad_groups, grad_shards, param_groups, local_error, err, ski
     rank's parameter rows from grad_shards (and must honour skip_out). Every rank takes
     the same collectives in the same order, also when the step is skipped."""
     import torch.distributed as dist
+    from torch.distributed.distributed_c10d import _coalescing_manager
     err.copy_((local_error != 0).to(err.dtype).reshape(err.shape))
     dist.all_reduce(err, group=group)
     skip_out.copy_((err.reshape(-1)[:1] > 0).to(torch.int32))
-    for full, shard in zip(grad_groups, grad_shards):
-        dist.reduce_scatter_tensor(shard, full, group=group)
+    # each set of per-group collectives goes to the backend as one coalesced call (one NCCL
+    # group launch instead of one launch per parameter group)
+    with _coalescing_manager(group=group):
+        for full, shard in zip(grad_groups, grad_shards):
+            dist.reduce_scatter_tensor(shard, full, group=group)
     adam_fn(skip_out)
-    for full in param_groups:
-        chunk = full.numel() // world
-        dist.all_gather_into_tensor(full, full[rank * chunk:(rank + 1) * chunk], group=group)
+    with _coalescing_manager(group=group):
+        for full in param_groups:
+            chunk = full.numel() // world
+            dist.all_gather_into_tensor(full, full[rank * chunk:(rank + 1) * chunk], group=group)
+
+
+def _attr(h, name):
+    v = getattr(h, name)
+    return v() if callable(v) else v
+
+
+def symmetric_buffer(numel: int, device, group=None):
+    """A zeroed fp32 buffer of `numel` elements in CUDA symmetric memory -- mapped by every
+    rank of `group` and bound to an NVLink multicast object when the GPUs support one --
+    and its multicast address (None without multicast support). Collective: every rank
+    calls it with the same `numel`, in the same order. The buffer is its own allocation, so
+    the multicast address maps exactly the tensor's bytes."""
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm
+    t = symm._SymmetricMemory.empty_strided_p2p((numel,), (1,), torch.float32, torch.device(device))
+    t.zero_()
+    h = symm.rendezvous(t, group if group is not None else dist.group.WORLD)
+    ok = (bool(_attr(h, "has_multicast_support")) and int(_attr(h, "offset")) == 0
+          and int(_attr(h, "buffer_ptrs")[_attr(h, "rank")]) == t.data_ptr()
+          and int(_attr(h, "buffer_size")) >= 4 * numel)
+    mc = int(_attr(h, "multicast_ptr")) if ok else 0
+    return t, h, (mc if mc else None)

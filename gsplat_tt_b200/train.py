@@ -67,6 +67,8 @@ lib.gs_train_count_pairs.restype = ctypes.c_int
 lib.gs_train_count_pairs.argtypes = [_G, _i64, _C, _i32, _CFG, ctypes.POINTER(_i64), _vp, _sz, _vp]
 lib.gs_sparse_adam.restype = ctypes.c_int
 lib.gs_sparse_adam.argtypes = [_G, _G, _G, _G, _vp, _i64, _i64, _CFG, _vp, _vp]
+lib.gs_sparse_adam_multicast.restype = ctypes.c_int
+lib.gs_sparse_adam_multicast.argtypes = [_G, _G, _G, _G, _G, _vp, _vp, _i64, _i64, _CFG, _vp, _vp]
 lib.gs_train_project_view.restype = ctypes.c_int
 lib.gs_train_project_view.argtypes = [_G, _i64, _C, _CFG, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _vp, _vp, _i64, ctypes.POINTER(_i64), _vp, _sz, _vp]
@@ -128,9 +130,11 @@ class GroupBuffer:
     the groups hold the visibility counts of a gradient buffer, so one allreduce covers
     gradients and counts."""
 
-    def __init__(self, n: int, sh_degree: int, device, extra: int = 0, rows: int | None = None):
+    def __init__(self, n: int, sh_degree: int, device, extra: int = 0, rows: int | None = None,
+                 alloc=None):
         """rows >= n: rows allocated per group (the owner-sharded optimizer pads every group
-        to world * rows-per-rank rows; the padding rows stay zero)."""
+        to world * rows-per-rank rows; the padding rows stay zero). alloc(numel), when given,
+        returns the zeroed flat fp32 buffer (symmetric memory for multicast updates)."""
         self.n, self.K = n, (sh_degree + 1) ** 2
         self.rows = n if rows is None else int(rows)
         sizes = _group_sizes(self.rows, self.K)
@@ -141,7 +145,8 @@ class GroupBuffer:
             self.offsets.append(off)
             off += (s + 3) // 4 * 4
         self.extra_offset = off
-        self.flat = torch.zeros(off + extra, dtype=torch.float32, device=device)
+        self.flat = torch.zeros(off + extra, dtype=torch.float32, device=device) if alloc is None \
+            else alloc(off + extra)
         shapes = [(n, 3), (n, 3), (n, 4), (n,), (n, self.K, 3)]
         self.views = {name: self.flat[o:o + int(np.prod(shape))].view(*shape)
                       for name, o, shape in zip(PARAM_NAMES, self.offsets, shapes)}
@@ -152,10 +157,11 @@ class GroupBuffer:
     def __getitem__(self, k):
         return self.views[k]
 
-    def c_struct(self, row0: int = 0) -> GsGaussians:
-        """Group pointers, optionally starting at row `row0` of every group."""
-        return GsGaussians(*[self.views[k].data_ptr() + 4 * row0 * w
-                             for k, w in zip(PARAM_NAMES, self.widths)])
+    def c_struct(self, row0: int = 0, base: int | None = None) -> GsGaussians:
+        """Group pointers, optionally starting at row `row0` of every group; `base` replaces
+        the buffer's own address (e.g. by its multicast address)."""
+        b = self.flat.data_ptr() if base is None else base
+        return GsGaussians(*[b + 4 * (o + row0 * w) for o, w in zip(self.offsets, self.widths)])
 
     def load(self, params: dict) -> None:
         for k in PARAM_NAMES:
@@ -178,7 +184,7 @@ class Trainer:
 
     def __init__(self, params: dict, cfg: TrainConfig, n_views: int, height: int, width: int,
                  pair_capacity: int | None = None, device=None, process_group=None,
-                 sharded_optimizer: bool = True):
+                 sharded_optimizer: bool = True, multicast: bool = True):
         if not torch.cuda.is_available():
             raise RuntimeError("Trainer needs a CUDA device")
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
@@ -195,11 +201,30 @@ class Trainer:
         from .dist import shard_rows
         self.rows_per = shard_rows(self.n, self.world) if self.sharded else self.n
         rows = self.rows_per * self.world if self.sharded else self.n
-        self.params = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows)
+        # parameters and gradients in symmetric memory when the update can go through NVLink
+        # multicast (gs_sparse_adam_multicast); otherwise NCCL collectives
+        self._symm = {}
+        alloc = {}
+        if self.sharded and multicast and self.device.type == "cuda":
+            from .dist import symmetric_buffer
+
+            def symm_alloc(key):
+                def f(numel):
+                    t, h, mc = symmetric_buffer(numel, self.device, self.pg)
+                    self._symm[key] = (h, mc)
+                    return t
+                return f
+            alloc = {"params": symm_alloc("params"), "grads": symm_alloc("grads")}
+        self.params = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows, alloc=alloc.get("params"))
         self.params.load(params)
         self.m = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows)
         self.v = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows)
-        self.grads = GroupBuffer(self.n, cfg.sh_degree, self.device, extra=rows + 1, rows=rows)
+        self.grads = GroupBuffer(self.n, cfg.sh_degree, self.device, extra=rows + 1, rows=rows,
+                                 alloc=alloc.get("grads"))
+        self.multicast = bool(self._symm) and all(mc for _, mc in self._symm.values())
+        if self.multicast:
+            self._vis_scratch = torch.zeros(self.rows_per, dtype=torch.float32, device=self.device)
+            self._fence = torch.zeros(1, dtype=torch.float32, device=self.device)
         self.vis_counts = self.grads.extra[:self.n]
         self.err_slot = self.grads.extra[rows:]
         if self.sharded:
@@ -302,6 +327,9 @@ class Trainer:
         # boundary) rides along so every rank agrees on skipping Adam
         off = (-self.ws.data_ptr()) % 256
         errw = self.ws[off:off + 4].view(torch.int32)
+        if self.multicast:
+            self._multicast_adam(errw, st)
+            return
         if self.sharded:
             self._sharded_adam(errw, st)
             return
@@ -330,6 +358,28 @@ class Trainer:
         param_groups = [self.params.padded[k] for k in PARAM_NAMES]
         sharded_update(grad_groups, shards, param_groups, errw, self.err_slot, self._err_i32,
                        self.rank, self.world, adam, self.pg)
+
+    def _multicast_adam(self, errw, st) -> None:
+        """Owner-sharded update through NVLink multicast (gs_sparse_adam_multicast): the
+        error allreduce doubles as the barrier after which every GPU's partial gradients
+        are complete; the one-float allreduce after the update keeps every GPU from reading
+        parameters or rewriting its gradients before all updates have landed."""
+        import torch.distributed as dist
+        self.err_slot.copy_((errw != 0).to(torch.float32).reshape(1))
+        dist.all_reduce(self.err_slot, group=self.pg)
+        self._err_i32.copy_((self.err_slot > 0).to(torch.int32))
+        row0 = self.rank * self.rows_per
+        mc_p, mc_g = self._symm["params"][1], self._symm["grads"][1]
+        p, m, v = (b.c_struct(row0) for b in (self.params, self.m, self.v))
+        pm = self.params.c_struct(row0, base=mc_p)
+        gm = self.grads.c_struct(row0, base=mc_g)
+        vis_mc = mc_g + 4 * (self.grads.extra_offset + row0)
+        check(lib.gs_sparse_adam_multicast(ctypes.byref(p), ctypes.byref(pm), ctypes.byref(m),
+                                           ctypes.byref(v), ctypes.byref(gm), vis_mc,
+                                           self._vis_scratch.data_ptr(), self.rows_per,
+                                           self.step_count, ctypes.byref(self.ccfg),
+                                           self._err_i32.data_ptr(), st))
+        dist.all_reduce(self._fence, group=self.pg)
 
     def project_view(self, w2c, K, H, W) -> dict:
         """Projection, intersections, sorted pairs and tile ranges of one view (parity API)."""

@@ -148,7 +148,9 @@ def run(args, rank: int, world: int, local: int) -> dict:
     cfg = train_cfg()
     # GS_BENCH_SHARDED=0: allreduce + replicated Adam instead of the owner-sharded optimizer
     sharded = os.environ.get("GS_BENCH_SHARDED", "1") != "0"
-    tr = Trainer(params, cfg, per, H, W, device=dev, sharded_optimizer=sharded)
+    # GS_BENCH_MULTICAST=0: the sharded update through NCCL instead of NVLink multicast
+    multicast = os.environ.get("GS_BENCH_MULTICAST", "1") != "0"
+    tr = Trainer(params, cfg, per, H, W, device=dev, sharded_optimizer=sharded, multicast=multicast)
     del params
     cams = [(cm.w2c, cm.K, H, W) for cm in mine]
     pairs0 = tr.count_pairs(cams)
@@ -220,6 +222,8 @@ def run(args, rank: int, world: int, local: int) -> dict:
                    "gaussians": c["n"], "views": V, "width": W, "height": H, "tile": 16,
                    "parallelism": f"dp{world} over views" + (
                        "" if world == 1 else
+                       " + owner-sharded Adam with NVLink-multicast gradient sum and parameter "
+                       "broadcast (gs_sparse_adam_multicast)" if tr.multicast else
                        " + NCCL reduce-scatter / all-gather, owner-sharded Adam" if tr.sharded
                        else " + NCCL allreduce, replicated Adam"),
                    "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},

@@ -305,6 +305,27 @@ gs_status gs_sparse_adam(const gs_gaussians* params, const gs_gaussians* exp_avg
                          const gs_train_config* cfg, const unsigned int* error_word,
                          void* stream);
 
+/* Owner-sharded sparse Adam of one GPU of a multi-GPU step, with the gradient sum and the
+ * parameter broadcast done through NVLink multicast (NVSwitch) inside the kernels. Replaces
+ * the allreduce + gs_sparse_adam pair of the view-parallel trainer (the reference has no
+ * multi-GPU trainer; its per-step optimizer is gsplat/train_oracle.py:434-470).
+ *   params / exp_avg / exp_avg_sq: this GPU's `rows` rows (local memory);
+ *   params_mc: the same parameter rows through the parameters' multicast mapping (the
+ *     update is written there, i.e. into every GPU's copy);
+ *   grads_mc / vis_counts_mc: the same rows of every GPU's partial gradients / visibility
+ *     counts through their multicast mapping (read as sums over the GPUs);
+ *   vis_scratch: `rows` floats of local device scratch (receives the summed counts);
+ *   skip: device word, non-zero = skip the update (a failed step on any GPU).
+ * rows is a multiple of 4 and every pointer 16-byte aligned. The caller synchronises the
+ * GPUs before the call (every partial gradient written) and after it (no GPU reads the
+ * parameters or rewrites its gradients while another is still in the call). */
+gs_status gs_sparse_adam_multicast(const gs_gaussians* params, const gs_gaussians* params_mc,
+                                   const gs_gaussians* exp_avg, const gs_gaussians* exp_avg_sq,
+                                   const gs_gaussians* grads_mc, const float* vis_counts_mc,
+                                   float* vis_scratch, int64_t rows, int64_t step,
+                                   const gs_train_config* cfg, const unsigned int* skip,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif
