@@ -78,24 +78,25 @@ def sharded_update(grad_groups, grad_shards, param_groups, local_error, err, ski
             dist.all_gather_into_tensor(full, full[rank * chunk:(rank + 1) * chunk], group=group)
 
 
-def _attr(h, name):
-    v = getattr(h, name)
-    return v() if callable(v) else v
-
 
 def symmetric_buffer(numel: int, device, group=None):
     """A zeroed fp32 buffer of `numel` elements in CUDA symmetric memory -- mapped by every
     rank of `group` and bound to an NVLink multicast object when the GPUs support one --
-    and its multicast address (None without multicast support). Collective: every rank
-    calls it with the same `numel`, in the same order. The buffer is its own allocation, so
-    the multicast address maps exactly the tensor's bytes."""
+    its handle, and its multicast address (None without multicast support). Collective:
+    every rank calls it with the same `numel`, in the same order. The buffer is its own
+    allocation (not carved from a pool), so the multicast address maps the tensor's bytes
+    from its first one; that is checked through the handle's view of this rank's buffer."""
     import torch.distributed as dist
     import torch.distributed._symmetric_memory as symm
-    t = symm._SymmetricMemory.empty_strided_p2p((numel,), (1,), torch.float32, torch.device(device))
+    from torch._C._autograd import DeviceType
+    device = torch.device(device)
+    t = symm._SymmetricMemory.empty_strided_p2p((numel,), (1,), torch.float32, device)
     t.zero_()
-    h = symm.rendezvous(t, group if group is not None else dist.group.WORLD)
-    ok = (bool(_attr(h, "has_multicast_support")) and int(_attr(h, "offset")) == 0
-          and int(_attr(h, "buffer_ptrs")[_attr(h, "rank")]) == t.data_ptr()
-          and int(_attr(h, "buffer_size")) >= 4 * numel)
-    mc = int(_attr(h, "multicast_ptr")) if ok else 0
+    pg = group if group is not None else dist.group.WORLD
+    symm.enable_symm_mem_for_group(pg.group_name)
+    h = symm.rendezvous(t, pg)
+    ok = (symm._SymmetricMemory.has_multicast_support(DeviceType.CUDA, device.index)
+          and int(h.buffer_ptrs[h.rank]) == t.data_ptr()
+          and int(h.buffer_size) >= 4 * numel)
+    mc = int(h.multicast_ptr) if ok else 0
     return t, h, (mc if mc else None)

@@ -182,3 +182,55 @@ def test_shard_rows():
     for n in (1, 5, 1000, 12345):
         for w in (1, 2, 4, 8):
             assert shard_rows(n, w) * w >= n
+
+
+class _FakeHandle:
+    """Stands in for torch's symmetric-memory handle with the interface of its type stub
+    (properties rank / buffer_ptrs / buffer_size / multicast_ptr)."""
+
+    def __init__(self, t, mc):
+        self._t, self._mc = t, mc
+
+    @property
+    def rank(self):
+        return 0
+
+    @property
+    def buffer_ptrs(self):
+        return [self._t.data_ptr()]
+
+    @property
+    def buffer_size(self):
+        return self._t.numel() * 4
+
+    @property
+    def multicast_ptr(self):
+        return self._mc
+
+
+@pytest.mark.parametrize("supported", [True, False])
+def test_symmetric_buffer_host_logic(monkeypatch, supported):
+    """symmetric_buffer against a fake of the symmetric-memory API (the real one needs CUDA):
+    the static multicast query takes (device type, index), the handle's fields are properties."""
+    import torch.distributed._symmetric_memory as symm
+    from gsplat_tt_b200 import dist as gd
+
+    class FakeSM:
+        @staticmethod
+        def empty_strided_p2p(size, stride, dtype, device, group_name=None, alloc_id=None):
+            assert stride == (1,) and dtype == torch.float32
+            return torch.full(size, 7.0)
+
+        @staticmethod
+        def has_multicast_support(device_type, device_idx):
+            assert isinstance(device_idx, int)
+            return supported
+
+    monkeypatch.setattr(symm, "_SymmetricMemory", FakeSM)
+    monkeypatch.setattr(symm, "rendezvous", lambda t, g: _FakeHandle(t, 0x7F0000000000))
+    monkeypatch.setattr(symm, "enable_symm_mem_for_group", lambda name: None)
+    monkeypatch.setattr(torch.distributed, "group",
+                        type("G", (), {"WORLD": type("PG", (), {"group_name": "0"})()}))
+    t, h, mc = gd.symmetric_buffer(16, "cpu:0")
+    assert t.numel() == 16 and float(t.abs().max()) == 0.0  # zeroed
+    assert mc == (0x7F0000000000 if supported else None)

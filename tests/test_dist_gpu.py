@@ -65,6 +65,10 @@ def _worker(rank, world, port, q):
                     for k in ref)
         q.put((rank, diff, moved, used_mc))
         dist.barrier()
+    except Exception:  # report at once instead of leaving the parent waiting on the queue
+        import traceback
+        q.put((rank, "error", traceback.format_exc(), None))
+        raise
     finally:
         dist.destroy_process_group()
 
@@ -77,9 +81,18 @@ def test_sharded_optimizer_matches_allreduce_on_two_gpus():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=300) for _ in range(2)]
+    res = []
+    while len(res) < 2:
+        res.append(q.get(timeout=300))
+        if res[-1][1] == "error":  # the other rank ends through its process-group timeout
+            break
     for p in procs:
         p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    errors = [r for r in res if r[1] == "error"]
+    assert not errors, errors[0][2]
+    for p in procs:
         assert p.exitcode == 0
     for rank, diff, moved, used_mc in res:
         print(f"rank {rank}: multicast update {'used' if used_mc else 'unavailable'}; "
