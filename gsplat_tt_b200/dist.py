@@ -92,9 +92,7 @@ def symmetric_buffer(numel: int, device, group=None):
     device = torch.device(device)
     t = symm._SymmetricMemory.empty_strided_p2p((numel,), (1,), torch.float32, device)
     t.zero_()
-    pg = group if group is not None else dist.group.WORLD
-    symm.enable_symm_mem_for_group(pg.group_name)
-    h = symm.rendezvous(t, pg)
+    h = symm.rendezvous(t, group if group is not None else dist.group.WORLD)
     ok = (symm._SymmetricMemory.has_multicast_support(DeviceType.CUDA, device.index)
           and int(h.buffer_ptrs[h.rank]) == t.data_ptr()
           and int(h.buffer_size) >= 4 * numel)

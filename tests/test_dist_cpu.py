@@ -228,7 +228,6 @@ def test_symmetric_buffer_host_logic(monkeypatch, supported):
 
     monkeypatch.setattr(symm, "_SymmetricMemory", FakeSM)
     monkeypatch.setattr(symm, "rendezvous", lambda t, g: _FakeHandle(t, 0x7F0000000000))
-    monkeypatch.setattr(symm, "enable_symm_mem_for_group", lambda name: None)
     monkeypatch.setattr(torch.distributed, "group",
                         type("G", (), {"WORLD": type("PG", (), {"group_name": "0"})()}))
     t, h, mc = gd.symmetric_buffer(16, "cpu:0")

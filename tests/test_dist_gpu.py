@@ -98,5 +98,6 @@ def test_sharded_optimizer_matches_allreduce_on_two_gpus():
         print(f"rank {rank}: multicast update {'used' if used_mc else 'unavailable'}; "
               f"max diff vs allreduce {diff}")
         assert moved > 0.0, "Adam did not update the parameters"
-        # two ranks: a + b is the same in any order, so the paths agree bit for bit
-        assert diff["multicast"] == 0.0 and diff["nccl"] == 0.0, (rank, diff)
+        # the sums of two ranks are order-free, but the backward rasteriser accumulates
+        # per-Gaussian gradients with float atomics, so two runs differ in the last bits
+        assert diff["multicast"] <= 1e-6 and diff["nccl"] <= 1e-6, (rank, diff)
