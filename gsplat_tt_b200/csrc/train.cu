@@ -830,16 +830,18 @@ constexpr int kParamStride = kParamThreads + 1;  // shared row stride: consecuti
 
 template <int DEG>
 __global__ void __launch_bounds__(kParamThreads, 4)
-k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCfg cfg,
-            const float* __restrict__ grad2d, const uint64_t* __restrict__ touch, GMut G) {
+k_param_bwd(GConst P, int64_t n, int64_t row_begin, int64_t row_end, const TCam* __restrict__ cams,
+            int n_views, TCfg cfg, const float* __restrict__ grad2d,
+            const uint64_t* __restrict__ touch, GMut G) {
+    // rows [row_begin, row_end) of the n Gaussians (n is the stride of the per-view arrays)
     constexpr int K = (DEG + 1) * (DEG + 1);
     constexpr int ROW = 3 * K;
     extern __shared__ float s_param[];
     float* s_sh = s_param;                          // [ROW][kParamStride]
     float* s_gsh = s_param + ROW * kParamStride;    // [ROW][kParamStride]
     const int tid = threadIdx.x;
-    const int64_t g0 = (int64_t)blockIdx.x * kParamThreads;
-    const int rows = (int)min((int64_t)kParamThreads, n - g0);
+    const int64_t g0 = row_begin + (int64_t)blockIdx.x * kParamThreads;
+    const int rows = (int)min((int64_t)kParamThreads, row_end - g0);
     for (int i = tid; i < rows * ROW; i += kParamThreads) {
         const int t = i / ROW, c = i - t * ROW;
         s_sh[c * kParamStride + t] = P.sh[g0 * ROW + i];
@@ -847,7 +849,7 @@ k_param_bwd(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCf
     for (int c = 0; c < ROW; ++c) s_gsh[c * kParamStride + tid] = 0.0f;
     __syncthreads();
     const int64_t g = g0 + tid;
-    if (g < n) {
+    if (g < row_end) {
         const uint64_t mask = touch[g];
         double gm[3] = {0.0, 0.0, 0.0};
         double G3[6] = {0.0, 0.0, 0.0, 0.0, 0.0, 0.0};  // 00 01 02 11 12 22
@@ -1734,6 +1736,35 @@ extern "C" gs_status gs_sparse_adam(const gs_gaussians* params, const gs_gaussia
     return launch_adam(A, vis_counts, error_word, (cudaStream_t)stream);
 }
 
+// Projection backward of rows [row_begin, row_end) from the per-view 2D gradients that
+// the step's views left in the workspace.
+static gs_status launch_param_bwd(const gs_gaussians* params, const gs_gaussians* grads, int64_t n,
+                                  int64_t row_begin, int64_t row_end, int n_views,
+                                  const gs_train_config& cfg, int H, int W, const TrainWs& L,
+                                  cudaStream_t st) {
+    if (row_end <= row_begin) return GS_OK;
+    KernelTimer kt("param_bwd", st);
+    const GConst P = gconst(params);
+    const TCfg c = make_tcfg(cfg, H, W);
+    GMut G{grads->means, grads->log_scales, grads->quats, grads->opacity_logits, grads->sh};
+    const unsigned int nb = div_up(row_end - row_begin, kParamThreads);
+    const int K = (cfg.sh_degree + 1) * (cfg.sh_degree + 1);
+    const size_t smem = 2 * (size_t)3 * K * kParamStride * sizeof(float);
+#define GS_PBWD(D_) k_param_bwd<D_><<<nb, kParamThreads, smem, st>>>(P, n, row_begin, row_end, L.cams, n_views, c, L.grad2d, L.touch, G)
+    switch (cfg.sh_degree) {
+        case 0: GS_PBWD(0); break;
+        case 1: GS_PBWD(1); break;
+        case 2: GS_PBWD(2); break;
+        default:
+            GS_CUDA_CHECK(cudaFuncSetAttribute(k_param_bwd<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+            GS_PBWD(3);
+            break;
+    }
+#undef GS_PBWD
+    GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
 extern "C" gs_status gs_sparse_adam_multicast(const gs_gaussians* params,
                                               const gs_gaussians* params_mc,
                                               const gs_gaussians* exp_avg,
@@ -1788,6 +1819,41 @@ extern "C" gs_status gs_sparse_adam_multicast(const gs_gaussians* params,
     return GS_OK;
 }
 
+extern "C" gs_status gs_train_param_backward(const gs_gaussians* params,
+                                             const gs_gaussians* grads, int64_t n,
+                                             int64_t row_begin, int64_t row_end,
+                                             const gs_camera* cams, int32_t n_views,
+                                             const gs_train_config* cfg, int64_t pair_capacity,
+                                             void* workspace, size_t workspace_bytes,
+                                             void* stream) {
+    clear_error();
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(params && grads && cams && workspace, "gs_train_param_backward: null argument");
+    GS_ARG_CHECK(n > 0 && n < (1ll << 32) && n_views >= 1 && n_views <= 64,
+                 "gs_train_param_backward: bad n or n_views");
+    GS_ARG_CHECK(row_begin >= 0 && row_begin <= row_end && row_end <= n,
+                 "gs_train_param_backward: rows [%lld, %lld) outside [0, %lld)",
+                 (long long)row_begin, (long long)row_end, (long long)n);
+    GS_ARG_CHECK(pair_capacity >= 1 && pair_capacity < (1ll << 30),
+                 "gs_train_param_backward: pair_capacity must be in [1, 2^30)");
+    GS_ARG_CHECK(((uintptr_t)params->quats & 15) == 0 && ((uintptr_t)grads->quats & 15) == 0,
+                 "gs_train_param_backward: quats must be 16-byte aligned");
+    int H = 0, W = 0;
+    for (int v = 0; v < n_views; ++v) {
+        GS_ARG_CHECK(image_fits(cams[v].height, cams[v].width, cfg->tile_size),
+                     "gs_train_param_backward: bad camera %d", v);
+        H = std::max(H, (int)cams[v].height);
+        W = std::max(W, (int)cams[v].width);
+    }
+    Workspace ws(workspace, workspace_bytes);
+    TrainWs L;
+    train_layout(ws, L, n, n_views, H, W, cfg->tile_size, pair_capacity);
+    GS_ARG_CHECK(ws.ok(), "gs_train_param_backward: workspace too small");
+    return launch_param_bwd(params, grads, n, row_begin, row_end, n_views, *cfg, H, W, L,
+                            (cudaStream_t)stream);
+}
+
 extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussians* exp_avg,
                                    const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
                                    float* vis_counts, int64_t n, int64_t step,
@@ -1802,7 +1868,9 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
     if (cs != GS_OK) return cs;
     GS_ARG_CHECK(params && grads && vis_counts && cams && targets && view_losses,
                  "gs_train_step: null argument");
-    GS_ARG_CHECK(!apply_adam || (exp_avg && exp_avg_sq), "gs_train_step: Adam needs moments");
+    GS_ARG_CHECK(apply_adam >= 0 && apply_adam <= GS_STEP_DEFER_PARAM_BWD,
+                 "gs_train_step: apply_adam must be 0, 1 or GS_STEP_DEFER_PARAM_BWD");
+    GS_ARG_CHECK(apply_adam != 1 || (exp_avg && exp_avg_sq), "gs_train_step: Adam needs moments");
     GS_ARG_CHECK(n > 0 && n < (1ll << 32), "gs_train_step: n must be in [1, 2^32)");
     GS_ARG_CHECK(n_views >= 1 && n_views <= 64, "gs_train_step: n_views must be in [1, 64]");
     GS_ARG_CHECK(pair_capacity >= 1 && pair_capacity < (1ll << 30),
@@ -1893,23 +1961,10 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
         GS_CUDA_CHECK(cudaMemcpyAsync(pairs, L.pairs, n_views * sizeof(int64_t),
                                       cudaMemcpyDeviceToDevice, st));
     }
+    if (apply_adam == GS_STEP_DEFER_PARAM_BWD) return GS_OK;
     {
-        KernelTimer kt("param_bwd", st);
-        TCfg c = make_tcfg(*cfg, H, W);
-        GMut G{grads->means, grads->log_scales, grads->quats, grads->opacity_logits, grads->sh};
-        const unsigned int nb = div_up(n, kParamThreads);
-        const int K = (cfg->sh_degree + 1) * (cfg->sh_degree + 1);
-        const size_t smem = 2 * (size_t)3 * K * kParamStride * sizeof(float);
-        switch (cfg->sh_degree) {
-            case 0: k_param_bwd<0><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
-            case 1: k_param_bwd<1><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
-            case 2: k_param_bwd<2><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G); break;
-            default:
-                GS_CUDA_CHECK(cudaFuncSetAttribute(k_param_bwd<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-                k_param_bwd<3><<<nb, kParamThreads, smem, st>>>(P, n, L.cams, n_views, c, L.grad2d, L.touch, G);
-                break;
-        }
-        GS_CHECK_LAUNCH();
+        gs_status ps = launch_param_bwd(params, grads, n, 0, n, n_views, *cfg, H, W, L, st);
+        if (ps != GS_OK) return ps;
     }
     if (apply_adam) {
         const AdamParams A = make_adam(params, exp_avg, exp_avg_sq, grads, n, step, cfg);

@@ -69,6 +69,9 @@ lib.gs_sparse_adam.restype = ctypes.c_int
 lib.gs_sparse_adam.argtypes = [_G, _G, _G, _G, _vp, _i64, _i64, _CFG, _vp, _vp]
 lib.gs_sparse_adam_multicast.restype = ctypes.c_int
 lib.gs_sparse_adam_multicast.argtypes = [_G, _G, _G, _G, _G, _vp, _vp, _i64, _i64, _CFG, _vp, _vp]
+lib.gs_train_param_backward.restype = ctypes.c_int
+lib.gs_train_param_backward.argtypes = [_G, _G, _i64, _i64, _i64, _C, _i32, _CFG, _i64, _vp, _sz, _vp]
+GS_STEP_DEFER_PARAM_BWD = 2
 lib.gs_train_project_view.restype = ctypes.c_int
 lib.gs_train_project_view.argtypes = [_G, _i64, _C, _CFG, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _vp, _vp, _i64, ctypes.POINTER(_i64), _vp, _sz, _vp]
@@ -184,7 +187,7 @@ class Trainer:
 
     def __init__(self, params: dict, cfg: TrainConfig, n_views: int, height: int, width: int,
                  pair_capacity: int | None = None, device=None, process_group=None,
-                 sharded_optimizer: bool = True, multicast: bool = True):
+                 sharded_optimizer: bool = True, multicast: bool = True, mc_chunks: int = 4):
         if not torch.cuda.is_available():
             raise RuntimeError("Trainer needs a CUDA device")
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
@@ -198,9 +201,16 @@ class Trainer:
         self.world = torch.distributed.get_world_size(process_group) if dist_on else 1
         self.rank = torch.distributed.get_rank(process_group) if dist_on else 0
         self.sharded = bool(sharded_optimizer) and self.world > 1
+        # Row layout of the sharded update: the rows are padded to chunks * world * q rows.
+        # Through multicast, chunk c's rows [c * world * q, (c + 1) * world * q) are updated
+        # once every GPU has finished their projection backward, rank r owning the q rows
+        # at offset r * q, so the update of one chunk overlaps the backward of the next.
+        # Through NCCL, rank r owns the contiguous rows [r * rows_per, (r + 1) * rows_per).
         from .dist import shard_rows
-        self.rows_per = shard_rows(self.n, self.world) if self.sharded else self.n
-        rows = self.rows_per * self.world if self.sharded else self.n
+        self.chunks = max(1, int(mc_chunks)) if (self.sharded and multicast) else 1
+        self.q = shard_rows(-(-self.n // self.chunks), self.world) if self.sharded else self.n
+        rows = self.chunks * self.world * self.q if self.sharded else self.n
+        self.rows_per = rows // self.world if self.sharded else self.n
         # parameters and gradients in symmetric memory when the update can go through NVLink
         # multicast (gs_sparse_adam_multicast); otherwise NCCL collectives
         self._symm = {}
@@ -223,8 +233,10 @@ class Trainer:
                                  alloc=alloc.get("grads"))
         self.multicast = bool(self._symm) and all(mc for _, mc in self._symm.values())
         if self.multicast:
-            self._vis_scratch = torch.zeros(self.rows_per, dtype=torch.float32, device=self.device)
+            self._vis_scratch = torch.zeros(self.q, dtype=torch.float32, device=self.device)
             self._fence = torch.zeros(1, dtype=torch.float32, device=self.device)
+            self._comm = torch.cuda.Stream(device=self.device)
+            self._chunk_done = [torch.cuda.Event() for _ in range(self.chunks)]
         self.vis_counts = self.grads.extra[:self.n]
         self.err_slot = self.grads.extra[rows:]
         if self.sharded:
@@ -293,10 +305,11 @@ class Trainer:
         st = torch.cuda.current_stream().cuda_stream
         p, m, v, g = (b.c_struct() for b in (self.params, self.m, self.v, self.grads))
         single = self.world == 1
+        mode = 1 if single else (GS_STEP_DEFER_PARAM_BWD if self.multicast else 0)
         while True:
             code = lib.gs_train_step(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
                                      self.vis_counts.data_ptr(), self.n, self.step_count, arr, tptr,
-                                     len(cams), ctypes.byref(self.ccfg), int(single),
+                                     len(cams), ctypes.byref(self.ccfg), mode,
                                      self.losses.data_ptr(),
                                      None if images is None else images.data_ptr(),
                                      None if grad2d is None else grad2d.data_ptr(),
@@ -304,7 +317,7 @@ class Trainer:
                                      self.ws.numel(), st)
             check(code)
             if not single:
-                self._allreduce_and_adam(st)
+                self._allreduce_and_adam(st, arr)
             if not check_errors:
                 break
             if single:
@@ -322,13 +335,13 @@ class Trainer:
         self.step_count += 1
         return self.losses
 
-    def _allreduce_and_adam(self, st) -> None:
+    def _allreduce_and_adam(self, st, arr) -> None:
         # error word of this rank's step (first 4 bytes at the workspace's first 256-byte
         # boundary) rides along so every rank agrees on skipping Adam
         off = (-self.ws.data_ptr()) % 256
         errw = self.ws[off:off + 4].view(torch.int32)
         if self.multicast:
-            self._multicast_adam(errw, st)
+            self._multicast_adam(errw, arr)
             return
         if self.sharded:
             self._sharded_adam(errw, st)
@@ -359,26 +372,46 @@ class Trainer:
         sharded_update(grad_groups, shards, param_groups, errw, self.err_slot, self._err_i32,
                        self.rank, self.world, adam, self.pg)
 
-    def _multicast_adam(self, errw, st) -> None:
-        """Owner-sharded update through NVLink multicast (gs_sparse_adam_multicast): the
-        error allreduce doubles as the barrier after which every GPU's partial gradients
-        are complete; the one-float allreduce after the update keeps every GPU from reading
-        parameters or rewriting its gradients before all updates have landed."""
+    def _multicast_adam(self, errw, arr) -> None:
+        """Owner-sharded update through NVLink multicast (gs_sparse_adam_multicast),
+        pipelined over row chunks: the projection backward of chunk c runs on the step's
+        stream; on a second stream a one-float allreduce (the barrier after which every
+        GPU's chunk-c gradients are complete; for chunk 0 it also sums the ranks' error
+        flags) is followed by the multicast update of this rank's rows of chunk c, while
+        the backward of chunk c + 1 proceeds. A last allreduce keeps every GPU from reading
+        parameters or rewriting gradients before all updates have landed."""
         import torch.distributed as dist
-        self.err_slot.copy_((errw != 0).to(torch.float32).reshape(1))
-        dist.all_reduce(self.err_slot, group=self.pg)
-        self._err_i32.copy_((self.err_slot > 0).to(torch.int32))
-        row0 = self.rank * self.rows_per
+        cur = torch.cuda.current_stream()
+        comm = self._comm
+        span = self.world * self.q
+        p, g = self.params.c_struct(), self.grads.c_struct()
         mc_p, mc_g = self._symm["params"][1], self._symm["grads"][1]
-        p, m, v = (b.c_struct(row0) for b in (self.params, self.m, self.v))
-        pm = self.params.c_struct(row0, base=mc_p)
-        gm = self.grads.c_struct(row0, base=mc_g)
-        vis_mc = mc_g + 4 * (self.grads.extra_offset + row0)
-        check(lib.gs_sparse_adam_multicast(ctypes.byref(p), ctypes.byref(pm), ctypes.byref(m),
-                                           ctypes.byref(v), ctypes.byref(gm), vis_mc,
-                                           self._vis_scratch.data_ptr(), self.rows_per,
-                                           self.step_count, ctypes.byref(self.ccfg),
-                                           self._err_i32.data_ptr(), st))
+        self.err_slot.copy_((errw != 0).to(torch.float32).reshape(1))
+        for c in range(self.chunks):
+            b, e = c * span, min((c + 1) * span, self.n)
+            if e > b:
+                check(lib.gs_train_param_backward(ctypes.byref(p), ctypes.byref(g), self.n, b, e, arr,
+                                                  len(arr), ctypes.byref(self.ccfg), self.capacity,
+                                                  self.ws.data_ptr(), self.ws.numel(), cur.cuda_stream))
+            self._chunk_done[c].record(cur)
+            with torch.cuda.stream(comm):
+                comm.wait_event(self._chunk_done[c])
+                if c == 0:
+                    dist.all_reduce(self.err_slot, group=self.pg)
+                    self._err_i32.copy_((self.err_slot > 0).to(torch.int32))
+                else:
+                    dist.all_reduce(self._fence, group=self.pg)
+                row0 = b + self.rank * self.q
+                pr, mr, vr = (buf.c_struct(row0) for buf in (self.params, self.m, self.v))
+                pm = self.params.c_struct(row0, base=mc_p)
+                gm = self.grads.c_struct(row0, base=mc_g)
+                vis_mc = mc_g + 4 * (self.grads.extra_offset + row0)
+                check(lib.gs_sparse_adam_multicast(ctypes.byref(pr), ctypes.byref(pm), ctypes.byref(mr),
+                                                   ctypes.byref(vr), ctypes.byref(gm), vis_mc,
+                                                   self._vis_scratch.data_ptr(), self.q,
+                                                   self.step_count, ctypes.byref(self.ccfg),
+                                                   self._err_i32.data_ptr(), comm.cuda_stream))
+        cur.wait_stream(comm)
         dist.all_reduce(self._fence, group=self.pg)
 
     def project_view(self, w2c, K, H, W) -> dict:

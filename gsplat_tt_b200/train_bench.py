@@ -223,7 +223,8 @@ def run(args, rank: int, world: int, local: int) -> dict:
                    "parallelism": f"dp{world} over views" + (
                        "" if world == 1 else
                        " + owner-sharded Adam with NVLink-multicast gradient sum and parameter "
-                       "broadcast (gs_sparse_adam_multicast)" if tr.multicast else
+                       f"broadcast (gs_sparse_adam_multicast), pipelined over {tr.chunks} row chunks "
+                       "with the projection backward" if tr.multicast else
                        " + NCCL reduce-scatter / all-gather, owner-sharded Adam" if tr.sharded
                        else " + NCCL allreduce, replicated Adam"),
                    "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},

@@ -254,6 +254,10 @@ typedef struct gs_train_config {
  *   pair_capacity bounds the (Gaussian, tile) pairs of one view; if a view needs more,
  *   the step leaves params and moments untouched and gs_workspace_error() reports
  *   GS_ERR_OVERFLOW (grow the capacity with gs_train_count_pairs and retry).
+ *   apply_adam = GS_STEP_DEFER_PARAM_BWD stops after the views: the projection backward
+ *   (grads) is left to gs_train_param_backward, called with the same workspace and
+ *   arguments, over row ranges (a multi-GPU caller overlaps the update of one range with
+ *   the backward of the next); vis_counts are written as usual.
  *   All work is ordered on `stream`: with two or more views, views alternate between
  *   `stream` and an internal stream of the library (created once per device) that is
  *   forked from `stream` after the projection and joined back to it before the parameter
@@ -262,6 +266,8 @@ typedef struct gs_train_config {
  * forward_fast, gsplat/train_loss.py:126 loss_and_grad_device, blend_backward_dev.py:444
  * ref_slots_fast, gsplat/t2_param_backward.py:244 t2_step (extended to SH1-3 and
  * multiple views) and gsplat/train_oracle.py:434 sparse_adam_step. */
+#define GS_STEP_DEFER_PARAM_BWD 2
+
 gs_status gs_train_step(const gs_gaussians* params, const gs_gaussians* exp_avg,
                         const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
                         float* vis_counts, int64_t n, int64_t step, const gs_camera* cams,
@@ -304,6 +310,17 @@ gs_status gs_sparse_adam(const gs_gaussians* params, const gs_gaussians* exp_avg
                          const float* vis_counts, int64_t n, int64_t step,
                          const gs_train_config* cfg, const unsigned int* error_word,
                          void* stream);
+
+/* Projection backward (2D gradients -> grads of means, log-scales, quaternions, opacity
+ * logits and SH) of Gaussian rows [row_begin, row_end) after a gs_train_step call with
+ * apply_adam = GS_STEP_DEFER_PARAM_BWD on the same workspace, n, cams, n_views, cfg and
+ * pair_capacity. Rows outside the range are not touched. gsplat/t2_param_backward.py:123-192
+ * projection_backward_sh0, extended to SH1-3 and summed over the step's views. */
+gs_status gs_train_param_backward(const gs_gaussians* params, const gs_gaussians* grads,
+                                  int64_t n, int64_t row_begin, int64_t row_end,
+                                  const gs_camera* cams, int32_t n_views,
+                                  const gs_train_config* cfg, int64_t pair_capacity,
+                                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* Owner-sharded sparse Adam of one GPU of a multi-GPU step, with the gradient sum and the
  * parameter broadcast done through NVLink multicast (NVSwitch) inside the kernels. Replaces
