@@ -227,4 +227,6 @@ def test_host_targets_match_device_targets():
     for losses, g in results[1:]:
         np.testing.assert_allclose(losses, results[0][0], rtol=1e-6)
         for k in ot.PARAM_NAMES:
-            assert ot.rel_error(g[k], results[0][1][k]) <= 1e-5, k
+            # elementwise relative error (floor 1e-4 of the largest): gradients that nearly
+            # cancel carry the atomics-order noise of two runs at a few 1e-5
+            assert ot.rel_error(g[k], results[0][1][k]) <= 1e-4, k
