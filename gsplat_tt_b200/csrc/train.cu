@@ -1182,7 +1182,20 @@ k_mc_reduce_counts(const float* __restrict__ counts_mc, float* __restrict__ coun
 // One parameter group of this GPU's rows: G.p / G.m / G.v point at the rows' local copies,
 // g_mc / p_mc at the same rows through the gradient / parameter multicast mappings. The
 // group's element count is a multiple of 4 and every pointer 16-byte aligned. The update
-// arithmetic is adam_update's, element for element, as in k_sparse_adam.
+// arithmetic is adam_update's, element for element, as in k_sparse_adam. Each thread
+// issues the load-reduces of kMcUnroll float4s (grid-strided slabs) before using any. The
+// link, not the SMs, bounds the kernel: two 256-thread blocks per SM with four requests in
+// flight per thread move the same bytes per second as sixteen blocks with one, and leave
+// most of each SM to the projection backward of the next row chunk running beside it.
+#ifndef GS_MC_UNROLL
+#define GS_MC_UNROLL 4
+#endif
+#ifndef GS_MC_BLOCKS_PER_SM
+#define GS_MC_BLOCKS_PER_SM 2
+#endif
+constexpr int kMcUnroll = GS_MC_UNROLL;
+constexpr int kMcBlocksPerSm = GS_MC_BLOCKS_PER_SM;
+
 template <int W>
 __global__ void __launch_bounds__(256)
 k_sparse_adam_mc(AdamParams A, const float* __restrict__ vis, const unsigned int* __restrict__ skip,
@@ -1191,29 +1204,43 @@ k_sparse_adam_mc(AdamParams A, const float* __restrict__ vis, const unsigned int
     const AdamGroup& G = A.grp[group];
     const uint32_t n4 = (uint32_t)(G.count / 4);
     const uint32_t stride = gridDim.x * blockDim.x;
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
-        const uint32_t e = 4u * i;
-        const uint32_t r0 = e / W, r3 = (e + 3u) / W;
-        bool any = false;
-        for (uint32_t r = r0; r <= r3; ++r) any |= vis[r] > 0.0f;
-        if (!any) continue;
-        const float4 g4 = mc_ld_add_v4(g_mc + e);
-        float4 p4 = reinterpret_cast<const float4*>(G.p)[i];
-        float4 m4 = reinterpret_cast<const float4*>(G.m)[i];
-        float4 v4 = reinterpret_cast<const float4*>(G.v)[i];
-        float* pp = &p4.x;
-        float* mm = &m4.x;
-        float* vv = &v4.x;
-        const float* gg = &g4.x;
+    for (uint32_t base = blockIdx.x * blockDim.x + threadIdx.x; base < n4;
+         base += stride * (uint32_t)kMcUnroll) {
+        float4 g4[kMcUnroll];
+        bool live[kMcUnroll];
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-            const uint32_t ek = e + (uint32_t)k;
-            const uint32_t row = ek / W;
-            if (vis[row] > 0.0f) adam_update(A, G, (int)(ek - row * W), gg[k], pp[k], mm[k], vv[k]);
+        for (int u = 0; u < kMcUnroll; ++u) {
+            const uint32_t i = base + (uint32_t)u * stride;
+            live[u] = false;
+            if (i < n4) {
+                const uint32_t e = 4u * i;
+                const uint32_t r0 = e / W, r3 = (e + 3u) / W;
+                for (uint32_t r = r0; r <= r3; ++r) live[u] |= vis[r] > 0.0f;
+            }
+            if (live[u]) g4[u] = mc_ld_add_v4(g_mc + 4ull * i);
         }
-        mc_st_v4(p_mc + e, p4);
-        reinterpret_cast<float4*>(G.m)[i] = m4;
-        reinterpret_cast<float4*>(G.v)[i] = v4;
+#pragma unroll
+        for (int u = 0; u < kMcUnroll; ++u) {
+            if (!live[u]) continue;
+            const uint32_t i = base + (uint32_t)u * stride;
+            const uint32_t e = 4u * i;
+            float4 p4 = reinterpret_cast<const float4*>(G.p)[i];
+            float4 m4 = reinterpret_cast<const float4*>(G.m)[i];
+            float4 v4 = reinterpret_cast<const float4*>(G.v)[i];
+            float* pp = &p4.x;
+            float* mm = &m4.x;
+            float* vv = &v4.x;
+            const float* gg = &g4[u].x;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const uint32_t ek = e + (uint32_t)k;
+                const uint32_t row = ek / W;
+                if (vis[row] > 0.0f) adam_update(A, G, (int)(ek - row * W), gg[k], pp[k], mm[k], vv[k]);
+            }
+            mc_st_v4(p_mc + e, p4);
+            reinterpret_cast<float4*>(G.m)[i] = m4;
+            reinterpret_cast<float4*>(G.v)[i] = v4;
+        }
     }
     mc_release();
 }
@@ -1802,7 +1829,8 @@ extern "C" gs_status gs_sparse_adam_multicast(const gs_gaussians* params,
     for (int i = 0; i < 5; ++i) {
         const AdamGroup& G = A.grp[i];
         const unsigned int blocks =
-            (unsigned int)std::min<int64_t>(div_up(div_up(G.count, 4), 256), kNumSMs * 16);
+            (unsigned int)std::min<int64_t>(div_up(div_up(G.count, 4), 256 * kMcUnroll),
+                                            kNumSMs * kMcBlocksPerSm);
 #define GS_ADAM_MC(W_) k_sparse_adam_mc<W_><<<blocks, 256, 0, st>>>(A, vis_scratch, skip, i, Gm[i], Pm[i])
         switch (G.width) {
             case 1: GS_ADAM_MC(1); break;
