@@ -235,8 +235,17 @@ class Trainer:
         if self.multicast:
             self._vis_scratch = torch.zeros(self.q, dtype=torch.float32, device=self.device)
             self._fence = torch.zeros(1, dtype=torch.float32, device=self.device)
-            self._comm = torch.cuda.Stream(device=self.device)
+            # The update's stream and its barriers' NCCL stream run at high priority, so
+            # their blocks are scheduled ahead of the pending blocks of the backward of the
+            # next chunk instead of after all of them.
+            self._comm = torch.cuda.Stream(device=self.device, priority=-1)
             self._chunk_done = [torch.cuda.Event() for _ in range(self.chunks)]
+            self._barrier_pg = self.pg
+            if self.pg is None and torch.distributed.get_backend() == "nccl":
+                opts = torch.distributed.ProcessGroupNCCL.Options()
+                opts.is_high_priority_stream = True
+                self._barrier_pg = torch.distributed.new_group(pg_options=opts,
+                                                               device_id=self.device)
         self.vis_counts = self.grads.extra[:self.n]
         self.err_slot = self.grads.extra[rows:]
         if self.sharded:
@@ -397,10 +406,10 @@ class Trainer:
             with torch.cuda.stream(comm):
                 comm.wait_event(self._chunk_done[c])
                 if c == 0:
-                    dist.all_reduce(self.err_slot, group=self.pg)
+                    dist.all_reduce(self.err_slot, group=self._barrier_pg)
                     self._err_i32.copy_((self.err_slot > 0).to(torch.int32))
                 else:
-                    dist.all_reduce(self._fence, group=self.pg)
+                    dist.all_reduce(self._fence, group=self._barrier_pg)
                 row0 = b + self.rank * self.q
                 pr, mr, vr = (buf.c_struct(row0) for buf in (self.params, self.m, self.v))
                 pm = self.params.c_struct(row0, base=mc_p)
@@ -412,7 +421,7 @@ class Trainer:
                                                    self.step_count, ctypes.byref(self.ccfg),
                                                    self._err_i32.data_ptr(), comm.cuda_stream))
         cur.wait_stream(comm)
-        dist.all_reduce(self._fence, group=self.pg)
+        dist.all_reduce(self._fence, group=self._barrier_pg)
 
     def project_view(self, w2c, K, H, W) -> dict:
         """Projection, intersections, sorted pairs and tile ranges of one view (parity API)."""
