@@ -118,8 +118,11 @@ def dist_setup(args):
     if world > 1:
         import datetime
         import torch.distributed as dist
-        backend = "nccl" if args.impl == "b200" else "gloo"
-        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300))
+        if args.impl == "b200":  # bound to this rank's GPU (no device guessing in barriers)
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     return rank, world, local
 
 
