@@ -50,6 +50,14 @@ def shard_rows(n: int, world: int) -> int:
     return max(4, -(-n // (4 * world)) * 4)
 
 
+def owned_rows(chunk: int, rank: int, world: int, q: int) -> tuple[int, int]:
+    """[begin, end) of the rows rank owns in row chunk `chunk` of the pipelined multicast
+    update: chunk c spans rows [c * world * q, (c + 1) * world * q) and rank r owns the q
+    rows at offset r * q inside it."""
+    b = chunk * world * q + rank * q
+    return b, b + q
+
+
 def sharded_update(grad_groups, grad_shards, param_groups, local_error, err, skip_out, rank: int,
                    world: int, adam_fn, group=None) -> None:
     """One owner-sharded optimizer update, enqueued asynchronously on the current stream.

@@ -25,7 +25,7 @@ import torch
 
 from . import _lib
 from ._lib import check, lib
-from .dist import reduce_step_buffer
+from .dist import owned_rows, reduce_step_buffer
 
 PARAM_NAMES = ("means", "log_scales", "quats", "opacity_logits", "sh")
 DEFAULT_LR = {"means": 1.6e-4, "log_scales": 5e-3, "quats": 1e-3, "opacity_logits": 0.05,
@@ -410,7 +410,7 @@ class Trainer:
                     self._err_i32.copy_((self.err_slot > 0).to(torch.int32))
                 else:
                     dist.all_reduce(self._fence, group=self._barrier_pg)
-                row0 = b + self.rank * self.q
+                row0 = owned_rows(c, self.rank, self.world, self.q)[0]
                 pr, mr, vr = (buf.c_struct(row0) for buf in (self.params, self.m, self.v))
                 pm = self.params.c_struct(row0, base=mc_p)
                 gm = self.grads.c_struct(row0, base=mc_g)

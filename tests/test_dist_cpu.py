@@ -1,11 +1,14 @@
 """The view-parallel trainer's host plumbing on CPU with gloo, world size 2: the view split,
 the single allreduce of gradients + visibility counts + error flags (every rank takes the
-same skip decision), and a rank that dies before the collective (the survivor's collective
-fails within the process-group timeout instead of hanging)."""
+same skip decision), the owner-sharded update (reduce-scatter, Adam on owned rows,
+all-gather) against the allreduce, the chunked row ownership of the multicast update, the
+symmetric-buffer host logic against a fake of torch's API, and a rank that dies before the
+collective (the survivor's collective fails within the process-group timeout)."""
 import datetime
 import os
 import socket
 
+import numpy as np
 import pytest
 import torch
 import torch.multiprocessing as mp
@@ -233,3 +236,22 @@ def test_symmetric_buffer_host_logic(monkeypatch, supported):
     t, h, mc = gd.symmetric_buffer(16, "cpu:0")
     assert t.numel() == 16 and float(t.abs().max()) == 0.0  # zeroed
     assert mc == (0x7F0000000000 if supported else None)
+
+
+@pytest.mark.parametrize("n,world,chunks", [(5001, 2, 4), (6_000_000, 8, 4), (7, 4, 4), (1000, 3, 1)])
+def test_owned_rows_partition_the_padded_rows(n, world, chunks):
+    """Chunked ownership of the multicast update: every padded row has exactly one owner,
+    every owner's range starts on a 16-byte boundary, and the padding covers n."""
+    from gsplat_tt_b200.dist import owned_rows, shard_rows
+    q = shard_rows(-(-n // chunks), world)
+    total = chunks * world * q
+    assert total >= n and q % 4 == 0
+    seen = np.zeros(total, np.int32) if total < 10_000_000 else None
+    spans = sorted(owned_rows(c, r, world, q) for c in range(chunks) for r in range(world))
+    assert spans[0][0] == 0 and spans[-1][1] == total
+    for (b0, e0), (b1, _) in zip(spans, spans[1:]):
+        assert e0 == b1 and b0 % 4 == 0
+    if seen is not None:
+        for b, e in spans:
+            seen[b:e] += 1
+        assert (seen == 1).all()
