@@ -66,3 +66,42 @@ def test_product_path_fails_loudly_without_library(tmp_path, monkeypatch):
     with pytest.raises(ImportError):
         exec(compile(src, "x", "exec"), ns)
     importlib.reload(L)
+
+
+def test_training_update_argument_errors_need_no_device():
+    """The row-range projection backward and the multicast update reject bad arguments on
+    the host (no device call is made before the checks)."""
+    from gsplat_tt_b200._lib import GS_ERR_ARG, lib
+    from gsplat_tt_b200.train import GsCamera, GsGaussians, TrainConfig, camera_struct
+    import numpy as np
+    cfg = TrainConfig(sh_degree=3).c_struct()
+    g = GsGaussians(16, 16, 16, 16, 16)  # fake aligned addresses: never dereferenced
+    cams = (GsCamera * 1)(camera_struct(np.eye(4), np.eye(3), 64, 64))
+    ws = ctypes.c_void_p(256)
+    # rows outside [0, n)
+    assert lib.gs_train_param_backward(ctypes.byref(g), ctypes.byref(g), 100, 50, 101, cams, 1,
+                                       ctypes.byref(cfg), 1000, ws, 1 << 30, None) == GS_ERR_ARG
+    assert b"outside" in lib.gs_last_error()
+    assert lib.gs_train_param_backward(ctypes.byref(g), ctypes.byref(g), 100, 60, 50, cams, 1,
+                                       ctypes.byref(cfg), 1000, ws, 1 << 30, None) == GS_ERR_ARG
+    # workspace too small for the layout
+    assert lib.gs_train_param_backward(ctypes.byref(g), ctypes.byref(g), 100, 0, 100, cams, 1,
+                                       ctypes.byref(cfg), 1000, ws, 16, None) == GS_ERR_ARG
+    assert b"workspace" in lib.gs_last_error()
+    # multicast update: rows must be a multiple of 4, pointers 16-byte aligned
+    skip = ctypes.c_void_p(16)
+    args = [ctypes.byref(g)] * 5
+    assert lib.gs_sparse_adam_multicast(*args, ctypes.c_void_p(16), ctypes.c_void_p(16), 6, 0,
+                                        ctypes.byref(cfg), skip, None) == GS_ERR_ARG
+    assert b"multiple of 4" in lib.gs_last_error()
+    bad = GsGaussians(16, 16, 20, 16, 16)
+    assert lib.gs_sparse_adam_multicast(ctypes.byref(bad), *args[1:], ctypes.c_void_p(16),
+                                        ctypes.c_void_p(16), 8, 0, ctypes.byref(cfg), skip,
+                                        None) == GS_ERR_ARG
+    assert b"16-byte" in lib.gs_last_error()
+    # a deferred step mode outside {0, 1, 2}
+    tg = (ctypes.c_void_p * 1)(16)
+    assert lib.gs_train_step(ctypes.byref(g), ctypes.byref(g), ctypes.byref(g), ctypes.byref(g),
+                             ctypes.c_void_p(16), 100, 0, cams, tg, 1, ctypes.byref(cfg), 3,
+                             ctypes.c_void_p(16), None, None, None, 1000, ws, 1 << 30,
+                             None) == GS_ERR_ARG
