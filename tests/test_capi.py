@@ -58,21 +58,21 @@ def test_argument_errors_need_no_device():
 
 
 def test_product_path_fails_loudly_without_library(tmp_path, monkeypatch):
-    import importlib
     import gsplat_tt_b200._lib as L
     monkeypatch.setattr(L, "LIB_PATH", str(tmp_path / "missing.so"))
     src = open(L.__file__).read()
     ns = {"__file__": str(tmp_path / "_lib.py"), "__name__": "x"}
     with pytest.raises(ImportError):
         exec(compile(src, "x", "exec"), ns)
-    importlib.reload(L)
+    # the module itself is untouched (the copy ran in its own namespace): no reload, which
+    # would replace the library handle whose signatures other modules have declared
 
 
 def test_training_update_argument_errors_need_no_device():
     """The row-range projection backward and the multicast update reject bad arguments on
     the host (no device call is made before the checks)."""
-    from gsplat_tt_b200._lib import GS_ERR_ARG, lib
-    from gsplat_tt_b200.train import GsCamera, GsGaussians, TrainConfig, camera_struct
+    from gsplat_tt_b200._lib import GS_ERR_ARG
+    from gsplat_tt_b200.train import GsCamera, GsGaussians, TrainConfig, camera_struct, lib
     import numpy as np
     cfg = TrainConfig(sh_degree=3).c_struct()
     g = GsGaussians(16, 16, 16, 16, 16)  # fake aligned addresses: never dereferenced
