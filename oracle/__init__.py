@@ -6,6 +6,8 @@
 * ``oracle.train`` -- numpy restatement of the reference's training-path models
   (tiled fp32 forward, L1/SSIM loss, blend backward, projection backward incl. SH1-3,
   sparse Adam).
+* ``oracle.train_pool`` -- the oracle's multi-view training step with one view per
+  spawned worker process (the CPU baseline on all host cores).
 
 Only ``tests/``, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg use
 this package.

@@ -154,3 +154,26 @@ def test_exact_backward_agrees_with_reference_formula(tiled):
     g64 = ot.backward_2d_exact(pr, tiled["dL_dimage"], H, W, cfg)
     ok = ~tiled["tie_g"]
     assert ot.rel_error(g64[ok], tiled["g2d"][ok]) <= 2e-3
+
+
+def test_view_pool_step_equals_sequential_train_step():
+    """The process-parallel oracle step (the CPU baseline's driver) gives train_step's
+    result exactly: per-view work in worker processes, gradients summed in view order."""
+    from gsplat_tt_b200 import scenes
+    from oracle.train_pool import ViewPool
+    params = scenes.cluster_scene(1500, sh_degree=3, seed=7)
+    params["means"] = (params["means"] * 0.5).astype(np.float32)
+    params["log_scales"] = (params["log_scales"] + 1.5).astype(np.float32)
+    H, W = 32, 48
+    cams = [(c.w2c, c.K, H, W) for c in scenes.sphere_cameras(3, 3.5, 40.0, W, H)]
+    tg = [np.random.default_rng(i).uniform(0, 1, (H, W, 3)).astype(np.float32) for i in range(3)]
+    cfg = ot.Cfg(sh_degree=3, tile=16)
+    zeros = {k: np.zeros_like(np.asarray(v, np.float32)) for k, v in params.items()}
+    ref = ot.train_step(params, zeros, zeros, 0, cams, tg, cfg)
+    with ViewPool(params, cfg, workers=2) as pool:
+        got = pool.step(zeros, zeros, 0, cams, tg)
+    assert got["loss"] == ref["loss"]
+    np.testing.assert_array_equal(got["visible"], ref["visible"])
+    for k in ot.PARAM_NAMES:
+        np.testing.assert_array_equal(got["grads"][k], ref["grads"][k])
+        np.testing.assert_array_equal(got["params"][k], ref["params"][k])
