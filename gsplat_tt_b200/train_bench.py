@@ -266,8 +266,9 @@ def cpu_baseline(name: str, budget_s: float = 20.0, workers: int | None = None) 
     from oracle.train_pool import ViewPool
     scale = 8
     c = scenes.CONFIGS[name]
-    if workers is None:
-        workers = max(1, min(os.cpu_count() or 1, c["views"]))
+    if workers is None:  # the cores this process may run on, up to one per view of the step
+        avail = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+        workers = max(1, min(avail or 1, c["views"]))
     params, cams, tgts, n, H, W = _oracle_sample(name, scale, views=workers)
     cfg = ot.Cfg(sh_degree=3, tile=16)
     zeros = {k: np.zeros_like(v) for k, v in params.items()}
