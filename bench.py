@@ -5,11 +5,16 @@
 
 Workloads (BASELINE.json metric "train-step Mpix/s (fwd+bwd+Adam) and sort keys/s"):
   train -- config C5 (6M Gaussians, SH3, 32 views of 1920x1080 split over the ranks,
-           gradients summed by an NCCL allreduce, sparse Adam on every rank); a step is
-           one full training step. Metric: Mpix/s = 32 * 1920 * 1080 / step time.
+           owner-sharded sparse Adam with the gradient sum and parameter broadcast over
+           NVLink); a step is one full training step. Metric: Mpix/s = 32 * 1920 * 1080 /
+           step time. The line also carries `sort_c2`: the sort workload below measured
+           in the same process at the same N (--no-sort skips it).
   sort  -- config C2 (2^24 Zipf (uint64 key, uint32 value) pairs, 45 key bits); a step is
            one stable sort per rank (independent per-GPU sorts, weak scaling).
            Metric: sorted pairs/s over all ranks.
+
+The reference arm (--impl reference) runs the reference's CPU implementation of the same
+workload (oracle/baseline.py) on rank 0 and loads nothing of this repository's library.
 
 Timing: W untimed steps, then K steps between barrier + synchronize, CUDA events on the
 launching stream, max over ranks. `value` has inputs resident in HBM; `e2e` goes through
@@ -167,36 +172,15 @@ def sort_algorithmic_bytes(n: int, key_bits: int) -> tuple[float, float]:
     return pass_bytes / npass, pass_bytes + 8.0 * n
 
 
-def cpu_sort_baseline(keys, vals, budget_s: float = 15.0) -> dict:
-    """The reference's sort_and_bin (oracle/_ref) on this host's cores, else the C port."""
-    os.environ.setdefault("GSPLAT_TT_NUM_THREADS", str(os.cpu_count()))
-    from oracle import display as od
-    ref = od.reference_module()
-    n = keys.size
-    if ref is not None:
-        tiles = (keys >> np.uint64(32)).astype(np.int64)
-        depth = (keys & np.uint64(0xFFFFFFFF)).astype(np.uint32).view(np.float32)
-        dv = np.empty(n, np.float32)
-        dv[vals] = depth
-        gids = vals.astype(np.int64)
-        fn = lambda: ref.sort(gids, tiles, dv, 120, 68)  # noqa: E731
-        kind, cores = "reference", int(os.environ.get("GSPLAT_TT_NUM_THREADS", os.cpu_count()))
-    else:
-        fn = lambda: od.sort_pairs(keys, vals)  # noqa: E731
-        kind, cores = "port", 1
-    fn()
-    t0, iters = time.perf_counter(), 0
-    while True:
-        fn()
-        iters += 1
-        el = time.perf_counter() - t0
-        if el > budget_s or iters >= 20:
-            break
-    return {"value": n * iters / el, "unit": "pairs/s", "cores": cores, "kind": kind,
-            "sample": f"{iters} full C2 sorts of {n} pairs"}
-
-
 C2_PASS_DRAM_BYTES = 204.86e6 + 156.46e6
+SORT_METRIC = "sort keys/s (C2: 2^24 Zipf uint64/uint32 pairs, 45 key bits)"
+
+
+def sort_config(world: int) -> dict:
+    return {"workload": "C2 radix sort, one 2^24-pair instance per GPU",
+            "pairs_per_gpu": SORT_N, "key_bits": SORT_KEY_BITS, "tiles": 8160,
+            "l2": "inputs larger than L2 (201 MB keys+values per GPU)",
+            "parallelism": f"independent sorts x{world}"}
 
 
 def run_sort(args, rank, world, local) -> dict:
@@ -278,14 +262,11 @@ def run_sort(args, rank, world, local) -> dict:
     peaks = measured_peaks()
     achieved = per_launch_bytes / (avg_ms / 1e3) / 1e9
     out = {
-        "metric": "sort keys/s (C2: 2^24 Zipf uint64/uint32 pairs, 45 key bits)",
+        "metric": SORT_METRIC,
         "value": value, "unit": "pairs/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "u64", "data": "synthetic",
-        "config": {"workload": "C2 radix sort, one 2^24-pair instance per GPU",
-                   "pairs_per_gpu": n, "key_bits": SORT_KEY_BITS, "tiles": 8160,
-                   "l2": "inputs larger than L2 (201 MB keys+values per GPU)",
-                   "parallelism": f"independent sorts x{world}"},
+        "config": sort_config(world),
         "e2e": {"value": sum_over_ranks(float(n), world) / (e2e_ms / 1e3), "unit": "pairs/s",
                 "h2d_bytes_per_step": 12 * n, "d2h_bytes_per_step": 4 * n},
         "gpu_launches": int(args.steps * (2 + (SORT_KEY_BITS + 7) // 8)),
@@ -293,7 +274,7 @@ def run_sort(args, rank, world, local) -> dict:
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"],
                      # dram__bytes_read.sum + dram__bytes_write.sum of one middle pass of this
-                     # workload under ncu (profiles/k_onesweep_pass_c2.md)
+                     # workload under ncu
                      "traffic": C2_PASS_DRAM_BYTES,
                      "peak_source": peaks["source"], "avg_launch_ms": avg_ms,
                      "algorithmic_bytes_per_launch": per_launch_bytes},
@@ -301,22 +282,64 @@ def run_sort(args, rank, world, local) -> dict:
         "clocks": clk.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle.baseline import cpu_sort_baseline
         out["cpu_baseline"] = cpu_sort_baseline(keys, vals)
     return out
 
 
 def run_sort_reference(args) -> dict:
     from gsplat_tt_b200 import scenes
+    from oracle.baseline import cpu_sort_baseline
     keys, vals = scenes.c2_pairs()
     b = cpu_sort_baseline(keys, vals, budget_s=max(5.0, 2.0 * args.steps))
-    return {"impl": "reference", "metric": "sort keys/s (C2: 2^24 Zipf uint64/uint32 pairs, 45 key bits)",
+    return {"impl": "reference", "metric": SORT_METRIC,
             "value": b["value"], "unit": "pairs/s", "n_gpus": 1, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": keys.size / b["value"] * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "u64",
-            "data": "synthetic", "config": {"workload": "C2 radix sort", "pairs": int(keys.size)},
-            "cpu_baseline": b,
+            "data": "synthetic", "config": sort_config(1), "cpu_baseline": b,
             "e2e": {"value": b["value"], "unit": "pairs/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+
+
+# ---------------------------------------------------------------- train workload
+
+TRAIN_METRIC = "train-step Mpix/s (fwd+bwd+Adam)"
+
+
+def train_config(name: str, views: int | None = None) -> dict:
+    """The training workload's config keys, shared by both arms."""
+    from gsplat_tt_b200 import scenes
+    c = scenes.CONFIGS[name]
+    V = c["views"] if views is None else views
+    return {"workload": f"{name.upper()} train step: {c['n']} Gaussians SH3, {V} views "
+                        f"{c['width']}x{c['height']}, "
+                        f"{'L1+SSIM' if c['ssim'] else 'L1'}, sparse Adam",
+            "gaussians": c["n"], "views": V, "width": c["width"], "height": c["height"],
+            "tile": 16, "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"}
+
+
+def run_train_reference(args) -> dict:
+    """The reference arm of the training workload: the oracle port of the reference's numpy
+    training models on the host's cores, on a bounded sample of the same workload."""
+    from oracle.baseline import train_cpu_baseline
+    name = os.environ.get("GS_BENCH_CONFIG", "c5")
+    b = train_cpu_baseline(name, budget_s=max(10.0, 3.0 * args.steps))
+    cfg = train_config(name)
+    cfg["parallelism"] = f"CPU: {b['cores']} worker processes, one view each"
+    return {"impl": "reference", "metric": TRAIN_METRIC, "value": b["value"],
+            "unit": "Mpix/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic", "config": cfg,
+            "cpu_baseline": b,
+            "e2e": {"value": b["value"], "unit": "Mpix/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def sort_summary(s: dict) -> dict:
+    """The C2 sort measurement carried inside the training line (every N, every rank)."""
+    keys = ("metric", "value", "unit", "ms_per_step", "scaling", "config", "e2e", "roofline",
+            "gpu_launches", "clocks", "cpu_baseline")
+    return {k: s[k] for k in keys if k in s}
 
 
 # ---------------------------------------------------------------- main
@@ -327,32 +350,33 @@ def main() -> None:
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--workload", choices=["train", "sort"], default=None)
+    ap.add_argument("--workload", choices=["train", "sort"], default="train")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-sort", action="store_true",
+                    help="train workload: skip the C2 sort measurement carried in the line")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    workload = args.workload
-    if workload is None:
-        try:
-            from gsplat_tt_b200 import train  # noqa: F401
-            workload = "train"
-        except ImportError:
-            workload = "sort"
     rank, world, local = dist_setup(args)
     if args.impl == "reference":
+        # the reference's CPU implementation only: nothing here loads libgs200.so
         if rank == 0:
-            if workload == "sort":
-                out = run_sort_reference(args)
-            else:
-                from gsplat_tt_b200 import train_bench
-                out = train_bench.run_reference(args)
+            out = run_sort_reference(args) if args.workload == "sort" else run_train_reference(args)
+            if args.workload == "train" and not args.no_sort:
+                out["sort_c2"] = sort_summary(run_sort_reference(args))
             print(json.dumps(out), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
         return
-    if workload == "sort":
+    if args.workload == "sort":
         out = run_sort(args, rank, world, local)
     else:
         from gsplat_tt_b200 import train_bench
         out = train_bench.run(args, rank, world, local)
+        if not args.no_sort:
+            import torch
+            torch.cuda.empty_cache()
+            out["sort_c2"] = sort_summary(run_sort(args, rank, world, local))
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:

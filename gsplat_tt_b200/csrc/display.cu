@@ -8,7 +8,6 @@
 // precondition for bit-exact pair counts, sorted orders and tile ranges.
 #include <cstdarg>
 #include <cstring>
-#include <mutex>
 
 #include "common.cuh"
 #include "scan.cuh"
@@ -705,31 +704,21 @@ static constexpr int64_t kNoAllocMaxGaussians = 1ll << 24;
 static constexpr int64_t kNoAllocScratch = (kNoAllocMaxGaussians + kProjBlock - 1) / kProjBlock + 1;
 static __device__ __align__(256) int64_t g_project_scratch[kNoAllocScratch];
 
-static constexpr int kNoAllocMaxDevices = 64;
-static std::mutex g_project_scratch_mu;
-static int64_t* g_project_scratch_addr[kNoAllocMaxDevices] = {};
-
-// Device address of g_project_scratch on the current device. In host code the array's
-// name is only a host-side stand-in, so the address is looked up once per device (with
-// that device current) and cached.
+// Device address of g_project_scratch in the current device's current context. In host
+// code the array's name is only a host-side stand-in, so the address is looked up on every
+// call (cudaGetSymbolAddress allocates nothing): module memory belongs to a CUDA context,
+// and a cached address would go stale after a device reset or under another context.
 static gs_status project_scratch_address(int64_t** out) {
-    int dev = 0;
-    GS_CUDA_CHECK(cudaGetDevice(&dev));
-    GS_ARG_CHECK(dev >= 0 && dev < kNoAllocMaxDevices,
-                 "gs_project_noalloc: device %d is beyond the %d devices it supports", dev,
-                 kNoAllocMaxDevices);
-    std::lock_guard<std::mutex> lock(g_project_scratch_mu);
-    if (g_project_scratch_addr[dev] == nullptr) {
-        int64_t* ptr = nullptr;
-        const cudaError_t err = cudaGetSymbolAddress((void**)&ptr, g_project_scratch);
-        if (err != cudaSuccess || ptr == nullptr) {
-            set_error("gs_project_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
-                      cudaGetErrorString(err));
-            return GS_ERR_CUDA;
-        }
-        g_project_scratch_addr[dev] = ptr;
+    int64_t* ptr = nullptr;
+    const cudaError_t err = cudaGetSymbolAddress((void**)&ptr, g_project_scratch);
+    if (err != cudaSuccess || ptr == nullptr) {
+        int dev = -1;
+        cudaGetDevice(&dev);
+        set_error("gs_project_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                  cudaGetErrorString(err));
+        return GS_ERR_CUDA;
     }
-    *out = g_project_scratch_addr[dev];
+    *out = ptr;
     return GS_OK;
 }
 
@@ -744,15 +733,15 @@ extern "C" gs_status gs_project_noalloc(const float* means, const float* cov3d, 
                                         int64_t* num_visible_host, void* stream) {
     clear_error();
     cudaStream_t st = (cudaStream_t)stream;
-    GS_ARG_CHECK(n >= 0 && n <= kNoAllocMaxGaussians,
-                 "gs_project_noalloc: n = %lld, but at most %lld Gaussians fit its fixed "
-                 "scratch; use gs_project with a workspace for more",
-                 (long long)n, (long long)kNoAllocMaxGaussians);
     if (use_isoellipse) {
         set_error("gs_project_noalloc: use_isoellipse is not supported");
         return GS_ERR_UNSUPPORTED;
     }
-    GS_ARG_CHECK(height > 0 && width > 0, "gs_project_noalloc: bad sizes");
+    GS_ARG_CHECK(n >= 0 && height > 0 && width > 0, "gs_project_noalloc: bad sizes");
+    GS_ARG_CHECK(n <= kNoAllocMaxGaussians,
+                 "gs_project_noalloc: n = %lld, but at most %lld Gaussians fit its fixed "
+                 "scratch; use gs_project with a workspace for more",
+                 (long long)n, (long long)kNoAllocMaxGaussians);
     GS_ARG_CHECK(e && K, "gs_project_noalloc: extrinsics/intrinsics (host) required");
     GS_ARG_CHECK(num_visible_dev, "gs_project_noalloc: num_visible_dev required");
     if (n > 0)

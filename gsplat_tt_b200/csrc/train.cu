@@ -1821,7 +1821,7 @@ extern "C" gs_status gs_sparse_adam_multicast(const gs_gaussians* params,
         all |= (uintptr_t)A.grp[i].p | (uintptr_t)A.grp[i].m | (uintptr_t)A.grp[i].v |
                (uintptr_t)Gm[i] | (uintptr_t)Pm[i];
     GS_ARG_CHECK((all & 15u) == 0, "gs_sparse_adam_multicast: every pointer must be 16-byte aligned");
-    KernelTimer kt("sparse_adam", st);
+    KernelTimer kt("sparse_adam_mc", st);
     const uint32_t rows4 = (uint32_t)(rows / 4);
     k_mc_reduce_counts<<<(unsigned)std::min<int64_t>(div_up(rows4, 256), kNumSMs * 8), 256, 0, st>>>(
         vis_counts_mc, vis_scratch, rows4, skip);

@@ -132,6 +132,11 @@ def random_targets(cams: list[Camera], seed: int = 1) -> list[np.ndarray]:
     return [rng.uniform(0.0, 1.0, (c.height, c.width, 3)).astype(np.float32) for c in cams]
 
 
+# Per-group Adam learning rates of configs[3] (C4; C5 uses the same): SH band 0 at 2.5e-3
+# and bands 1-3 at 1/20 of it, as the reference's DEFAULT_LR (gsplat/train_oracle.py:422-423).
+LR_BASELINE = {"means": 1.6e-4, "log_scales": 5e-3, "quats": 1e-3, "opacity_logits": 5e-2,
+               "sh_dc": 2.5e-3, "sh_rest": 2.5e-3 / 20.0}
+
 CONFIGS = {
     # name: (N, views, width, height, focal, radius, loss)
     "c3": dict(n=500_000, views=1, width=1024, height=1024, f=900.0, radius=4.0,

@@ -452,28 +452,3 @@ class Trainer:
         out["pairs"] = P.value
         return out
 
-
-def smoke_step() -> None:
-    """One small SH3 training step on cuda:0 checked against the oracle (used by smoke())."""
-    from oracle import train as ot
-    from . import scenes
-    params = scenes.cluster_scene(3000, sh_degree=3, seed=5)
-    params["means"] = (params["means"] * 0.5).astype(np.float32)
-    params["log_scales"] = (params["log_scales"] + 1.5).astype(np.float32)
-    H, W = 64, 96
-    cams = [(scenes.look_at((0.2, -0.1, -3.5)), scenes.intrinsics(90.0, W, H), H, W)]
-    tg = [np.random.default_rng(3).uniform(0, 1, (H, W, 3)).astype(np.float32)]
-    cfg = TrainConfig(sh_degree=3, tile_size=16)
-    tr = Trainer(params, cfg, 1, H, W)
-    tr.ensure_capacity(cams)
-    images = torch.empty((1, H, W, 3), device=tr.device)
-    tr.step(cams, tg, check_errors=True, images=images)
-    ocfg = ot.Cfg(sh_degree=3, tile=16)
-    pr = ot.project(params, cams[0][0], cams[0][1], H, W, ocfg)
-    fw = ot.forward(pr, H, W, ocfg)
-    ok = ~fw["ties"]
-    err = float(np.abs(images[0].cpu().numpy() - fw["image"])[ok].max())
-    L, _ = ot.loss_ssim(fw["image"], tg[0])
-    lerr = abs(float(tr.losses[0].item()) - L) / max(abs(L), 1e-12)
-    assert err <= 1e-4, f"train forward image max-abs {err}"
-    assert lerr <= 1e-4, f"train loss rel err {lerr}"

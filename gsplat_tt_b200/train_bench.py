@@ -24,8 +24,7 @@ from ._lib import check, lib, timing_report
 from .dist import view_slice
 from .train import TrainConfig, Trainer
 
-LR_BASELINE = {"means": 1.6e-4, "log_scales": 5e-3, "quats": 1e-3, "opacity_logits": 5e-2,
-               "sh_dc": 2.5e-3, "sh_rest": 2.5e-3 / 20.0}
+LR_BASELINE = scenes.LR_BASELINE
 
 
 def config_name() -> str:
@@ -45,9 +44,15 @@ def train_cfg() -> TrainConfig:
                        lr=dict(LR_BASELINE), betas=(0.9, 0.999), eps=1e-15)
 
 
-def _kernel_bytes(name: str, n: int, views: int, pairs: float, px: int) -> float | None:
-    """Algorithmic DRAM bytes of one timed launch of the HBM-bound kernels (the minimum the
-    algorithm moves, not what the implementation happens to move):
+# Measured NVLink rate used as the multicast update's denominator: a peer copy of 770 GB/s
+# per direction per GPU on this pool's B200s (900 GB/s nominal).
+NVLINK_GBS = 770.0
+
+
+def _kernel_bytes(name: str, n: int, views: int, pairs: float, launches_per_step: float,
+                  adam_rows: int, world: int, q: int) -> float | None:
+    """Algorithmic bytes of ONE timed launch of the kernels with a byte model (the minimum
+    the algorithm moves, not what the implementation happens to move):
 
     * train_project (one launch for all of the rank's views): the SH3 parameters once
       (236 B per Gaussian) and per view the 52 B record (mean 8, conic 12, colour 12,
@@ -56,10 +61,16 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, px: int) -> float
     * tile_sort_emit (pair emission fused into the first tile-sort pass): 16 B per Gaussian
       read (depth order, first-pair offset, rectangle), 8 B per pair written;
     * tile_sort_pass (the second tile-sort pass): 8 B per pair read, 4 B per pair written;
+    * param_bwd: per row the parameters read and their gradients written (236 B each) and
+      the 2D-gradient rows (36 B) of every view; the step's launches split the N rows
+      (one launch on one GPU, one per row chunk with the pipelined multicast update);
     * sparse_adam (the five group launches under one timer): 28 B per parameter value
-      (p, m, v, g read; p, m, v written) for the 59 values of each row;
-    * param_bwd: the parameters read and their gradients written (236 B each per Gaussian)
-      and the 2D-gradient rows (36 B) of every view.
+      (p, m, v, g read; p, m, v written) for the 59 values of each row this rank updates
+      (all N rows on one GPU, its owned rows with the NCCL owner-sharded update);
+    * sparse_adam_mc (NVLink, bytes per direction per GPU): in a launch this GPU owns q
+      rows of a chunk of world * q rows; its partial gradients and count of every row of the
+      chunk leave it for the switch's load-reduce (world * q * 240 B) and its q updated
+      rows leave it for the multicast store (q * 236 B); the same amount arrives.
     The rasterisers and the loss filters are SM-issue bound and have no entry."""
     if name == "train_project":
         return n * 236.0 + views * n * 52.0
@@ -69,16 +80,18 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, px: int) -> float
         return pairs * 8.0 + n * 16.0
     if name == "tile_sort_pass":
         return pairs * 12.0
-    if name == "sparse_adam":
-        return n * 59 * 28.0
     if name == "param_bwd":
-        return n * 472.0 + views * n * 36.0
+        return (n * 472.0 + views * n * 36.0) / max(launches_per_step, 1.0)
+    if name == "sparse_adam":
+        return adam_rows * 59 * 28.0 / max(launches_per_step, 1.0)
+    if name == "sparse_adam_mc":
+        return q * (world * 240.0 + 236.0)
     return None
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch measured by ncu on
 # the C4 scene with one view (3M Gaussians, 21,898,068 pairs), and the unit the traffic
-# scales with when the bench's workload is larger (profiles/train_kernels_c4_1view.md).
+# scales with when the bench's workload is larger.
 NCU_TRAFFIC_C4_1VIEW = {
     "tile_sort_emit": (172.1e6, "pairs"),
     "tile_sort_pass": (247.2e6, "pairs"),
@@ -94,20 +107,26 @@ def _traffic(name: str, pairs: float) -> float | None:
 
 
 def summarize_kernels(rep: dict, ksteps: int, n: int, views: int, pairs: float, px: int,
-                      peaks: dict):
+                      peaks: dict, adam_rows: int | None = None, world: int = 1, q: int = 0):
     """Per-kernel figures from the library's timer report ({name: (total ms, launches)} over
     ksteps steps), the roofline object for the largest kernel with an HBM byte model, and
-    the sort's share of the step."""
+    the sort's share of the step. adam_rows: rows this rank's sparse Adam updates per step
+    (default n); world, q: GPUs and owned rows per chunk of the multicast update."""
+    adam_rows = n if adam_rows is None else adam_rows
     per_kernel = {}
     for k, (tot, cnt) in rep.items():
         avg = tot / cnt
-        entry = {"ms_per_launch": avg, "launches_per_step": cnt / ksteps,
-                 "ms_per_step": tot / ksteps}
-        b = _kernel_bytes(k, n, views, pairs, px)
+        lps = cnt / ksteps
+        entry = {"ms_per_launch": avg, "launches_per_step": lps, "ms_per_step": tot / ksteps}
+        b = _kernel_bytes(k, n, views, pairs, lps, adam_rows, world, q)
         if b is not None:
             gbs = b / (avg / 1e3) / 1e9
-            entry.update({"algorithmic_bytes": b, "achieved_gbs": gbs,
-                          "frac_hbm": gbs / peaks["hbm_gbs"]})
+            if k == "sparse_adam_mc":
+                entry.update({"link_bytes_per_direction": b, "achieved_link_gbs": gbs,
+                              "frac_nvlink": gbs / NVLINK_GBS})
+            else:
+                entry.update({"algorithmic_bytes": b, "achieved_gbs": gbs,
+                              "frac_hbm": gbs / peaks["hbm_gbs"]})
         per_kernel[k] = entry
     # the largest kernel with an HBM byte model (the rasterisers, which take more time, are
     # SM-issue bound: about 72 % issue-active at 1-2 % of DRAM bandwidth per ncu)
@@ -211,7 +230,9 @@ def run(args, rank: int, world: int, local: int) -> dict:
     lib.gs_timing_reset()
     pairs = tr.pairs.float().mean().item()
     peaks = measured_peaks()
-    per_kernel, roofline, sort_in_step = summarize_kernels(rep, ksteps, tr.n, per, pairs, H * W, peaks)
+    adam_rows = tr.n if world == 1 else (tr.chunks * tr.q if tr.multicast else tr.rows_per)
+    per_kernel, roofline, sort_in_step = summarize_kernels(rep, ksteps, tr.n, per, pairs, H * W,
+                                                           peaks, adam_rows, world, tr.q)
     out = {
         "metric": "train-step Mpix/s (fwd+bwd+Adam)",
         "value": value, "unit": "Mpix/s", "n_gpus": world, "steps": args.steps,
@@ -240,64 +261,6 @@ def run(args, rank: int, world: int, local: int) -> dict:
     if sort_in_step is not None:
         out["sort_in_step"] = sort_in_step
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        out["cpu_baseline"] = cpu_baseline(name)
+        from oracle.baseline import train_cpu_baseline
+        out["cpu_baseline"] = train_cpu_baseline(name)
     return out
-
-
-def _oracle_sample(name: str, scale: int, views: int = 1):
-    """The config at 1/scale^2 of the pixels and Gaussians (same density), `views` views."""
-    c = scenes.CONFIGS[name]
-    n = c["n"] // (scale * scale)
-    H, W = c["height"] // scale, c["width"] // scale
-    f = c["f"] / scale
-    cams = scenes.sphere_cameras(views, c["radius"], f, W, H)
-    params = scenes.cluster_scene(n, sh_degree=3, seed=0)
-    tgts = [np.random.default_rng(1000 + i).uniform(0, 1, (H, W, 3)).astype(np.float32)
-            for i in range(views)]
-    return params, cams, tgts, n, H, W
-
-
-def cpu_baseline(name: str, budget_s: float = 20.0, workers: int | None = None) -> dict:
-    """The oracle port of the reference's numpy training models (the reference's CPU
-    implementation of this path is numpy) on this host's cores: a multi-view step at
-    reduced size with one view per worker process (oracle.train_pool), gradients summed
-    and sparse Adam applied once per step, as the reference's per-view loop does."""
-    from oracle import train as ot
-    from oracle.train_pool import ViewPool
-    scale = 8
-    c = scenes.CONFIGS[name]
-    if workers is None:  # the cores this process may run on, up to one per view of the step
-        avail = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-        workers = max(1, min(avail or 1, c["views"]))
-    params, cams, tgts, n, H, W = _oracle_sample(name, scale, views=workers)
-    cfg = ot.Cfg(sh_degree=3, tile=16)
-    zeros = {k: np.zeros_like(v) for k, v in params.items()}
-    vcams = [(cm.w2c, cm.K, H, W) for cm in cams]
-    with ViewPool(params, cfg, workers) as pool:
-        pool.step(zeros, zeros, 0, vcams[:workers], tgts[:workers], lr=LR_BASELINE)  # warm-up
-        t0 = time.perf_counter()
-        iters = 0
-        while True:
-            pool.step(zeros, zeros, 0, vcams, tgts, lr=LR_BASELINE)
-            iters += 1
-            el = time.perf_counter() - t0
-            if el > budget_s or iters >= 3:
-                break
-    return {"value": workers * H * W * iters / el / 1e6, "unit": "Mpix/s", "cores": workers,
-            "kind": "port",
-            "sample": f"{iters} oracle steps of {workers} views {W}x{H} (one per worker process) "
-                      f"with {n} Gaussians ({name.upper()} at 1/{scale * scale} pixels and "
-                      "Gaussians)"}
-
-
-def run_reference(args) -> dict:
-    name = config_name()
-    b = cpu_baseline(name, budget_s=max(10.0, 3.0 * args.steps))
-    return {"impl": "reference", "metric": "train-step Mpix/s (fwd+bwd+Adam)", "value": b["value"],
-            "unit": "Mpix/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": None, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{name.upper()} train step (oracle port, reduced sample)"},
-            "cpu_baseline": b,
-            "e2e": {"value": b["value"], "unit": "Mpix/s", "h2d_bytes_per_step": 0,
-                    "d2h_bytes_per_step": 0}}

@@ -109,8 +109,10 @@ size_t gs_project_workspace_size(int64_t n);
  *   fixed 512 KB array inside libgs200.so, present on every device that loads the library
  *   until the process exits; it bounds n to at most 16,777,216 (2^24) Gaussians, and a
  *   larger n returns GS_ERR_ARG. It calls no allocator.
- *   The first call on a device looks up that array's device address (cudaGetSymbolAddress)
- *   and caches it; make that first call before any stream capture.
+ *   Every call looks up that array's device address in the calling thread's current
+ *   context (cudaGetSymbolAddress, which allocates nothing); the first call in a context
+ *   also loads the library's device code there, so make that first call before any stream
+ *   capture. Arguments are checked in gs_project's order.
  *   All calls share the one array: calls that may overlap on the GPU (different streams or
  *   host threads without ordering between them) race and corrupt each other's results.
  *   Nothing is left over between calls that a later call depends on. */

@@ -26,11 +26,13 @@ _u32 = ctypes.POINTER(ctypes.c_uint32)
 _u64 = ctypes.POINTER(ctypes.c_uint64)
 
 
-def build(ref: bool = False) -> None:
-    """Compile liboracle.so (and, with ref=True, oracle/_ref from the reference sources)."""
+def build(ref: bool = False, ref_root: str | None = None) -> None:
+    """Compile liboracle.so (and, with ref=True, oracle/_ref from the reference sources at
+    ref_root, default $GSPLAT_TT_REFERENCE)."""
     targets = ["oracle"] + (["ref"] if ref else [])
+    extra = [f"REF={ref_root}"] if ref_root else []
     subprocess.check_call(["make", "-s", "-C", _HERE, *targets,
-                           f"PY={sys.executable}"])
+                           f"PY={sys.executable}", *extra])
 
 
 def lib():

@@ -2,7 +2,9 @@
 
 Run in a container where the reference is available (it is not on the GPU box):
 
-    python tests/golden/make_golden.py [--ref /root/reference] [--only display,sort,train]
+    python tests/golden/make_golden.py --ref <reference root> [--only display,sort,train]
+
+(--ref defaults to $GSPLAT_TT_REFERENCE.)
 
 * display.npz -- config C1 (seeded scene of gsplat_tt_b200.scenes.c1_scene) through
   the reference's own compiled CPU pipeline (oracle/_ref/_gsplat_cpu, built from the
@@ -88,11 +90,12 @@ def make_sort(ref) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("GSPLAT_TT_REFERENCE"),
+                    required="GSPLAT_TT_REFERENCE" not in os.environ)
     ap.add_argument("--only", default="display,sort,train")
     a = ap.parse_args()
     parts = a.only.split(",")
-    od.build(ref=True)
+    od.build(ref=True, ref_root=a.ref)
     ref = od.reference_module()
     if ref is None:
         sys.exit("oracle/_ref was not built (is the reference at --ref?)")

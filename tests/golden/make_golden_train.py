@@ -120,11 +120,14 @@ def make_tiled(bbd, tl, t2) -> None:
           "tie Gaussians", int(tie_g.sum()), "visible", int(vis.sum()))
 
 
-def main(ref_root: str = "/root/reference") -> None:
+def main(ref_root: str) -> None:
     to, bbd, tl, t2 = _import_ref(ref_root)
     make_t0(ref_root, to)
     make_tiled(bbd, tl, t2)
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("GSPLAT_TT_REFERENCE")
+    if not root:
+        sys.exit("usage: make_golden_train.py <reference root> (or set GSPLAT_TT_REFERENCE)")
+    main(root)

@@ -40,3 +40,25 @@ def test_summary_without_traffic_entry():
     rep = {"sparse_adam": (2.0, 1), "raster_bwd": (30.0, 1)}
     per_kernel, roof, sort = tb.summarize_kernels(rep, 1, 1000, 1, 5000.0, 100, PEAKS)
     assert roof["kernel"] == "sparse_adam" and roof["traffic"] is None and sort is None
+
+
+def test_chunked_and_owner_sharded_launches_are_charged_their_own_rows():
+    """At N > 1 the projection backward runs once per row chunk and the multicast update
+    moves link bytes, not HBM bytes: no kernel may read above the peak."""
+    n, views, world, q, chunks = 6_000_000, 4, 8, 187_500, 4
+    rep = {"param_bwd": (2.41 * 2, 4 * 2), "sparse_adam_mc": (3.28 * 2, 4 * 2),
+           "tile_sort_emit": (2.0, 8)}
+    per_kernel, roof, _ = tb.summarize_kernels(rep, 2, n, views, 4.6e7, 1920 * 1080, PEAKS,
+                                               adam_rows=chunks * q, world=world, q=q)
+    pb = per_kernel["param_bwd"]
+    assert pb["algorithmic_bytes"] == pytest.approx((n * 472.0 + views * n * 36.0) / 4)
+    assert pb["frac_hbm"] < 1.0
+    mc = per_kernel["sparse_adam_mc"]
+    assert "frac_hbm" not in mc
+    assert mc["link_bytes_per_direction"] == pytest.approx(q * (world * 240 + 236))
+    assert mc["frac_nvlink"] == pytest.approx(mc["achieved_link_gbs"] / tb.NVLINK_GBS)
+    assert roof["kernel"] in ("param_bwd", "tile_sort_emit")
+    # NCCL owner-sharded update: the rank's own rows
+    per_kernel, _, _ = tb.summarize_kernels({"sparse_adam": (1.0, 1)}, 1, n, views, 1.0, 1,
+                                            PEAKS, adam_rows=n // world, world=world)
+    assert per_kernel["sparse_adam"]["algorithmic_bytes"] == pytest.approx(n // world * 59 * 28)

@@ -80,3 +80,12 @@ def test_noalloc_projection_rejects_more_gaussians_than_its_scratch_holds():
                                   None, None)
     assert code == 1  # GS_ERR_ARG
     assert b"at most 16777216" in lib.gs_last_error()
+    # the same checks in the same order as gs_project: the unsupported option first, then
+    # a negative size as a bad size
+    code = lib.gs_project_noalloc(None, None, e, k, None, None, 0.0, (1 << 24) + 1, 8, 8, 0,
+                                  1e-4, 3.0, 1, None, None, None, None, None, None, None, None,
+                                  None, None)
+    assert code == 5  # GS_ERR_UNSUPPORTED
+    code = lib.gs_project_noalloc(None, None, e, k, None, None, 0.0, -1, 8, 8, 0, 1e-4, 3.0, 0,
+                                  None, None, None, None, None, None, None, None, None, None)
+    assert code == 1 and b"bad sizes" in lib.gs_last_error()
