@@ -80,6 +80,35 @@ void gso_cull_and_blend(const float* means_2d, const float* covs_2d, const float
                         float mb_contrib_floor, int cull_disabled,
                         float transmittance_threshold, float* image, int64_t* stats);
 
+/* ------------------------------------------------------------------------------
+ * Training path (oracle/gs_train_oracle.c): C restatement of the numpy training models
+ * of oracle/train.py (forward and backward_2d_exact), multithreaded over tiles, for the
+ * parity checks at full benchmark sizes. sorted_ids: Gaussian ids sorted by tile, then
+ * depth bits; tile_ranges: tiles_x * tiles_y rows of [start, end).
+ * ------------------------------------------------------------------------------ */
+
+/* gsplat/blend_backward_dev.py:404-438 forward_fast (oracle/train.py forward): image
+ * H*W*3, final_T H*W, n_contrib H*W (pairs up to the last blended one), ties H*W (a
+ * decision within 4e-6 relative of its threshold). Returns the number of blended
+ * (pair, pixel) evaluations, or -1 for tile > 32. */
+int64_t gso_train_forward(const float* means2d, const float* conic, const float* opacity,
+                          const float* colors, const int64_t* sorted_ids,
+                          const int64_t* tile_ranges, int height, int width, int tile,
+                          float alpha_max, float alpha_min, float t_min, const float* background,
+                          float* image, float* final_T, int32_t* n_contrib, uint8_t* ties,
+                          int threads);
+
+/* gsplat/blend_backward_ref.py:134-249 terms, float64 back to front (oracle/train.py
+ * backward_2d_exact): grads N*9 float64 (dmx, dmy, dA, dB, dC, dopacity, dr, dg, db);
+ * tie_gaussians (N, may be NULL) marks Gaussians touched by a near-threshold decision.
+ * Returns 0, or -1 for tile > 32. */
+int gso_train_backward(const float* means2d, const float* conic, const float* opacity,
+                       const float* colors, const int64_t* sorted_ids,
+                       const int64_t* tile_ranges, int height, int width, int tile,
+                       float alpha_max, float alpha_min, float t_min, const float* background,
+                       const float* dL_dimage, int64_t n, double* grads, uint8_t* tie_gaussians,
+                       int threads);
+
 /* y[i] = logf(x[i]) with the host C library (checks the device logf reproduction). */
 void gso_logf_array(const float* x, float* y, int64_t n);
 

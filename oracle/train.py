@@ -119,8 +119,10 @@ def sh_basis_grad(dirs, degree):
 
 
 def _exp(x, ft):
-    """exp rounded once to `ft` (computed in float64): the correctly rounded value the
-    device reproduces, in place of numpy's float32 exp."""
+    """exp rounded once to `ft` (computed in float64): the correctly rounded value, in place
+    of numpy's float32 exp (whose last bit is implementation-defined), for the projection's
+    scales and opacities (which the device reproduces) and the rasteriser's Gaussian
+    weights (which the device evaluates with its own exp, covered by the tolerances)."""
     return np.exp(np.asarray(x, np.float64)).astype(ft)
 
 
@@ -282,7 +284,7 @@ def forward(proj, H, W, cfg: Cfg) -> dict:
         Af, Bf, Cf, P0, Lx, Ly = cf
         du, dv = xx - centre, yy - centre
         pw = (P0 + du * (Lx + Af * du + Bf * dv) + dv * (Ly + Cf * dv)).astype(f32)
-        raw = op[g][:, None, None] * np.exp(np.minimum(pw, f32(0)))
+        raw = op[g][:, None, None] * _exp(np.minimum(pw, f32(0)), f32)
         al = np.minimum(raw, amax).astype(f32)
         Tn = T[:n] * (one - al)
         taint[:n] |= ~done[:n] & (near(al, amin) | near(raw, amax)
@@ -339,7 +341,7 @@ def backward_2d(proj, image, dL_dimage, H, W, cfg: Cfg, ties: bool = False):
                                           mxl, myl, centre)
         du, dv = xx - centre, yy - centre
         power = (P0 + du * (Lx + Af * du + Bf * dv) + dv * (Ly + Cf * dv)).astype(f32)
-        wgt = np.exp(np.minimum(power, f32(0))).astype(f32)
+        wgt = _exp(np.minimum(power, f32(0)), f32)
         raw = op[g][:, None, None] * wgt
         clamp = raw > amax
         alpha = np.where(clamp, amax, raw).astype(f32)
@@ -412,7 +414,7 @@ def backward_2d_exact(proj, dL_dimage, H, W, cfg: Cfg, ties: bool = False):
                                           mxl, myl, centre)
         du, dv = xx - centre, yy - centre
         power = (P0 + du * (Lx + Af * du + Bf * dv) + dv * (Ly + Cf * dv)).astype(f32)
-        wgt = np.exp(np.minimum(power, f32(0))).astype(f32)
+        wgt = _exp(np.minimum(power, f32(0)), f32)
         raw = op[g][:, None, None] * wgt
         clamp = raw > amax
         alpha = np.where(clamp, amax, raw).astype(f32)
@@ -427,7 +429,7 @@ def backward_2d_exact(proj, dL_dimage, H, W, cfg: Cfg, ties: bool = False):
         T[:n] = np.where(live, T[:n] * (one - alpha), T[:n])
         recs.append((n, g, mxl, myl, power, wgt, clamp, alpha, live))
     Tc = T.astype(np.float64)
-    behind = Tc * (Gp * np.asarray(cfg.background, np.float64)).sum(-1)
+    behind = Tc * (Gp * np.asarray(cfg.background, f32).astype(np.float64)).sum(-1)
     grads = np.zeros((N, 9), np.float64)
     for (n, g, mxl, myl, power, wgt, clamp, alpha, live) in reversed(recs):
         a, w = alpha.astype(np.float64), wgt.astype(np.float64)
