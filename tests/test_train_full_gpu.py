@@ -88,14 +88,18 @@ def _full_view(name, ssim):
     fw = tf.forward(pr, H, W, ocfg, pairs=pairs)
     ok = ~fw["ties"]
     assert ok.mean() > 0.99
-    assert np.abs(img - fw["image"])[ok].max() <= IMG_TOL
+    img_err = float(np.abs(img - fw["image"])[ok].max())
+    print(f"{name}: image max-abs {img_err:.2e} on {ok.mean():.4%} of pixels")
+    assert img_err <= IMG_TOL
     # the loss and the 2D backward are evaluated on the device's own image
     L, dimg = (ot.loss_ssim if ssim else ot.loss_l1)(img, target, lam)
     assert abs(float(tr.losses[0].item()) - L) <= 1e-5 * abs(L)
     gref, ties = tf.backward_2d_exact(pr, dimg, H, W, ocfg, ties=True, pairs=pairs)
     keep = ~ties
     assert keep.mean() > 0.85  # a tainted pixel marks every later pair reaching it
-    assert ot.rel_error(g2d[keep], gref[keep]) <= GRAD_TOL
+    g_err = ot.rel_error(g2d[keep], gref[keep])
+    print(f"{name}: 2D gradients rel {g_err:.2e} on {keep.mean():.2%} of Gaussians")
+    assert g_err <= GRAD_TOL
     del gref, fw
     # The projection backward and Adam are per-row maps (a row's result depends on its own
     # parameters and 2D gradient only), so above 600k Gaussians they are checked on a
@@ -113,8 +117,10 @@ def _full_view(name, ssim):
     del pr
     gp = ot.param_backward(sub, g2d[idx], w2c, K, H, W, ocfg, ft=np.float64)
     dev = {k: v[idx] for k, v in tr.grads.numpy().items()}
+    errs = {k: ot.rel_error(dev[k], gp[k]) for k in ot.PARAM_NAMES}
+    print(f"{name}: parameter gradients rel " + ", ".join(f"{k} {e:.2e}" for k, e in errs.items()))
     for k in ot.PARAM_NAMES:
-        assert ot.rel_error(dev[k], gp[k]) <= GRAD_TOL, k
+        assert errs[k] <= GRAD_TOL, k
     del gp
     zeros = {k: np.zeros_like(v) for k, v in sub.items()}
     p1, m1, v1 = ot.sparse_adam(sub, dev, zeros, zeros, 0, vis[idx], tr.cfg.lr)
