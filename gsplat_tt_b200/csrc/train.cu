@@ -1493,6 +1493,85 @@ static bool is_host_pointer(const void* p) {
     return a.type == cudaMemoryTypeHost || a.type == cudaMemoryTypeUnregistered;
 }
 
+// The loss's constants: 11-tap Gaussian (sigma 1.5) filter weights and lambda_dssim.
+static LossCfg make_loss_cfg(const gs_train_config& cfg) {
+    LossCfg LC;
+    double taps[11], sum = 0.0;
+    for (int k = 0; k < 11; ++k) {
+        const double xk = k - 5;
+        taps[k] = std::exp(-(xk * xk) / (2.0 * 1.5 * 1.5));
+        sum += taps[k];
+    }
+    for (int k = 0; k < 11; ++k) LC.taps[k] = (float)(taps[k] / sum);
+    // (1 - lambda) L1 [+ lambda (1 - SSIM)]; a pure L1 loss is lambda = 0 without SSIM.
+    LC.lambda = cfg.lambda_dssim;
+    LC.H = LC.W = 0;
+    LC.inv_n = 0.0f;
+    return LC;
+}
+
+static gs_status ssim_smem_attributes() {
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_ssim_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(SsimFwdSmem)));
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_ssim_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sizeof(SsimBwdSmem)));
+    return GS_OK;
+}
+
+// Forward rasteriser of one sorted view into img (H*W*3) and the lane's final T / counts.
+static gs_status launch_raster_fwd(const TCfg& c, const ViewLane& V, const ProjView& pvv, int vh,
+                                   int vw, float* img, cudaStream_t st) {
+    KernelTimer kt("raster_fwd", st);
+    const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
+    if (c.tile == 16)
+        k_train_fwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
+    else
+        k_train_fwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
+    GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
+// Loss of one view and its gradient dimg; the loss lands in *loss_out (device) from the
+// two float64 accumulators at acc (zeroed by the caller). dmu / dxx / dxy: SSIM scratch.
+static gs_status launch_loss(const float* img, const float* target, int vh, int vw, int use_ssim,
+                             LossCfg LC, float* dmu, float* dxx, float* dxy, float* dimg,
+                             double* acc, float* loss_out, cudaStream_t st) {
+    KernelTimer kt("loss", st);
+    LC.H = vh;
+    LC.W = vw;
+    LC.inv_n = (float)(1.0 / (3.0 * vh * vw));
+    const int64_t n3 = (int64_t)vh * vw * 3;
+    if (use_ssim) {
+        dim3 grid(div_up(vw, kSsimT), div_up(vh, kSsimT));
+        k_ssim_fwd<<<grid, 256, sizeof(SsimFwdSmem), st>>>(img, target, LC, dmu, dxx, dxy, acc);
+        GS_CHECK_LAUNCH();
+        k_ssim_bwd<<<grid, 256, sizeof(SsimBwdSmem), st>>>(img, target, dmu, dxx, dxy, LC, dimg);
+    } else {
+        k_loss_l1<<<(unsigned int)std::min<int64_t>(div_up(n3, 256), kNumSMs * 8), 256, 0, st>>>(
+            img, target, n3, LC, dimg, acc);
+    }
+    GS_CHECK_LAUNCH();
+    k_loss_finalize<<<1, 1, 0, st>>>(acc, LC, use_ssim, loss_out);
+    GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
+// Backward rasteriser of one view: 2D-gradient rows g2 from dimg and the lane's final T /
+// counts of the same view's forward.
+static gs_status launch_raster_bwd(const TCfg& c, const ViewLane& V, const ProjView& pvv, int vh,
+                                   int vw, const float* dimg, float* g2, cudaStream_t st) {
+    KernelTimer kt("raster_bwd", st);
+    const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
+    if (c.tile == 16)
+        k_train_bwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
+                                                                        V.final_T, V.ncon, g2);
+    else
+        k_train_bwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
+                                                                         V.final_T, V.ncon, g2);
+    GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
 static gs_status run_view(int64_t n, int v, const gs_camera& cam, const gs_train_config& cfg,
                           LossCfg LC, const float* target, float* images, float* grad2d_out,
                           float* view_losses, TrainWs& L, ViewLane& V, int64_t cap,
@@ -1520,49 +1599,15 @@ static gs_status run_view(int64_t n, int v, const gs_camera& cam, const gs_train
     if (s != GS_OK) return s;
     const ProjView pvv = L.pv.view(v, n);
     float* img = images ? images + (size_t)v * vh * vw * 3 : V.image;
-    const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
-    {
-        KernelTimer kt("raster_fwd", st);
-        if (c.tile == 16)
-            k_train_fwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
-        else
-            k_train_fwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
-        GS_CHECK_LAUNCH();
-    }
-    LC.H = vh;
-    LC.W = vw;
-    LC.inv_n = (float)(1.0 / (3.0 * vh * vw));
+    s = launch_raster_fwd(c, V, pvv, vh, vw, img, st);
+    if (s != GS_OK) return s;
     if (host_target && LS != nullptr) GS_CUDA_CHECK(cudaStreamWaitEvent(st, LS->staged[lane], 0));
-    {
-        KernelTimer kt("loss", st);
-        const int64_t n3 = (int64_t)vh * vw * 3;
-        if (cfg.use_ssim) {
-            dim3 grid(div_up(vw, kSsimT), div_up(vh, kSsimT));
-            k_ssim_fwd<<<grid, 256, sizeof(SsimFwdSmem), st>>>(img, target, LC, V.dmu, V.dxx,
-                                                               V.dxy, L.loss_acc + 2 * v);
-            GS_CHECK_LAUNCH();
-            k_ssim_bwd<<<grid, 256, sizeof(SsimBwdSmem), st>>>(img, target, V.dmu, V.dxx, V.dxy,
-                                                               LC, V.dimg);
-        } else {
-            k_loss_l1<<<(unsigned int)std::min<int64_t>(div_up(n3, 256), kNumSMs * 8), 256, 0, st>>>(
-                img, target, n3, LC, V.dimg, L.loss_acc + 2 * v);
-        }
-        GS_CHECK_LAUNCH();
-        k_loss_finalize<<<1, 1, 0, st>>>(L.loss_acc + 2 * v, LC, cfg.use_ssim, view_losses + v);
-        GS_CHECK_LAUNCH();
-    }
+    s = launch_loss(img, target, vh, vw, cfg.use_ssim, LC, V.dmu, V.dxx, V.dxy, V.dimg,
+                    L.loss_acc + 2 * v, view_losses + v, st);
+    if (s != GS_OK) return s;
     if (host_target && LS != nullptr) GS_CUDA_CHECK(cudaEventRecord(LS->consumed[lane], st));
-    {
-        KernelTimer kt("raster_bwd", st);
-        float* g2 = L.grad2d + (size_t)v * n * kGradStride;
-        if (c.tile == 16)
-            k_train_bwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, V.dimg,
-                                                     V.final_T, V.ncon, g2);
-        else
-            k_train_bwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, V.dimg,
-                                                      V.final_T, V.ncon, g2);
-        GS_CHECK_LAUNCH();
-    }
+    s = launch_raster_bwd(c, V, pvv, vh, vw, V.dimg, L.grad2d + (size_t)v * n * kGradStride, st);
+    if (s != GS_OK) return s;
     if (grad2d_out) {
         k_export_grad2d<<<div_up(n, 256), 256, 0, st>>>(L.grad2d, L.touch, n, v,
                                                         grad2d_out + (size_t)v * n * 9);
@@ -1683,6 +1728,137 @@ extern "C" gs_status gs_train_project_view(const gs_gaussians* params, int64_t n
     if (*pairs_host > 0)
         GS_CUDA_CHECK(cudaMemcpyAsync(sorted_ids, V.svals, *pairs_host * sizeof(uint32_t),
                                       cudaMemcpyDeviceToDevice, st));
+    return GS_OK;
+}
+
+// ------------------------------------------------------------------ stage entry points
+//
+// One view's forward, loss and backward as separate calls, in the order of the reference's
+// staged chain (forward_fast -> loss_and_grad_device -> ref_slots_fast -> t2_step). The
+// forward leaves the view's projected records, sorted pairs, tile ranges, final
+// transmittance and per-pixel counts in a training workspace laid out for one view; the
+// backward and gs_train_param_backward read them from there.
+
+static gs_status stage_layout(const char* who, int64_t n, const gs_camera* cam,
+                              const gs_train_config* cfg, int64_t cap, void* workspace,
+                              size_t workspace_bytes, TrainWs& L) {
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(cam != nullptr && workspace != nullptr, "%s: null argument", who);
+    GS_ARG_CHECK(n > 0 && n < (1ll << 32), "%s: n must be in [1, 2^32)", who);
+    GS_ARG_CHECK(cap >= 1 && cap < (1ll << 30), "%s: pair_capacity must be in [1, 2^30)", who);
+    GS_ARG_CHECK(image_fits(cam->height, cam->width, cfg->tile_size),
+                 "%s: image must be 1..%d tile rows and 1..65535 tile columns", who, kMaxTileRows);
+    Workspace ws(workspace, workspace_bytes);
+    train_layout(ws, L, n, 1, cam->height, cam->width, cfg->tile_size, cap);
+    GS_ARG_CHECK(ws.ok(), "%s: workspace too small (%zu < %zu)", who, workspace_bytes,
+                 gs_train_workspace_size(n, cfg->sh_degree, 1, cam->height, cam->width,
+                                         cfg->tile_size, cap));
+    return GS_OK;
+}
+
+extern "C" gs_status gs_render_fwd(const gs_gaussians* params, int64_t n, const gs_camera* cam,
+                                   const gs_train_config* cfg, float* image, float* final_T,
+                                   int32_t* n_contrib, float* vis_counts, int64_t* pairs,
+                                   int64_t pair_capacity, void* workspace,
+                                   size_t workspace_bytes, void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    GS_ARG_CHECK(params && image, "gs_render_fwd: null argument");
+    GS_ARG_CHECK(((uintptr_t)params->quats & 15) == 0, "gs_render_fwd: quats must be 16-byte aligned");
+    TrainWs L;
+    gs_status s = stage_layout("gs_render_fwd", n, cam, cfg, pair_capacity, workspace,
+                               workspace_bytes, L);
+    if (s != GS_OK) return s;
+    const int H = cam->height, W = cam->width;
+    GS_CUDA_CHECK(cudaMemsetAsync(L.err, 0, sizeof(unsigned int), st));
+    GS_CUDA_CHECK(cudaMemsetAsync(L.touch, 0, n * sizeof(uint64_t), st));
+    if (vis_counts) GS_CUDA_CHECK(cudaMemsetAsync(vis_counts, 0, n * sizeof(float), st));
+    const TCam tc = make_tcam(*cam);
+    const TCfg c = make_tcfg(*cfg, H, W);
+    GS_CUDA_CHECK(cudaMemcpyAsync(L.cams, &tc, sizeof(TCam), cudaMemcpyHostToDevice, st));
+    // with_grad: the view's 2D-gradient rows are zeroed for the later gs_render_bwd
+    s = project_views(gconst(params), n, 1, c, L, vis_counts, true, st);
+    if (s != GS_OK) return s;
+    ViewLane& V = L.lane[0];
+    s = sort_view(n, c, 0, L, V, pair_capacity, st);
+    if (s != GS_OK) return s;
+    s = launch_raster_fwd(c, V, L.pv.view(0, n), H, W, image, st);
+    if (s != GS_OK) return s;
+    const size_t px = (size_t)H * W;
+    if (final_T)
+        GS_CUDA_CHECK(cudaMemcpyAsync(final_T, V.final_T, px * sizeof(float), cudaMemcpyDeviceToDevice, st));
+    if (n_contrib)
+        GS_CUDA_CHECK(cudaMemcpyAsync(n_contrib, V.ncon, px * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+    if (pairs)
+        GS_CUDA_CHECK(cudaMemcpyAsync(pairs, L.pairs, sizeof(int64_t), cudaMemcpyDeviceToDevice, st));
+    return GS_OK;
+}
+
+static void loss_layout(Workspace& ws, int32_t height, int32_t width, double** acc, float** dmu,
+                        float** dxx, float** dxy) {
+    const size_t px3 = (size_t)height * width * 3;
+    *acc = ws.take<double>(2);
+    *dmu = ws.take<float>(px3);
+    *dxx = ws.take<float>(px3);
+    *dxy = ws.take<float>(px3);
+}
+
+extern "C" size_t gs_loss_workspace_size(int32_t height, int32_t width) {
+    if (height < 1) height = 1;
+    if (width < 1) width = 1;
+    WorkspaceSizer z;
+    const size_t px3 = (size_t)height * width * 3;
+    z.take<double>(2);
+    z.take<float>(px3);
+    z.take<float>(px3);
+    z.take<float>(px3);
+    return z.bytes();
+}
+
+extern "C" gs_status gs_loss(const float* image, const float* target, int32_t height,
+                             int32_t width, const gs_train_config* cfg, float* loss,
+                             float* dL_dimage, void* workspace, size_t workspace_bytes,
+                             void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(image && target && loss && dL_dimage && workspace, "gs_loss: null argument");
+    GS_ARG_CHECK(height > 0 && width > 0, "gs_loss: bad sizes");
+    Workspace ws(workspace, workspace_bytes);
+    double* acc;
+    float *dmu, *dxx, *dxy;
+    loss_layout(ws, height, width, &acc, &dmu, &dxx, &dxy);
+    GS_ARG_CHECK(ws.ok(), "gs_loss: workspace too small (%zu < %zu)", workspace_bytes,
+                 gs_loss_workspace_size(height, width));
+    if (cfg->use_ssim) {
+        gs_status ss = ssim_smem_attributes();
+        if (ss != GS_OK) return ss;
+    }
+    GS_CUDA_CHECK(cudaMemsetAsync(acc, 0, 2 * sizeof(double), st));
+    return launch_loss(image, target, height, width, cfg->use_ssim, make_loss_cfg(*cfg), dmu, dxx,
+                       dxy, dL_dimage, acc, loss, st);
+}
+
+extern "C" gs_status gs_render_bwd(int64_t n, const gs_camera* cam, const gs_train_config* cfg,
+                                   const float* dL_dimage, float* grad2d, int64_t pair_capacity,
+                                   void* workspace, size_t workspace_bytes, void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    GS_ARG_CHECK(dL_dimage, "gs_render_bwd: null dL_dimage");
+    TrainWs L;
+    gs_status s = stage_layout("gs_render_bwd", n, cam, cfg, pair_capacity, workspace,
+                               workspace_bytes, L);
+    if (s != GS_OK) return s;
+    const int H = cam->height, W = cam->width;
+    const TCfg c = make_tcfg(*cfg, H, W);
+    s = launch_raster_bwd(c, L.lane[0], L.pv.view(0, n), H, W, dL_dimage, L.grad2d, st);
+    if (s != GS_OK) return s;
+    if (grad2d) {
+        k_export_grad2d<<<div_up(n, 256), 256, 0, st>>>(L.grad2d, L.touch, n, 0, grad2d);
+        GS_CHECK_LAUNCH();
+    }
     return GS_OK;
 }
 
@@ -1931,24 +2107,10 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
     // vector may go out of scope afterwards.
     GS_CUDA_CHECK(cudaMemcpyAsync(L.cams, hc.data(), n_views * sizeof(TCam), cudaMemcpyHostToDevice, st));
 
-    LossCfg LC;
-    {
-        double taps[11], sum = 0.0;
-        for (int k = 0; k < 11; ++k) {
-            const double xk = k - 5;
-            taps[k] = std::exp(-(xk * xk) / (2.0 * 1.5 * 1.5));
-            sum += taps[k];
-        }
-        for (int k = 0; k < 11; ++k) LC.taps[k] = (float)(taps[k] / sum);
-        // (1 - lambda) L1 [+ lambda (1 - SSIM)]; a pure L1 loss is lambda = 0 without SSIM.
-        LC.lambda = cfg->lambda_dssim;
-    }
-
+    const LossCfg LC = make_loss_cfg(*cfg);
     if (cfg->use_ssim) {
-        GS_CUDA_CHECK(cudaFuncSetAttribute(k_ssim_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)sizeof(SsimFwdSmem)));
-        GS_CUDA_CHECK(cudaFuncSetAttribute(k_ssim_bwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           (int)sizeof(SsimBwdSmem)));
+        gs_status ss = ssim_smem_attributes();
+        if (ss != GS_OK) return ss;
     }
     {
         gs_status s = project_views(P, n, n_views, make_tcfg(*cfg, H, W), L, vis_counts, true, st);

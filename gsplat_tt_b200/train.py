@@ -72,6 +72,14 @@ lib.gs_sparse_adam_multicast.argtypes = [_G, _G, _G, _G, _G, _vp, _vp, _i64, _i6
 lib.gs_train_param_backward.restype = ctypes.c_int
 lib.gs_train_param_backward.argtypes = [_G, _G, _i64, _i64, _i64, _C, _i32, _CFG, _i64, _vp, _sz, _vp]
 GS_STEP_DEFER_PARAM_BWD = 2
+lib.gs_render_fwd.restype = ctypes.c_int
+lib.gs_render_fwd.argtypes = [_G, _i64, _C, _CFG, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _sz, _vp]
+lib.gs_loss.restype = ctypes.c_int
+lib.gs_loss.argtypes = [_vp, _vp, _i32, _i32, _CFG, _vp, _vp, _vp, _sz, _vp]
+lib.gs_loss_workspace_size.restype = _sz
+lib.gs_loss_workspace_size.argtypes = [_i32, _i32]
+lib.gs_render_bwd.restype = ctypes.c_int
+lib.gs_render_bwd.argtypes = [_i64, _C, _CFG, _vp, _vp, _i64, _vp, _sz, _vp]
 lib.gs_train_project_view.restype = ctypes.c_int
 lib.gs_train_project_view.argtypes = [_G, _i64, _C, _CFG, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                       _vp, _vp, _i64, ctypes.POINTER(_i64), _vp, _sz, _vp]
@@ -452,3 +460,88 @@ class Trainer:
         out["pairs"] = P.value
         return out
 
+
+class StagedView:
+    """One view's training step as separate stage calls, in the order of the reference's
+    staged chain: ``forward`` (gsplat/blend_backward_dev.py:404 forward_fast, through
+    gs_render_fwd), ``loss`` (gsplat/train_loss.py:126 loss_and_grad_device / :166
+    loss_and_grad_l1, gs_loss), ``backward`` (blend_backward_dev.py:444 ref_slots_fast
+    summed per Gaussian, gs_render_bwd), ``param_backward`` (gsplat/t2_param_backward.py:123
+    projection backward into ``trainer.grads``, gs_train_param_backward) and ``adam``
+    (gsplat/train_oracle.py:434 sparse_adam_step, gs_sparse_adam). It works on the
+    parameters, moments and gradients of a single-GPU ``Trainer`` and keeps its own one-view
+    workspace; each stage must follow the previous one on the same view."""
+
+    def __init__(self, trainer: "Trainer", height: int, width: int):
+        self.tr = trainer
+        self.H, self.W = int(height), int(width)
+        cfg = trainer.cfg
+        self.ws = torch.empty(lib.gs_train_workspace_size(trainer.n, cfg.sh_degree, 1, self.H, self.W,
+                                                          cfg.tile_size, trainer.capacity),
+                              dtype=torch.uint8, device=trainer.device)
+        self.lws = torch.empty(lib.gs_loss_workspace_size(self.H, self.W), dtype=torch.uint8,
+                               device=trainer.device)
+        self.cam = None
+        self.pairs = torch.zeros(1, dtype=torch.int64, device=trainer.device)
+
+    def forward(self, w2c, K):
+        """Image (H, W, 3) of the view; also sets trainer.vis_counts for this view."""
+        tr = self.tr
+        self.cam = camera_struct(w2c, K, self.H, self.W)
+        img = torch.empty((self.H, self.W, 3), dtype=torch.float32, device=tr.device)
+        self.final_T = torch.empty((self.H, self.W), dtype=torch.float32, device=tr.device)
+        self.n_contrib = torch.empty((self.H, self.W), dtype=torch.int32, device=tr.device)
+        p = tr.params.c_struct()
+        check(lib.gs_render_fwd(ctypes.byref(p), tr.n, ctypes.byref(self.cam), ctypes.byref(tr.ccfg),
+                                img.data_ptr(), self.final_T.data_ptr(), self.n_contrib.data_ptr(),
+                                tr.vis_counts.data_ptr(), self.pairs.data_ptr(), tr.capacity,
+                                self.ws.data_ptr(), self.ws.numel(),
+                                torch.cuda.current_stream().cuda_stream))
+        return img
+
+    def overflowed(self) -> bool:
+        """True when the forward's pairs exceeded the trainer's pair capacity."""
+        code = lib.gs_workspace_error(self.ws.data_ptr(), torch.cuda.current_stream().cuda_stream)
+        if code not in (_lib.GS_OK, _lib.GS_ERR_OVERFLOW):
+            check(code)
+        return code == _lib.GS_ERR_OVERFLOW
+
+    def loss(self, image, target):
+        """(loss as a 1-element device tensor, dL/dimage (H, W, 3))."""
+        tr = self.tr
+        t = target if isinstance(target, torch.Tensor) else torch.from_numpy(
+            np.ascontiguousarray(target, np.float32))
+        t = t.to(tr.device, torch.float32).contiguous()
+        loss = torch.empty(1, dtype=torch.float32, device=tr.device)
+        dimg = torch.empty_like(image)
+        check(lib.gs_loss(image.data_ptr(), t.data_ptr(), self.H, self.W, ctypes.byref(tr.ccfg),
+                          loss.data_ptr(), dimg.data_ptr(), self.lws.data_ptr(), self.lws.numel(),
+                          torch.cuda.current_stream().cuda_stream))
+        return loss, dimg
+
+    def backward(self, dL_dimage):
+        """Per-Gaussian 2D gradients (N, 9): dmx, dmy, dA, dB, dC, dopacity, dr, dg, db."""
+        tr = self.tr
+        g2d = torch.empty((tr.n, 9), dtype=torch.float32, device=tr.device)
+        check(lib.gs_render_bwd(tr.n, ctypes.byref(self.cam), ctypes.byref(tr.ccfg),
+                                dL_dimage.contiguous().data_ptr(), g2d.data_ptr(), tr.capacity,
+                                self.ws.data_ptr(), self.ws.numel(),
+                                torch.cuda.current_stream().cuda_stream))
+        return g2d
+
+    def param_backward(self) -> None:
+        """Parameter gradients of the view into trainer.grads."""
+        tr = self.tr
+        p, g = tr.params.c_struct(), tr.grads.c_struct()
+        check(lib.gs_train_param_backward(ctypes.byref(p), ctypes.byref(g), tr.n, 0, tr.n,
+                                          ctypes.byref(self.cam), 1, ctypes.byref(tr.ccfg),
+                                          tr.capacity, self.ws.data_ptr(), self.ws.numel(),
+                                          torch.cuda.current_stream().cuda_stream))
+
+    def adam(self, step: int) -> None:
+        """Sparse Adam over the rows visible in the view."""
+        tr = self.tr
+        p, m, v, g = (b.c_struct() for b in (tr.params, tr.m, tr.v, tr.grads))
+        check(lib.gs_sparse_adam(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
+                                 tr.vis_counts.data_ptr(), tr.n, int(step), ctypes.byref(tr.ccfg),
+                                 None, torch.cuda.current_stream().cuda_stream))

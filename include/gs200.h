@@ -302,6 +302,50 @@ gs_status gs_train_project_view(const gs_gaussians* params, int64_t n, const gs_
                                 int64_t pair_capacity, int64_t* pairs_host, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/* ------------------------------------------------------------------------------
+ * Training stages of one view, as separate calls (the reference's staged chain):
+ * gs_render_fwd -> gs_loss -> gs_render_bwd -> gs_train_param_backward (rows [0, n),
+ * n_views = 1) -> gs_sparse_adam. The forward leaves the view's projected records, sorted
+ * pairs, tile ranges, final transmittance and per-pixel pair counts in `workspace` (a
+ * training workspace of gs_train_workspace_size(n, sh_degree, 1, H, W, tile, pair_capacity)
+ * bytes); the backward and gs_train_param_backward read them from there, so they take the
+ * same workspace, n, cam, cfg and pair_capacity, with no other call on that workspace in
+ * between. A pair overflow is reported by gs_workspace_error(workspace) after the forward.
+ * ------------------------------------------------------------------------------ */
+
+/* gsplat/blend_backward_dev.py:404-438 forward_fast (with the projection of
+ * gsplat/t2_param_backward.py:81-120 and the pairs of blend_backward_dev.py:76-112):
+ * projection + SH colour, tile intersection, sort, tile ranges and the training-rule
+ * forward rasteriser of one view. image H*W*3 (device); final_T H*W and n_contrib H*W
+ * (pairs up to the last blended one) are optional copies of the state the backward uses;
+ * vis_counts (nullable, N floats) is set to 1 where the Gaussian is visible (for
+ * gs_sparse_adam); pairs (nullable, device int64) receives the pair count. */
+gs_status gs_render_fwd(const gs_gaussians* params, int64_t n, const gs_camera* cam,
+                        const gs_train_config* cfg, float* image, float* final_T,
+                        int32_t* n_contrib, float* vis_counts, int64_t* pairs,
+                        int64_t pair_capacity, void* workspace, size_t workspace_bytes,
+                        void* stream);
+
+/* gsplat/train_loss.py:126-165 loss_and_grad_device ((1 - lambda) L1 + lambda (1 - SSIM),
+ * 11x11 Gaussian window, sigma 1.5, zero padding) when cfg->use_ssim, else
+ * train_loss.py:166-171 loss_and_grad_l1 ((1 - lambda) L1): the loss of image against
+ * target (both H*W*3, device) into *loss (device float) and its gradient into dL_dimage
+ * (H*W*3). workspace: gs_loss_workspace_size(height, width) bytes. */
+gs_status gs_loss(const float* image, const float* target, int32_t height, int32_t width,
+                  const gs_train_config* cfg, float* loss, float* dL_dimage, void* workspace,
+                  size_t workspace_bytes, void* stream);
+size_t gs_loss_workspace_size(int32_t height, int32_t width);
+
+/* gsplat/blend_backward_dev.py:444-517 ref_slots_fast summed per Gaussian
+ * (gsplat/t2_param_backward.py:50-61 segment_reduce): the blend backward of the view of the
+ * last gs_render_fwd on `workspace`, replayed back to front from its final transmittance,
+ * given dL_dimage (H*W*3, device). The per-Gaussian 2D gradients stay in the workspace for
+ * gs_train_param_backward; grad2d (nullable, device, N*9: dmx, dmy, dA, dB, dC, dopacity,
+ * dr, dg, db) receives a copy. */
+gs_status gs_render_bwd(int64_t n, const gs_camera* cam, const gs_train_config* cfg,
+                        const float* dL_dimage, float* grad2d, int64_t pair_capacity,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
 /* Sparse Adam over rows with vis_counts > 0 (gsplat/train_oracle.py:434-470
  * sparse_adam_step; gsplat/t2_param_backward.py:195-223 adam_step): fp32 arithmetic,
  * moments stored fp32 or bf16 per cfg->bf16_moments, lr per group with SH band 0 at
@@ -316,7 +360,7 @@ gs_status gs_sparse_adam(const gs_gaussians* params, const gs_gaussians* exp_avg
 /* Projection backward (2D gradients -> grads of means, log-scales, quaternions, opacity
  * logits and SH) of Gaussian rows [row_begin, row_end) after a gs_train_step call with
  * apply_adam = GS_STEP_DEFER_PARAM_BWD on the same workspace, n, cams, n_views, cfg and
- * pair_capacity. Rows outside the range are not touched. gsplat/t2_param_backward.py:123-192
+ * pair_capacity, or after gs_render_fwd + gs_render_bwd (n_views = 1). Rows outside the range are not touched. gsplat/t2_param_backward.py:123-192
  * projection_backward_sh0, extended to SH1-3 and summed over the step's views. */
 gs_status gs_train_param_backward(const gs_gaussians* params, const gs_gaussians* grads,
                                   int64_t n, int64_t row_begin, int64_t row_end,

@@ -105,3 +105,34 @@ def test_training_update_argument_errors_need_no_device():
                              ctypes.c_void_p(16), 100, 0, cams, tg, 1, ctypes.byref(cfg), 3,
                              ctypes.c_void_p(16), None, None, None, 1000, ws, 1 << 30,
                              None) == GS_ERR_ARG
+
+
+def test_stage_entry_points_argument_errors_need_no_device():
+    """gs_render_fwd / gs_loss / gs_render_bwd check their arguments and workspace sizes on
+    the host before any device call."""
+    from gsplat_tt_b200._lib import GS_ERR_ARG
+    from gsplat_tt_b200.train import GsGaussians, TrainConfig, camera_struct, lib
+    import numpy as np
+    cfg = TrainConfig(sh_degree=3).c_struct()
+    g = GsGaussians(16, 16, 16, 16, 16)
+    cam = camera_struct(np.eye(4), np.eye(3), 64, 64)
+    ws = ctypes.c_void_p(256)
+    p = ctypes.c_void_p(16)
+    assert lib.gs_render_fwd(None, 100, ctypes.byref(cam), ctypes.byref(cfg), p, None, None, None,
+                             None, 1000, ws, 1 << 30, None) == GS_ERR_ARG
+    assert lib.gs_render_fwd(ctypes.byref(g), 100, ctypes.byref(cam), ctypes.byref(cfg), p, None,
+                             None, None, None, 1000, ws, 16, None) == GS_ERR_ARG
+    assert b"workspace too small" in lib.gs_last_error()
+    bad = GsGaussians(16, 16, 20, 16, 16)
+    assert lib.gs_render_fwd(ctypes.byref(bad), 100, ctypes.byref(cam), ctypes.byref(cfg), p, None,
+                             None, None, None, 1000, ws, 1 << 30, None) == GS_ERR_ARG
+    assert b"16-byte" in lib.gs_last_error()
+    big = camera_struct(np.eye(4), np.eye(3), 64, 70000 * 16)
+    assert lib.gs_render_bwd(100, ctypes.byref(big), ctypes.byref(cfg), p, None, 1000, ws, 1 << 30,
+                             None) == GS_ERR_ARG
+    assert lib.gs_render_bwd(100, ctypes.byref(cam), ctypes.byref(cfg), None, None, 1000, ws,
+                             1 << 30, None) == GS_ERR_ARG
+    assert lib.gs_loss_workspace_size(64, 64) >= 3 * 64 * 64 * 3 * 4
+    assert lib.gs_loss(p, p, 64, 64, ctypes.byref(cfg), p, p, ws, 16, None) == GS_ERR_ARG
+    assert b"workspace too small" in lib.gs_last_error()
+    assert lib.gs_loss(p, None, 64, 64, ctypes.byref(cfg), p, p, ws, 1 << 30, None) == GS_ERR_ARG

@@ -230,3 +230,52 @@ def test_host_targets_match_device_targets():
             # elementwise relative error (floor 1e-4 of the largest): gradients that nearly
             # cancel carry the atomics-order noise of two runs at a few 1e-5
             assert ot.rel_error(g[k], results[0][1][k]) <= 1e-4, k
+
+
+@pytest.mark.parametrize("deg,tile,ssim", [(3, 16, True), (1, 32, False)])
+def test_staged_chain_matches_train_step_and_oracle(deg, tile, ssim):
+    """gs_render_fwd -> gs_loss -> gs_render_bwd -> gs_train_param_backward -> gs_sparse_adam
+    through the C ABI: the same image and loss as gs_train_step on the view (the same
+    kernels), the same 2D and parameter gradients up to the order of the backward's float
+    atomics, the same Adam update; and the oracle's image, loss and 2D gradients."""
+    import torch
+    from gsplat_tt_b200.train import StagedView
+    params = small_scene(8000, deg, seed=40 + deg)
+    H, W = 72, 104
+    cams = cams_for(1, H, W, 100.0, seed=6)
+    target = scenes.random_targets([scenes.Camera(cams[0][0], cams[0][1], H, W)], seed=3)[0]
+    lam = 0.2 if ssim else 0.0
+    ref, img_ref, g2d_ref = run_step(params, deg, tile, cams, [target], ssim=ssim, lam=lam)
+
+    tr, _ = trainer(params, deg, tile, 1, H, W, use_ssim=ssim, lambda_dssim=lam)
+    tr.ensure_capacity(cams)
+    sv = StagedView(tr, H, W)
+    img = sv.forward(cams[0][0], cams[0][1])
+    assert not sv.overflowed()
+    loss, dimg = sv.loss(img, target)
+    g2d = sv.backward(dimg)
+    sv.param_backward()
+    sv.adam(0)
+    torch.cuda.synchronize()
+    img_np = img.cpu().numpy()
+    np.testing.assert_array_equal(img_np, img_ref[0])
+    assert float(loss.item()) == float(ref.losses[0].item())
+    assert ot.rel_error(g2d.cpu().numpy(), g2d_ref[0]) <= 1e-4
+    for k in ot.PARAM_NAMES:
+        assert ot.rel_error(tr.grads.numpy()[k], ref.grads.numpy()[k]) <= 1e-4, k
+        d_ref = ref.params.numpy()[k] - np.asarray(params[k], np.float32)
+        d_dev = tr.params.numpy()[k] - np.asarray(params[k], np.float32)
+        assert ot.rel_error(d_dev, d_ref) <= 1e-4, k
+    np.testing.assert_array_equal(tr.vis_counts.cpu().numpy(), ref.vis_counts.cpu().numpy())
+    # the oracle: forward, loss and the exact 2D backward
+    cfg = ot.Cfg(sh_degree=deg, tile=tile)
+    pr = ot.project(params, cams[0][0], cams[0][1], H, W, cfg)
+    fw = ot.forward(pr, H, W, cfg)
+    ok = ~fw["ties"]
+    assert np.abs(img_np - fw["image"])[ok].max() <= IMG_TOL
+    np.testing.assert_array_equal(sv.n_contrib.cpu().numpy()[ok], fw["n_contrib"][ok])
+    L, dref = (ot.loss_ssim if ssim else ot.loss_l1)(img_np, target, lam)
+    assert abs(float(loss.item()) - L) <= 1e-5 * abs(L)
+    assert np.abs(dimg.cpu().numpy() - dref).max() <= 1e-5 * np.abs(dref).max()
+    gex, ties = ot.backward_2d_exact(pr, dimg.cpu().numpy(), H, W, cfg, ties=True)
+    assert ot.rel_error(g2d.cpu().numpy()[~ties], gex[~ties]) <= GRAD_TOL
