@@ -89,14 +89,16 @@ void gso_cull_and_blend(const float* means_2d, const float* covs_2d, const float
 
 /* gsplat/blend_backward_dev.py:404-438 forward_fast (oracle/train.py forward): image
  * H*W*3, final_T H*W, n_contrib H*W (pairs up to the last blended one), ties H*W (a
- * decision within 4e-6 relative of its threshold). Returns the number of blended
- * (pair, pixel) evaluations, or -1 for tile > 32. */
+ * decision within 4e-6 relative of its threshold); tile_reach (nullable, one per tile):
+ * the number of leading pairs of the tile's list read before every pixel stopped (the
+ * whole list when one never did). Returns the number of blended (pair, pixel)
+ * evaluations, or -1 for tile > 32. */
 int64_t gso_train_forward(const float* means2d, const float* conic, const float* opacity,
                           const float* colors, const int64_t* sorted_ids,
                           const int64_t* tile_ranges, int height, int width, int tile,
                           float alpha_max, float alpha_min, float t_min, const float* background,
                           float* image, float* final_T, int32_t* n_contrib, uint8_t* ties,
-                          int threads);
+                          int64_t* tile_reach, int threads);
 
 /* gsplat/blend_backward_ref.py:134-249 terms, float64 back to front (oracle/train.py
  * backward_2d_exact): grads N*9 float64 (dmx, dmy, dA, dB, dC, dopacity, dr, dg, db);

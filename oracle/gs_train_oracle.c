@@ -46,6 +46,7 @@ typedef struct {
     float *image, *final_T;
     int32_t *n_contrib;
     uint8_t *ties;
+    int64_t *tile_reach;
     /* backward inputs / outputs */
     const float *dimg;
     double *grads;
@@ -178,7 +179,8 @@ static void* forward_worker(void* arg) {
     for (;;) {
         const int64_t t = __atomic_fetch_add(&J->next_tile, 1, __ATOMIC_RELAXED);
         if (t >= ntiles) break;
-        tile_forward(J, t, S, &nl);
+        const int64_t reach = tile_forward(J, t, S, &nl);
+        if (J->tile_reach) J->tile_reach[t] = reach;
         const int tile = J->tile;
         const int ox = (int)(t % J->tx) * tile, oy = (int)(t / J->tx) * tile;
         for (int p = 0; p < tile * tile; ++p) {
@@ -358,7 +360,7 @@ int64_t gso_train_forward(const float* means2d, const float* conic, const float*
                           const int64_t* tile_ranges, int height, int width, int tile,
                           float alpha_max, float alpha_min, float t_min, const float* background,
                           float* image, float* final_T, int32_t* n_contrib, uint8_t* ties,
-                          int threads) {
+                          int64_t* tile_reach, int threads) {
     Job J;
     if (fill_job(&J, means2d, conic, opacity, colors, sorted_ids, tile_ranges, height, width,
                  tile, alpha_max, alpha_min, t_min, background) != 0)
@@ -367,6 +369,7 @@ int64_t gso_train_forward(const float* means2d, const float* conic, const float*
     J.final_T = final_T;
     J.n_contrib = n_contrib;
     J.ties = ties;
+    J.tile_reach = tile_reach;
     run_threads(&J, forward_worker, threads);
     return J.n_live;
 }

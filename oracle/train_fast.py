@@ -31,7 +31,7 @@ def _lib():
     if not _BOUND:
         c_i, c_f = ctypes.c_int, ctypes.c_float
         L.gso_train_forward.argtypes = [_f, _f, _f, _f, _i64, _i64, c_i, c_i, c_i, c_f, c_f, c_f,
-                                        _f, _f, _f, _i32, _u8, c_i]
+                                        _f, _f, _f, _i32, _u8, _i64, c_i]
         L.gso_train_forward.restype = ctypes.c_int64
         L.gso_train_backward.argtypes = [_f, _f, _f, _f, _i64, _i64, c_i, c_i, c_i, c_f, c_f, c_f,
                                          _f, _f, ctypes.c_int64, _d, _u8, c_i]
@@ -80,7 +80,8 @@ def _common(proj, cfg):
 
 
 def forward(proj, H, W, cfg: ot.Cfg, pairs=None, nthreads: int | None = None) -> dict:
-    """oracle.train.forward: image, final_T, n_contrib, ties, n_pairs, n_live. `pairs`:
+    """oracle.train.forward: image, final_T, n_contrib, ties, n_pairs, n_live, and
+    tile_reach (per tile, the leading pairs read before every pixel stopped). `pairs`:
     (sorted ids, tile ranges) when the caller has them (sorted_pairs otherwise)."""
     ids, rng = sorted_pairs(proj, H, W, cfg.tile) if pairs is None else pairs
     m2, con, op, col, bg = _common(proj, cfg)
@@ -88,14 +89,15 @@ def forward(proj, H, W, cfg: ot.Cfg, pairs=None, nthreads: int | None = None) ->
     T = np.empty((H, W), np.float32)
     nc = np.empty((H, W), np.int32)
     ties = np.empty((H, W), np.uint8)
+    reach = np.zeros(rng.shape[0], np.int64)
     nl = _lib().gso_train_forward(_p(m2, _f), _p(con, _f), _p(op, _f), _p(col, _f), _p(ids, _i64),
                                   _p(rng, _i64), H, W, cfg.tile, cfg.alpha_max, cfg.alpha_min,
                                   cfg.t_min, _p(bg, _f), _p(img, _f), _p(T, _f), _p(nc, _i32),
-                                  _p(ties, _u8), nthreads or threads())
+                                  _p(ties, _u8), _p(reach, _i64), nthreads or threads())
     if nl < 0:
         raise ValueError("tile size above 32")
     return {"image": img, "final_T": T, "n_contrib": nc, "ties": ties.astype(bool),
-            "n_pairs": int(ids.size), "n_live": int(nl)}
+            "n_pairs": int(ids.size), "n_live": int(nl), "tile_reach": reach}
 
 
 def backward_2d_exact(proj, dL_dimage, H, W, cfg: ot.Cfg, ties: bool = False, pairs=None,
