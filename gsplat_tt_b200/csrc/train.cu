@@ -162,8 +162,24 @@ struct PixLayout {
     static constexpr uint32_t kBandMask = (1u << PPT) - 1u;
 };
 
-constexpr int kRasterBatch = 128;  // pairs staged per batch
-constexpr int kRasterPPT = 4;      // pixels per thread: 64 threads per 16x16 tile
+// Pixels per thread and pairs staged per batch of the forward and backward rasterisers
+// (4 pixels per thread: 64 threads per 16x16 tile).
+#ifndef GS_FWD_PPT
+#define GS_FWD_PPT 4
+#endif
+#ifndef GS_BWD_PPT
+#define GS_BWD_PPT 4
+#endif
+#ifndef GS_FWD_BATCH
+#define GS_FWD_BATCH 128
+#endif
+#ifndef GS_BWD_BATCH
+#define GS_BWD_BATCH 128
+#endif
+constexpr int kFwdPPT = GS_FWD_PPT;
+constexpr int kBwdPPT = GS_BWD_PPT;
+constexpr int kFwdBatch = GS_FWD_BATCH;
+constexpr int kBwdBatch = GS_BWD_BATCH;
 
 template <int TILE, int PPT>
 __global__ void __launch_bounds__(TILE * TILE / PPT)
@@ -171,7 +187,7 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             TCfg cfg, int H, int W, float* __restrict__ image, float* __restrict__ final_T,
             int32_t* __restrict__ n_contrib) {
     using LY = PixLayout<TILE, PPT>;
-    constexpr int NB = kRasterBatch;
+    constexpr int NB = kFwdBatch;
     constexpr int NP = PPT / 2;  // pixel pairs per thread, each blended with packed fp32x2 math
     static_assert(PPT % 2 == 0, "pixels are processed in pairs");
     __shared__ RPair sp[NB];
@@ -310,7 +326,7 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             const float* __restrict__ final_T, const int32_t* __restrict__ n_contrib,
             float* __restrict__ grad2d) {
     using LY = PixLayout<TILE, PPT>;
-    constexpr int NB = kRasterBatch;
+    constexpr int NB = kBwdBatch;
     constexpr int NP = PPT / 2;  // pixel pairs per thread (packed fp32x2 math)
     static_assert(PPT % 2 == 0, "pixels are processed in pairs");
     __shared__ BPair sp[NB];
@@ -1048,8 +1064,8 @@ __global__ void k_export_grad2d(const float* __restrict__ grad2d, const uint64_t
 
 struct AdamGroup {
     float* p;
-    float* m;
-    float* v;
+    void* m;             // fp32 values, or bf16 values when AdamParams::bf16 is set
+    void* v;
     const float* g;
     int64_t count;       // elements
     int width;           // elements per Gaussian row
@@ -1070,6 +1086,52 @@ __device__ __forceinline__ float bf16_round(float x) {
     return __uint_as_float(u);
 }
 
+// Adam moments in memory: fp32 (4 bytes a value) or bfloat16 (2 bytes a value; the stored
+// bits are the upper half of an fp32 that adam_update has already rounded to bf16, so
+// storing truncates nothing and loading shifts the bits back).
+template <bool BF>
+struct MomentStore;
+
+template <>
+struct MomentStore<false> {
+    static constexpr unsigned kAlign4 = 16;  // bytes of four values
+    __device__ __forceinline__ static float4 ld4(const void* p, uint32_t i) {
+        return reinterpret_cast<const float4*>(p)[i];
+    }
+    __device__ __forceinline__ static void st4(void* p, uint32_t i, const float4& v) {
+        reinterpret_cast<float4*>(p)[i] = v;
+    }
+    __device__ __forceinline__ static float ld(const void* p, uint32_t e) {
+        return reinterpret_cast<const float*>(p)[e];
+    }
+    __device__ __forceinline__ static void st(void* p, uint32_t e, float v) {
+        reinterpret_cast<float*>(p)[e] = v;
+    }
+};
+
+template <>
+struct MomentStore<true> {
+    static constexpr unsigned kAlign4 = 8;
+    __device__ __forceinline__ static float lo(uint32_t w) { return __uint_as_float(w << 16); }
+    __device__ __forceinline__ static float hi(uint32_t w) { return __uint_as_float(w & 0xFFFF0000u); }
+    __device__ __forceinline__ static uint32_t pack(float a, float b) {
+        return (__float_as_uint(a) >> 16) | (__float_as_uint(b) & 0xFFFF0000u);
+    }
+    __device__ __forceinline__ static float4 ld4(const void* p, uint32_t i) {
+        const uint2 w = reinterpret_cast<const uint2*>(p)[i];
+        return make_float4(lo(w.x), hi(w.x), lo(w.y), hi(w.y));
+    }
+    __device__ __forceinline__ static void st4(void* p, uint32_t i, const float4& v) {
+        reinterpret_cast<uint2*>(p)[i] = make_uint2(pack(v.x, v.y), pack(v.z, v.w));
+    }
+    __device__ __forceinline__ static float ld(const void* p, uint32_t e) {
+        return __uint_as_float((uint32_t)reinterpret_cast<const uint16_t*>(p)[e] << 16);
+    }
+    __device__ __forceinline__ static void st(void* p, uint32_t e, float v) {
+        reinterpret_cast<uint16_t*>(p)[e] = (uint16_t)(__float_as_uint(v) >> 16);
+    }
+};
+
 // One Adam update of element e (column col of its row) when its row is visible.
 __device__ __forceinline__ void adam_update(const AdamParams& A, const AdamGroup& G, int col,
                                             float g, float& p, float& m, float& v) {
@@ -1086,10 +1148,11 @@ __device__ __forceinline__ void adam_update(const AdamParams& A, const AdamGroup
 // (a compile-time width turns the row / column split into a multiply-shift). With VEC, four
 // consecutive elements per thread through 16-byte loads and stores (the group's arrays are
 // 16-byte aligned); the count's remainder modulo 4 is done element by element.
-template <int W, bool VEC>
+template <int W, bool VEC, bool BF>
 __global__ void __launch_bounds__(256)
 k_sparse_adam(AdamParams A, const float* __restrict__ vis, const unsigned int* __restrict__ err,
               int group) {
+    using MS = MomentStore<BF>;
     if (err != nullptr && *err != 0u) return;
     const AdamGroup& G = A.grp[group];
     const uint32_t count = (uint32_t)G.count;
@@ -1106,8 +1169,8 @@ k_sparse_adam(AdamParams A, const float* __restrict__ vis, const unsigned int* _
             if (!any) continue;
             const float4 g4 = reinterpret_cast<const float4*>(G.g)[i];
             float4 p4 = reinterpret_cast<const float4*>(G.p)[i];
-            float4 m4 = reinterpret_cast<const float4*>(G.m)[i];
-            float4 v4 = reinterpret_cast<const float4*>(G.v)[i];
+            float4 m4 = MS::ld4(G.m, i);
+            float4 v4 = MS::ld4(G.v, i);
             float* pp = &p4.x;
             float* mm = &m4.x;
             float* vv = &v4.x;
@@ -1119,19 +1182,19 @@ k_sparse_adam(AdamParams A, const float* __restrict__ vis, const unsigned int* _
                 if (vis[row] > 0.0f) adam_update(A, G, (int)(ek - row * W), gg[k], pp[k], mm[k], vv[k]);
             }
             reinterpret_cast<float4*>(G.p)[i] = p4;
-            reinterpret_cast<float4*>(G.m)[i] = m4;
-            reinterpret_cast<float4*>(G.v)[i] = v4;
+            MS::st4(G.m, i, m4);
+            MS::st4(G.v, i, v4);
         }
         done = n4 * 4u;
     }
     for (uint32_t e = done + t0; e < count; e += stride) {
         const uint32_t row = e / W;
         if (!(vis[row] > 0.0f)) continue;
-        float p = G.p[e], m = G.m[e], v = G.v[e];
+        float p = G.p[e], m = MS::ld(G.m, e), v = MS::ld(G.v, e);
         adam_update(A, G, (int)(e - row * W), G.g[e], p, m, v);
         G.p[e] = p;
-        G.m[e] = m;
-        G.v[e] = v;
+        MS::st(G.m, e, m);
+        MS::st(G.v, e, v);
     }
 }
 
@@ -1196,10 +1259,11 @@ k_mc_reduce_counts(const float* __restrict__ counts_mc, float* __restrict__ coun
 constexpr int kMcUnroll = GS_MC_UNROLL;
 constexpr int kMcBlocksPerSm = GS_MC_BLOCKS_PER_SM;
 
-template <int W>
+template <int W, bool BF>
 __global__ void __launch_bounds__(256)
 k_sparse_adam_mc(AdamParams A, const float* __restrict__ vis, const unsigned int* __restrict__ skip,
                  int group, const float* g_mc, float* p_mc) {
+    using MS = MomentStore<BF>;
     if (*skip != 0u) return;
     const AdamGroup& G = A.grp[group];
     const uint32_t n4 = (uint32_t)(G.count / 4);
@@ -1225,8 +1289,8 @@ k_sparse_adam_mc(AdamParams A, const float* __restrict__ vis, const unsigned int
             const uint32_t i = base + (uint32_t)u * stride;
             const uint32_t e = 4u * i;
             float4 p4 = reinterpret_cast<const float4*>(G.p)[i];
-            float4 m4 = reinterpret_cast<const float4*>(G.m)[i];
-            float4 v4 = reinterpret_cast<const float4*>(G.v)[i];
+            float4 m4 = MS::ld4(G.m, i);
+            float4 v4 = MS::ld4(G.v, i);
             float* pp = &p4.x;
             float* mm = &m4.x;
             float* vv = &v4.x;
@@ -1238,8 +1302,8 @@ k_sparse_adam_mc(AdamParams A, const float* __restrict__ vis, const unsigned int
                 if (vis[row] > 0.0f) adam_update(A, G, (int)(ek - row * W), gg[k], pp[k], mm[k], vv[k]);
             }
             mc_st_v4(p_mc + e, p4);
-            reinterpret_cast<float4*>(G.m)[i] = m4;
-            reinterpret_cast<float4*>(G.v)[i] = v4;
+            MS::st4(G.m, i, m4);
+            MS::st4(G.v, i, v4);
         }
     }
     mc_release();
@@ -1524,9 +1588,9 @@ static gs_status launch_raster_fwd(const TCfg& c, const ViewLane& V, const ProjV
     KernelTimer kt("raster_fwd", st);
     const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
     if (c.tile == 16)
-        k_train_fwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
+        k_train_fwd<16, kFwdPPT><<<tiles, 256 / kFwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
     else
-        k_train_fwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
+        k_train_fwd<32, kFwdPPT><<<tiles, 1024 / kFwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
     GS_CHECK_LAUNCH();
     return GS_OK;
 }
@@ -1563,10 +1627,10 @@ static gs_status launch_raster_bwd(const TCfg& c, const ViewLane& V, const ProjV
     KernelTimer kt("raster_bwd", st);
     const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
     if (c.tile == 16)
-        k_train_bwd<16, kRasterPPT><<<tiles, 256 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
+        k_train_bwd<16, kBwdPPT><<<tiles, 256 / kBwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
                                                                         V.final_T, V.ncon, g2);
     else
-        k_train_bwd<32, kRasterPPT><<<tiles, 1024 / kRasterPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
+        k_train_bwd<32, kBwdPPT><<<tiles, 1024 / kBwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
                                                                          V.final_T, V.ncon, g2);
     GS_CHECK_LAUNCH();
     return GS_OK;
@@ -1903,12 +1967,16 @@ static gs_status launch_adam(const AdamParams& A, const float* vis, const unsign
         const AdamGroup& G = A.grp[i];
         const int64_t cnt = G.count;
         GS_ARG_CHECK(cnt < (1ll << 32), "sparse Adam: a parameter group exceeds 2^32 elements");
-        const bool vec = (((uintptr_t)G.p | (uintptr_t)G.m | (uintptr_t)G.v | (uintptr_t)G.g) & 15u) == 0;
+        const uintptr_t mom_align = A.bf16 ? 7u : 15u;  // four moments: 8 or 16 bytes
+        const bool vec = (((uintptr_t)G.p | (uintptr_t)G.g) & 15u) == 0 &&
+                         (((uintptr_t)G.m | (uintptr_t)G.v) & mom_align) == 0;
         const unsigned int blocks =
             (unsigned int)std::min<int64_t>(div_up(vec ? div_up(cnt, 4) : cnt, 256), kNumSMs * 16);
 #define GS_ADAM(W_)                                                                             \
-    (vec ? k_sparse_adam<W_, true><<<blocks, 256, 0, st>>>(A, vis, err, i)                     \
-         : k_sparse_adam<W_, false><<<blocks, 256, 0, st>>>(A, vis, err, i))
+    (A.bf16 ? (vec ? k_sparse_adam<W_, true, true><<<blocks, 256, 0, st>>>(A, vis, err, i)      \
+                   : k_sparse_adam<W_, false, true><<<blocks, 256, 0, st>>>(A, vis, err, i))    \
+            : (vec ? k_sparse_adam<W_, true, false><<<blocks, 256, 0, st>>>(A, vis, err, i)     \
+                   : k_sparse_adam<W_, false, false><<<blocks, 256, 0, st>>>(A, vis, err, i)))
         switch (G.width) {
             case 1: GS_ADAM(1); break;
             case 3: GS_ADAM(3); break;
@@ -1992,11 +2060,13 @@ extern "C" gs_status gs_sparse_adam_multicast(const gs_gaussians* params,
                           grads_mc->opacity_logits, grads_mc->sh};
     float* Pm[5] = {params_mc->means, params_mc->log_scales, params_mc->quats,
                     params_mc->opacity_logits, params_mc->sh};
-    uintptr_t all = (uintptr_t)vis_counts_mc | (uintptr_t)vis_scratch;
-    for (int i = 0; i < 5; ++i)
-        all |= (uintptr_t)A.grp[i].p | (uintptr_t)A.grp[i].m | (uintptr_t)A.grp[i].v |
-               (uintptr_t)Gm[i] | (uintptr_t)Pm[i];
-    GS_ARG_CHECK((all & 15u) == 0, "gs_sparse_adam_multicast: every pointer must be 16-byte aligned");
+    uintptr_t all = (uintptr_t)vis_counts_mc | (uintptr_t)vis_scratch, mom = 0;
+    for (int i = 0; i < 5; ++i) {
+        all |= (uintptr_t)A.grp[i].p | (uintptr_t)Gm[i] | (uintptr_t)Pm[i];
+        mom |= (uintptr_t)A.grp[i].m | (uintptr_t)A.grp[i].v;
+    }
+    GS_ARG_CHECK((all & 15u) == 0 && (mom & (A.bf16 ? 7u : 15u)) == 0,
+                 "gs_sparse_adam_multicast: every pointer must be 16-byte aligned (bf16 moments: 8)");
     KernelTimer kt("sparse_adam_mc", st);
     const uint32_t rows4 = (uint32_t)(rows / 4);
     k_mc_reduce_counts<<<(unsigned)std::min<int64_t>(div_up(rows4, 256), kNumSMs * 8), 256, 0, st>>>(
@@ -2007,7 +2077,9 @@ extern "C" gs_status gs_sparse_adam_multicast(const gs_gaussians* params,
         const unsigned int blocks =
             (unsigned int)std::min<int64_t>(div_up(div_up(G.count, 4), 256 * kMcUnroll),
                                             kNumSMs * kMcBlocksPerSm);
-#define GS_ADAM_MC(W_) k_sparse_adam_mc<W_><<<blocks, 256, 0, st>>>(A, vis_scratch, skip, i, Gm[i], Pm[i])
+#define GS_ADAM_MC(W_)                                                                         \
+    (A.bf16 ? k_sparse_adam_mc<W_, true><<<blocks, 256, 0, st>>>(A, vis_scratch, skip, i, Gm[i], Pm[i]) \
+            : k_sparse_adam_mc<W_, false><<<blocks, 256, 0, st>>>(A, vis_scratch, skip, i, Gm[i], Pm[i]))
         switch (G.width) {
             case 1: GS_ADAM_MC(1); break;
             case 3: GS_ADAM_MC(3); break;

@@ -137,26 +137,29 @@ def _group_sizes(n: int, K: int) -> list[int]:
 
 class GroupBuffer:
     """The five parameter groups (or moments, or gradients) of N Gaussians in one flat
-    fp32 device buffer, each group starting on a 16-byte boundary. ``extra`` floats after
-    the groups hold the visibility counts of a gradient buffer, so one allreduce covers
-    gradients and counts."""
+    device buffer (fp32, or bfloat16 for bf16-stored Adam moments), each group starting on
+    a 16-byte boundary. ``extra`` values after the groups hold the visibility counts of a
+    gradient buffer, so one allreduce covers gradients and counts."""
 
     def __init__(self, n: int, sh_degree: int, device, extra: int = 0, rows: int | None = None,
-                 alloc=None):
+                 alloc=None, dtype=torch.float32):
         """rows >= n: rows allocated per group (the owner-sharded optimizer pads every group
         to world * rows-per-rank rows; the padding rows stay zero). alloc(numel), when given,
         returns the zeroed flat fp32 buffer (symmetric memory for multicast updates)."""
         self.n, self.K = n, (sh_degree + 1) ** 2
         self.rows = n if rows is None else int(rows)
+        self.dtype = dtype
+        self.esz = torch.empty(0, dtype=dtype).element_size()
+        align = 16 // self.esz
         sizes = _group_sizes(self.rows, self.K)
         self.widths = [s // self.rows for s in sizes]
         self.offsets = []
         off = 0
         for s in sizes:
             self.offsets.append(off)
-            off += (s + 3) // 4 * 4
+            off += (s + align - 1) // align * align
         self.extra_offset = off
-        self.flat = torch.zeros(off + extra, dtype=torch.float32, device=device) if alloc is None \
+        self.flat = torch.zeros(off + extra, dtype=dtype, device=device) if alloc is None \
             else alloc(off + extra)
         shapes = [(n, 3), (n, 3), (n, 4), (n,), (n, self.K, 3)]
         self.views = {name: self.flat[o:o + int(np.prod(shape))].view(*shape)
@@ -172,7 +175,7 @@ class GroupBuffer:
         """Group pointers, optionally starting at row `row0` of every group; `base` replaces
         the buffer's own address (e.g. by its multicast address)."""
         b = self.flat.data_ptr() if base is None else base
-        return GsGaussians(*[b + 4 * (o + row0 * w) for o, w in zip(self.offsets, self.widths)])
+        return GsGaussians(*[b + self.esz * (o + row0 * w) for o, w in zip(self.offsets, self.widths)])
 
     def load(self, params: dict) -> None:
         for k in PARAM_NAMES:
@@ -181,7 +184,8 @@ class GroupBuffer:
             self.views[k].copy_(src.reshape(self.views[k].shape))
 
     def numpy(self) -> dict:
-        return {k: v.detach().cpu().numpy() for k, v in self.views.items()}
+        """Host fp32 copies of the groups (bfloat16 values widen exactly)."""
+        return {k: v.detach().float().cpu().numpy() for k, v in self.views.items()}
 
 
 class Trainer:
@@ -235,8 +239,10 @@ class Trainer:
             alloc = {"params": symm_alloc("params"), "grads": symm_alloc("grads")}
         self.params = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows, alloc=alloc.get("params"))
         self.params.load(params)
-        self.m = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows)
-        self.v = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows)
+        # bf16 moments are stored as 2-byte values (half the moment bytes Adam moves)
+        mdt = torch.bfloat16 if cfg.bf16_moments else torch.float32
+        self.m = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows, dtype=mdt)
+        self.v = GroupBuffer(self.n, cfg.sh_degree, self.device, rows=rows, dtype=mdt)
         self.grads = GroupBuffer(self.n, cfg.sh_degree, self.device, extra=rows + 1, rows=rows,
                                  alloc=alloc.get("grads"))
         self.multicast = bool(self._symm) and all(mc for _, mc in self._symm.values())

@@ -235,7 +235,9 @@ typedef struct gs_train_config {
     float lambda_dssim;      /* 0.2 */
     float lr_means, lr_log_scales, lr_quats, lr_opacity, lr_sh_dc, lr_sh_rest;
     float beta1, beta2, eps;
-    int32_t bf16_moments;    /* moments stored as bf16 values (round to nearest even) */
+    int32_t bf16_moments;    /* moments stored as bfloat16 (round to nearest even): the
+                                exp_avg / exp_avg_sq arrays then hold 2-byte values and their
+                                gs_gaussians pointers are read as 16-bit arrays */
 } gs_train_config;
 
 /* One training step over n_views views (<= 64) of one rank.
@@ -348,8 +350,9 @@ gs_status gs_render_bwd(int64_t n, const gs_camera* cam, const gs_train_config* 
 
 /* Sparse Adam over rows with vis_counts > 0 (gsplat/train_oracle.py:434-470
  * sparse_adam_step; gsplat/t2_param_backward.py:195-223 adam_step): fp32 arithmetic,
- * moments stored fp32 or bf16 per cfg->bf16_moments, lr per group with SH band 0 at
- * lr_sh_dc and bands >= 1 at lr_sh_rest. `error_word` (nullable, device) is checked
+ * moments stored as fp32 arrays or, with cfg->bf16_moments, as bfloat16 arrays (2 bytes a
+ * value, rounded to nearest even after each update, the reference's bf16 mode), lr per
+ * group with SH band 0 at lr_sh_dc and bands >= 1 at lr_sh_rest. `error_word` (nullable, device) is checked
  * first: a non-zero value (a failed gs_train_step) skips the update. */
 gs_status gs_sparse_adam(const gs_gaussians* params, const gs_gaussians* exp_avg,
                          const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
