@@ -124,6 +124,7 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
         uint32_t peers = 0xffffffffu;
 #pragma unroll
         for (int b = 0; b < kRadixBits; ++b) {  // bits above digit_bits are 0 in every lane
+            if (b >= digit_bits) break;         // a narrower last digit needs fewer ballots
             const uint32_t bit = (d >> b) & 1u;
             const uint32_t m = __ballot_sync(0xffffffffu, bit);
             peers &= bit ? m : ~m;

@@ -2,9 +2,13 @@
 // item source: the first pass of the training tile sort emits its items itself.
 //
 // Pair order before the sort (the order the stable sort must preserve within a tile):
-// Gaussians in depth order, each Gaussian's tiles row-major inside its rectangle;
-// key = tile id (ty * tiles_x + tx), value = Gaussian id. Sorting that stably by tile id
-// gives the reference's (tile, depth bits, Gaussian id) order (src/gsplat_cpu/sort.cpp:24-27).
+// Gaussians in depth order, each Gaussian's tiles row-major inside its rectangle. The
+// rectangle is taken at a coarser grid (tile coordinates >> shift: shift 1 = the 2x2-tile
+// super-tiles), key = cell id (cy * cells_x + cx), value = the Gaussian's depth index.
+// Sorting that stably by cell id gives each cell's Gaussians in depth order; with shift 0
+// that is the reference's (tile, depth bits, Gaussian id) order
+// (src/gsplat_cpu/sort.cpp:24-27) and with shift 1 the tile filter (train_project.cu)
+// derives it per tile.
 #pragma once
 
 #include "onesweep.cuh"
@@ -17,7 +21,8 @@ struct RectPairSource {
     const uint32_t* tfirst;  // per 4096-pair tile: depth index of the Gaussian holding its first pair
     const uint32_t* last;    // [0]: depth index of the last Gaussian with pairs
     const ushort4* rect;     // per depth-ordered Gaussian: tile columns x0..x1, rows y0..y1
-    int tiles_x;
+    int tiles_x;             // cells per row of the (coarser) grid the keys index
+    int shift;               // cell = tile >> shift
 
     // The tile's pairs come from depth-ordered Gaussians gf..gl (at most `valid` of them,
     // each has at least one pair), taken in chunks of 256, one per thread. A thread writes
@@ -50,8 +55,10 @@ struct RectPairSource {
         for (uint32_t c0 = gf; c0 <= gl; c0 += kSortThreads, par ^= 1) {
             const uint32_t i = c0 + (uint32_t)tid;
             if (i <= gl) {
-                const uint32_t off = goff[i], end = goff[i + 1], gid = order[i];
-                const ushort4 r = rect[i];
+                const uint32_t off = goff[i], end = goff[i + 1], gid = i;
+                const ushort4 r0 = rect[i];
+                const ushort4 r = make_ushort4(r0.x >> shift, r0.y >> shift, r0.z >> shift,
+                                               r0.w >> shift);
                 const uint32_t p0 = max(off, lo_p), p1 = min(end, hi_p);
                 if (p1 > p0 && p1 - p0 <= kOwnPairs) {
                     const uint32_t w = (uint32_t)r.y - (uint32_t)r.x + 1u;
@@ -75,8 +82,10 @@ struct RectPairSource {
             if (tid == 0) s_nbig[par] = 0u;
             for (uint32_t q = (uint32_t)warp; q < nbig; q += kSortWarps) {
                 const uint32_t bi = s_big[par][q];
-                const uint32_t off = goff[bi], end = goff[bi + 1], gid = order[bi];
-                const ushort4 r = rect[bi];
+                const uint32_t off = goff[bi], end = goff[bi + 1], gid = bi;
+                const ushort4 r0 = rect[bi];
+                const ushort4 r = make_ushort4(r0.x >> shift, r0.y >> shift, r0.z >> shift,
+                                               r0.w >> shift);
                 const uint32_t p0 = max(off, lo_p), p1 = min(end, hi_p);
                 const uint32_t w = (uint32_t)r.y - (uint32_t)r.x + 1u;
                 for (uint32_t p = p0 + (uint32_t)lane; p < p1; p += 32u) {

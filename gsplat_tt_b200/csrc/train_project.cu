@@ -233,45 +233,62 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
         blk[v * blk_stride + blockIdx.x] = (int64_t)s_tot[v];
 }
 
-// Pair counts of the Gaussians in depth order (`order` = Gaussian ids sorted by depth
-// bits, stable), one total per block for the offset scan.
+// Super-tile pairs of a Gaussian with tiles (cnt > 0): the 2x2-tile super-tiles its tile
+// rectangle touches.
+__device__ __forceinline__ uint32_t super_count(uint32_t cnt, ushort4 r) {
+    return cnt == 0u ? 0u
+                     : (uint32_t)((r.y >> 1) - (r.x >> 1) + 1) * (uint32_t)((r.w >> 1) - (r.z >> 1) + 1);
+}
+
+// Super-tile pair counts of the Gaussians in depth order (`order` = Gaussian ids sorted by
+// depth bits, stable), one total per block for the offset scan.
 __global__ void __launch_bounds__(kProjThreads)
-k_sorted_count(const uint32_t* __restrict__ cnt, const uint32_t* __restrict__ order, int64_t n,
-               int64_t* __restrict__ blk) {
+k_sorted_count(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
+               const uint32_t* __restrict__ order, int64_t n, int64_t* __restrict__ blk) {
     __shared__ int64_t smem[33];
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const uint32_t c = (i < n) ? cnt[order[i]] : 0u;
+    uint32_t c = 0u;
+    if (i < n) {
+        const uint32_t g = order[i];
+        c = super_count(cnt[g], rect[g]);
+    }
     int64_t total;
     block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
     if (threadIdx.x == 0) blk[blockIdx.x] = total;
 }
 
-// First pair of each Gaussian in depth order (goff, n + 1 entries; goff[n] = pairs),
-// clamped to the pair capacity (DEV_OVERFLOW when the pairs exceed it), and its tile
-// rectangle in depth order (rect_d, so the tile sort reads it without a gather). Also, per
-// 4096-pair tile of the tile sort, the depth index of the Gaussian holding the tile's
-// first pair (tfirst), and the depth index of the last Gaussian with pairs (Gaussians
-// without pairs sort after every Gaussian with pairs).
+// First super-tile pair of each Gaussian in depth order (goff, n + 1 entries; goff[n] =
+// super pairs), clamped to the pair capacity (DEV_OVERFLOW when they exceed it), and its
+// tile rectangle in depth order (rect_d, read by the tile sort and the tile filter without
+// a gather). Also, per 4096-item tile of the super-tile sort, the depth index of the
+// Gaussian holding the tile's first item (tfirst), the depth index of the last Gaussian
+// with pairs (Gaussians without pairs sort after every Gaussian with pairs), and the
+// number of super-tile pairs (super_total).
 __global__ void __launch_bounds__(kProjThreads)
 k_pair_offsets(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
                const uint32_t* __restrict__ order, int64_t n,
                const int64_t* __restrict__ blk_offsets, int64_t capacity,
                uint32_t* __restrict__ goff, ushort4* __restrict__ rect_d,
                uint32_t* __restrict__ tfirst, int64_t tfirst_len,
-               uint32_t* __restrict__ last, unsigned int* __restrict__ err) {
+               uint32_t* __restrict__ last, int64_t* __restrict__ super_total,
+               unsigned int* __restrict__ err) {
     __shared__ int64_t smem[33];
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t g = (i < n) ? order[i] : 0u;
-    const uint32_t c = (i < n) ? cnt[g] : 0u;
+    const ushort4 rg = (i < n) ? rect[g] : make_ushort4(0, 0, 0, 0);
+    const uint32_t c = (i < n) ? super_count(cnt[g], rg) : 0u;
     int64_t total;
     const int64_t off = blk_offsets[blockIdx.x] + block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
     uint32_t cn = __shfl_down_sync(0xffffffffu, c, 1);
     if ((threadIdx.x & 31) == 31) cn = (i + 1 < n) ? cnt[order[i + 1]] : 0u;
     if (i >= n) return;
     goff[i] = (uint32_t)min(off, capacity);
-    if (i == n - 1) goff[n] = (uint32_t)min(off + (int64_t)c, capacity);
+    if (i == n - 1) {
+        goff[n] = (uint32_t)min(off + (int64_t)c, capacity);
+        *super_total = off + (int64_t)c;
+    }
     if (c == 0) return;
-    rect_d[i] = rect[g];
+    rect_d[i] = rg;
     if (off + (int64_t)c > capacity) atomicOr(err, DEV_OVERFLOW);
     for (int64_t b = (off + kTileItems - 1) / kTileItems;
          b * kTileItems < off + (int64_t)c && b < tfirst_len; ++b)
@@ -281,16 +298,20 @@ k_pair_offsets(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rec
 
 // Per tile row, +1 at column x0 and -1 at column x1 + 1 for every row of every Gaussian's
 // tile rectangle (a row-wise difference array, (tiles_x + 1) x tiles_y ints): a prefix
-// sum along each row then gives the pairs per tile. Summed in shared memory per block
-// when the grid fits `smem_bins`, then added to the global array.
+// sum along each row then gives the pairs per tile. The same for the 2x2-tile super-tile
+// grid ((sx + 1) x sy ints, after the tile grid's). Summed in shared memory per block
+// when both grids fit `smem_bins`, then added to the global arrays.
 __global__ void __launch_bounds__(1024)
 k_tile_diff(const ushort4* __restrict__ rect, const uint32_t* __restrict__ cnt, int64_t n,
             int tiles_x, int tiles_y, int smem_bins, int* __restrict__ diff) {
     extern __shared__ int s_diff[];
     const int gw = tiles_x + 1;
-    const int bins = gw * tiles_y;
+    const int sgw = (tiles_x + 1) / 2 + 1, sgh = (tiles_y + 1) / 2;
+    const int tbins = gw * tiles_y;
+    const int bins = tbins + sgw * sgh;
     const bool local = bins <= smem_bins;
     int* d = local ? s_diff : diff;
+    int* ds = d + tbins;
     if (local) {
         for (int i = threadIdx.x; i < bins; i += blockDim.x) s_diff[i] = 0;
         __syncthreads();
@@ -303,6 +324,10 @@ k_tile_diff(const ushort4* __restrict__ rect, const uint32_t* __restrict__ cnt, 
         for (int y = r.z; y <= (int)r.w; ++y) {
             atomicAdd(&d[y * gw + r.x], 1);
             atomicAdd(&d[y * gw + r.y + 1], -1);
+        }
+        for (int y = r.z >> 1; y <= (int)(r.w >> 1); ++y) {
+            atomicAdd(&ds[y * sgw + (r.x >> 1)], 1);
+            atomicAdd(&ds[y * sgw + (r.y >> 1) + 1], -1);
         }
     }
     if (local) {
@@ -323,13 +348,14 @@ k_tile_diff(const ushort4* __restrict__ rect, const uint32_t* __restrict__ cnt, 
 __global__ void __launch_bounds__(1024)
 k_tile_finish(const int* __restrict__ diff, int tiles_x, int tiles_y, int npass,
               const int64_t* __restrict__ pairs, int64_t capacity, int2* __restrict__ ranges,
-              uint32_t* __restrict__ digit_offsets) {
+              uint32_t* __restrict__ digit_offsets, unsigned int* __restrict__ err) {
     __shared__ uint32_t s_rows[kMaxTileRows];
     __shared__ uint32_t s_hist[4][256];
     __shared__ uint32_t smem[33];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
     const int gw = tiles_x + 1;
     if (*pairs > capacity) {
+        if (threadIdx.x == 0 && err != nullptr) atomicOr(err, DEV_OVERFLOW);
         for (int t = threadIdx.x; t < tiles_x * tiles_y; t += blockDim.x) ranges[t] = make_int2(0, 0);
         for (int i = threadIdx.x; i < npass * 256; i += blockDim.x) digit_offsets[i] = 0u;
         return;
@@ -423,24 +449,83 @@ void launch_project(const GConst& P, int64_t n, const TCam* cams, int n_views, c
     }
 }
 
+// The per-tile lists from the super-tile lists: one block per 2x2-tile super-tile reads
+// the super-tile's items (depth indices, in depth order) in chunks and hands each one to
+// the (up to four) tiles of the super-tile its tile rectangle covers, keeping the order:
+// every tile's list is the depth-ordered list of the Gaussians covering it, exactly what a
+// stable sort of all (tile, Gaussian) pairs by tile gives. Nothing is written when the
+// view's pairs exceed the capacity (the ranges are empty then).
+__global__ void __launch_bounds__(kFilterThreads)
+k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict__ super_ranges,
+              const ushort4* __restrict__ rect_d, const uint32_t* __restrict__ order,
+              const int2* __restrict__ ranges, int tiles_x, int tiles_y,
+              const int64_t* __restrict__ pairs, int64_t capacity,
+              uint32_t* __restrict__ svals) {
+    __shared__ uint32_t smem[33];
+    if (*pairs > capacity) return;
+    const int sx_n = (tiles_x + 1) / 2;
+    const int sid = blockIdx.x;
+    const int sx = sid % sx_n, sy = sid / sx_n;
+    const int2 sr = super_ranges[sid];
+    if (sr.y <= sr.x) return;
+    int tx[4], ty[4], base[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        tx[q] = 2 * sx + (q & 1);
+        ty[q] = 2 * sy + (q >> 1);
+        base[q] = (tx[q] < tiles_x && ty[q] < tiles_y) ? ranges[ty[q] * tiles_x + tx[q]].x : 0;
+    }
+    uint32_t run01 = 0u, run23 = 0u;  // items already written per tile, two 16-bit counts each
+    for (int c0 = sr.x; c0 < sr.y; c0 += kFilterThreads) {
+        const int k = c0 + (int)threadIdx.x;
+        uint32_t f[4] = {0u, 0u, 0u, 0u}, gid = 0u;
+        if (k < sr.y) {
+            const uint32_t di = super_sorted[k];
+            const ushort4 r = rect_d[di];
+            gid = order[di];
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+                f[q] = (tx[q] < tiles_x && ty[q] < tiles_y && tx[q] >= r.x && tx[q] <= r.y &&
+                        ty[q] >= r.z && ty[q] <= r.w) ? 1u : 0u;
+        }
+        // block-wide exclusive prefix of the four flags, two per 32-bit word (a chunk holds
+        // at most kFilterThreads items, far below 2^16)
+        uint32_t t01, t23;
+        const uint32_t e01 = block_exclusive_scan<uint32_t>(f[0] | (f[1] << 16), smem, &t01);
+        const uint32_t e23 = block_exclusive_scan<uint32_t>(f[2] | (f[3] << 16), smem, &t23);
+        const uint32_t pos01 = run01 + e01, pos23 = run23 + e23;
+        if (f[0]) svals[base[0] + (pos01 & 0xFFFFu)] = gid;
+        if (f[1]) svals[base[1] + (pos01 >> 16)] = gid;
+        if (f[2]) svals[base[2] + (pos23 & 0xFFFFu)] = gid;
+        if (f[3]) svals[base[3] + (pos23 >> 16)] = gid;
+        run01 += t01;
+        run23 += t23;
+    }
+}
+
 void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int64_t* blk,
                          cudaStream_t st) {
-    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, order, n, blk);
+    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, pv.rect, order, n, blk);
 }
 
 void launch_pair_offsets(const ProjView& pv, const uint32_t* order, int64_t n,
                          const int64_t* blk_offsets, int64_t capacity, uint32_t* goff,
                          ushort4* rect_d, uint32_t* tfirst, int64_t tfirst_len, uint32_t* last,
-                         unsigned int* err, cudaStream_t st) {
+                         int64_t* super_total, unsigned int* err, cudaStream_t st) {
     k_pair_offsets<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(
         pv.cnt, pv.rect, order, n, blk_offsets, capacity, goff, rect_d, tfirst, tfirst_len, last,
-        err);
+        super_total, err);
 }
 
-gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y, int npass,
-                             const int64_t* pairs, int64_t capacity, int* diff, int2* ranges,
-                             uint32_t* digit_offsets, cudaStream_t st) {
-    const int bins = (tiles_x + 1) * tiles_y;
+int tile_diff_ints(int tiles_x, int tiles_y) {
+    return (tiles_x + 1) * tiles_y + ((tiles_x + 1) / 2 + 1) * ((tiles_y + 1) / 2);
+}
+
+gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y,
+                             int super_npass, const int64_t* pairs, int64_t capacity, int* diff,
+                             int2* ranges, int2* super_ranges, uint32_t* super_digit_offsets,
+                             unsigned int* err, cudaStream_t st) {
+    const int bins = tile_diff_ints(tiles_x, tiles_y);
     constexpr int kSmemBins = 40960;  // 160 KB
     const size_t smem = bins <= kSmemBins ? (size_t)bins * sizeof(int) : 0;
     GS_CUDA_CHECK(cudaMemsetAsync(diff, 0, (size_t)bins * sizeof(int), st));
@@ -450,10 +535,25 @@ gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int til
     k_tile_diff<<<grid, 1024, smem, st>>>(pv.rect, pv.cnt, n, tiles_x, tiles_y,
                                           smem ? kSmemBins : 0, diff);
     GS_CHECK_LAUNCH();
-    k_tile_finish<<<1, 1024, 0, st>>>(diff, tiles_x, tiles_y, npass, pairs, capacity, ranges,
-                                      digit_offsets);
+    // tile ranges, then the super-tile ranges and the super-tile sort's digit offsets
+    k_tile_finish<<<1, 1024, 0, st>>>(diff, tiles_x, tiles_y, 0, pairs, capacity, ranges,
+                                      nullptr, err);
+    GS_CHECK_LAUNCH();
+    const int sx_n = (tiles_x + 1) / 2, sy_n = (tiles_y + 1) / 2;
+    k_tile_finish<<<1, 1024, 0, st>>>(diff + (tiles_x + 1) * tiles_y, sx_n, sy_n, super_npass,
+                                      pairs, capacity, super_ranges, super_digit_offsets, nullptr);
     GS_CHECK_LAUNCH();
     return GS_OK;
+}
+
+void launch_tile_filter(const uint32_t* super_sorted, const int2* super_ranges,
+                        const ushort4* rect_d, const uint32_t* order, const int2* ranges,
+                        int tiles_x, int tiles_y, const int64_t* pairs, int64_t capacity,
+                        uint32_t* svals, cudaStream_t st) {
+    const int nsuper = ((tiles_x + 1) / 2) * ((tiles_y + 1) / 2);
+    k_tile_filter<<<nsuper, kFilterThreads, 0, st>>>(super_sorted, super_ranges, rect_d, order,
+                                                     ranges, tiles_x, tiles_y, pairs, capacity,
+                                                     svals);
 }
 
 }  // namespace gs

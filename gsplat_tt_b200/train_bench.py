@@ -58,9 +58,8 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, launches_per_step
       (236 B per Gaussian) and per view the 52 B record (mean 8, conic 12, colour 12,
       opacity 4, depth key 4, rectangle 8, pair count 4);
     * radix_pass32 (one pass of the depth sort over N): 4 B key + 4 B value read and written;
-    * tile_sort_emit (pair emission fused into the first tile-sort pass): 16 B per Gaussian
-      read (depth order, first-pair offset, rectangle), 8 B per pair written;
-    * tile_sort_pass (the second tile-sort pass): 8 B per pair read, 4 B per pair written;
+    * tile_filter (the per-tile lists from the sorted super-tile lists): 4 B per (Gaussian,
+      tile) pair written, a lower bound (its reads are per super-tile item);
     * param_bwd: per row the parameters read and their gradients written (236 B each) and
       the 2D-gradient rows (36 B) of every view; the step's launches split the N rows
       (one launch on one GPU, one per row chunk with the pipelined multicast update);
@@ -71,15 +70,15 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, launches_per_step
       rows of a chunk of world * q rows; its partial gradients and count of every row of the
       chunk leave it for the switch's load-reduce (world * q * 240 B) and its q updated
       rows leave it for the multicast store (q * 236 B); the same amount arrives.
-    The rasterisers and the loss filters are SM-issue bound and have no entry."""
+    The rasterisers and the loss filters are SM-issue bound and have no entry; the two
+    passes of the super-tile sort (tile_sort_emit, tile_sort_pass) move per super-tile item
+    bytes whose count the timer does not see, and have no entry either."""
     if name == "train_project":
         return n * 236.0 + views * n * 52.0
     if name == "radix_pass32":
         return n * 16.0
-    if name == "tile_sort_emit":
-        return pairs * 8.0 + n * 16.0
-    if name == "tile_sort_pass":
-        return pairs * 12.0
+    if name == "tile_filter":
+        return pairs * 4.0
     if name == "param_bwd":
         return (n * 472.0 + views * n * 36.0) / max(launches_per_step, 1.0)
     if name == "sparse_adam":
@@ -142,7 +141,8 @@ def summarize_kernels(rep: dict, ksteps: int, n: int, views: int, pairs: float, 
                         f"({', '.join(f'{k} {v:.1f} ms' for k, v in raster.items())} per step) "
                         "are SM-issue bound and have no HBM roofline"}
     sort_parts = {k: per_kernel[k] for k in ("radix_hist", "radix_pass32", "pair_offsets",
-                                             "tile_counts", "tile_sort_emit", "tile_sort_pass")
+                                             "tile_counts", "tile_sort_emit", "tile_sort_pass",
+                                             "tile_filter")
                   if k in per_kernel}
     sort_in_step = None
     if sort_parts:

@@ -1,6 +1,6 @@
 """bench.py's training summary on a synthetic kernel-timer report (host only): per-kernel
-HBM fractions, the roofline object on the largest HBM-bound kernel, the ncu traffic
-scaling, and the sort's share of the step."""
+HBM fractions, the roofline object on the largest kernel with an HBM byte model, and the
+sort's share of the step."""
 import pytest
 
 from gsplat_tt_b200 import train_bench as tb
@@ -14,8 +14,9 @@ def test_summary_picks_largest_hbm_kernel_and_scales_traffic():
     rep = {  # name: (total ms over ksteps steps, launches)
         "train_project": (12.4, 2),
         "radix_pass32": (14.8, 256),
-        "tile_sort_emit": (26.0, 64),
-        "tile_sort_pass": (18.8, 64),
+        "tile_sort_emit": (16.0, 64),
+        "tile_sort_pass": (8.8, 64),
+        "tile_filter": (6.0, 64),
         "raster_fwd": (33.2, 64),
         "raster_bwd": (74.2, 64),
         "loss": (11.7, 64),
@@ -23,16 +24,18 @@ def test_summary_picks_largest_hbm_kernel_and_scales_traffic():
         "sparse_adam": (3.4, 2),
     }
     per_kernel, roof, sort = tb.summarize_kernels(rep, ksteps, n, views, pairs, px, PEAKS)
-    assert roof["kernel"] == "tile_sort_emit"          # raster_bwd is larger but issue-bound
+    assert roof["kernel"] == "radix_pass32"            # raster_bwd is larger but issue-bound
     assert "achieved_gbs" not in per_kernel["raster_bwd"]
-    e = per_kernel["tile_sort_emit"]
-    assert e["ms_per_step"] == pytest.approx(13.0)
-    assert e["algorithmic_bytes"] == pytest.approx(pairs * 8 + n * 16)
-    assert roof["achieved"] == pytest.approx(e["algorithmic_bytes"] / (26.0 / 64 / 1e3) / 1e9)
+    assert "achieved_gbs" not in per_kernel["tile_sort_emit"]   # per super-tile item bytes
+    e = per_kernel["radix_pass32"]
+    assert e["ms_per_step"] == pytest.approx(7.4)
+    assert e["algorithmic_bytes"] == pytest.approx(n * 16)
+    assert roof["achieved"] == pytest.approx(e["algorithmic_bytes"] / (14.8 / 256 / 1e3) / 1e9)
     assert roof["frac"] == pytest.approx(roof["achieved"] / 6541.5)
-    assert roof["traffic"] == pytest.approx(172.1e6 * pairs / 21898068.0)
+    assert roof["traffic"] is None
     assert "raster_bwd 37.1 ms" in roof["note"]
-    assert sort["ms_per_step"] == pytest.approx((14.8 + 26.0 + 18.8) / 2)
+    assert per_kernel["tile_filter"]["algorithmic_bytes"] == pytest.approx(pairs * 4)
+    assert sort["ms_per_step"] == pytest.approx((14.8 + 16.0 + 8.8 + 6.0) / 2)
     assert per_kernel["train_project"]["algorithmic_bytes"] == pytest.approx(n * 236 + views * n * 52)
 
 
@@ -47,7 +50,7 @@ def test_chunked_and_owner_sharded_launches_are_charged_their_own_rows():
     moves link bytes, not HBM bytes: no kernel may read above the peak."""
     n, views, world, q, chunks = 6_000_000, 4, 8, 187_500, 4
     rep = {"param_bwd": (2.41 * 2, 4 * 2), "sparse_adam_mc": (3.28 * 2, 4 * 2),
-           "tile_sort_emit": (2.0, 8)}
+           "tile_filter": (2.0, 8)}
     per_kernel, roof, _ = tb.summarize_kernels(rep, 2, n, views, 4.6e7, 1920 * 1080, PEAKS,
                                                adam_rows=chunks * q, world=world, q=q)
     pb = per_kernel["param_bwd"]
@@ -57,7 +60,7 @@ def test_chunked_and_owner_sharded_launches_are_charged_their_own_rows():
     assert "frac_hbm" not in mc
     assert mc["link_bytes_per_direction"] == pytest.approx(q * (world * 240 + 236))
     assert mc["frac_nvlink"] == pytest.approx(mc["achieved_link_gbs"] / tb.NVLINK_GBS)
-    assert roof["kernel"] in ("param_bwd", "tile_sort_emit")
+    assert roof["kernel"] in ("param_bwd", "tile_filter")
     # NCCL owner-sharded update: the rank's own rows
     per_kernel, _, _ = tb.summarize_kernels({"sparse_adam": (1.0, 1)}, 1, n, views, 1.0, 1,
                                             PEAKS, adam_rows=n // world, world=world)
