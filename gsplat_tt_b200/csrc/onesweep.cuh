@@ -122,12 +122,19 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
     for (int j = 0; j < kSortItems; ++j) {
         const uint32_t d = GS_DIGIT(key[j]);
         uint32_t peers = 0xffffffffu;
+        if (digit_bits == kRadixBits) {
 #pragma unroll
-        for (int b = 0; b < kRadixBits; ++b) {  // bits above digit_bits are 0 in every lane
-            if (b >= digit_bits) break;         // a narrower last digit needs fewer ballots
-            const uint32_t bit = (d >> b) & 1u;
-            const uint32_t m = __ballot_sync(0xffffffffu, bit);
-            peers &= bit ? m : ~m;
+            for (int b = 0; b < kRadixBits; ++b) {
+                const uint32_t bit = (d >> b) & 1u;
+                const uint32_t m = __ballot_sync(0xffffffffu, bit);
+                peers &= bit ? m : ~m;
+            }
+        } else {  // a narrower last digit needs fewer ballots (higher bits are 0 in every lane)
+            for (int b = 0; b < digit_bits; ++b) {
+                const uint32_t bit = (d >> b) & 1u;
+                const uint32_t m = __ballot_sync(0xffffffffu, bit);
+                peers &= bit ? m : ~m;
+            }
         }
         const int leader = 31 - __clz(peers);
         uint32_t old = 0;

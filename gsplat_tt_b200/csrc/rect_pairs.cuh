@@ -4,11 +4,11 @@
 // Pair order before the sort (the order the stable sort must preserve within a tile):
 // Gaussians in depth order, each Gaussian's tiles row-major inside its rectangle. The
 // rectangle is taken at a coarser grid (tile coordinates >> shift: shift 1 = the 2x2-tile
-// super-tiles), key = cell id (cy * cells_x + cx), value = the Gaussian's depth index.
-// Sorting that stably by cell id gives each cell's Gaussians in depth order; with shift 0
-// that is the reference's (tile, depth bits, Gaussian id) order
-// (src/gsplat_cpu/sort.cpp:24-27) and with shift 1 the tile filter (train_project.cu)
-// derives it per tile.
+// super-tiles), key = cell id (cy * cells_x + cx). With shift 0 the value is the Gaussian
+// id and sorting stably by cell id gives the reference's (tile, depth bits, Gaussian id)
+// order (src/gsplat_cpu/sort.cpp:24-27); with shift 1 the value is Gaussian id << 4 | the
+// mask of the super-tile's four tiles the Gaussian's rectangle covers (bit 2 * row +
+// column), from which the tile filter (train_project.cu) derives each tile's list.
 #pragma once
 
 #include "onesweep.cuh"
@@ -33,6 +33,18 @@ struct RectPairSource {
     // warp-striped items from shared memory.
     static constexpr uint32_t kOwnPairs = 32;
 
+    // Value of the item of (depth-ordered Gaussian with id gid and tile rectangle r0, cell
+    // (cx, cy)).
+    __device__ __forceinline__ uint32_t value(uint32_t gid, ushort4 r0, uint32_t cx,
+                                              uint32_t cy) const {
+        if (shift == 0) return gid;
+        const uint32_t x = 2u * cx, y = 2u * cy;
+        const uint32_t cols = (x >= r0.x && x <= r0.y ? 1u : 0u) | (x + 1u >= r0.x && x + 1u <= r0.y ? 2u : 0u);
+        const uint32_t m = (y >= r0.z && y <= r0.w ? cols : 0u) |
+                           (y + 1u >= r0.z && y + 1u <= r0.w ? cols << 2 : 0u);
+        return (gid << 4) | m;
+    }
+
     __device__ __forceinline__ void load(SortSmem<uint32_t>& S, uint32_t tile, int64_t base,
                                          int valid, int64_t n, uint32_t pad,
                                          uint32_t (&key)[kSortItems],
@@ -55,7 +67,7 @@ struct RectPairSource {
         for (uint32_t c0 = gf; c0 <= gl; c0 += kSortThreads, par ^= 1) {
             const uint32_t i = c0 + (uint32_t)tid;
             if (i <= gl) {
-                const uint32_t off = goff[i], end = goff[i + 1], gid = i;
+                const uint32_t off = goff[i], end = goff[i + 1], gid = order[i];
                 const ushort4 r0 = rect[i];
                 const ushort4 r = make_ushort4(r0.x >> shift, r0.y >> shift, r0.z >> shift,
                                                r0.w >> shift);
@@ -66,7 +78,7 @@ struct RectPairSource {
                     uint32_t ty = r.z + j0 / w, tx = r.x + j0 % w;
                     for (uint32_t p = p0; p < p1; ++p) {
                         S.keys[p - lo_p] = ty * tx_n + tx;
-                        S.vals[p - lo_p] = gid;
+                        S.vals[p - lo_p] = value(gid, r0, tx, ty);
                         if (++tx > r.y) {
                             tx = r.x;
                             ++ty;
@@ -82,7 +94,7 @@ struct RectPairSource {
             if (tid == 0) s_nbig[par] = 0u;
             for (uint32_t q = (uint32_t)warp; q < nbig; q += kSortWarps) {
                 const uint32_t bi = s_big[par][q];
-                const uint32_t off = goff[bi], end = goff[bi + 1], gid = bi;
+                const uint32_t off = goff[bi], end = goff[bi + 1], gid = order[bi];
                 const ushort4 r0 = rect[bi];
                 const ushort4 r = make_ushort4(r0.x >> shift, r0.y >> shift, r0.z >> shift,
                                                r0.w >> shift);
@@ -90,8 +102,9 @@ struct RectPairSource {
                 const uint32_t w = (uint32_t)r.y - (uint32_t)r.x + 1u;
                 for (uint32_t p = p0 + (uint32_t)lane; p < p1; p += 32u) {
                     const uint32_t j = p - off;
-                    S.keys[p - lo_p] = (r.z + j / w) * tx_n + r.x + j % w;
-                    S.vals[p - lo_p] = gid;
+                    const uint32_t cy = r.z + j / w, cx = r.x + j % w;
+                    S.keys[p - lo_p] = cy * tx_n + cx;
+                    S.vals[p - lo_p] = value(gid, r0, cx, cy);
                 }
             }
         }

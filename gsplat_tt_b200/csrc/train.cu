@@ -1513,6 +1513,13 @@ static gs_status project_views(const GConst& P, int64_t n, int n_views, const TC
     return GS_OK;
 }
 
+// Largest Gaussian count (exclusive) sorted through super-tiles: the packed sort value
+// holds id << 4, so 2^28. A build option so the direct tile sort can be exercised on small
+// scenes too.
+#ifndef GS_SUPER_TILE_MAX_N
+#define GS_SUPER_TILE_MAX_N (1ll << 28)
+#endif
+
 // Depth order, pair offsets, tile counts / ranges and the tile sort of one projected view.
 static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, ViewLane& V,
                            int64_t cap, cudaStream_t st) {
@@ -1523,39 +1530,42 @@ static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, Vie
     gs_status s = radix_sort_pairs32(pv.dsort, nullptr, nullptr, n, 32, nullptr, V.order, V.radix,
                                      V.radix_bytes, st, &rerr, L.err);
     if (s != GS_OK) return s;
-    launch_sorted_count(pv, V.order, n, V.blk2, st);
+    // The tile lists come from a stable sort of the (Gaussian, 2x2-tile super-tile) pairs
+    // -- about 0.43 of the (Gaussian, tile) pairs at the benchmark sizes -- and a filter that
+    // hands each super-tile's depth-ordered items to its four tiles (shift 1), or, when the
+    // Gaussian ids do not fit the 28 bits the packed sort value leaves, from a sort of the
+    // (Gaussian, tile) pairs themselves (shift 0).
+    const int shift = (n < (int64_t)GS_SUPER_TILE_MAX_N) ? 1 : 0;
+    launch_sorted_count(pv, V.order, n, shift, V.blk2, st);
     GS_CHECK_LAUNCH();
     scan_block_totals<int64_t><<<1, 1024, 0, st>>>(V.blk2, nb, nullptr);
     GS_CHECK_LAUNCH();
-    // The tile lists come from a stable sort of the (Gaussian, 2x2-tile super-tile) pairs
-    // -- about 0.43 of the (Gaussian, tile) pairs at the benchmark sizes -- and a filter that
-    // hands each super-tile's depth-ordered items to its four tiles.
-    const int sx_n = (cfg.tiles_x + 1) / 2, sy_n = (cfg.tiles_y + 1) / 2;
-    const int nsuper = sx_n * sy_n;
-    const int super_bits = bits_for(nsuper > 1 ? nsuper - 1 : 1);
-    const int npass = radix_num_passes(super_bits);
+    const int cells_x = shift ? (cfg.tiles_x + 1) / 2 : cfg.tiles_x;
+    const int cells = shift ? cells_x * ((cfg.tiles_y + 1) / 2) : cfg.tiles_x * cfg.tiles_y;
+    const int key_bits = bits_for(cells > 1 ? cells - 1 : 1);
+    const int npass = radix_num_passes(key_bits);
     {
         KernelTimer kt("pair_offsets", st);
         GS_CUDA_CHECK(cudaMemsetAsync(V.tlast, 0, sizeof(uint32_t), st));
         launch_pair_offsets(pv, V.order, n, V.blk2, cap, V.goff, V.rect_d, V.tfirst, V.tfirst_len,
-                            V.tlast, V.stotal, L.err, st);
+                            V.tlast, shift, V.stotal, L.err, st);
         GS_CHECK_LAUNCH();
     }
     {
         KernelTimer kt("tile_counts", st);
-        s = launch_tile_counts(pv, n, cfg.tiles_x, cfg.tiles_y, npass, L.pairs + view, cap,
+        s = launch_tile_counts(pv, n, cfg.tiles_x, cfg.tiles_y, shift, npass, L.pairs + view, cap,
                                V.tdiff, V.ranges, V.sranges, V.tdig, L.err, st);
         if (s != GS_OK) return s;
     }
-    const RectPairSource src{V.order, V.goff, V.tfirst, V.tlast, V.rect_d, sx_n, 1};
-    s = radix_sort_rect_pairs(src, V.stotal, cap, super_bits, V.tdig, V.ssorted, V.radix,
-                              V.radix_bytes, st, L.err);
+    const RectPairSource src{V.order, V.goff, V.tfirst, V.tlast, V.rect_d, cells_x, shift};
+    s = radix_sort_rect_pairs(src, V.stotal, cap, key_bits, V.tdig, shift ? V.ssorted : V.svals,
+                              V.radix, V.radix_bytes, st, L.err);
     if (s != GS_OK) return s;
-    {
+    if (shift) {
         KernelTimer kt("tile_filter", st);
-        launch_tile_filter(V.ssorted, V.sranges, V.rect_d, V.order, V.ranges, cfg.tiles_x,
-                           cfg.tiles_y, L.pairs + view, cap, V.svals, st);
-        GS_CHECK_LAUNCH();
+        s = launch_tile_filter(V.ssorted, V.sranges, V.ranges, cfg.tiles_x, cfg.tiles_y,
+                               L.pairs + view, cap, V.svals, st);
+        if (s != GS_OK) return s;
     }
     return GS_OK;
 }

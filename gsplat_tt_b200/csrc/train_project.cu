@@ -233,50 +233,51 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
         blk[v * blk_stride + blockIdx.x] = (int64_t)s_tot[v];
 }
 
-// Super-tile pairs of a Gaussian with tiles (cnt > 0): the 2x2-tile super-tiles its tile
-// rectangle touches.
-__device__ __forceinline__ uint32_t super_count(uint32_t cnt, ushort4 r) {
-    return cnt == 0u ? 0u
-                     : (uint32_t)((r.y >> 1) - (r.x >> 1) + 1) * (uint32_t)((r.w >> 1) - (r.z >> 1) + 1);
+// Items of a Gaussian with tiles (cnt > 0) in the tile sort: with shift 1 the 2x2-tile
+// super-tiles its tile rectangle touches, with shift 0 its tiles.
+__device__ __forceinline__ uint32_t cell_count(uint32_t cnt, ushort4 r, int shift) {
+    return (cnt == 0u || shift == 0)
+               ? cnt
+               : (uint32_t)((r.y >> 1) - (r.x >> 1) + 1) * (uint32_t)((r.w >> 1) - (r.z >> 1) + 1);
 }
 
 // Super-tile pair counts of the Gaussians in depth order (`order` = Gaussian ids sorted by
 // depth bits, stable), one total per block for the offset scan.
 __global__ void __launch_bounds__(kProjThreads)
 k_sorted_count(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
-               const uint32_t* __restrict__ order, int64_t n, int64_t* __restrict__ blk) {
+               const uint32_t* __restrict__ order, int64_t n, int shift,
+               int64_t* __restrict__ blk) {
     __shared__ int64_t smem[33];
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     uint32_t c = 0u;
     if (i < n) {
         const uint32_t g = order[i];
-        c = super_count(cnt[g], rect[g]);
+        c = cell_count(cnt[g], rect[g], shift);
     }
     int64_t total;
     block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
     if (threadIdx.x == 0) blk[blockIdx.x] = total;
 }
 
-// First super-tile pair of each Gaussian in depth order (goff, n + 1 entries; goff[n] =
-// super pairs), clamped to the pair capacity (DEV_OVERFLOW when they exceed it), and its
-// tile rectangle in depth order (rect_d, read by the tile sort and the tile filter without
-// a gather). Also, per 4096-item tile of the super-tile sort, the depth index of the
-// Gaussian holding the tile's first item (tfirst), the depth index of the last Gaussian
-// with pairs (Gaussians without pairs sort after every Gaussian with pairs), and the
-// number of super-tile pairs (super_total).
+// First tile-sort item (cell_count) of each Gaussian in depth order (goff, n + 1 entries;
+// goff[n] = items), clamped to the pair capacity (DEV_OVERFLOW when they exceed it), and its
+// tile rectangle in depth order (rect_d, read by the tile sort without a gather). Also, per
+// 4096-item tile of the tile sort, the depth index of the Gaussian holding the tile's first
+// item (tfirst), the depth index of the last Gaussian with pairs (Gaussians without pairs
+// sort after every Gaussian with pairs), and the number of items (super_total).
 __global__ void __launch_bounds__(kProjThreads)
 k_pair_offsets(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
                const uint32_t* __restrict__ order, int64_t n,
                const int64_t* __restrict__ blk_offsets, int64_t capacity,
                uint32_t* __restrict__ goff, ushort4* __restrict__ rect_d,
                uint32_t* __restrict__ tfirst, int64_t tfirst_len,
-               uint32_t* __restrict__ last, int64_t* __restrict__ super_total,
+               uint32_t* __restrict__ last, int shift, int64_t* __restrict__ super_total,
                unsigned int* __restrict__ err) {
     __shared__ int64_t smem[33];
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const uint32_t g = (i < n) ? order[i] : 0u;
     const ushort4 rg = (i < n) ? rect[g] : make_ushort4(0, 0, 0, 0);
-    const uint32_t c = (i < n) ? super_count(cnt[g], rg) : 0u;
+    const uint32_t c = (i < n) ? cell_count(cnt[g], rg, shift) : 0u;
     int64_t total;
     const int64_t off = blk_offsets[blockIdx.x] + block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
     uint32_t cn = __shfl_down_sync(0xffffffffu, c, 1);
@@ -345,10 +346,22 @@ k_tile_diff(const ushort4* __restrict__ rect, const uint32_t* __restrict__ cnt, 
 // with (t >> 8p) & 255 == d. When the view's pairs exceed the capacity (reported through
 // DEV_OVERFLOW by k_pair_offsets) every range is left empty, so no later kernel reads
 // past the sorted-pair buffer.
+struct GridFinish {
+    const int* diff;
+    int tiles_x, tiles_y, npass;
+    int2* ranges;
+    uint32_t* digit_offsets;
+    unsigned int* err;
+};
+
 __global__ void __launch_bounds__(1024)
-k_tile_finish(const int* __restrict__ diff, int tiles_x, int tiles_y, int npass,
-              const int64_t* __restrict__ pairs, int64_t capacity, int2* __restrict__ ranges,
-              uint32_t* __restrict__ digit_offsets, unsigned int* __restrict__ err) {
+k_tile_finish(GridFinish g0, GridFinish g1, const int64_t* __restrict__ pairs, int64_t capacity) {
+    const GridFinish& G = blockIdx.x == 0 ? g0 : g1;  // one block per grid
+    const int* __restrict__ diff = G.diff;
+    const int tiles_x = G.tiles_x, tiles_y = G.tiles_y, npass = G.npass;
+    int2* __restrict__ ranges = G.ranges;
+    uint32_t* __restrict__ digit_offsets = G.digit_offsets;
+    unsigned int* __restrict__ err = G.err;
     __shared__ uint32_t s_rows[kMaxTileRows];
     __shared__ uint32_t s_hist[4][256];
     __shared__ uint32_t smem[33];
@@ -449,81 +462,104 @@ void launch_project(const GConst& P, int64_t n, const TCam* cams, int n_views, c
     }
 }
 
-// The per-tile lists from the super-tile lists: one block per 2x2-tile super-tile reads
-// the super-tile's items (depth indices, in depth order) in chunks and hands each one to
-// the (up to four) tiles of the super-tile its tile rectangle covers, keeping the order:
-// every tile's list is the depth-ordered list of the Gaussians covering it, exactly what a
-// stable sort of all (tile, Gaussian) pairs by tile gives. Nothing is written when the
-// view's pairs exceed the capacity (the ranges are empty then).
+// The per-tile lists from the super-tile lists: one block per 2x2-tile super-tile, its
+// items (Gaussian id << 4 | mask of the super-tile's tiles its rectangle covers, in depth
+// order) split into one contiguous part per warp. Each warp counts its part's items per
+// tile, one barrier gives every warp its offsets, and each warp walks its part again 32
+// items at a time, appending each item to the lists of the tiles in its mask, in order (a
+// ballot per tile gives every lane its slot; the lanes of a tile store to consecutive ids).
+// Every tile's list is then the depth-ordered list of the Gaussians covering it, exactly
+// what a stable sort of all (tile, Gaussian) pairs by tile gives. Loads run kFilterAhead
+// steps ahead. Nothing is written when the view's pairs exceed the capacity (the ranges are
+// empty then).
 __global__ void __launch_bounds__(kFilterThreads)
-k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict__ super_ranges,
-              const ushort4* __restrict__ rect_d, const uint32_t* __restrict__ order,
+k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict__ sranges,
               const int2* __restrict__ ranges, int tiles_x, int tiles_y,
               const int64_t* __restrict__ pairs, int64_t capacity,
               uint32_t* __restrict__ svals) {
-    __shared__ uint32_t smem[33];
+    constexpr int NW = kFilterThreads / 32;
+    __shared__ uint32_t s_cnt[NW][4];
     if (*pairs > capacity) return;
-    const int sx_n = (tiles_x + 1) / 2;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sid = blockIdx.x;
-    const int sx = sid % sx_n, sy = sid / sx_n;
-    const int2 sr = super_ranges[sid];
+    const int2 sr = sranges[sid];
     if (sr.y <= sr.x) return;
-    int tx[4], ty[4], base[4];
+    const int len = sr.y - sr.x;
+    const int beg = sr.x + (int)((int64_t)len * warp / NW);
+    const int end = sr.x + (int)((int64_t)len * (warp + 1) / NW);
+    const uint32_t lt = (1u << lane) - 1u;
+    uint32_t c[4] = {0u, 0u, 0u, 0u};
+    for (int k0 = beg; k0 < end; k0 += 32 * kFilterAhead) {
+        uint32_t v[kFilterAhead];
+#pragma unroll
+        for (int a = 0; a < kFilterAhead; ++a) {
+            const int k = k0 + a * 32 + lane;
+            v[a] = (k < end) ? super_sorted[k] : 0u;
+        }
+#pragma unroll
+        for (int a = 0; a < kFilterAhead; ++a)
+#pragma unroll
+            for (int q = 0; q < 4; ++q) c[q] += (v[a] >> q) & 1u;
+    }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-        tx[q] = 2 * sx + (q & 1);
-        ty[q] = 2 * sy + (q >> 1);
-        base[q] = (tx[q] < tiles_x && ty[q] < tiles_y) ? ranges[ty[q] * tiles_x + tx[q]].x : 0;
+        const uint32_t t = __reduce_add_sync(0xffffffffu, c[q]);
+        if (lane == 0) s_cnt[warp][q] = t;
     }
-    uint32_t run01 = 0u, run23 = 0u;  // items already written per tile, two 16-bit counts each
-    for (int c0 = sr.x; c0 < sr.y; c0 += kFilterThreads) {
-        const int k = c0 + (int)threadIdx.x;
-        uint32_t f[4] = {0u, 0u, 0u, 0u}, gid = 0u;
-        if (k < sr.y) {
-            const uint32_t di = super_sorted[k];
-            const ushort4 r = rect_d[di];
-            gid = order[di];
+    __syncthreads();
+    const int sx_n = (tiles_x + 1) / 2;
+    const int tx0 = 2 * (sid % sx_n), ty0 = 2 * (sid / sx_n);
+    uint32_t* dst[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q)
-                f[q] = (tx[q] < tiles_x && ty[q] < tiles_y && tx[q] >= r.x && tx[q] <= r.y &&
-                        ty[q] >= r.z && ty[q] <= r.w) ? 1u : 0u;
+    for (int q = 0; q < 4; ++q) {
+        const int tx = tx0 + (q & 1), ty = ty0 + (q >> 1);
+        uint32_t off = 0u;
+        for (int w = 0; w < warp; ++w) off += s_cnt[w][q];
+        // a tile outside the grid is in no item's mask
+        dst[q] = svals + ((tx < tiles_x && ty < tiles_y) ? ranges[ty * tiles_x + tx].x : 0) + off;
+    }
+    for (int k0 = beg; k0 < end; k0 += 32 * kFilterAhead) {
+        uint32_t v[kFilterAhead];
+#pragma unroll
+        for (int a = 0; a < kFilterAhead; ++a) {
+            const int k = k0 + a * 32 + lane;
+            v[a] = (k < end) ? super_sorted[k] : 0u;
         }
-        // block-wide exclusive prefix of the four flags, two per 32-bit word (a chunk holds
-        // at most kFilterThreads items, far below 2^16)
-        uint32_t t01, t23;
-        const uint32_t e01 = block_exclusive_scan<uint32_t>(f[0] | (f[1] << 16), smem, &t01);
-        const uint32_t e23 = block_exclusive_scan<uint32_t>(f[2] | (f[3] << 16), smem, &t23);
-        const uint32_t pos01 = run01 + e01, pos23 = run23 + e23;
-        if (f[0]) svals[base[0] + (pos01 & 0xFFFFu)] = gid;
-        if (f[1]) svals[base[1] + (pos01 >> 16)] = gid;
-        if (f[2]) svals[base[2] + (pos23 & 0xFFFFu)] = gid;
-        if (f[3]) svals[base[3] + (pos23 >> 16)] = gid;
-        run01 += t01;
-        run23 += t23;
+#pragma unroll
+        for (int a = 0; a < kFilterAhead; ++a) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const bool hit = (v[a] >> q) & 1u;
+                const uint32_t b = __ballot_sync(0xffffffffu, hit);
+                if (hit) dst[q][__popc(b & lt)] = v[a] >> 4;
+                dst[q] += __popc(b);
+            }
+        }
     }
 }
 
-void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int64_t* blk,
-                         cudaStream_t st) {
-    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, pv.rect, order, n, blk);
+void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int shift,
+                         int64_t* blk, cudaStream_t st) {
+    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, pv.rect, order, n,
+                                                                    shift, blk);
 }
 
 void launch_pair_offsets(const ProjView& pv, const uint32_t* order, int64_t n,
                          const int64_t* blk_offsets, int64_t capacity, uint32_t* goff,
                          ushort4* rect_d, uint32_t* tfirst, int64_t tfirst_len, uint32_t* last,
-                         int64_t* super_total, unsigned int* err, cudaStream_t st) {
+                         int shift, int64_t* super_total, unsigned int* err, cudaStream_t st) {
     k_pair_offsets<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(
         pv.cnt, pv.rect, order, n, blk_offsets, capacity, goff, rect_d, tfirst, tfirst_len, last,
-        super_total, err);
+        shift, super_total, err);
 }
 
 int tile_diff_ints(int tiles_x, int tiles_y) {
     return (tiles_x + 1) * tiles_y + ((tiles_x + 1) / 2 + 1) * ((tiles_y + 1) / 2);
 }
 
-gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y,
-                             int super_npass, const int64_t* pairs, int64_t capacity, int* diff,
-                             int2* ranges, int2* super_ranges, uint32_t* super_digit_offsets,
+gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y, int shift,
+                             int npass, const int64_t* pairs, int64_t capacity, int* diff,
+                             int2* ranges, int2* super_ranges, uint32_t* digit_offsets,
                              unsigned int* err, cudaStream_t st) {
     const int bins = tile_diff_ints(tiles_x, tiles_y);
     constexpr int kSmemBins = 40960;  // 160 KB
@@ -535,25 +571,26 @@ gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int til
     k_tile_diff<<<grid, 1024, smem, st>>>(pv.rect, pv.cnt, n, tiles_x, tiles_y,
                                           smem ? kSmemBins : 0, diff);
     GS_CHECK_LAUNCH();
-    // tile ranges, then the super-tile ranges and the super-tile sort's digit offsets
-    k_tile_finish<<<1, 1024, 0, st>>>(diff, tiles_x, tiles_y, 0, pairs, capacity, ranges,
-                                      nullptr, err);
-    GS_CHECK_LAUNCH();
+    // block 0: tile ranges; block 1: super-tile ranges; the sort's digit
+    // offsets from the grid it sorts by (super-tiles with shift 1, tiles with shift 0)
     const int sx_n = (tiles_x + 1) / 2, sy_n = (tiles_y + 1) / 2;
-    k_tile_finish<<<1, 1024, 0, st>>>(diff + (tiles_x + 1) * tiles_y, sx_n, sy_n, super_npass,
-                                      pairs, capacity, super_ranges, super_digit_offsets, nullptr);
+    const GridFinish tiles{diff, tiles_x, tiles_y, shift ? 0 : npass, ranges,
+                           shift ? nullptr : digit_offsets, err};
+    const GridFinish supers{diff + (tiles_x + 1) * tiles_y, sx_n, sy_n, shift ? npass : 0,
+                            super_ranges, shift ? digit_offsets : nullptr, nullptr};
+    k_tile_finish<<<2, 1024, 0, st>>>(tiles, supers, pairs, capacity);
     GS_CHECK_LAUNCH();
     return GS_OK;
 }
 
-void launch_tile_filter(const uint32_t* super_sorted, const int2* super_ranges,
-                        const ushort4* rect_d, const uint32_t* order, const int2* ranges,
-                        int tiles_x, int tiles_y, const int64_t* pairs, int64_t capacity,
-                        uint32_t* svals, cudaStream_t st) {
+gs_status launch_tile_filter(const uint32_t* super_sorted, const int2* super_ranges,
+                             const int2* ranges, int tiles_x, int tiles_y, const int64_t* pairs,
+                             int64_t capacity, uint32_t* svals, cudaStream_t st) {
     const int nsuper = ((tiles_x + 1) / 2) * ((tiles_y + 1) / 2);
-    k_tile_filter<<<nsuper, kFilterThreads, 0, st>>>(super_sorted, super_ranges, rect_d, order,
-                                                     ranges, tiles_x, tiles_y, pairs, capacity,
-                                                     svals);
+    k_tile_filter<<<nsuper, kFilterThreads, 0, st>>>(super_sorted, super_ranges, ranges, tiles_x,
+                                                     tiles_y, pairs, capacity, svals);
+    GS_CHECK_LAUNCH();
+    return GS_OK;
 }
 
 }  // namespace gs
