@@ -1322,8 +1322,9 @@ constexpr int kLanes = GS_TRAIN_LANES;
 struct ViewLane {
     int64_t* blk2;
     uint32_t* order;   // Gaussian ids sorted by depth
-    uint32_t* goff;    // first pair of each depth-ordered Gaussian (n + 1)
-    ushort4* rect_d;   // tile rectangle of each depth-ordered Gaussian with pairs
+    uint32_t* goff;    // first tile-sort item of each depth-ordered Gaussian (n + 1)
+    ushort4* rect_d;   // tile rectangle of each depth-ordered Gaussian
+    uint32_t* ccnt;    // tile-sort items of each depth-ordered Gaussian
     uint32_t* tfirst;  // per 4096-item super-tile sort tile: depth index of its first item's Gaussian
     int64_t tfirst_len;
     uint32_t* tlast;   // depth index of the last Gaussian with pairs
@@ -1389,6 +1390,7 @@ static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int 
         V.order = ws.template take<uint32_t>(n);
         V.goff = ws.template take<uint32_t>(n + 1);
         V.rect_d = ws.template take<ushort4>(n);
+        V.ccnt = ws.template take<uint32_t>(n);
         V.tfirst_len = div_up(cap, kTileItems) + 1;
         V.tfirst = ws.template take<uint32_t>(V.tfirst_len);
         V.tlast = ws.template take<uint32_t>(1);
@@ -1525,18 +1527,18 @@ static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, Vie
                            int64_t cap, cudaStream_t st) {
     const unsigned int nb = div_up(n, kProjThreads);
     const ProjView pv = L.pv.view(view, n);
-    // Gaussians in (depth bits, id) order; those without pairs sort last.
-    unsigned int* rerr = nullptr;
-    gs_status s = radix_sort_pairs32(pv.dsort, nullptr, nullptr, n, 32, nullptr, V.order, V.radix,
-                                     V.radix_bytes, st, &rerr, L.err);
-    if (s != GS_OK) return s;
     // The tile lists come from a stable sort of the (Gaussian, 2x2-tile super-tile) pairs
     // -- about 0.43 of the (Gaussian, tile) pairs at the benchmark sizes -- and a filter that
     // hands each super-tile's depth-ordered items to its four tiles (shift 1), or, when the
     // Gaussian ids do not fit the 28 bits the packed sort value leaves, from a sort of the
     // (Gaussian, tile) pairs themselves (shift 0).
     const int shift = (n < (int64_t)GS_SUPER_TILE_MAX_N) ? 1 : 0;
-    launch_sorted_count(pv, V.order, n, shift, V.blk2, st);
+    // Gaussians in (depth bits, id) order, those without pairs last; the last pass also
+    // writes each one's rectangle and tile-sort item count in depth order.
+    const GaussianCellSink sink{pv.cnt, pv.rect, shift, V.rect_d, V.ccnt};
+    gs_status s = radix_sort_depth(pv.dsort, n, sink, V.order, V.radix, V.radix_bytes, st, L.err);
+    if (s != GS_OK) return s;
+    launch_sorted_count(V.ccnt, n, V.blk2, st);
     GS_CHECK_LAUNCH();
     scan_block_totals<int64_t><<<1, 1024, 0, st>>>(V.blk2, nb, nullptr);
     GS_CHECK_LAUNCH();
@@ -1547,8 +1549,8 @@ static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, Vie
     {
         KernelTimer kt("pair_offsets", st);
         GS_CUDA_CHECK(cudaMemsetAsync(V.tlast, 0, sizeof(uint32_t), st));
-        launch_pair_offsets(pv, V.order, n, V.blk2, cap, V.goff, V.rect_d, V.tfirst, V.tfirst_len,
-                            V.tlast, shift, V.stotal, L.err, st);
+        launch_pair_offsets(V.ccnt, n, V.blk2, cap, V.goff, V.tfirst, V.tfirst_len, V.tlast,
+                            V.stotal, L.err, st);
         GS_CHECK_LAUNCH();
     }
     {

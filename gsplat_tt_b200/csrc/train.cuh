@@ -59,14 +59,11 @@ TCfg make_tcfg(const gs_train_config& c, int H, int W);
 void launch_project(const GConst& P, int64_t n, const TCam* cams, int n_views, const TCfg& cfg,
                     const ProjView& pv, int64_t* blk, int64_t blk_stride, uint64_t* touch,
                     float* vis_counts, float* grad2d, cudaStream_t st);
-// Tile sort by 2x2-tile super-tiles (shift 1) when Gaussian ids fit 28 bits (the sorted
-// value packs id << 4 | a 4-bit tile mask), else directly by tile (shift 0).
-void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int shift,
-                         int64_t* blk, cudaStream_t st);
-void launch_pair_offsets(const ProjView& pv, const uint32_t* order, int64_t n,
-                         const int64_t* blk_offsets, int64_t capacity, uint32_t* goff,
-                         ushort4* rect_d, uint32_t* tfirst, int64_t tfirst_len, uint32_t* last,
-                         int shift, int64_t* super_total, unsigned int* err, cudaStream_t st);
+// Offsets of the tile-sort items from their counts in depth order (ccnt).
+void launch_sorted_count(const uint32_t* ccnt, int64_t n, int64_t* blk, cudaStream_t st);
+void launch_pair_offsets(const uint32_t* ccnt, int64_t n, const int64_t* blk_offsets,
+                         int64_t capacity, uint32_t* goff, uint32_t* tfirst, int64_t tfirst_len,
+                         uint32_t* last, int64_t* total, unsigned int* err, cudaStream_t st);
 // ints of the two row-wise difference arrays (tile grid, then 2x2-tile super-tile grid)
 int tile_diff_ints(int tiles_x, int tiles_y);
 gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y, int shift,

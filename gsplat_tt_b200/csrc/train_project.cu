@@ -233,63 +233,42 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
         blk[v * blk_stride + blockIdx.x] = (int64_t)s_tot[v];
 }
 
-// Items of a Gaussian with tiles (cnt > 0) in the tile sort: with shift 1 the 2x2-tile
-// super-tiles its tile rectangle touches, with shift 0 its tiles.
-__device__ __forceinline__ uint32_t cell_count(uint32_t cnt, ushort4 r, int shift) {
-    return (cnt == 0u || shift == 0)
-               ? cnt
-               : (uint32_t)((r.y >> 1) - (r.x >> 1) + 1) * (uint32_t)((r.w >> 1) - (r.z >> 1) + 1);
-}
-
-// Super-tile pair counts of the Gaussians in depth order (`order` = Gaussian ids sorted by
-// depth bits, stable), one total per block for the offset scan.
+// Block totals of the tile-sort item counts of the Gaussians in depth order (ccnt, written
+// by the depth sort's last pass), for the offset scan.
 __global__ void __launch_bounds__(kProjThreads)
-k_sorted_count(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
-               const uint32_t* __restrict__ order, int64_t n, int shift,
-               int64_t* __restrict__ blk) {
+k_sorted_count(const uint32_t* __restrict__ ccnt, int64_t n, int64_t* __restrict__ blk) {
     __shared__ int64_t smem[33];
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    uint32_t c = 0u;
-    if (i < n) {
-        const uint32_t g = order[i];
-        c = cell_count(cnt[g], rect[g], shift);
-    }
+    const uint32_t c = (i < n) ? ccnt[i] : 0u;
     int64_t total;
     block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
     if (threadIdx.x == 0) blk[blockIdx.x] = total;
 }
 
-// First tile-sort item (cell_count) of each Gaussian in depth order (goff, n + 1 entries;
-// goff[n] = items), clamped to the pair capacity (DEV_OVERFLOW when they exceed it), and its
-// tile rectangle in depth order (rect_d, read by the tile sort without a gather). Also, per
+// First tile-sort item of each Gaussian in depth order (goff, n + 1 entries; goff[n] =
+// items), clamped to the pair capacity (DEV_OVERFLOW when they exceed it). Also, per
 // 4096-item tile of the tile sort, the depth index of the Gaussian holding the tile's first
 // item (tfirst), the depth index of the last Gaussian with pairs (Gaussians without pairs
-// sort after every Gaussian with pairs), and the number of items (super_total).
+// sort after every Gaussian with pairs), and the number of items (total).
 __global__ void __launch_bounds__(kProjThreads)
-k_pair_offsets(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
-               const uint32_t* __restrict__ order, int64_t n,
+k_pair_offsets(const uint32_t* __restrict__ ccnt, int64_t n,
                const int64_t* __restrict__ blk_offsets, int64_t capacity,
-               uint32_t* __restrict__ goff, ushort4* __restrict__ rect_d,
-               uint32_t* __restrict__ tfirst, int64_t tfirst_len,
-               uint32_t* __restrict__ last, int shift, int64_t* __restrict__ super_total,
+               uint32_t* __restrict__ goff, uint32_t* __restrict__ tfirst, int64_t tfirst_len,
+               uint32_t* __restrict__ last, int64_t* __restrict__ total_out,
                unsigned int* __restrict__ err) {
     __shared__ int64_t smem[33];
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const uint32_t g = (i < n) ? order[i] : 0u;
-    const ushort4 rg = (i < n) ? rect[g] : make_ushort4(0, 0, 0, 0);
-    const uint32_t c = (i < n) ? cell_count(cnt[g], rg, shift) : 0u;
+    const uint32_t c = (i < n) ? ccnt[i] : 0u;
     int64_t total;
     const int64_t off = blk_offsets[blockIdx.x] + block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
-    uint32_t cn = __shfl_down_sync(0xffffffffu, c, 1);
-    if ((threadIdx.x & 31) == 31) cn = (i + 1 < n) ? cnt[order[i + 1]] : 0u;
     if (i >= n) return;
+    const uint32_t cn = (i + 1 < n) ? ccnt[i + 1] : 0u;
     goff[i] = (uint32_t)min(off, capacity);
     if (i == n - 1) {
         goff[n] = (uint32_t)min(off + (int64_t)c, capacity);
-        *super_total = off + (int64_t)c;
+        *total_out = off + (int64_t)c;
     }
     if (c == 0) return;
-    rect_d[i] = rg;
     if (off + (int64_t)c > capacity) atomicOr(err, DEV_OVERFLOW);
     for (int64_t b = (off + kTileItems - 1) / kTileItems;
          b * kTileItems < off + (int64_t)c && b < tfirst_len; ++b)
@@ -538,19 +517,15 @@ k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict_
     }
 }
 
-void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int shift,
-                         int64_t* blk, cudaStream_t st) {
-    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, pv.rect, order, n,
-                                                                    shift, blk);
+void launch_sorted_count(const uint32_t* ccnt, int64_t n, int64_t* blk, cudaStream_t st) {
+    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(ccnt, n, blk);
 }
 
-void launch_pair_offsets(const ProjView& pv, const uint32_t* order, int64_t n,
-                         const int64_t* blk_offsets, int64_t capacity, uint32_t* goff,
-                         ushort4* rect_d, uint32_t* tfirst, int64_t tfirst_len, uint32_t* last,
-                         int shift, int64_t* super_total, unsigned int* err, cudaStream_t st) {
+void launch_pair_offsets(const uint32_t* ccnt, int64_t n, const int64_t* blk_offsets,
+                         int64_t capacity, uint32_t* goff, uint32_t* tfirst, int64_t tfirst_len,
+                         uint32_t* last, int64_t* total, unsigned int* err, cudaStream_t st) {
     k_pair_offsets<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(
-        pv.cnt, pv.rect, order, n, blk_offsets, capacity, goff, rect_d, tfirst, tfirst_len, last,
-        shift, super_total, err);
+        ccnt, n, blk_offsets, capacity, goff, tfirst, tfirst_len, last, total, err);
 }
 
 int tile_diff_ints(int tiles_x, int tiles_y) {
