@@ -128,6 +128,37 @@ __device__ __forceinline__ RPair stage_pair(float4 p0, float4 p1, float p2, floa
     return q;
 }
 
+// The forward rasteriser keeps, per pair it stages (at the pair's position in the tile's
+// sorted list), the float64-derived coefficients and the reach masks: qc = (P0, Lx, Ly,
+// bits of the row mask), qcols = the column mask. The backward, which only replays pairs
+// the forward staged, takes them from there instead of recomputing them; the opacity,
+// colour and conic are read from the projected records as in stage_pair, so every value
+// is identical to the forward's.
+__device__ __forceinline__ float4 pack_cache(const RPair& q) {
+    return make_float4(q.P0, q.Lx, q.Ly, __uint_as_float(q.rows));
+}
+
+__device__ __forceinline__ RPair stage_pair_cached(float4 p0, float4 p1, float p2, float4 qc,
+                                                   uint32_t qcols, float ox, float oy,
+                                                   float& mxl, float& myl) {
+    RPair q;
+    mxl = __fsub_rn(p0.x, ox);
+    myl = __fsub_rn(p0.y, oy);
+    q.Af = __fmul_rn(-0.5f, p0.z);
+    q.Bf = -p0.w;
+    q.Cf = __fmul_rn(-0.5f, p1.x);
+    q.P0 = qc.x;
+    q.Lx = qc.y;
+    q.Ly = qc.z;
+    q.op = p1.y;
+    q.r = p1.z;
+    q.g = p1.w;
+    q.b = p2;
+    q.rows = __float_as_uint(qc.w);
+    q.cols = qcols;
+    return q;
+}
+
 // power = P0 + du (Lx + Af du + Bf dv) + dv (Ly + Cf dv), every product and sum rounded
 // separately in the reference's order (gsplat/blend_backward_ref.py:88-92): the forward and
 // backward kernels and the oracle evaluate bit-identical powers, so only exp can move a
@@ -185,7 +216,8 @@ template <int TILE, int PPT>
 __global__ void __launch_bounds__(TILE * TILE / PPT)
 k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals, ProjView pv,
             TCfg cfg, int H, int W, float* __restrict__ image, float* __restrict__ final_T,
-            int32_t* __restrict__ n_contrib) {
+            int32_t* __restrict__ n_contrib, float4* __restrict__ qc,
+            uint32_t* __restrict__ qcols) {
     using LY = PixLayout<TILE, PPT>;
     constexpr int NB = kFwdBatch;
     constexpr int NP = PPT / 2;  // pixel pairs per thread, each blended with packed fp32x2 math
@@ -220,7 +252,10 @@ k_train_fwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
         for (int s = threadIdx.x; s < NB && b0 + s < rg.y; s += LY::kThreads) {
             const uint32_t g = svals[b0 + s];
             float mxl, myl;
-            sp[s] = stage_pair<TILE>(pv.p0[g], pv.p1[g], pv.p2[g], ox, oy, centre, amin, mxl, myl);
+            const RPair q = stage_pair<TILE>(pv.p0[g], pv.p1[g], pv.p2[g], ox, oy, centre, amin, mxl, myl);
+            sp[s] = q;
+            qc[b0 + s] = pack_cache(q);
+            qcols[b0 + s] = q.cols;
         }
         __syncthreads();
         const int nb = min(NB, rg.y - b0);
@@ -324,6 +359,7 @@ __global__ void __launch_bounds__(TILE * TILE / PPT)
 k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals, ProjView pv,
             TCfg cfg, int H, int W, const float* __restrict__ dimg,
             const float* __restrict__ final_T, const int32_t* __restrict__ n_contrib,
+            const float4* __restrict__ qc, const uint32_t* __restrict__ qcols,
             float* __restrict__ grad2d) {
     using LY = PixLayout<TILE, PPT>;
     constexpr int NB = kBwdBatch;
@@ -390,7 +426,8 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             const uint32_t g = svals[rg.x + lo + s];
             const float4 p0 = pv.p0[g], p1 = pv.p1[g];
             BPair bp;
-            bp.q = stage_pair<TILE>(p0, p1, pv.p2[g], ox, oy, centre, amin, bp.mxl, bp.myl);
+            bp.q = stage_pair_cached(p0, p1, pv.p2[g], qc[rg.x + lo + s], qcols[rg.x + lo + s], ox,
+                                     oy, bp.mxl, bp.myl);
             bp.A = p0.z;
             bp.B = p0.w;
             bp.C = p1.x;
@@ -1334,6 +1371,8 @@ struct ViewLane {
     int2* sranges;     // per super-tile [start, end) into ssorted
     uint32_t* ssorted; // depth indices sorted by (super-tile, depth order)
     uint32_t* svals;   // Gaussian ids sorted by (tile, depth bits, id)
+    float4* qc;        // per sorted pair the forward staged: P0, Lx, Ly, row mask (for the backward)
+    uint32_t* qcols;   // per sorted pair the forward staged: column mask
     char* radix;
     size_t radix_bytes;
     int2* ranges;
@@ -1400,6 +1439,8 @@ static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int 
         V.sranges = ws.template take<int2>(((W / tile + 2) / 2) * ((H / tile + 2) / 2));
         V.ssorted = ws.template take<uint32_t>(cap);
         V.svals = ws.template take<uint32_t>(cap);
+        V.qc = ws.template take<float4>(cap);
+        V.qcols = ws.template take<uint32_t>(cap);
         // one scratch region serves the depth sort (N, 32 bits) and the tile sort (P, tile bits)
         V.radix_bytes = std::max(radix_workspace_bytes(n, 32, 4), radix_workspace_bytes(cap, tile_bits, 4));
         V.radix = ws.template take<char>(V.radix_bytes);
@@ -1616,9 +1657,9 @@ static gs_status launch_raster_fwd(const TCfg& c, const ViewLane& V, const ProjV
     KernelTimer kt("raster_fwd", st);
     const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
     if (c.tile == 16)
-        k_train_fwd<16, kFwdPPT><<<tiles, 256 / kFwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
+        k_train_fwd<16, kFwdPPT><<<tiles, 256 / kFwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon, V.qc, V.qcols);
     else
-        k_train_fwd<32, kFwdPPT><<<tiles, 1024 / kFwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon);
+        k_train_fwd<32, kFwdPPT><<<tiles, 1024 / kFwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, img, V.final_T, V.ncon, V.qc, V.qcols);
     GS_CHECK_LAUNCH();
     return GS_OK;
 }
@@ -1656,10 +1697,10 @@ static gs_status launch_raster_bwd(const TCfg& c, const ViewLane& V, const ProjV
     const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
     if (c.tile == 16)
         k_train_bwd<16, kBwdPPT><<<tiles, 256 / kBwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
-                                                                        V.final_T, V.ncon, g2);
+                                                                        V.final_T, V.ncon, V.qc, V.qcols, g2);
     else
         k_train_bwd<32, kBwdPPT><<<tiles, 1024 / kBwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
-                                                                         V.final_T, V.ncon, g2);
+                                                                         V.final_T, V.ncon, V.qc, V.qcols, g2);
     GS_CHECK_LAUNCH();
     return GS_OK;
 }
