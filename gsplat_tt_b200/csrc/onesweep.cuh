@@ -81,23 +81,17 @@ struct GlobalSource {
     }
 };
 
-// Extra per-item output a pass writes beside each value at its output position (nothing by
-// default; the training depth sort writes per-Gaussian data in depth order this way).
-struct NoSink {
-    __device__ __forceinline__ void operator()(uint32_t, uint32_t) const {}
-};
-
 // One pass over the digit_bits-bit digit at `shift` (key bits above it are ignored). The
 // item count is n_host when n_dev is null, else *n_dev if
 // it is at most n_host; a larger *n_dev (a capacity overflow, which the caller reports)
 // sorts nothing, so no write can land past the caller's buffers. keys_out may be null on
 // the last pass (values only).
-template <typename KeyT, typename Src, typename Sink = NoSink>
+template <typename KeyT, typename Src>
 __global__ void __launch_bounds__(kSortThreads, sizeof(KeyT) == 4 ? 4 : 3)
 k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
                 const int64_t* __restrict__ n_dev, int64_t n_host, int shift, int digit_bits,
                 const uint32_t* __restrict__ digit_offsets, uint32_t* __restrict__ lookback,
-                uint32_t* __restrict__ tile_counter, unsigned int* __restrict__ err, Sink sink) {
+                uint32_t* __restrict__ tile_counter, unsigned int* __restrict__ err) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SortSmem<KeyT>& S = *reinterpret_cast<SortSmem<KeyT>*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -241,7 +235,6 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
         const uint32_t out = S.gbase[dd] + ((uint32_t)i - S.local_off[dd]);
         if (keys_out) keys_out[out] = k;
         vals_out[out] = S.vals[i];
-        sink(out, S.vals[i]);
     }
 #undef GS_DIGIT
 }

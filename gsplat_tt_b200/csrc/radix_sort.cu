@@ -68,11 +68,11 @@ size_t radix_workspace_bytes(int64_t n, int key_bits, int key_bytes) {
 
 int radix_num_passes(int key_bits) { return (key_bits + kRadixBits - 1) / kRadixBits; }
 
-template <typename KeyT, typename Sink = NoSink>
+template <typename KeyT>
 gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64_t* n_dev,
                              int64_t n_cap, int key_bits, KeyT* keys_out, uint32_t* vals_out,
                              void* workspace, size_t workspace_bytes, cudaStream_t st,
-                             unsigned int** err_out, unsigned int* err_ext, Sink sink = Sink()) {
+                             unsigned int** err_out, unsigned int* err_ext) {
     const int npass = radix_num_passes(key_bits);
     const int64_t ntiles = (n_cap + kTileItems - 1) / kTileItems + 1;
     Workspace ws(workspace, workspace_bytes);
@@ -103,9 +103,7 @@ gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64
         GS_CHECK_LAUNCH();
     }
     const size_t smem = sizeof(SortSmem<KeyT>);
-    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<KeyT, GlobalSource<KeyT>, NoSink>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<KeyT, GlobalSource<KeyT>, Sink>,
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<KeyT, GlobalSource<KeyT>>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const KeyT* kin = keys;
     const uint32_t* vin = vals;
@@ -115,15 +113,10 @@ gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64
         KeyT* kout = last ? keys_out : ((p & 1) ? kb : ka);
         uint32_t* vout = last ? vals_out : ((p & 1) ? vb : va);
         KernelTimer kt(sizeof(KeyT) == 8 ? "radix_pass" : "radix_pass32", st);
-        const int shift = p * kRadixBits, dbits = std::min(kRadixBits, key_bits - p * kRadixBits);
-        if (last)  // the caller's sink writes beside the final values
-            k_onesweep_pass<KeyT, GlobalSource<KeyT>, Sink><<<grid, kSortThreads, smem, st>>>(
-                GlobalSource<KeyT>{kin, vin}, kout, vout, n_dev, n_cap, shift, dbits,
-                hist + p * kRadix, look + (size_t)p * ntiles * kRadix, counters + p, err, sink);
-        else
-            k_onesweep_pass<KeyT, GlobalSource<KeyT>, NoSink><<<grid, kSortThreads, smem, st>>>(
-                GlobalSource<KeyT>{kin, vin}, kout, vout, n_dev, n_cap, shift, dbits,
-                hist + p * kRadix, look + (size_t)p * ntiles * kRadix, counters + p, err, NoSink{});
+        k_onesweep_pass<KeyT><<<grid, kSortThreads, smem, st>>>(
+            GlobalSource<KeyT>{kin, vin}, kout, vout, n_dev, n_cap, p * kRadixBits,
+            std::min(kRadixBits, key_bits - p * kRadixBits), hist + p * kRadix,
+            look + (size_t)p * ntiles * kRadix, counters + p, err);
         GS_CHECK_LAUNCH();
         kin = kout;
         vin = vout;
@@ -145,14 +138,6 @@ gs_status radix_sort_pairs32(const uint32_t* keys, const uint32_t* vals, const i
                              unsigned int** err_out, unsigned int* err_ext) {
     return radix_sort_pairs_t<uint32_t>(keys, vals, n_dev, n_cap, key_bits, keys_out, vals_out,
                                         workspace, workspace_bytes, st, err_out, err_ext);
-}
-
-gs_status radix_sort_depth(const uint32_t* keys, int64_t n, const GaussianCellSink& sink,
-                           uint32_t* order_out, void* workspace, size_t workspace_bytes,
-                           cudaStream_t st, unsigned int* err_ext) {
-    return radix_sort_pairs_t<uint32_t, GaussianCellSink>(keys, nullptr, nullptr, n, 32, nullptr,
-                                                          order_out, workspace, workspace_bytes,
-                                                          st, nullptr, err_ext, sink);
 }
 
 // Training tile sort: the first pass draws its items from the Gaussians' tile rectangles
@@ -192,7 +177,7 @@ gs_status radix_sort_rect_pairs(const RectPairSource& src, const int64_t* n_dev,
         KernelTimer kt("tile_sort_emit", st);
         k_onesweep_pass<uint32_t, RectPairSource><<<grid, kSortThreads, smem, st>>>(
             src, npass == 1 ? nullptr : ka, npass == 1 ? vals_out : va, n_dev, n_cap, 0,
-            std::min(kRadixBits, key_bits), digit_offsets, look, counters, err, NoSink{});
+            std::min(kRadixBits, key_bits), digit_offsets, look, counters, err);
         GS_CHECK_LAUNCH();
     }
     const uint32_t* kin = ka;
@@ -205,7 +190,7 @@ gs_status radix_sort_rect_pairs(const RectPairSource& src, const int64_t* n_dev,
         k_onesweep_pass<uint32_t, GlobalSource<uint32_t>><<<grid, kSortThreads, smem, st>>>(
             GlobalSource<uint32_t>{kin, vin}, kout, vout, n_dev, n_cap, p * kRadixBits,
             std::min(kRadixBits, key_bits - p * kRadixBits), digit_offsets + p * kRadix,
-            look + (size_t)p * ntiles * kRadix, counters + p, err, NoSink{});
+            look + (size_t)p * ntiles * kRadix, counters + p, err);
         GS_CHECK_LAUNCH();
         kin = kout;
         vin = vout;

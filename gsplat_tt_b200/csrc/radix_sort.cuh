@@ -25,31 +25,6 @@ gs_status radix_sort_pairs32(const uint32_t* keys, const uint32_t* vals, const i
                              void* workspace, size_t workspace_bytes, cudaStream_t st,
                              unsigned int** err_out, unsigned int* err_ext = nullptr);
 
-// Written by the last pass of the training depth sort beside each Gaussian id (in depth
-// order): its tile rectangle and its number of tile-sort items -- the 2x2-tile super-tiles
-// its rectangle touches (shift 1) or its tiles (shift 0); 0 for a Gaussian without tiles.
-struct GaussianCellSink {
-    const uint32_t* cnt;   // per Gaussian: tiles in its rectangle
-    const ushort4* rect;   // per Gaussian: tile rectangle x0, x1, y0, y1
-    int shift;
-    ushort4* rect_out;
-    uint32_t* cnt_out;
-    __device__ __forceinline__ void operator()(uint32_t out, uint32_t g) const {
-        const ushort4 r = rect[g];
-        const uint32_t c = cnt[g];
-        rect_out[out] = r;
-        cnt_out[out] = (c == 0u || shift == 0)
-                           ? c
-                           : (uint32_t)((r.y >> 1) - (r.x >> 1) + 1) * (uint32_t)((r.w >> 1) - (r.z >> 1) + 1);
-    }
-};
-
-// Stable sort of the n Gaussians by the 32-bit keys (ids as values) into order_out, the
-// sink writing each Gaussian's rectangle and item count in depth order.
-gs_status radix_sort_depth(const uint32_t* keys, int64_t n, const GaussianCellSink& sink,
-                           uint32_t* order_out, void* workspace, size_t workspace_bytes,
-                           cudaStream_t st, unsigned int* err_ext);
-
 struct RectPairSource;
 // Stable sort by tile id of the (Gaussian, tile) pairs that `src` generates (rect_pairs.cuh),
 // *n_dev pairs (at most n_cap); digit_offsets holds each pass's exclusive digit offsets.

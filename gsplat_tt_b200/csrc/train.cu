@@ -1574,12 +1574,14 @@ static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, Vie
     // Gaussian ids do not fit the 28 bits the packed sort value leaves, from a sort of the
     // (Gaussian, tile) pairs themselves (shift 0).
     const int shift = (n < (int64_t)GS_SUPER_TILE_MAX_N) ? 1 : 0;
-    // Gaussians in (depth bits, id) order, those without pairs last; the last pass also
-    // writes each one's rectangle and tile-sort item count in depth order.
-    const GaussianCellSink sink{pv.cnt, pv.rect, shift, V.rect_d, V.ccnt};
-    gs_status s = radix_sort_depth(pv.dsort, n, sink, V.order, V.radix, V.radix_bytes, st, L.err);
+    // Gaussians in (depth bits, id) order, those without pairs last.
+    unsigned int* rerr = nullptr;
+    gs_status s = radix_sort_pairs32(pv.dsort, nullptr, nullptr, n, 32, nullptr, V.order, V.radix,
+                                     V.radix_bytes, st, &rerr, L.err);
     if (s != GS_OK) return s;
-    launch_sorted_count(V.ccnt, n, V.blk2, st);
+    // each one's rectangle and tile-sort item count in depth order (one gather), and the
+    // per-block item totals
+    launch_sorted_count(pv, V.order, n, shift, V.rect_d, V.ccnt, V.blk2, st);
     GS_CHECK_LAUNCH();
     scan_block_totals<int64_t><<<1, 1024, 0, st>>>(V.blk2, nb, nullptr);
     GS_CHECK_LAUNCH();

@@ -59,8 +59,11 @@ TCfg make_tcfg(const gs_train_config& c, int H, int W);
 void launch_project(const GConst& P, int64_t n, const TCam* cams, int n_views, const TCfg& cfg,
                     const ProjView& pv, int64_t* blk, int64_t blk_stride, uint64_t* touch,
                     float* vis_counts, float* grad2d, cudaStream_t st);
-// Offsets of the tile-sort items from their counts in depth order (ccnt).
-void launch_sorted_count(const uint32_t* ccnt, int64_t n, int64_t* blk, cudaStream_t st);
+// Per depth-ordered Gaussian: its rectangle and tile-sort item count (shift 1: 2x2-tile
+// super-tiles, used while Gaussian ids fit 28 bits; shift 0: tiles), and block totals; then
+// the items' offsets from those counts.
+void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int shift,
+                         ushort4* rect_d, uint32_t* ccnt, int64_t* blk, cudaStream_t st);
 void launch_pair_offsets(const uint32_t* ccnt, int64_t n, const int64_t* blk_offsets,
                          int64_t capacity, uint32_t* goff, uint32_t* tfirst, int64_t tfirst_len,
                          uint32_t* last, int64_t* total, unsigned int* err, cudaStream_t st);

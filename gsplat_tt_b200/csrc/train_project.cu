@@ -233,13 +233,28 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
         blk[v * blk_stride + blockIdx.x] = (int64_t)s_tot[v];
 }
 
-// Block totals of the tile-sort item counts of the Gaussians in depth order (ccnt, written
-// by the depth sort's last pass), for the offset scan.
+// The Gaussians in depth order (`order` = ids sorted by depth bits, stable): each one's
+// tile rectangle (rect_d) and its number of tile-sort items (ccnt: the 2x2-tile super-tiles
+// its rectangle touches with shift 1, its tiles with shift 0, 0 without tiles), gathered
+// once, and the per-block item totals for the offset scan.
 __global__ void __launch_bounds__(kProjThreads)
-k_sorted_count(const uint32_t* __restrict__ ccnt, int64_t n, int64_t* __restrict__ blk) {
+k_sorted_count(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
+               const uint32_t* __restrict__ order, int64_t n, int shift,
+               ushort4* __restrict__ rect_d, uint32_t* __restrict__ ccnt,
+               int64_t* __restrict__ blk) {
     __shared__ int64_t smem[33];
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    const uint32_t c = (i < n) ? ccnt[i] : 0u;
+    uint32_t c = 0u;
+    if (i < n) {
+        const uint32_t g = order[i];
+        const ushort4 r = rect[g];
+        const uint32_t t = cnt[g];
+        c = (t == 0u || shift == 0)
+                ? t
+                : (uint32_t)((r.y >> 1) - (r.x >> 1) + 1) * (uint32_t)((r.w >> 1) - (r.z >> 1) + 1);
+        rect_d[i] = r;
+        ccnt[i] = c;
+    }
     int64_t total;
     block_exclusive_scan<int64_t>((int64_t)c, smem, &total);
     if (threadIdx.x == 0) blk[blockIdx.x] = total;
@@ -517,8 +532,10 @@ k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict_
     }
 }
 
-void launch_sorted_count(const uint32_t* ccnt, int64_t n, int64_t* blk, cudaStream_t st) {
-    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(ccnt, n, blk);
+void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int shift,
+                         ushort4* rect_d, uint32_t* ccnt, int64_t* blk, cudaStream_t st) {
+    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, pv.rect, order, n,
+                                                                    shift, rect_d, ccnt, blk);
 }
 
 void launch_pair_offsets(const uint32_t* ccnt, int64_t n, const int64_t* blk_offsets,
