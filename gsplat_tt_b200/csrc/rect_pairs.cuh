@@ -25,13 +25,17 @@ struct RectPairSource {
     int shift;               // cell = tile >> shift
 
     // The tile's pairs come from depth-ordered Gaussians gf..gl (at most `valid` of them,
-    // each has at least one pair), taken in chunks of 256, one per thread. A thread writes
+    // each has at least one pair), taken in chunks of kGaussPerThread per thread. A thread writes
     // the pairs of its Gaussian that fall in the tile into the tile's shared key / value
     // arrays itself, walking the rectangle row-major, when there are at most kOwnPairs of
     // them; longer runs are queued and written by whole warps (lanes striding over the
     // run), so one large Gaussian does not serialise its warp. The thread then takes its
     // warp-striped items from shared memory.
     static constexpr uint32_t kOwnPairs = 32;
+#ifndef GS_EMIT_GAUSS_PER_THREAD
+#define GS_EMIT_GAUSS_PER_THREAD 2
+#endif
+    static constexpr uint32_t kGaussPerThread = GS_EMIT_GAUSS_PER_THREAD;
 
     // Value of the item of (depth-ordered Gaussian with id gid and tile rectangle r0, cell
     // (cx, cy)).
@@ -53,7 +57,9 @@ struct RectPairSource {
         // before its first barrier, and chunk k + 2 (the next writer of that buffer) starts
         // only after every warp has passed chunk k + 1's first barrier. Each counter is
         // read by all threads between chunk k's two barriers and cleared after the second.
-        __shared__ uint32_t s_big[2][kSortThreads];
+        // A chunk is kGaussPerThread Gaussians per thread (most have a handful of items).
+        constexpr uint32_t kChunk = kSortThreads * kGaussPerThread;
+        __shared__ uint32_t s_big[2][kChunk];
         __shared__ uint32_t s_nbig[2];
         const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
         const uint32_t lo_p = (uint32_t)base, hi_p = (uint32_t)(base + valid);
@@ -64,9 +70,11 @@ struct RectPairSource {
         if (tid < 2) s_nbig[tid] = 0u;
         __syncthreads();
         int par = 0;
-        for (uint32_t c0 = gf; c0 <= gl; c0 += kSortThreads, par ^= 1) {
-            const uint32_t i = c0 + (uint32_t)tid;
-            if (i <= gl) {
+        for (uint32_t c0 = gf; c0 <= gl; c0 += kChunk, par ^= 1) {
+#pragma unroll
+            for (uint32_t u = 0; u < kGaussPerThread; ++u) {
+                const uint32_t i = c0 + u * kSortThreads + (uint32_t)tid;
+                if (i > gl) continue;
                 const uint32_t off = goff[i], end = goff[i + 1], gid = order[i];
                 const ushort4 r0 = rect[i];
                 const ushort4 r = make_ushort4(r0.x >> shift, r0.y >> shift, r0.z >> shift,
