@@ -1540,20 +1540,34 @@ extern "C" size_t gs_train_workspace_size(int64_t n, int32_t sh_degree, int32_t 
 
 // Every view's projection in one pass over the parameters (cameras already in L.cams),
 // then each view's pair total in L.pairs[v].
-static gs_status project_views(const GConst& P, int64_t n, int n_views, const TCfg& cfg,
-                               TrainWs& L, float* vis_counts, bool with_grad, cudaStream_t st) {
-    {
-        KernelTimer kt("train_project", st);
-        ProjView pv = L.pv;
-        if (with_grad) pv.dkey = nullptr;  // raw depth bits are only exported by project_view
-        launch_project(P, n, L.cams, n_views, cfg, pv, L.blk, L.blk_stride, L.touch, vis_counts,
-                       with_grad ? L.grad2d : nullptr, st);
-        GS_CHECK_LAUNCH();
-    }
+static_assert(GS_PROJECT_ROW_ALIGN % kProjThreads == 0, "row chunks must start on a projection block");
+
+// The projection kernel over rows [row_begin, row_end) of every view.
+static gs_status project_rows(const GConst& P, int64_t n, int64_t row_begin, int64_t row_end,
+                              int n_views, const TCfg& cfg, TrainWs& L, float* vis_counts,
+                              bool with_grad, cudaStream_t st) {
+    KernelTimer kt("train_project", st);
+    ProjView pv = L.pv;
+    if (with_grad) pv.dkey = nullptr;  // raw depth bits are only exported by project_view
+    launch_project(P, n, row_begin, row_end, L.cams, n_views, cfg, pv, L.blk, L.blk_stride,
+                   L.touch, vis_counts, with_grad ? L.grad2d : nullptr, st);
+    GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
+// Every view's pair total from the projection's per-block totals.
+static gs_status scan_view_pairs(int64_t n, int n_views, TrainWs& L, cudaStream_t st) {
     scan_block_totals_segments<int64_t><<<n_views, 1024, 0, st>>>(L.blk, div_up(n, kProjThreads),
                                                                   L.blk_stride, L.pairs);
     GS_CHECK_LAUNCH();
     return GS_OK;
+}
+
+static gs_status project_views(const GConst& P, int64_t n, int n_views, const TCfg& cfg,
+                               TrainWs& L, float* vis_counts, bool with_grad, cudaStream_t st) {
+    gs_status s = project_rows(P, n, 0, n, n_views, cfg, L, vis_counts, with_grad, st);
+    if (s != GS_OK) return s;
+    return scan_view_pairs(n, n_views, L, st);
 }
 
 // Largest Gaussian count (exclusive) sorted through super-tiles: the packed sort value
@@ -2201,6 +2215,59 @@ extern "C" gs_status gs_train_param_backward(const gs_gaussians* params,
                             (cudaStream_t)stream);
 }
 
+// The views' cameras into the workspace. A copy from pageable memory returns once the
+// source has been staged, so the host vector may go out of scope afterwards.
+static gs_status upload_cams(const gs_camera* cams, int n_views, TrainWs& L, cudaStream_t st) {
+    std::vector<TCam> hc(n_views);
+    for (int v = 0; v < n_views; ++v) hc[v] = make_tcam(cams[v]);
+    GS_CUDA_CHECK(cudaMemcpyAsync(L.cams, hc.data(), n_views * sizeof(TCam), cudaMemcpyHostToDevice, st));
+    return GS_OK;
+}
+
+extern "C" gs_status gs_train_project_rows(const gs_gaussians* params, float* vis_counts,
+                                           int64_t n, int64_t row_begin, int64_t row_end,
+                                           const gs_camera* cams, int32_t n_views,
+                                           const gs_train_config* cfg, int64_t pair_capacity,
+                                           void* workspace, size_t workspace_bytes,
+                                           void* stream) {
+    clear_error();
+    cudaStream_t st = (cudaStream_t)stream;
+    gs_status cs = check_cfg(cfg);
+    if (cs != GS_OK) return cs;
+    GS_ARG_CHECK(params && vis_counts && cams && workspace, "gs_train_project_rows: null argument");
+    GS_ARG_CHECK(n > 0 && n < (1ll << 32) && n_views >= 1 && n_views <= 64,
+                 "gs_train_project_rows: bad n or n_views");
+    GS_ARG_CHECK(row_begin >= 0 && row_begin <= row_end && row_end <= n &&
+                     row_begin % GS_PROJECT_ROW_ALIGN == 0 &&
+                     (row_end % GS_PROJECT_ROW_ALIGN == 0 || row_end == n),
+                 "gs_train_project_rows: rows [%lld, %lld) must lie in [0, %lld) on multiples "
+                 "of %d", (long long)row_begin, (long long)row_end, (long long)n,
+                 GS_PROJECT_ROW_ALIGN);
+    GS_ARG_CHECK(pair_capacity >= 1 && pair_capacity < (1ll << 30),
+                 "gs_train_project_rows: pair_capacity must be in [1, 2^30)");
+    GS_ARG_CHECK(((uintptr_t)params->quats & 15) == 0,
+                 "gs_train_project_rows: quats must be 16-byte aligned");
+    int H = 0, W = 0;
+    for (int v = 0; v < n_views; ++v) {
+        GS_ARG_CHECK(image_fits(cams[v].height, cams[v].width, cfg->tile_size),
+                     "gs_train_project_rows: bad camera %d", v);
+        H = std::max(H, (int)cams[v].height);
+        W = std::max(W, (int)cams[v].width);
+    }
+    Workspace ws(workspace, workspace_bytes);
+    TrainWs L;
+    train_layout(ws, L, n, n_views, H, W, cfg->tile_size, pair_capacity);
+    GS_ARG_CHECK(ws.ok(), "gs_train_project_rows: workspace too small");
+    if (row_end == row_begin) return GS_OK;
+    const int64_t rows = row_end - row_begin;
+    GS_CUDA_CHECK(cudaMemsetAsync(L.touch + row_begin, 0, rows * sizeof(uint64_t), st));
+    GS_CUDA_CHECK(cudaMemsetAsync(vis_counts + row_begin, 0, rows * sizeof(float), st));
+    gs_status s = upload_cams(cams, n_views, L, st);
+    if (s != GS_OK) return s;
+    return project_rows(gconst(params), n, row_begin, row_end, n_views, make_tcfg(*cfg, H, W), L,
+                        vis_counts, true, st);
+}
+
 extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussians* exp_avg,
                                    const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
                                    float* vis_counts, int64_t n, int64_t step,
@@ -2215,8 +2282,11 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
     if (cs != GS_OK) return cs;
     GS_ARG_CHECK(params && grads && vis_counts && cams && targets && view_losses,
                  "gs_train_step: null argument");
+    const bool projected = (apply_adam & GS_STEP_PROJECTED) != 0;
+    apply_adam &= ~GS_STEP_PROJECTED;
     GS_ARG_CHECK(apply_adam >= 0 && apply_adam <= GS_STEP_DEFER_PARAM_BWD,
-                 "gs_train_step: apply_adam must be 0, 1 or GS_STEP_DEFER_PARAM_BWD");
+                 "gs_train_step: apply_adam must be 0, 1 or GS_STEP_DEFER_PARAM_BWD, "
+                 "optionally with GS_STEP_PROJECTED");
     GS_ARG_CHECK(apply_adam != 1 || (exp_avg && exp_avg_sq), "gs_train_step: Adam needs moments");
     GS_ARG_CHECK(n > 0 && n < (1ll << 32), "gs_train_step: n must be in [1, 2^32)");
     GS_ARG_CHECK(n_views >= 1 && n_views <= 64, "gs_train_step: n_views must be in [1, 64]");
@@ -2241,22 +2311,22 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
                                          pair_capacity));
     const GConst P = gconst(params);
     GS_CUDA_CHECK(cudaMemsetAsync(L.err, 0, sizeof(unsigned int), st));
-    GS_CUDA_CHECK(cudaMemsetAsync(L.touch, 0, n * sizeof(uint64_t), st));
-    GS_CUDA_CHECK(cudaMemsetAsync(vis_counts, 0, n * sizeof(float), st));
     GS_CUDA_CHECK(cudaMemsetAsync(L.loss_acc, 0, 2 * n_views * sizeof(double), st));
-    std::vector<TCam> hc(n_views);
-    for (int v = 0; v < n_views; ++v) hc[v] = make_tcam(cams[v]);
-    // A copy from pageable memory returns once the source has been staged, so the host
-    // vector may go out of scope afterwards.
-    GS_CUDA_CHECK(cudaMemcpyAsync(L.cams, hc.data(), n_views * sizeof(TCam), cudaMemcpyHostToDevice, st));
-
     const LossCfg LC = make_loss_cfg(*cfg);
     if (cfg->use_ssim) {
         gs_status ss = ssim_smem_attributes();
         if (ss != GS_OK) return ss;
     }
-    {
-        gs_status s = project_views(P, n, n_views, make_tcfg(*cfg, H, W), L, vis_counts, true, st);
+    if (projected) {
+        // gs_train_project_rows has projected every row of these views into the workspace
+        gs_status s = scan_view_pairs(n, n_views, L, st);
+        if (s != GS_OK) return s;
+    } else {
+        GS_CUDA_CHECK(cudaMemsetAsync(L.touch, 0, n * sizeof(uint64_t), st));
+        GS_CUDA_CHECK(cudaMemsetAsync(vis_counts, 0, n * sizeof(float), st));
+        gs_status s = upload_cams(cams, n_views, L, st);
+        if (s != GS_OK) return s;
+        s = project_views(P, n, n_views, make_tcfg(*cfg, H, W), L, vis_counts, true, st);
         if (s != GS_OK) return s;
     }
     // Views round-robin over the lanes; lanes 1.. run on auxiliary streams forked from the

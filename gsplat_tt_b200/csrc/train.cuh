@@ -56,9 +56,11 @@ TCfg make_tcfg(const gs_train_config& c, int H, int W);
 // train_project.cu (compiled without FMA contraction)
 // Projects every view (cams: device array of n_views cameras) in one pass; pv arrays are
 // [n_views][n], blk holds each view's per-block pair totals at v * blk_stride.
-void launch_project(const GConst& P, int64_t n, const TCam* cams, int n_views, const TCfg& cfg,
-                    const ProjView& pv, int64_t* blk, int64_t blk_stride, uint64_t* touch,
-                    float* vis_counts, float* grad2d, cudaStream_t st);
+// Rows [row_begin, row_end) of the n; row_begin a multiple of kProjThreads.
+void launch_project(const GConst& P, int64_t n, int64_t row_begin, int64_t row_end,
+                    const TCam* cams, int n_views, const TCfg& cfg, const ProjView& pv,
+                    int64_t* blk, int64_t blk_stride, uint64_t* touch, float* vis_counts,
+                    float* grad2d, cudaStream_t st);
 // Per depth-ordered Gaussian: its rectangle and tile-sort item count (shift 1: 2x2-tile
 // super-tiles, used while Gaussian ids fit 28 bits; shift 0: tiles), and block totals; then
 // the items' offsets from those counts.

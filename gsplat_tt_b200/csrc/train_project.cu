@@ -19,10 +19,13 @@ __device__ __forceinline__ float exp_rounded(float x) { return (float)exp((doubl
 // scales, 3D covariance, opacity), then projects it into every view. View v's records go
 // to pv arrays at [v * n + g], its per-block pair totals to blk[v * blk_stride + block].
 // The Gaussian's Adam visibility count is added once and its touched-view mask written
-// once; a touched view's 2D-gradient row is zeroed for the backward's atomics.
+// once; a touched view's 2D-gradient row is zeroed for the backward's atomics. The launch
+// covers rows [row_begin, row_end) of the n, row_begin a multiple of the block size, so a
+// block's totals land in the same blk slot whichever row range launched it.
 template <int DEG>
 __global__ void __launch_bounds__(kProjThreads, 4)
-k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views, TCfg cfg,
+k_train_project(GConst P, int64_t n, int64_t row_begin, int64_t row_end,
+                const TCam* __restrict__ cams, int n_views, TCfg cfg,
                 ProjView pv, int64_t* __restrict__ blk, int64_t blk_stride,
                 uint64_t* __restrict__ touch, float* __restrict__ vis_counts,
                 float* __restrict__ grad2d) {
@@ -34,10 +37,10 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
     for (int i = threadIdx.x; i < n_views * (int)(sizeof(TCam) / 4); i += blockDim.x)
         reinterpret_cast<uint32_t*>(s_cam)[i] = reinterpret_cast<const uint32_t*>(cams)[i];
     for (int i = threadIdx.x; i < n_views; i += blockDim.x) s_tot[i] = 0ull;
-    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t g = row_begin + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     {
-        const int64_t g0 = (int64_t)blockIdx.x * blockDim.x;
-        const int rows = (int)min((int64_t)blockDim.x, n - g0);
+        const int64_t g0 = row_begin + (int64_t)blockIdx.x * blockDim.x;
+        const int rows = (int)min((int64_t)blockDim.x, row_end - g0);
         const float* src = P.sh + (size_t)g0 * ROW;
         const int total = rows * ROW;
         if (((uintptr_t)src & 15u) == 0) {
@@ -50,7 +53,7 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
         }
         __syncthreads();
     }
-    const bool live = g < n;
+    const bool live = g < row_end;
     float m0 = 0.f, m1 = 0.f, m2 = 0.f, op = 0.f;
     float S[3][3];
     if (live) {
@@ -229,8 +232,9 @@ k_train_project(GConst P, int64_t n, const TCam* __restrict__ cams, int n_views,
         if (vis_counts != nullptr && nvis > 0.0f) vis_counts[g] += nvis;
     }
     __syncthreads();
+    const int64_t b = row_begin / kProjThreads + blockIdx.x;
     for (int v = threadIdx.x; v < n_views; v += blockDim.x)
-        blk[v * blk_stride + blockIdx.x] = (int64_t)s_tot[v];
+        blk[v * blk_stride + b] = (int64_t)s_tot[v];
 }
 
 // The Gaussians in depth order (`order` = ids sorted by depth bits, stable): each one's
@@ -434,26 +438,27 @@ k_tile_finish(GridFinish g0, GridFinish g1, const int64_t* __restrict__ pairs, i
     }
 }
 
-void launch_project(const GConst& P, int64_t n, const TCam* cams, int n_views, const TCfg& cfg,
-                    const ProjView& pv, int64_t* blk, int64_t blk_stride, uint64_t* touch,
-                    float* vis_counts, float* grad2d, cudaStream_t st) {
-    const unsigned int nb = div_up(n, kProjThreads);
+void launch_project(const GConst& P, int64_t n, int64_t row_begin, int64_t row_end,
+                    const TCam* cams, int n_views, const TCfg& cfg, const ProjView& pv,
+                    int64_t* blk, int64_t blk_stride, uint64_t* touch, float* vis_counts,
+                    float* grad2d, cudaStream_t st) {
+    if (row_end <= row_begin) return;
+    const unsigned int nb = div_up(row_end - row_begin, kProjThreads);
     const size_t smem = (size_t)kProjThreads * 3 * cfg.K * sizeof(float);
+#define GS_PROJ(D_)                                                                        \
+    k_train_project<D_><<<nb, kProjThreads, smem, st>>>(P, n, row_begin, row_end, cams,     \
+                                                        n_views, cfg, pv, blk, blk_stride, \
+                                                        touch, vis_counts, grad2d)
     switch (cfg.sh_degree) {
-        case 0:
-            k_train_project<0><<<nb, kProjThreads, smem, st>>>(P, n, cams, n_views, cfg, pv, blk, blk_stride, touch, vis_counts, grad2d);
-            break;
-        case 1:
-            k_train_project<1><<<nb, kProjThreads, smem, st>>>(P, n, cams, n_views, cfg, pv, blk, blk_stride, touch, vis_counts, grad2d);
-            break;
-        case 2:
-            k_train_project<2><<<nb, kProjThreads, smem, st>>>(P, n, cams, n_views, cfg, pv, blk, blk_stride, touch, vis_counts, grad2d);
-            break;
+        case 0: GS_PROJ(0); break;
+        case 1: GS_PROJ(1); break;
+        case 2: GS_PROJ(2); break;
         default:
             cudaFuncSetAttribute(k_train_project<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            k_train_project<3><<<nb, kProjThreads, smem, st>>>(P, n, cams, n_views, cfg, pv, blk, blk_stride, touch, vis_counts, grad2d);
+            GS_PROJ(3);
             break;
     }
+#undef GS_PROJ
 }
 
 // The per-tile lists from the super-tile lists: one block per 2x2-tile super-tile, its

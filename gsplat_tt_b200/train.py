@@ -71,7 +71,11 @@ lib.gs_sparse_adam_multicast.restype = ctypes.c_int
 lib.gs_sparse_adam_multicast.argtypes = [_G, _G, _G, _G, _G, _vp, _vp, _i64, _i64, _CFG, _vp, _vp]
 lib.gs_train_param_backward.restype = ctypes.c_int
 lib.gs_train_param_backward.argtypes = [_G, _G, _i64, _i64, _i64, _C, _i32, _CFG, _i64, _vp, _sz, _vp]
+lib.gs_train_project_rows.restype = ctypes.c_int
+lib.gs_train_project_rows.argtypes = [_G, _vp, _i64, _i64, _i64, _C, _i32, _CFG, _i64, _vp, _sz, _vp]
 GS_STEP_DEFER_PARAM_BWD = 2
+GS_STEP_PROJECTED = 4
+GS_PROJECT_ROW_ALIGN = 256
 lib.gs_render_fwd.restype = ctypes.c_int
 lib.gs_render_fwd.argtypes = [_G, _i64, _C, _CFG, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _sz, _vp]
 lib.gs_loss.restype = ctypes.c_int
@@ -254,6 +258,7 @@ class Trainer:
             # next chunk instead of after all of them.
             self._comm = torch.cuda.Stream(device=self.device, priority=-1)
             self._chunk_done = [torch.cuda.Event() for _ in range(self.chunks)]
+            self._chunk_updated = [torch.cuda.Event() for _ in range(self.chunks)]
             self._barrier_pg = self.pg
             if self.pg is None and torch.distributed.get_backend() == "nccl":
                 opts = torch.distributed.ProcessGroupNCCL.Options()
@@ -273,9 +278,12 @@ class Trainer:
         self._err_i32 = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.capacity = int(pair_capacity) if pair_capacity else 0
         self.ws = None
+        # cameras whose projection the previous step already left in the workspace
+        self._projected = None
         self._alloc(max(self.capacity, 1))
 
     def _alloc(self, capacity: int) -> None:
+        self._projected = None
         self.capacity = capacity
         nb = lib.gs_train_workspace_size(self.n, self.cfg.sh_degree, self.n_views, self.H, self.W,
                                          self.cfg.tile_size, capacity)
@@ -290,6 +298,7 @@ class Trainer:
         return arr
 
     def count_pairs(self, cams) -> list[int]:
+        self._projected = None  # the count projects into the step workspace
         arr = self._cams(cams)
         out = (_i64 * len(cams))()
         p = self.params.c_struct()
@@ -318,9 +327,21 @@ class Trainer:
                 ts.append(t.to(self.device, torch.float32).contiguous())
         return ts
 
-    def step(self, cams, targets, check_errors: bool = False, images=None, grad2d=None):
+    @staticmethod
+    def _cams_key(cams) -> tuple:
+        return tuple((np.asarray(w2c, np.float32).tobytes(), np.asarray(K, np.float32).tobytes(),
+                      int(H), int(W)) for (w2c, K, H, W) in cams)
+
+    def step(self, cams, targets, check_errors: bool = False, images=None, grad2d=None,
+             next_cams=None):
+        """One step. next_cams (the next step's views, optional): project them at the end
+        of this step, after the update -- through multicast, row chunk by row chunk as each
+        chunk's update lands on every GPU, overlapped with the update of the later chunks --
+        so that the next call with those cameras starts at the sort."""
         if len(cams) != self.n_views:
             raise ValueError(f"expected {self.n_views} views, got {len(cams)}")
+        if next_cams is not None and len(next_cams) != self.n_views:
+            raise ValueError(f"expected {self.n_views} next views, got {len(next_cams)}")
         tg = self._targets(targets)
         self._keep = tg
         tptr = (ctypes.c_void_p * len(tg))(*[t.data_ptr() for t in tg])
@@ -329,10 +350,15 @@ class Trainer:
         p, m, v, g = (b.c_struct() for b in (self.params, self.m, self.v, self.grads))
         single = self.world == 1
         mode = 1 if single else (GS_STEP_DEFER_PARAM_BWD if self.multicast else 0)
+        key = self._cams_key(cams)
+        projected, self._projected = self._projected == key, None
+        # a step that may be redone (check_errors) does not project ahead
+        nxt = None if (next_cams is None or check_errors) else self._cams(next_cams)
         while True:
+            flags = mode | (GS_STEP_PROJECTED if projected else 0)
             code = lib.gs_train_step(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
                                      self.vis_counts.data_ptr(), self.n, self.step_count, arr, tptr,
-                                     len(cams), ctypes.byref(self.ccfg), mode,
+                                     len(cams), ctypes.byref(self.ccfg), flags,
                                      self.losses.data_ptr(),
                                      None if images is None else images.data_ptr(),
                                      None if grad2d is None else grad2d.data_ptr(),
@@ -340,9 +366,14 @@ class Trainer:
                                      self.ws.numel(), st)
             check(code)
             if not single:
-                self._allreduce_and_adam(st, arr)
+                self._allreduce_and_adam(st, arr, nxt)
+            elif nxt is not None:
+                self._project_rows(nxt, 0, self.n, st)
+            if nxt is not None:
+                self._projected = self._cams_key(next_cams)
             if not check_errors:
                 break
+            projected = False
             if single:
                 code = lib.gs_workspace_error(self.ws.data_ptr(), st)
                 failed = code != _lib.GS_OK
@@ -358,22 +389,30 @@ class Trainer:
         self.step_count += 1
         return self.losses
 
-    def _allreduce_and_adam(self, st, arr) -> None:
+    def _project_rows(self, arr, b: int, e: int, st) -> None:
+        p = self.params.c_struct()
+        check(lib.gs_train_project_rows(ctypes.byref(p), self.vis_counts.data_ptr(), self.n, b, e,
+                                        arr, len(arr), ctypes.byref(self.ccfg), self.capacity,
+                                        self.ws.data_ptr(), self.ws.numel(), st))
+
+    def _allreduce_and_adam(self, st, arr, nxt=None) -> None:
         # error word of this rank's step (first 4 bytes at the workspace's first 256-byte
         # boundary) rides along so every rank agrees on skipping Adam
         off = (-self.ws.data_ptr()) % 256
         errw = self.ws[off:off + 4].view(torch.int32)
         if self.multicast:
-            self._multicast_adam(errw, arr)
+            self._multicast_adam(errw, arr, nxt)
             return
         if self.sharded:
             self._sharded_adam(errw, st)
-            return
-        reduce_step_buffer(self.grads.flat, self.err_slot, errw, self._err_i32, self.pg)
-        p, m, v, g = (b.c_struct() for b in (self.params, self.m, self.v, self.grads))
-        check(lib.gs_sparse_adam(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
-                                 self.vis_counts.data_ptr(), self.n, self.step_count,
-                                 ctypes.byref(self.ccfg), self._err_i32.data_ptr(), st))
+        else:
+            reduce_step_buffer(self.grads.flat, self.err_slot, errw, self._err_i32, self.pg)
+            p, m, v, g = (b.c_struct() for b in (self.params, self.m, self.v, self.grads))
+            check(lib.gs_sparse_adam(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
+                                     self.vis_counts.data_ptr(), self.n, self.step_count,
+                                     ctypes.byref(self.ccfg), self._err_i32.data_ptr(), st))
+        if nxt is not None:
+            self._project_rows(nxt, 0, self.n, st)
 
     def _sharded_adam(self, errw, st) -> None:
         """Owner-sharded update (dist.sharded_update): reduce-scatter gradients and counts,
@@ -395,14 +434,19 @@ class Trainer:
         sharded_update(grad_groups, shards, param_groups, errw, self.err_slot, self._err_i32,
                        self.rank, self.world, adam, self.pg)
 
-    def _multicast_adam(self, errw, arr) -> None:
+    def _multicast_adam(self, errw, arr, nxt=None) -> None:
         """Owner-sharded update through NVLink multicast (gs_sparse_adam_multicast),
         pipelined over row chunks: the projection backward of chunk c runs on the step's
         stream; on a second stream a one-float allreduce (the barrier after which every
         GPU's chunk-c gradients are complete; for chunk 0 it also sums the ranks' error
         flags) is followed by the multicast update of this rank's rows of chunk c, while
-        the backward of chunk c + 1 proceeds. A last allreduce keeps every GPU from reading
-        parameters or rewriting gradients before all updates have landed."""
+        the backward of chunk c + 1 proceeds. Without next-step cameras (nxt), a last
+        allreduce keeps every GPU from reading parameters or rewriting gradients before all
+        updates have landed. With them, each chunk's update is followed by its own
+        allreduce (every GPU's update of the chunk has landed, and every GPU has read its
+        gradients and visibility counts), after which the step's stream projects the next
+        step's views over the chunk's rows (gs_train_project_rows, which also zeroes their
+        visibility counts) while the later chunks are still being updated."""
         import torch.distributed as dist
         cur = torch.cuda.current_stream()
         comm = self._comm
@@ -434,8 +478,23 @@ class Trainer:
                                                    self._vis_scratch.data_ptr(), self.q,
                                                    self.step_count, ctypes.byref(self.ccfg),
                                                    self._err_i32.data_ptr(), comm.cuda_stream))
+                if nxt is not None:
+                    dist.all_reduce(self._fence, group=self._barrier_pg)
+                    self._chunk_updated[c].record(comm)
+        if nxt is None:
+            cur.wait_stream(comm)
+            dist.all_reduce(self._fence, group=self._barrier_pg)
+            return
+        # Projection chunks start on block boundaries: chunk c's rows lie in update chunks
+        # <= c, all of which have landed once chunk c's event has fired.
+        A = GS_PROJECT_ROW_ALIGN
+        for c in range(self.chunks):
+            b = min(c * span // A * A, self.n)
+            e = self.n if c == self.chunks - 1 else min((c + 1) * span // A * A, self.n)
+            cur.wait_event(self._chunk_updated[c])
+            if e > b:
+                self._project_rows(nxt, b, e, cur.cuda_stream)
         cur.wait_stream(comm)
-        dist.all_reduce(self._fence, group=self._barrier_pg)
 
     def project_view(self, w2c, K, H, W) -> dict:
         """Projection, intersections, sorted pairs and tile ranges of one view (parity API)."""
@@ -493,6 +552,7 @@ class StagedView:
     def forward(self, w2c, K):
         """Image (H, W, 3) of the view; also sets trainer.vis_counts for this view."""
         tr = self.tr
+        tr._projected = None  # vis_counts are rewritten
         self.cam = camera_struct(w2c, K, self.H, self.W)
         img = torch.empty((self.H, self.W, 3), dtype=torch.float32, device=tr.device)
         self.final_T = torch.empty((self.H, self.W), dtype=torch.float32, device=tr.device)
@@ -547,6 +607,7 @@ class StagedView:
     def adam(self, step: int) -> None:
         """Sparse Adam over the rows visible in the view."""
         tr = self.tr
+        tr._projected = None  # the parameters change
         p, m, v, g = (b.c_struct() for b in (tr.params, tr.m, tr.v, tr.grads))
         check(lib.gs_sparse_adam(ctypes.byref(p), ctypes.byref(m), ctypes.byref(v), ctypes.byref(g),
                                  tr.vis_counts.data_ptr(), tr.n, int(step), ctypes.byref(tr.ccfg),

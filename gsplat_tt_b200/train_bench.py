@@ -54,7 +54,9 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, launches_per_step
     """Algorithmic bytes of ONE timed launch of the kernels with a byte model (the minimum
     the algorithm moves, not what the implementation happens to move):
 
-    * train_project (one launch for all of the rank's views): the SH3 parameters once
+    * train_project (all of the rank's views in one pass over the rows; the step's
+      launches split the N rows -- one launch, or one per row chunk when the next step's
+      projection follows the multicast update chunk by chunk): the SH3 parameters once
       (236 B per Gaussian) and per view the 52 B record (mean 8, conic 12, colour 12,
       opacity 4, depth key 4, rectangle 8, pair count 4);
     * radix_pass32 (one pass of the depth sort over N): 4 B key + 4 B value read and written;
@@ -74,7 +76,7 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, launches_per_step
     passes of the super-tile sort (tile_sort_emit, tile_sort_pass) move per super-tile item
     bytes whose count the timer does not see, and have no entry either."""
     if name == "train_project":
-        return n * 236.0 + views * n * 52.0
+        return (n * 236.0 + views * n * 52.0) / max(launches_per_step, 1.0)
     if name == "radix_pass32":
         return n * 16.0
     if name == "tile_filter":
@@ -151,6 +153,17 @@ def summarize_kernels(rep: dict, ksteps: int, n: int, views: int, pairs: float, 
     return per_kernel, roofline, sort_in_step
 
 
+def ranks_list(x: float, world: int) -> list[float]:
+    """x of every rank, in rank order (one small allreduce)."""
+    if world == 1:
+        return [x]
+    import torch.distributed as dist
+    t = torch.zeros(world, dtype=torch.float64, device="cuda")
+    t[dist.get_rank()] = x
+    dist.all_reduce(t)
+    return [float(v) for v in t.tolist()]
+
+
 def run(args, rank: int, world: int, local: int) -> dict:
     from bench import ClockSampler, barrier, max_over_ranks, measured_peaks  # noqa: E402
     name = config_name()
@@ -169,16 +182,23 @@ def run(args, rank: int, world: int, local: int) -> dict:
     sharded = os.environ.get("GS_BENCH_SHARDED", "1") != "0"
     # GS_BENCH_MULTICAST=0: the sharded update through NCCL instead of NVLink multicast
     multicast = os.environ.get("GS_BENCH_MULTICAST", "1") != "0"
-    tr = Trainer(params, cfg, per, H, W, device=dev, sharded_optimizer=sharded, multicast=multicast)
+    # GS_BENCH_MC_CHUNKS: row chunks of the pipelined multicast update (default 4)
+    chunks = int(os.environ.get("GS_BENCH_MC_CHUNKS", "4"))
+    tr = Trainer(params, cfg, per, H, W, device=dev, sharded_optimizer=sharded, multicast=multicast,
+                 mc_chunks=chunks)
     del params
     cams = [(cm.w2c, cm.K, H, W) for cm in mine]
+    # Every step trains on the same views, so each step hands them on as the next step's
+    # cameras: their projection runs at the end of the step, behind the update
+    # (GS_BENCH_PREFETCH=0: each step projects its own views at its start).
+    nxt = cams if os.environ.get("GS_BENCH_PREFETCH", "1") != "0" else None
     pairs0 = tr.count_pairs(cams)
     tr._alloc(int(max(pairs0) * 1.3) + 4096)
     targets = [torch.from_numpy(t).to(dev) for t in targets_host]
     st = torch.cuda.current_stream()
 
     for i in range(args.warmup):
-        tr.step(cams, targets, check_errors=(i == 0))
+        tr.step(cams, targets, check_errors=(i == 0), next_cams=nxt)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -186,13 +206,15 @@ def run(args, rank: int, world: int, local: int) -> dict:
         torch.cuda.synchronize()
         e0.record()
         for _ in range(args.steps):
-            tr.step(cams, targets)
+            tr.step(cams, targets, next_cams=nxt)
         e1.record()
         torch.cuda.synchronize()
         barrier(world)
     if lib.gs_workspace_error(tr.ws.data_ptr(), st.cuda_stream) != 0:
         raise RuntimeError("a timed step overflowed its pair buffers or timed out")
-    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    ms_rank = e0.elapsed_time(e1) / args.steps
+    ms = max_over_ranks(ms_rank, world)
+    ms_by_rank = ranks_list(ms_rank, world)
     total_px = V * H * W
     value = total_px / (ms / 1e3) / 1e6
     loss_now = float(tr.losses.sum().item())
@@ -202,14 +224,14 @@ def run(args, rank: int, world: int, local: int) -> dict:
     # overlapped with the other views' work -- and the loss read back to the host.
     pinned = [torch.from_numpy(t).pin_memory() for t in targets_host]
     for _ in range(2):
-        tr.step(cams, pinned)
+        tr.step(cams, pinned, next_cams=nxt)
         loss_host = tr.losses.sum().item()
     barrier(world)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     e0.record()
     for _ in range(args.steps):
-        tr.step(cams, pinned)
+        tr.step(cams, pinned, next_cams=nxt)
         loss_host = tr.losses.sum().item()
     e1.record()
     torch.cuda.synchronize()
@@ -223,7 +245,7 @@ def run(args, rank: int, world: int, local: int) -> dict:
     lib.gs_timing_enable(1)
     ksteps = max(2, min(args.steps, 5))
     for _ in range(ksteps):
-        tr.step(cams, targets)
+        tr.step(cams, targets, next_cams=nxt)
     torch.cuda.synchronize()
     lib.gs_timing_enable(0)
     rep = timing_report()
@@ -247,12 +269,16 @@ def run(args, rank: int, world: int, local: int) -> dict:
                        f"broadcast (gs_sparse_adam_multicast), pipelined over {tr.chunks} row chunks "
                        "with the projection backward" if tr.multicast else
                        " + NCCL reduce-scatter / all-gather, owner-sharded Adam" if tr.sharded
-                       else " + NCCL allreduce, replicated Adam"),
+                       else " + NCCL allreduce, replicated Adam") + (
+                       "; each step projects the next step's views after its update"
+                       + (", row chunk by row chunk as the chunks land" if tr.multicast else "")
+                       if nxt is not None else ""),
                    "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},
         "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
                 "h2d_bytes_per_step": int(sum(t.size * 4 for t in targets_host)),
                 "d2h_bytes_per_step": 4},
         "gpu_launches": int(sum(v["launches_per_step"] for v in per_kernel.values())),
+        "ms_per_step_by_rank": ms_by_rank,
         "pairs_per_view": pairs, "loss": loss_now,
         "kernels": per_kernel,
         "clocks": clk.summary(),

@@ -271,6 +271,10 @@ typedef struct gs_train_config {
  * ref_slots_fast, gsplat/t2_param_backward.py:244 t2_step (extended to SH1-3 and
  * multiple views) and gsplat/train_oracle.py:434 sparse_adam_step. */
 #define GS_STEP_DEFER_PARAM_BWD 2
+/* OR-ed into apply_adam: every row of these views was already projected into the
+ * workspace by gs_train_project_rows (same params, n, cams, n_views, cfg, vis_counts,
+ * pair_capacity and workspace), so the step starts at the pair-count scan. */
+#define GS_STEP_PROJECTED 4
 
 gs_status gs_train_step(const gs_gaussians* params, const gs_gaussians* exp_avg,
                         const gs_gaussians* exp_avg_sq, const gs_gaussians* grads,
@@ -279,6 +283,22 @@ gs_status gs_train_step(const gs_gaussians* params, const gs_gaussians* exp_avg,
                         const gs_train_config* cfg, int32_t apply_adam, float* view_losses,
                         float* images, float* grad2d, int64_t* pairs, int64_t pair_capacity,
                         void* workspace, size_t workspace_bytes, void* stream);
+/* The projection of rows [row_begin, row_end) of a step's views into the workspace, for a
+ * following gs_train_step with GS_STEP_PROJECTED: zeroes those rows of vis_counts and of
+ * the workspace's touched-view masks, uploads the cameras, and projects (2D mean, conic,
+ * opacity, colour, depth key, tile rectangle, pair count per view; visibility counts).
+ * row_begin and row_end lie on multiples of GS_PROJECT_ROW_ALIGN (row_end may be n). A
+ * multi-GPU caller projects the next step's views one row chunk at a time as soon as the
+ * chunk's parameters have been updated on every GPU, overlapping the projection with the
+ * update of the later chunks. Same stream rules as gs_train_step.
+ * No reference counterpart as one call: the projection half of
+ * gsplat/t2_param_backward.py:81-120 forward_lanes, split by rows. */
+#define GS_PROJECT_ROW_ALIGN 256
+gs_status gs_train_project_rows(const gs_gaussians* params, float* vis_counts, int64_t n,
+                                int64_t row_begin, int64_t row_end, const gs_camera* cams,
+                                int32_t n_views, const gs_train_config* cfg,
+                                int64_t pair_capacity, void* workspace, size_t workspace_bytes,
+                                void* stream);
 size_t gs_train_workspace_size(int64_t n, int32_t sh_degree, int32_t n_views, int32_t height,
                                int32_t width, int32_t tile_size, int64_t pair_capacity);
 

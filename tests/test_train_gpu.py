@@ -188,6 +188,65 @@ def test_overflow_retry_and_multi_step():
     assert np.isfinite(losses).all() and losses[-1] < losses[0]
 
 
+def test_projection_ahead_matches_projection_in_step():
+    """next_cams: the step projects the next step's views after its update
+    (gs_train_project_rows) and the next step starts at the pair-count scan
+    (GS_STEP_PROJECTED). Three steps that way give the losses, gradients and parameters of
+    three plain steps (up to the backward's float-atomics order); a projection made for
+    other cameras is discarded, and the step with the right cameras projects itself."""
+    import torch
+    params = small_scene(6000, 3, seed=21)
+    H, W = 64, 96
+    cams = cams_for(3, H, W, 90.0)
+    other = cams_for(3, H, W, 90.0, seed=9)
+    targets = [torch.from_numpy(t).cuda() for t in
+               scenes.random_targets([scenes.Camera(c[0], c[1], H, W) for c in cams], seed=22)]
+    runs = []
+    for mode in ("plain", "ahead", "wrong"):
+        tr, _ = trainer(params, 3, 16, len(cams), H, W)
+        tr.ensure_capacity(cams)
+        losses = []
+        for i in range(3):
+            nxt = None if mode == "plain" else (other if mode == "wrong" else cams)
+            losses.append(tr.step(cams, targets, next_cams=nxt).cpu().numpy().copy())
+            if mode == "ahead":
+                assert tr._projected is not None
+        torch.cuda.synchronize()
+        assert lib_error(tr) == 0
+        runs.append((np.array(losses), tr.grads.numpy(), tr.params.numpy()))
+    for losses, g, p in runs[1:]:
+        np.testing.assert_allclose(losses, runs[0][0], rtol=1e-6)
+        for k in ot.PARAM_NAMES:
+            assert ot.rel_error(g[k], runs[0][1][k]) <= 1e-4, k
+            np.testing.assert_allclose(p[k], runs[0][2][k], rtol=0, atol=1e-6)
+
+
+def lib_error(tr):
+    import torch
+    from gsplat_tt_b200._lib import lib
+    return lib.gs_workspace_error(tr.ws.data_ptr(), torch.cuda.current_stream().cuda_stream)
+
+
+def test_project_rows_argument_errors():
+    """gs_train_project_rows rejects row ranges off the GS_PROJECT_ROW_ALIGN grid."""
+    import torch
+    from gsplat_tt_b200 import _lib
+    from gsplat_tt_b200.train import GS_PROJECT_ROW_ALIGN
+    params = small_scene(1000, 3, seed=3)
+    H, W = 32, 48
+    cams = cams_for(1, H, W, 40.0)
+    tr, _ = trainer(params, 3, 16, 1, H, W)
+    arr = tr._cams(cams)
+    st = torch.cuda.current_stream().cuda_stream
+    for b, e in ((1, 1000), (0, 300), (GS_PROJECT_ROW_ALIGN, 1001), (512, 256)):
+        with pytest.raises(ValueError):
+            tr._project_rows(arr, b, e, st)
+    tr._project_rows(arr, 0, GS_PROJECT_ROW_ALIGN, st)
+    tr._project_rows(arr, GS_PROJECT_ROW_ALIGN, 1000, st)
+    torch.cuda.synchronize()
+    assert lib_error(tr) == _lib.GS_OK
+
+
 def test_bf16_moments_match_the_oracle_bf16_mode():
     """bf16 moment storage (gsplat/train_oracle.py:434-470, bf16 mode): the moments live in
     2-byte arrays, and two steps of the device's sparse Adam match the oracle's bf16 mode
