@@ -90,13 +90,12 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, launches_per_step
     return None
 
 
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch measured by ncu on
-# the C4 scene with one view (3M Gaussians, 21,898,068 pairs), and the unit the traffic
-# scales with when the bench's workload is larger.
-NCU_TRAFFIC_C4_1VIEW = {
-    "tile_sort_emit": (172.1e6, "pairs"),
-    "tile_sort_pass": (247.2e6, "pairs"),
-}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of a byte-modelled
+# kernel, measured by ncu on the C4 scene with one view, and the unit it scales with at the
+# bench's size. Empty: the depth-sort pass, the largest such kernel, keeps its keys and
+# values in L2 at C4 (24 MB) but not at C5 (96 MB), so no scaled C4 figure describes the
+# bench's launch, and the roofline object reports traffic null with that reason.
+NCU_TRAFFIC_C4_1VIEW: dict = {}
 C4_1VIEW_PAIRS = 21898068.0
 
 
@@ -137,7 +136,10 @@ def summarize_kernels(rep: dict, ksteps: int, n: int, views: int, pairs: float, 
     roofline = {"bound": "hbm", "kernel": dom_name, "achieved": d["achieved_gbs"],
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": d["frac_hbm"],
                 "traffic": _traffic(dom_name, pairs),
-                "traffic_source": "ncu dram bytes of one launch at C4 / 1 view, scaled by pairs",
+                "traffic_source": ("ncu dram bytes of one launch at C4 / 1 view, scaled by pairs"
+                                   if dom_name in NCU_TRAFFIC_C4_1VIEW else
+                                   "null: no ncu capture of this launch at the bench's size (the "
+                                   "C4 capture's keys stay in L2, the C5 launch's do not)"),
                 "peak_source": peaks["source"],
                 "note": "largest HBM-bound kernel of the step; the rasterisers "
                         f"({', '.join(f'{k} {v:.1f} ms' for k, v in raster.items())} per step) "

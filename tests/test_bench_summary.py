@@ -50,12 +50,16 @@ def test_chunked_and_owner_sharded_launches_are_charged_their_own_rows():
     moves link bytes, not HBM bytes: no kernel may read above the peak."""
     n, views, world, q, chunks = 6_000_000, 4, 8, 187_500, 4
     rep = {"param_bwd": (2.41 * 2, 4 * 2), "sparse_adam_mc": (3.28 * 2, 4 * 2),
-           "tile_filter": (2.0, 8)}
+           "tile_filter": (2.0, 8), "train_project": (1.6 * 2, 4 * 2)}
     per_kernel, roof, _ = tb.summarize_kernels(rep, 2, n, views, 4.6e7, 1920 * 1080, PEAKS,
                                                adam_rows=chunks * q, world=world, q=q)
     pb = per_kernel["param_bwd"]
     assert pb["algorithmic_bytes"] == pytest.approx((n * 472.0 + views * n * 36.0) / 4)
     assert pb["frac_hbm"] < 1.0
+    # the next step's projection, one launch per row chunk behind the update
+    tp = per_kernel["train_project"]
+    assert tp["algorithmic_bytes"] == pytest.approx((n * 236.0 + views * n * 52.0) / 4)
+    assert tp["frac_hbm"] < 1.0
     mc = per_kernel["sparse_adam_mc"]
     assert "frac_hbm" not in mc
     assert mc["link_bytes_per_direction"] == pytest.approx(q * (world * 240 + 236))
