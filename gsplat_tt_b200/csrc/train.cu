@@ -550,6 +550,17 @@ __global__ void k_loss_l1(const float* __restrict__ img, const float* __restrict
     }
 }
 
+// 4-byte asynchronous global -> shared copy (cp.async, no register staging), zero-filled
+// when `in` is false (nothing is read then; the source must still be a valid address).
+__device__ __forceinline__ void cp_async4(float* smem, const float* gmem, bool in) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem),
+                 "r"(in ? 4 : 0)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
 // SSIM tiles: 32 x 32 outputs per block of 256 threads, from a (42 x 42) patch (halo 5
 // for the 11-tap window). Horizontal pass: a thread filters 4 adjacent outputs of a patch
 // row from 14 values held in registers; vertical pass: a thread filters 4 adjacent rows
@@ -561,8 +572,8 @@ constexpr int kSsimS = 45;                    // padded patch row stride
 constexpr int kSsimHItems = kSsimP * (kSsimT / 4);  // 336 horizontal items of 4 outputs
 
 struct SsimFwdSmem {
-    float px[3][kSsimP][kSsimS];
-    float py[3][kSsimP][kSsimS];
+    float px[kSsimP][kSsimS];  // one channel's patch of each image
+    float py[kSsimP][kSsimS];
     float h[5][kSsimP][kSsimT];
 };
 struct SsimBwdSmem {
@@ -583,21 +594,29 @@ k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg
     __shared__ double red[2][8];
     const int tid = threadIdx.x;
     const int x0 = blockIdx.x * kSsimT, y0 = blockIdx.y * kSsimT;
-    for (int i = tid; i < kSsimP * kSsimP * 3; i += 256) {
-        const int r = i / (kSsimP * 3), rem = i - r * (kSsimP * 3);
-        const int c = rem / 3, ch = rem - c * 3;
-        const int yy = y0 - kHalo + r, xx = x0 - kHalo + c;
-        const bool in = yy >= 0 && yy < L.H && xx >= 0 && xx < L.W;
-        const size_t o = ((size_t)yy * L.W + xx) * 3 + ch;
-        S.px[ch][r][c] = in ? img[o] : 0.0f;
-        S.py[ch][r][c] = in ? tgt[o] : 0.0f;
-    }
-    __syncthreads();
+    // One channel's patch of both images at a time, copied asynchronously: channel 0 before
+    // the loop, channel ch + 1 once the horizontal pass of channel ch has consumed the
+    // patch, so the copies overlap the vertical pass (the other channels' bytes of the
+    // interleaved rows are L2 hits by then).
+    auto load_patch = [&](int ch) {
+        for (int i = tid; i < kSsimP * kSsimP; i += 256) {
+            const int r = i / kSsimP, c = i - r * kSsimP;
+            const int yy = y0 - kHalo + r, xx = x0 - kHalo + c;
+            const bool in = yy >= 0 && yy < L.H && xx >= 0 && xx < L.W;
+            const size_t o = in ? ((size_t)yy * L.W + xx) * 3 + ch : 0;
+            cp_async4(&S.px[r][c], img + o, in);
+            cp_async4(&S.py[r][c], tgt + o, in);
+        }
+        cp_async_commit();
+    };
+    load_patch(0);
     double s_l1 = 0.0, s_ssim = 0.0;
     const float C1 = 0.01f * 0.01f, C2 = 0.03f * 0.03f;
     const float w = -L.lambda * L.inv_n;
     const int vc = tid & 31, vr0 = (tid >> 5) * 4;  // vertical item: column, first of 4 rows
     for (int ch = 0; ch < 3; ++ch) {
+        cp_async_wait_all();
+        __syncthreads();
         for (int it = tid; it < kSsimHItems; it += 256) {
             const int r = it >> 3, c0 = (it & 7) * 4;
             // (x, y) and (x^2, y^2) filtered as packed fp32x2 pairs, x y on its own
@@ -605,7 +624,7 @@ k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg
             float pr[14];
 #pragma unroll
             for (int k = 0; k < 14; ++k) {
-                xy[k] = make_float2(S.px[ch][r][c0 + k], S.py[ch][r][c0 + k]);
+                xy[k] = make_float2(S.px[r][c0 + k], S.py[r][c0 + k]);
                 sq[k] = __fmul2_rn(xy[k], xy[k]);
                 pr[k] = __fmul_rn(xy[k].x, xy[k].y);
             }
@@ -627,7 +646,12 @@ k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg
                 S.h[4][r][c0 + o] = a4;
             }
         }
+        float ad[4];  // |x - y| of this thread's 4 pixels, before the patch is overwritten
+#pragma unroll
+        for (int o = 0; o < 4; ++o)
+            ad[o] = fabsf(S.px[vr0 + o + kHalo][vc + kHalo] - S.py[vr0 + o + kHalo][vc + kHalo]);
         __syncthreads();
+        if (ch + 1 < 3) load_patch(ch + 1);
         float m[5][4];
 #pragma unroll
         for (int q = 0; q < 4; q += 2) {  // quantities (0, 1) and (2, 3) packed
@@ -672,7 +696,7 @@ k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg
             dxx[po] = -Sw / D;
             dxy[po] = 2.0f * Sw / B;
             s_ssim += Sv;
-            s_l1 += fabsf(S.px[ch][vr0 + o + kHalo][vc + kHalo] - S.py[ch][vr0 + o + kHalo][vc + kHalo]);
+            s_l1 += ad[o];
         }
         __syncthreads();
     }
@@ -695,7 +719,7 @@ k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg
 
 // dL/dx = G*d_mu + 2 x G*d_xx + y G*d_xy + (1 - lambda)/n sign(x - y), per channel from
 // (42 x 42) patches of the planar maps; written interleaved (H, W, 3) like the image.
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(256, 5)
 k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt,
            const float* __restrict__ dmu, const float* __restrict__ dxx,
            const float* __restrict__ dxy, LossCfg L, float* __restrict__ dimg) {
@@ -705,17 +729,25 @@ k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt,
     const int x0 = blockIdx.x * kSsimT, y0 = blockIdx.y * kSsimT;
     const float wl1 = (1.0f - L.lambda) * L.inv_n;
     const int vc = tid & 31, vr0 = (tid >> 5) * 4;
-    for (int ch = 0; ch < 3; ++ch) {
+    // The three maps' patch of a channel, copied asynchronously: channel 0 before the loop,
+    // channel ch + 1 once the horizontal pass of channel ch has consumed the patch, so the
+    // copies overlap the vertical pass.
+    auto load_patch = [&](int ch) {
         const size_t plane = (size_t)ch * L.H * L.W;
         for (int i = tid; i < kSsimP * kSsimP; i += 256) {
             const int r = i / kSsimP, c = i - r * kSsimP;
             const int yy = y0 - kHalo + r, xx = x0 - kHalo + c;
             const bool in = yy >= 0 && yy < L.H && xx >= 0 && xx < L.W;
-            const size_t o = plane + (size_t)yy * L.W + xx;
-            S.p[0][r][c] = in ? dmu[o] : 0.0f;
-            S.p[1][r][c] = in ? dxx[o] : 0.0f;
-            S.p[2][r][c] = in ? dxy[o] : 0.0f;
+            const size_t o = in ? plane + (size_t)yy * L.W + xx : 0;
+            cp_async4(&S.p[0][r][c], dmu + o, in);
+            cp_async4(&S.p[1][r][c], dxx + o, in);
+            cp_async4(&S.p[2][r][c], dxy + o, in);
         }
+        cp_async_commit();
+    };
+    load_patch(0);
+    for (int ch = 0; ch < 3; ++ch) {
+        cp_async_wait_all();
         __syncthreads();
         for (int it = tid; it < kSsimHItems; it += 256) {
             const int r = it >> 3, c0 = (it & 7) * 4;
@@ -746,6 +778,17 @@ k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt,
             }
         }
         __syncthreads();
+        if (ch + 1 < 3) load_patch(ch + 1);  // the patch is free: S.h holds this channel now
+        // this thread's pixels of the channel, loaded ahead of the vertical pass
+        float xv4[4], yv4[4];
+#pragma unroll
+        for (int o = 0; o < 4; ++o) {
+            const int x = x0 + vc, y = y0 + vr0 + o;
+            const bool in = x < L.W && y < L.H;
+            const size_t io = in ? ((size_t)y * L.W + x) * 3 + ch : 0;
+            xv4[o] = in ? img[io] : 0.0f;
+            yv4[o] = in ? tgt[io] : 0.0f;
+        }
         float m[3][4];
         {
             float2 v[14];
@@ -777,7 +820,7 @@ k_ssim_bwd(const float* __restrict__ img, const float* __restrict__ tgt,
             const int x = x0 + vc, y = y0 + vr0 + o;
             if (x >= L.W || y >= L.H) continue;
             const size_t io = ((size_t)y * L.W + x) * 3 + ch;
-            const float xv = img[io], yv = tgt[io];
+            const float xv = xv4[o], yv = yv4[o];
             const float d = xv - yv;
             dimg[io] = m[0][o] + 2.0f * xv * m[1][o] + yv * m[2][o] +
                        wl1 * (float)((d > 0.0f) - (d < 0.0f));
