@@ -47,7 +47,7 @@ struct SortSmem {
     uint32_t vals[kTileItems];
     uint32_t warp_hist[kSortWarps][kRadix];
     uint32_t local_off[kRadix];
-    uint32_t gbase[kRadix];
+    uint32_t gbase[kRadix];  // digit's global offset minus its block-local offset
     uint32_t scan[kRadix];
     uint32_t tile;
 };
@@ -213,7 +213,9 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
         uint32_t wbase = 0;
 #pragma unroll
         for (int w = 0; w < kSortWarps; ++w) wbase += (w < warp) ? S.scan[w] : 0u;
-        S.local_off[d] = wbase + x - own;
+        const uint32_t lo = wbase + x - own;
+        S.local_off[d] = lo;
+        S.gbase[d] -= lo;  // the write-out then needs one word per item
     }
     __syncthreads();
 
@@ -232,7 +234,7 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
     for (int i = tid; i < valid; i += kSortThreads) {
         const KeyT k = S.keys[i];
         const uint32_t dd = GS_DIGIT(k);
-        const uint32_t out = S.gbase[dd] + ((uint32_t)i - S.local_off[dd]);
+        const uint32_t out = S.gbase[dd] + (uint32_t)i;
         if (keys_out) keys_out[out] = k;
         vals_out[out] = S.vals[i];
     }

@@ -1395,7 +1395,7 @@ k_sparse_adam_mc(AdamParams A, const float* __restrict__ vis, const unsigned int
 // (the caller's stream for lane 0) and its own copy of these buffers, so one view's
 // rasterisers run while the next view sorts.
 #ifndef GS_TRAIN_LANES
-#define GS_TRAIN_LANES 2
+#define GS_TRAIN_LANES 4
 #endif
 constexpr int kLanes = GS_TRAIN_LANES;
 

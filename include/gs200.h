@@ -262,10 +262,10 @@ typedef struct gs_train_config {
  *   (grads) is left to gs_train_param_backward, called with the same workspace and
  *   arguments, over row ranges (a multi-GPU caller overlaps the update of one range with
  *   the backward of the next); vis_counts are written as usual.
- *   All work is ordered on `stream`: with two or more views, views alternate between
- *   `stream` and an internal stream of the library (created once per device) that is
- *   forked from `stream` after the projection and joined back to it before the parameter
- *   backward, so the call stays capturable into a CUDA graph.
+ *   All work is ordered on `stream`: with two or more views, views go round-robin over
+ *   up to four lanes -- `stream` and internal streams of the library (created once per
+ *   device) forked from `stream` after the projection and joined back to it before the
+ *   parameter backward -- so the call stays capturable into a CUDA graph.
  * No counterpart in one reference call: it chains gsplat/blend_backward_dev.py:404
  * forward_fast, gsplat/train_loss.py:126 loss_and_grad_device, blend_backward_dev.py:444
  * ref_slots_fast, gsplat/t2_param_backward.py:244 t2_step (extended to SH1-3 and
