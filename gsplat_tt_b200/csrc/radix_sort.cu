@@ -145,7 +145,25 @@ gs_status radix_sort_pairs32(const uint32_t* keys, const uint32_t* vals, const i
 // caller supplies every pass's exclusive digit offsets (npass x 256), derived from the
 // per-tile pair counts, so no histogram pass over the pairs is needed; only values are
 // written by the last pass.
-gs_status radix_sort_rect_pairs(const RectPairSource& src, const int64_t* n_dev, int64_t n_cap,
+// The first pass of the tile sort for one super-tile shape.
+template <int SX, int SY>
+static gs_status launch_rect_pass(const RectPairArgs& a, uint32_t* keys_out, uint32_t* vals_out,
+                                  const int64_t* n_dev, int64_t n_cap, int digit_bits,
+                                  const uint32_t* digit_offsets, uint32_t* look,
+                                  uint32_t* counter, unsigned int* err, unsigned int grid,
+                                  cudaStream_t st) {
+    const size_t smem = sizeof(SortSmem<uint32_t>);
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, RectPairSource<SX, SY>>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    RectPairSource<SX, SY> src;
+    static_cast<RectPairArgs&>(src) = a;
+    k_onesweep_pass<uint32_t, RectPairSource<SX, SY>><<<grid, kSortThreads, smem, st>>>(
+        src, keys_out, vals_out, n_dev, n_cap, 0, digit_bits, digit_offsets, look, counter, err);
+    GS_CHECK_LAUNCH();
+    return GS_OK;
+}
+
+gs_status radix_sort_rect_pairs(const RectPairArgs& src, const int64_t* n_dev, int64_t n_cap,
                                 int key_bits, const uint32_t* digit_offsets, uint32_t* vals_out,
                                 void* workspace, size_t workspace_bytes, cudaStream_t st,
                                 unsigned int* err_ext) {
@@ -168,17 +186,26 @@ gs_status radix_sort_rect_pairs(const RectPairSource& src, const int64_t* n_dev,
     GS_CUDA_CHECK(cudaMemsetAsync(err, 0, (char*)(counters + npass) - (char*)err, st));
     if (err_ext) err = err_ext;
     const size_t smem = sizeof(SortSmem<uint32_t>);
-    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, RectPairSource>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, GlobalSource<uint32_t>>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     const unsigned int grid = (unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1);
     {
         KernelTimer kt("tile_sort_emit", st);
-        k_onesweep_pass<uint32_t, RectPairSource><<<grid, kSortThreads, smem, st>>>(
-            src, npass == 1 ? nullptr : ka, npass == 1 ? vals_out : va, n_dev, n_cap, 0,
-            std::min(kRadixBits, key_bits), digit_offsets, look, counters, err);
-        GS_CHECK_LAUNCH();
+        uint32_t* k1 = npass == 1 ? nullptr : ka;
+        uint32_t* v1 = npass == 1 ? vals_out : va;
+        const int db = std::min(kRadixBits, key_bits);
+        gs_status ls;
+        if (src.sx == 0 && src.sy == 0)
+            ls = launch_rect_pass<0, 0>(src, k1, v1, n_dev, n_cap, db, digit_offsets, look, counters, err, grid, st);
+        else if (src.sx == 1 && src.sy == 1)
+            ls = launch_rect_pass<1, 1>(src, k1, v1, n_dev, n_cap, db, digit_offsets, look, counters, err, grid, st);
+        else if (src.sx == 2 && src.sy == 1)
+            ls = launch_rect_pass<2, 1>(src, k1, v1, n_dev, n_cap, db, digit_offsets, look, counters, err, grid, st);
+        else {
+            set_error("tile sort: unsupported super-tile shape %dx%d", 1 << src.sx, 1 << src.sy);
+            return GS_ERR_ARG;
+        }
+        if (ls != GS_OK) return ls;
     }
     const uint32_t* kin = ka;
     const uint32_t* vin = va;

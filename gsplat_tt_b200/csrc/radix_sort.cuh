@@ -25,10 +25,11 @@ gs_status radix_sort_pairs32(const uint32_t* keys, const uint32_t* vals, const i
                              void* workspace, size_t workspace_bytes, cudaStream_t st,
                              unsigned int** err_out, unsigned int* err_ext = nullptr);
 
-struct RectPairSource;
-// Stable sort by tile id of the (Gaussian, tile) pairs that `src` generates (rect_pairs.cuh),
-// *n_dev pairs (at most n_cap); digit_offsets holds each pass's exclusive digit offsets.
-gs_status radix_sort_rect_pairs(const RectPairSource& src, const int64_t* n_dev, int64_t n_cap,
+struct RectPairArgs;
+// Stable sort by cell id of the (Gaussian, cell) items that `src` describes (rect_pairs.cuh;
+// cells of 2^sx x 2^sy tiles, sx and sy in {0, 1, 2}), *n_dev items (at most n_cap);
+// digit_offsets holds each pass's exclusive digit offsets.
+gs_status radix_sort_rect_pairs(const RectPairArgs& src, const int64_t* n_dev, int64_t n_cap,
                                 int key_bits, const uint32_t* digit_offsets, uint32_t* vals_out,
                                 void* workspace, size_t workspace_bytes, cudaStream_t st,
                                 unsigned int* err_ext);

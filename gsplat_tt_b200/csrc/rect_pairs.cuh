@@ -3,26 +3,33 @@
 //
 // Pair order before the sort (the order the stable sort must preserve within a tile):
 // Gaussians in depth order, each Gaussian's tiles row-major inside its rectangle. The
-// rectangle is taken at a coarser grid (tile coordinates >> shift: shift 1 = the 2x2-tile
-// super-tiles), key = cell id (cy * cells_x + cx). With shift 0 the value is the Gaussian
-// id and sorting stably by cell id gives the reference's (tile, depth bits, Gaussian id)
-// order (src/gsplat_cpu/sort.cpp:24-27); with shift 1 the value is Gaussian id << 4 | the
-// mask of the super-tile's four tiles the Gaussian's rectangle covers (bit 2 * row +
-// column), from which the tile filter (train_project.cu) derives each tile's list.
+// rectangle is taken at a coarser grid of super-tiles 2^sx tiles wide and 2^sy high (tile
+// column >> sx, row >> sy), key = cell id (cy * cells_x + cx). With sx = sy = 0 the value
+// is the Gaussian id and sorting stably by cell id gives the reference's (tile, depth bits,
+// Gaussian id) order (src/gsplat_cpu/sort.cpp:24-27); otherwise the value is Gaussian id
+// << Q | the mask of the super-tile's Q = 2^(sx + sy) tiles the Gaussian's rectangle
+// covers (bit row * 2^sx + column), from which the tile filter (train_project.cu) derives
+// each tile's list.
 #pragma once
 
 #include "onesweep.cuh"
 
 namespace gs {
 
-struct RectPairSource {
+// The host's description of the items; radix_sort_rect_pairs instantiates the source for
+// the super-tile shape (sx, sy).
+struct RectPairArgs {
     const uint32_t* order;   // Gaussian ids in depth order
     const uint32_t* goff;    // first pair of each depth-ordered Gaussian; n + 1 entries
     const uint32_t* tfirst;  // per 4096-pair tile: depth index of the Gaussian holding its first pair
     const uint32_t* last;    // [0]: depth index of the last Gaussian with pairs
     const ushort4* rect;     // per depth-ordered Gaussian: tile columns x0..x1, rows y0..y1
     int tiles_x;             // cells per row of the (coarser) grid the keys index
-    int shift;               // cell = tile >> shift
+    int sx, sy;              // cell = (tile column >> sx, tile row >> sy)
+};
+
+template <int SX, int SY>
+struct RectPairSource : RectPairArgs {
 
     // The tile's pairs come from depth-ordered Gaussians gf..gl (at most `valid` of them,
     // each has at least one pair), taken in chunks of kGaussPerThread per thread. A thread writes
@@ -41,12 +48,20 @@ struct RectPairSource {
     // (cx, cy)).
     __device__ __forceinline__ uint32_t value(uint32_t gid, ushort4 r0, uint32_t cx,
                                               uint32_t cy) const {
-        if (shift == 0) return gid;
-        const uint32_t x = 2u * cx, y = 2u * cy;
-        const uint32_t cols = (x >= r0.x && x <= r0.y ? 1u : 0u) | (x + 1u >= r0.x && x + 1u <= r0.y ? 2u : 0u);
-        const uint32_t m = (y >= r0.z && y <= r0.w ? cols : 0u) |
-                           (y + 1u >= r0.z && y + 1u <= r0.w ? cols << 2 : 0u);
-        return (gid << 4) | m;
+        if constexpr (SX == 0 && SY == 0) {
+            return gid;
+        } else {
+            constexpr uint32_t W = 1u << SX, H = 1u << SY;
+            // the rectangle's columns c0..c1 and rows q0..q1 inside the cell (it meets the cell)
+            const uint32_t x = cx << SX, y = cy << SY;
+            const uint32_t c0 = max((uint32_t)r0.x, x) - x, c1 = min((uint32_t)r0.y - x, W - 1u);
+            const uint32_t q0 = max((uint32_t)r0.z, y) - y, q1 = min((uint32_t)r0.w - y, H - 1u);
+            const uint32_t cols = ((2u << c1) - 1u) & ~((1u << c0) - 1u);
+            uint32_t rows = 0u;  // bit q * W for each covered row q
+#pragma unroll
+            for (uint32_t q = 0; q < H; ++q) rows |= (q >= q0 && q <= q1) ? 1u << (q * W) : 0u;
+            return (gid << (W * H)) | (cols * rows);
+        }
     }
 
     __device__ __forceinline__ void load(SortSmem<uint32_t>& S, uint32_t tile, int64_t base,
@@ -77,8 +92,7 @@ struct RectPairSource {
                 if (i > gl) continue;
                 const uint32_t off = goff[i], end = goff[i + 1], gid = order[i];
                 const ushort4 r0 = rect[i];
-                const ushort4 r = make_ushort4(r0.x >> shift, r0.y >> shift, r0.z >> shift,
-                                               r0.w >> shift);
+                const ushort4 r = make_ushort4(r0.x >> SX, r0.y >> SX, r0.z >> SY, r0.w >> SY);
                 const uint32_t p0 = max(off, lo_p), p1 = min(end, hi_p);
                 if (p1 > p0 && p1 - p0 <= kOwnPairs) {
                     const uint32_t w = (uint32_t)r.y - (uint32_t)r.x + 1u;
@@ -104,8 +118,7 @@ struct RectPairSource {
                 const uint32_t bi = s_big[par][q];
                 const uint32_t off = goff[bi], end = goff[bi + 1], gid = order[bi];
                 const ushort4 r0 = rect[bi];
-                const ushort4 r = make_ushort4(r0.x >> shift, r0.y >> shift, r0.z >> shift,
-                                               r0.w >> shift);
+                const ushort4 r = make_ushort4(r0.x >> SX, r0.y >> SX, r0.z >> SY, r0.w >> SY);
                 const uint32_t p0 = max(off, lo_p), p1 = min(end, hi_p);
                 const uint32_t w = (uint32_t)r.y - (uint32_t)r.x + 1u;
                 for (uint32_t p = p0 + (uint32_t)lane; p < p1; p += 32u) {

@@ -1,6 +1,7 @@
 // train.cu -- training path: rasterisers, loss, projection backward, sparse Adam and
 // the gs_train_step orchestration (one stream, no host synchronisation inside a step).
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <vector>
@@ -1613,24 +1614,43 @@ static gs_status project_views(const GConst& P, int64_t n, int n_views, const TC
     return scan_view_pairs(n, n_views, L, st);
 }
 
-// Largest Gaussian count (exclusive) sorted through super-tiles: the packed sort value
-// holds id << 4, so 2^28. A build option so the direct tile sort can be exercised on small
-// scenes too.
+// Largest Gaussian counts (exclusive) sorted through 4x2-tile super-tiles (the packed sort
+// value holds id << 8, so 2^24) and through 2x2-tile super-tiles (id << 4, 2^28); above
+// them the (Gaussian, tile) pairs are sorted directly. Build options, so the 2x2 path and
+// the direct tile sort can be exercised on small scenes too.
+#ifndef GS_WIDE_SUPER_TILE_MAX_N
+#define GS_WIDE_SUPER_TILE_MAX_N (1ll << 24)
+#endif
 #ifndef GS_SUPER_TILE_MAX_N
 #define GS_SUPER_TILE_MAX_N (1ll << 28)
 #endif
+
+// The tile sort's cell shape for n Gaussians: log2 of the super-tile width and height in
+// tiles (0, 0: the (Gaussian, tile) pairs themselves). GS_TILE_SORT_CELLS=4x2|2x2|1x1 in
+// the environment selects a shape for testing, where n allows it (read on every call).
+static void tile_sort_shape(int64_t n, int& sx, int& sy) {
+    sx = (n < (int64_t)GS_WIDE_SUPER_TILE_MAX_N) ? 2 : (n < (int64_t)GS_SUPER_TILE_MAX_N) ? 1 : 0;
+    const char* e = getenv("GS_TILE_SORT_CELLS");
+    if (e != nullptr) {
+        if (strcmp(e, "2x2") == 0 && n < (int64_t)GS_SUPER_TILE_MAX_N) sx = 1;
+        else if (strcmp(e, "1x1") == 0) sx = 0;
+    }
+    sy = sx ? 1 : 0;
+}
 
 // Depth order, pair offsets, tile counts / ranges and the tile sort of one projected view.
 static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, ViewLane& V,
                            int64_t cap, cudaStream_t st) {
     const unsigned int nb = div_up(n, kProjThreads);
     const ProjView pv = L.pv.view(view, n);
-    // The tile lists come from a stable sort of the (Gaussian, 2x2-tile super-tile) pairs
-    // -- about 0.43 of the (Gaussian, tile) pairs at the benchmark sizes -- and a filter that
-    // hands each super-tile's depth-ordered items to its four tiles (shift 1), or, when the
-    // Gaussian ids do not fit the 28 bits the packed sort value leaves, from a sort of the
-    // (Gaussian, tile) pairs themselves (shift 0).
-    const int shift = (n < (int64_t)GS_SUPER_TILE_MAX_N) ? 1 : 0;
+    // The tile lists come from a stable sort of the (Gaussian, super-tile) pairs and a filter
+    // that hands each super-tile's depth-ordered items to its tiles. Super-tiles are 4x2
+    // tiles (about 0.32 of the (Gaussian, tile) pairs at the benchmark sizes) while the
+    // Gaussian ids fit the 24 bits the packed sort value leaves, else 2x2 tiles (0.43; 28
+    // bits), else the (Gaussian, tile) pairs themselves are sorted (sx = sy = 0).
+    int sx, sy;
+    tile_sort_shape(n, sx, sy);
+    const bool super = sx != 0;
     // Gaussians in (depth bits, id) order, those without pairs last.
     unsigned int* rerr = nullptr;
     gs_status s = radix_sort_pairs32(pv.dsort, nullptr, nullptr, n, 32, nullptr, V.order, V.radix,
@@ -1638,12 +1658,12 @@ static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, Vie
     if (s != GS_OK) return s;
     // each one's rectangle and tile-sort item count in depth order (one gather), and the
     // per-block item totals
-    launch_sorted_count(pv, V.order, n, shift, V.rect_d, V.ccnt, V.blk2, st);
+    launch_sorted_count(pv, V.order, n, sx, sy, V.rect_d, V.ccnt, V.blk2, st);
     GS_CHECK_LAUNCH();
     scan_block_totals<int64_t><<<1, 1024, 0, st>>>(V.blk2, nb, nullptr);
     GS_CHECK_LAUNCH();
-    const int cells_x = shift ? (cfg.tiles_x + 1) / 2 : cfg.tiles_x;
-    const int cells = shift ? cells_x * ((cfg.tiles_y + 1) / 2) : cfg.tiles_x * cfg.tiles_y;
+    const int cells_x = super_cells(cfg.tiles_x, sx);
+    const int cells = cells_x * super_cells(cfg.tiles_y, sy);
     const int key_bits = bits_for(cells > 1 ? cells - 1 : 1);
     const int npass = radix_num_passes(key_bits);
     {
@@ -1655,17 +1675,17 @@ static gs_status sort_view(int64_t n, const TCfg& cfg, int view, TrainWs& L, Vie
     }
     {
         KernelTimer kt("tile_counts", st);
-        s = launch_tile_counts(pv, n, cfg.tiles_x, cfg.tiles_y, shift, npass, L.pairs + view, cap,
-                               V.tdiff, V.ranges, V.sranges, V.tdig, L.err, st);
+        s = launch_tile_counts(pv, n, cfg.tiles_x, cfg.tiles_y, sx, sy, npass, L.pairs + view,
+                               cap, V.tdiff, V.ranges, V.sranges, V.tdig, L.err, st);
         if (s != GS_OK) return s;
     }
-    const RectPairSource src{V.order, V.goff, V.tfirst, V.tlast, V.rect_d, cells_x, shift};
-    s = radix_sort_rect_pairs(src, V.stotal, cap, key_bits, V.tdig, shift ? V.ssorted : V.svals,
+    const RectPairArgs src{V.order, V.goff, V.tfirst, V.tlast, V.rect_d, cells_x, sx, sy};
+    s = radix_sort_rect_pairs(src, V.stotal, cap, key_bits, V.tdig, super ? V.ssorted : V.svals,
                               V.radix, V.radix_bytes, st, L.err);
     if (s != GS_OK) return s;
-    if (shift) {
+    if (super) {
         KernelTimer kt("tile_filter", st);
-        s = launch_tile_filter(V.ssorted, V.sranges, V.ranges, cfg.tiles_x, cfg.tiles_y,
+        s = launch_tile_filter(V.ssorted, V.sranges, V.ranges, cfg.tiles_x, cfg.tiles_y, sx, sy,
                                L.pairs + view, cap, V.svals, st);
         if (s != GS_OK) return s;
     }

@@ -61,23 +61,32 @@ void launch_project(const GConst& P, int64_t n, int64_t row_begin, int64_t row_e
                     const TCam* cams, int n_views, const TCfg& cfg, const ProjView& pv,
                     int64_t* blk, int64_t blk_stride, uint64_t* touch, float* vis_counts,
                     float* grad2d, cudaStream_t st);
-// Per depth-ordered Gaussian: its rectangle and tile-sort item count (shift 1: 2x2-tile
-// super-tiles, used while Gaussian ids fit 28 bits; shift 0: tiles), and block totals; then
-// the items' offsets from those counts.
-void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int shift,
+// Super-tiles of 2^sx x 2^sy tiles: cells along an axis of `tiles` tiles.
+__host__ __device__ __forceinline__ int super_cells(int tiles, int s) {
+    return (tiles + (1 << s) - 1) >> s;
+}
+// Per depth-ordered Gaussian: its rectangle and tile-sort item count (the 2^sx x 2^sy-tile
+// super-tiles it touches; its tiles with sx = sy = 0), and block totals; then the items'
+// offsets from those counts.
+void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int sx, int sy,
                          ushort4* rect_d, uint32_t* ccnt, int64_t* blk, cudaStream_t st);
 void launch_pair_offsets(const uint32_t* ccnt, int64_t n, const int64_t* blk_offsets,
                          int64_t capacity, uint32_t* goff, uint32_t* tfirst, int64_t tfirst_len,
                          uint32_t* last, int64_t* total, unsigned int* err, cudaStream_t st);
-// ints of the two row-wise difference arrays (tile grid, then 2x2-tile super-tile grid)
+// ints of the two row-wise difference arrays (tile grid, then a super-tile grid of at most
+// the 2x2-tile grid's size)
 int tile_diff_ints(int tiles_x, int tiles_y);
-gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y, int shift,
-                             int npass, const int64_t* pairs, int64_t capacity, int* diff,
+// Tile ranges, super-tile ranges and the tile sort's digit offsets (of the super-tile grid,
+// or of the tile grid with sx = sy = 0) from the projected rectangles.
+gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y, int sx,
+                             int sy, int npass, const int64_t* pairs, int64_t capacity, int* diff,
                              int2* ranges, int2* super_ranges, uint32_t* digit_offsets,
                              unsigned int* err, cudaStream_t st);
+// Super-tile shapes 2x2 (sx = sy = 1) and 4x2 (sx = 2, sy = 1).
 gs_status launch_tile_filter(const uint32_t* super_sorted, const int2* super_ranges,
-                             const int2* ranges, int tiles_x, int tiles_y, const int64_t* pairs,
-                             int64_t capacity, uint32_t* svals, cudaStream_t st);
+                             const int2* ranges, int tiles_x, int tiles_y, int sx, int sy,
+                             const int64_t* pairs, int64_t capacity, uint32_t* svals,
+                             cudaStream_t st);
 constexpr int kProjThreads = 256;
 constexpr int kFilterThreads = 256;  // eight warps share a super-tile in the tile filter
 constexpr int kFilterAhead = 4;      // 32-item steps whose loads the filter issues together

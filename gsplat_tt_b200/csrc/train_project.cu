@@ -238,12 +238,12 @@ k_train_project(GConst P, int64_t n, int64_t row_begin, int64_t row_end,
 }
 
 // The Gaussians in depth order (`order` = ids sorted by depth bits, stable): each one's
-// tile rectangle (rect_d) and its number of tile-sort items (ccnt: the 2x2-tile super-tiles
-// its rectangle touches with shift 1, its tiles with shift 0, 0 without tiles), gathered
-// once, and the per-block item totals for the offset scan.
+// tile rectangle (rect_d) and its number of tile-sort items (ccnt: the 2^sx x 2^sy-tile
+// super-tiles its rectangle touches, its tiles with sx = sy = 0, 0 without tiles),
+// gathered once, and the per-block item totals for the offset scan.
 __global__ void __launch_bounds__(kProjThreads)
 k_sorted_count(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
-               const uint32_t* __restrict__ order, int64_t n, int shift,
+               const uint32_t* __restrict__ order, int64_t n, int sx, int sy,
                ushort4* __restrict__ rect_d, uint32_t* __restrict__ ccnt,
                int64_t* __restrict__ blk) {
     __shared__ int64_t smem[33];
@@ -253,9 +253,9 @@ k_sorted_count(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rec
         const uint32_t g = order[i];
         const ushort4 r = rect[g];
         const uint32_t t = cnt[g];
-        c = (t == 0u || shift == 0)
+        c = (t == 0u || (sx | sy) == 0)
                 ? t
-                : (uint32_t)((r.y >> 1) - (r.x >> 1) + 1) * (uint32_t)((r.w >> 1) - (r.z >> 1) + 1);
+                : (uint32_t)((r.y >> sx) - (r.x >> sx) + 1) * (uint32_t)((r.w >> sy) - (r.z >> sy) + 1);
         rect_d[i] = r;
         ccnt[i] = c;
     }
@@ -297,15 +297,15 @@ k_pair_offsets(const uint32_t* __restrict__ ccnt, int64_t n,
 
 // Per tile row, +1 at column x0 and -1 at column x1 + 1 for every row of every Gaussian's
 // tile rectangle (a row-wise difference array, (tiles_x + 1) x tiles_y ints): a prefix
-// sum along each row then gives the pairs per tile. The same for the 2x2-tile super-tile
-// grid ((sx + 1) x sy ints, after the tile grid's). Summed in shared memory per block
-// when both grids fit `smem_bins`, then added to the global arrays.
+// sum along each row then gives the pairs per tile. The same for the grid of 2^sx x 2^sy
+// super-tiles ((cells_x + 1) x cells_y ints, after the tile grid's). Summed in shared
+// memory per block when both grids fit `smem_bins`, then added to the global arrays.
 __global__ void __launch_bounds__(1024)
 k_tile_diff(const ushort4* __restrict__ rect, const uint32_t* __restrict__ cnt, int64_t n,
-            int tiles_x, int tiles_y, int smem_bins, int* __restrict__ diff) {
+            int tiles_x, int tiles_y, int sx, int sy, int smem_bins, int* __restrict__ diff) {
     extern __shared__ int s_diff[];
     const int gw = tiles_x + 1;
-    const int sgw = (tiles_x + 1) / 2 + 1, sgh = (tiles_y + 1) / 2;
+    const int sgw = super_cells(tiles_x, sx) + 1, sgh = super_cells(tiles_y, sy);
     const int tbins = gw * tiles_y;
     const int bins = tbins + sgw * sgh;
     const bool local = bins <= smem_bins;
@@ -324,9 +324,9 @@ k_tile_diff(const ushort4* __restrict__ rect, const uint32_t* __restrict__ cnt, 
             atomicAdd(&d[y * gw + r.x], 1);
             atomicAdd(&d[y * gw + r.y + 1], -1);
         }
-        for (int y = r.z >> 1; y <= (int)(r.w >> 1); ++y) {
-            atomicAdd(&ds[y * sgw + (r.x >> 1)], 1);
-            atomicAdd(&ds[y * sgw + (r.y >> 1) + 1], -1);
+        for (int y = r.z >> sy; y <= (int)(r.w >> sy); ++y) {
+            atomicAdd(&ds[y * sgw + (r.x >> sx)], 1);
+            atomicAdd(&ds[y * sgw + (r.y >> sx) + 1], -1);
         }
     }
     if (local) {
@@ -461,9 +461,9 @@ void launch_project(const GConst& P, int64_t n, int64_t row_begin, int64_t row_e
 #undef GS_PROJ
 }
 
-// The per-tile lists from the super-tile lists: one block per 2x2-tile super-tile, its
-// items (Gaussian id << 4 | mask of the super-tile's tiles its rectangle covers, in depth
-// order) split into one contiguous part per warp. Each warp counts its part's items per
+// The per-tile lists from the super-tile lists: one block per super-tile of 2^SX x 2^SY
+// tiles, its items (Gaussian id << Q | mask of the super-tile's Q tiles its rectangle
+// covers, in depth order) split into one contiguous part per warp. Each warp counts its part's items per
 // tile, one barrier gives every warp its offsets, and each warp walks its part again 32
 // items at a time, appending each item to the lists of the tiles in its mask, in order (a
 // ballot per tile gives every lane its slot; the lanes of a tile store to consecutive ids).
@@ -471,13 +471,15 @@ void launch_project(const GConst& P, int64_t n, int64_t row_begin, int64_t row_e
 // what a stable sort of all (tile, Gaussian) pairs by tile gives. Loads run kFilterAhead
 // steps ahead. Nothing is written when the view's pairs exceed the capacity (the ranges are
 // empty then).
+template <int SX, int SY>
 __global__ void __launch_bounds__(kFilterThreads)
 k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict__ sranges,
               const int2* __restrict__ ranges, int tiles_x, int tiles_y,
               const int64_t* __restrict__ pairs, int64_t capacity,
               uint32_t* __restrict__ svals) {
     constexpr int NW = kFilterThreads / 32;
-    __shared__ uint32_t s_cnt[NW][4];
+    constexpr int Q = (1 << SX) * (1 << SY);  // tiles per super-tile = mask bits
+    __shared__ uint32_t s_cnt[NW][Q];
     if (*pairs > capacity) return;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int sid = blockIdx.x;
@@ -487,7 +489,9 @@ k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict_
     const int beg = sr.x + (int)((int64_t)len * warp / NW);
     const int end = sr.x + (int)((int64_t)len * (warp + 1) / NW);
     const uint32_t lt = (1u << lane) - 1u;
-    uint32_t c[4] = {0u, 0u, 0u, 0u};
+    uint32_t c[Q];
+#pragma unroll
+    for (int q = 0; q < Q; ++q) c[q] = 0u;
     for (int k0 = beg; k0 < end; k0 += 32 * kFilterAhead) {
         uint32_t v[kFilterAhead];
 #pragma unroll
@@ -498,20 +502,20 @@ k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict_
 #pragma unroll
         for (int a = 0; a < kFilterAhead; ++a)
 #pragma unroll
-            for (int q = 0; q < 4; ++q) c[q] += (v[a] >> q) & 1u;
+            for (int q = 0; q < Q; ++q) c[q] += (v[a] >> q) & 1u;
     }
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < Q; ++q) {
         const uint32_t t = __reduce_add_sync(0xffffffffu, c[q]);
         if (lane == 0) s_cnt[warp][q] = t;
     }
     __syncthreads();
-    const int sx_n = (tiles_x + 1) / 2;
-    const int tx0 = 2 * (sid % sx_n), ty0 = 2 * (sid / sx_n);
-    uint32_t* dst[4];
+    const int sx_n = super_cells(tiles_x, SX);
+    const int tx0 = (sid % sx_n) << SX, ty0 = (sid / sx_n) << SY;
+    uint32_t* dst[Q];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        const int tx = tx0 + (q & 1), ty = ty0 + (q >> 1);
+    for (int q = 0; q < Q; ++q) {
+        const int tx = tx0 + (q & ((1 << SX) - 1)), ty = ty0 + (q >> SX);
         uint32_t off = 0u;
         for (int w = 0; w < warp; ++w) off += s_cnt[w][q];
         // a tile outside the grid is in no item's mask
@@ -526,21 +530,34 @@ k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict_
         }
 #pragma unroll
         for (int a = 0; a < kFilterAhead; ++a) {
+            // an item's mask is a rectangle of the super-tile's tiles, so the lanes holding
+            // tile (row, column) are those covering the row and the column: W + H ballots
+            // instead of one per tile
+            constexpr int W = 1 << SX, H = 1 << SY;
+            constexpr uint32_t kRow = (1u << W) - 1u;
+            uint32_t spread = 0u;  // bit r * W of every row r
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const bool hit = (v[a] >> q) & 1u;
-                const uint32_t b = __ballot_sync(0xffffffffu, hit);
-                if (hit) dst[q][__popc(b & lt)] = v[a] >> 4;
+            for (int r = 0; r < H; ++r) spread |= 1u << (r * W);
+            uint32_t br[H], bc[W];
+#pragma unroll
+            for (int r = 0; r < H; ++r) br[r] = __ballot_sync(0xffffffffu, (v[a] >> (r * W)) & kRow);
+#pragma unroll
+            for (int c = 0; c < W; ++c) bc[c] = __ballot_sync(0xffffffffu, (v[a] >> c) & spread);
+            const uint32_t gid = v[a] >> Q;
+#pragma unroll
+            for (int q = 0; q < Q; ++q) {
+                const uint32_t b = br[q / W] & bc[q % W];
+                if ((b >> lane) & 1u) dst[q][__popc(b & lt)] = gid;
                 dst[q] += __popc(b);
             }
         }
     }
 }
 
-void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int shift,
+void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int sx, int sy,
                          ushort4* rect_d, uint32_t* ccnt, int64_t* blk, cudaStream_t st) {
     k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, pv.rect, order, n,
-                                                                    shift, rect_d, ccnt, blk);
+                                                                    sx, sy, rect_d, ccnt, blk);
 }
 
 void launch_pair_offsets(const uint32_t* ccnt, int64_t n, const int64_t* blk_offsets,
@@ -550,14 +567,19 @@ void launch_pair_offsets(const uint32_t* ccnt, int64_t n, const int64_t* blk_off
         ccnt, n, blk_offsets, capacity, goff, tfirst, tfirst_len, last, total, err);
 }
 
+// Sized for the finest super-tile grid (2x2 tiles); coarser grids use less of it.
 int tile_diff_ints(int tiles_x, int tiles_y) {
-    return (tiles_x + 1) * tiles_y + ((tiles_x + 1) / 2 + 1) * ((tiles_y + 1) / 2);
+    return (tiles_x + 1) * tiles_y + (super_cells(tiles_x, 1) + 1) * super_cells(tiles_y, 1);
 }
 
-gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y, int shift,
-                             int npass, const int64_t* pairs, int64_t capacity, int* diff,
+gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int tiles_y, int sx,
+                             int sy, int npass, const int64_t* pairs, int64_t capacity, int* diff,
                              int2* ranges, int2* super_ranges, uint32_t* digit_offsets,
                              unsigned int* err, cudaStream_t st) {
+    // the direct (Gaussian, tile) sort (sx = sy = 0) sorts by tiles; the super-tile ranges
+    // it does not use are still formed on the 2x2 grid
+    const bool direct = (sx | sy) == 0;
+    if (direct) sx = sy = 1;
     const int bins = tile_diff_ints(tiles_x, tiles_y);
     constexpr int kSmemBins = 40960;  // 160 KB
     const size_t smem = bins <= kSmemBins ? (size_t)bins * sizeof(int) : 0;
@@ -565,27 +587,39 @@ gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int til
     GS_CUDA_CHECK(cudaFuncSetAttribute(k_tile_diff, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)(kSmemBins * sizeof(int))));
     const int grid = (int)std::min<int64_t>(2 * kNumSMs, div_up(n, 1024));
-    k_tile_diff<<<grid, 1024, smem, st>>>(pv.rect, pv.cnt, n, tiles_x, tiles_y,
+    k_tile_diff<<<grid, 1024, smem, st>>>(pv.rect, pv.cnt, n, tiles_x, tiles_y, sx, sy,
                                           smem ? kSmemBins : 0, diff);
     GS_CHECK_LAUNCH();
-    // block 0: tile ranges; block 1: super-tile ranges; the sort's digit
-    // offsets from the grid it sorts by (super-tiles with shift 1, tiles with shift 0)
-    const int sx_n = (tiles_x + 1) / 2, sy_n = (tiles_y + 1) / 2;
-    const GridFinish tiles{diff, tiles_x, tiles_y, shift ? 0 : npass, ranges,
-                           shift ? nullptr : digit_offsets, err};
-    const GridFinish supers{diff + (tiles_x + 1) * tiles_y, sx_n, sy_n, shift ? npass : 0,
-                            super_ranges, shift ? digit_offsets : nullptr, nullptr};
+    // block 0: tile ranges; block 1: super-tile ranges; the sort's digit offsets from the
+    // grid it sorts by
+    const int sx_n = super_cells(tiles_x, sx), sy_n = super_cells(tiles_y, sy);
+    const GridFinish tiles{diff, tiles_x, tiles_y, direct ? npass : 0, ranges,
+                           direct ? digit_offsets : nullptr, err};
+    const GridFinish supers{diff + (tiles_x + 1) * tiles_y, sx_n, sy_n, direct ? 0 : npass,
+                            super_ranges, direct ? nullptr : digit_offsets, nullptr};
     k_tile_finish<<<2, 1024, 0, st>>>(tiles, supers, pairs, capacity);
     GS_CHECK_LAUNCH();
     return GS_OK;
 }
 
 gs_status launch_tile_filter(const uint32_t* super_sorted, const int2* super_ranges,
-                             const int2* ranges, int tiles_x, int tiles_y, const int64_t* pairs,
-                             int64_t capacity, uint32_t* svals, cudaStream_t st) {
-    const int nsuper = ((tiles_x + 1) / 2) * ((tiles_y + 1) / 2);
-    k_tile_filter<<<nsuper, kFilterThreads, 0, st>>>(super_sorted, super_ranges, ranges, tiles_x,
-                                                     tiles_y, pairs, capacity, svals);
+                             const int2* ranges, int tiles_x, int tiles_y, int sx, int sy,
+                             const int64_t* pairs, int64_t capacity, uint32_t* svals,
+                             cudaStream_t st) {
+    const int nsuper = super_cells(tiles_x, sx) * super_cells(tiles_y, sy);
+#define GS_FILTER(SX_, SY_)                                                                  \
+    k_tile_filter<SX_, SY_><<<nsuper, kFilterThreads, 0, st>>>(super_sorted, super_ranges,   \
+                                                               ranges, tiles_x, tiles_y,     \
+                                                               pairs, capacity, svals)
+    if (sx == 1 && sy == 1) {
+        GS_FILTER(1, 1);
+    } else if (sx == 2 && sy == 1) {
+        GS_FILTER(2, 1);
+    } else {
+        set_error("tile filter: unsupported super-tile shape %dx%d", 1 << sx, 1 << sy);
+        return GS_ERR_ARG;
+    }
+#undef GS_FILTER
     GS_CHECK_LAUNCH();
     return GS_OK;
 }

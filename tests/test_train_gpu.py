@@ -81,6 +81,17 @@ def test_project_view_bit_exact(deg, tile, H, W):
     np.testing.assert_array_equal(ranges, exp)
 
 
+@pytest.mark.parametrize("cells", ["4x2", "2x2", "1x1"])
+def test_tile_lists_bit_exact_for_every_sort_cell_shape(cells, monkeypatch):
+    """The per-tile lists (sorted ids) and ranges are the reference's stable (tile, depth,
+    id) order whichever cells the tile sort sorts by: 4x2-tile super-tiles (the default
+    below 2^24 Gaussians), 2x2-tile super-tiles (below 2^28) or the (Gaussian, tile) pairs
+    themselves (GS_TILE_SORT_CELLS selects the shape; the library reads it on every call).
+    Odd tile counts leave partial super-tiles on the right and bottom edges."""
+    monkeypatch.setenv("GS_TILE_SORT_CELLS", cells)
+    test_project_view_bit_exact(3, 16, 168, 200)
+
+
 def run_step(params, deg, tile, cams, targets, ssim=True, lam=0.2, **kw):
     import torch
     H, W = cams[0][2], cams[0][3]
