@@ -217,10 +217,12 @@ def run_sort(args, rank, world, local) -> dict:
     with ClockSampler(local) as clk:
         barrier(world)
         torch.cuda.synchronize()
+        l0 = lib.gs_launch_count()
         e0.record()
         for _ in range(args.steps):
             step()
         e1.record()
+        launches = lib.gs_launch_count() - l0
         torch.cuda.synchronize()
         barrier(world)
     check(lib.gs_workspace_error(ws.data_ptr(), st.cuda_stream))
@@ -269,7 +271,8 @@ def run_sort(args, rank, world, local) -> dict:
         "config": sort_config(world),
         "e2e": {"value": sum_over_ranks(float(n), world) / (e2e_ms / 1e3), "unit": "pairs/s",
                 "h2d_bytes_per_step": 12 * n, "d2h_bytes_per_step": 4 * n},
-        "gpu_launches": int(args.steps * (2 + (SORT_KEY_BITS + 7) // 8)),
+        # the library's kernels launched in the timed region, summed over the ranks
+        "gpu_launches": int(sum_over_ranks(float(launches), world)),
         "roofline": {"bound": "hbm", "kernel": "k_onesweep_pass<u64>", "achieved": achieved,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved / peaks["hbm_gbs"],

@@ -66,6 +66,7 @@ _sig("gs_sort_and_bin", status, vp, vp, vp, i64, i32, i32, vp, vp, vp, sz, vp)
 _sig("gs_sort_and_bin_workspace_size", sz, i64, i32, i32)
 _sig("gs_sort_pairs", status, vp, vp, i64, i32, vp, vp, vp, sz, vp)
 _sig("gs_sort_pairs_workspace_size", sz, i64, i32)
+_sig("gs_launch_count", i64)
 _sig("gs_timing_enable", None, i32)
 _sig("gs_timing_reset", None)
 _sig("gs_timing_report", i32, ctypes.c_char_p, sz, ctypes.POINTER(ctypes.c_double),

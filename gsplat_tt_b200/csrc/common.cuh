@@ -32,8 +32,12 @@ enum DeviceError : unsigned int {
         }                                                                          \
     } while (0)
 
+// Every kernel launch of the library is followed by exactly one GS_CHECK_LAUNCH, which
+// also counts it (gs_launch_count).
+void count_launch();
 #define GS_CHECK_LAUNCH()                                                          \
     do {                                                                           \
+        ::gs::count_launch();                                                      \
         cudaError_t err__ = cudaGetLastError();                                    \
         if (err__ != cudaSuccess) {                                                \
             ::gs::set_error("%s:%d: kernel launch: %s", __FILE__, __LINE__,        \

@@ -48,6 +48,7 @@ extern "C" gs_status gs_workspace_error(const void* workspace, void* stream) {
 // Off by default. When enabled, launch sites wrapped in gs::KernelTimer record a CUDA
 // event pair on the launching stream; gs_timing_report() synchronises those events
 // and returns per-kernel totals. bench.py uses it to time the dominant kernel live.
+#include <atomic>
 #include <map>
 #include <string>
 #include <vector>
@@ -88,7 +89,12 @@ KernelTimer::~KernelTimer() {
     t_timing.marks.push_back({name_, {(cudaEvent_t)start_, end}});
 }
 
+static std::atomic<int64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 }  // namespace gs
+
+extern "C" int64_t gs_launch_count(void) { return gs::g_launches.load(std::memory_order_relaxed); }
 
 extern "C" void gs_timing_enable(int32_t on) {
     gs::t_timing.enabled = on != 0;

@@ -167,7 +167,7 @@ def ranks_list(x: float, world: int) -> list[float]:
 
 
 def run(args, rank: int, world: int, local: int) -> dict:
-    from bench import ClockSampler, barrier, max_over_ranks, measured_peaks  # noqa: E402
+    from bench import ClockSampler, barrier, max_over_ranks, measured_peaks, sum_over_ranks  # noqa: E402
     name = config_name()
     c = scenes.CONFIGS[name]
     dev = torch.device("cuda", local)
@@ -206,10 +206,12 @@ def run(args, rank: int, world: int, local: int) -> dict:
     with ClockSampler(local) as clk:
         barrier(world)
         torch.cuda.synchronize()
+        l0 = lib.gs_launch_count()
         e0.record()
         for _ in range(args.steps):
             tr.step(cams, targets, next_cams=nxt)
         e1.record()
+        launches = lib.gs_launch_count() - l0
         torch.cuda.synchronize()
         barrier(world)
     if lib.gs_workspace_error(tr.ws.data_ptr(), st.cuda_stream) != 0:
@@ -279,7 +281,8 @@ def run(args, rank: int, world: int, local: int) -> dict:
         "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
                 "h2d_bytes_per_step": int(sum(t.size * 4 for t in targets_host)),
                 "d2h_bytes_per_step": 4},
-        "gpu_launches": int(sum(v["launches_per_step"] for v in per_kernel.values())),
+        # the library's kernels launched in the timed region, summed over the ranks
+        "gpu_launches": int(sum_over_ranks(float(launches), world)),
         "ms_per_step_by_rank": ms_by_rank,
         "pairs_per_view": pairs, "loss": loss_now,
         "kernels": per_kernel,

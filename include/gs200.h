@@ -64,6 +64,9 @@ gs_status gs_debug_logf_host(const float* x, float* y, int64_t n, void* stream);
  * instrumented kernel launch. gs_timing_report synchronises the recorded events and
  * writes up to max_kernels entries: kernel names ('\n'-separated) into `names`, total
  * milliseconds and launch counts; it returns the number of entries. */
+/* Kernels the library has launched in this process, on every device and thread (for
+ * benchmarks: launches inside a timed region). */
+int64_t gs_launch_count(void);
 void gs_timing_enable(int32_t on);
 void gs_timing_reset(void);
 int32_t gs_timing_report(char* names, size_t names_len, double* total_ms, int64_t* launches,
