@@ -88,7 +88,10 @@ gs_status launch_tile_filter(const uint32_t* super_sorted, const int2* super_ran
                              const int64_t* pairs, int64_t capacity, uint32_t* svals,
                              cudaStream_t st);
 constexpr int kProjThreads = 256;
-constexpr int kFilterThreads = 256;  // eight warps share a super-tile in the tile filter
+#ifndef GS_FILTER_THREADS
+#define GS_FILTER_THREADS 256
+#endif
+constexpr int kFilterThreads = GS_FILTER_THREADS;  // warps x 32 sharing a super-tile in the tile filter
 constexpr int kFilterAhead = 4;      // 32-item steps whose loads the filter issues together
 constexpr int kMaxViews = 64;  // views per training step (one bit each in the touched mask)
 constexpr int kMaxTileRows = 4096;  // tile rows the tile-count kernel handles

@@ -242,7 +242,7 @@ k_train_project(GConst P, int64_t n, int64_t row_begin, int64_t row_end,
 // super-tiles its rectangle touches, its tiles with sx = sy = 0, 0 without tiles),
 // gathered once, and the per-block item totals for the offset scan.
 __global__ void __launch_bounds__(kProjThreads)
-k_sorted_count(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rect,
+k_sorted_count(const ushort4* __restrict__ rect,
                const uint32_t* __restrict__ order, int64_t n, int sx, int sy,
                ushort4* __restrict__ rect_d, uint32_t* __restrict__ ccnt,
                int64_t* __restrict__ blk) {
@@ -252,7 +252,9 @@ k_sorted_count(const uint32_t* __restrict__ cnt, const ushort4* __restrict__ rec
     if (i < n) {
         const uint32_t g = order[i];
         const ushort4 r = rect[g];
-        const uint32_t t = cnt[g];
+        // the tile count follows from the rectangle (x1 < x0 for a Gaussian without tiles),
+        // so one 8-byte gather per Gaussian suffices
+        const uint32_t t = (r.y >= r.x) ? (uint32_t)(r.y - r.x + 1) * (uint32_t)(r.w - r.z + 1) : 0u;
         c = (t == 0u || (sx | sy) == 0)
                 ? t
                 : (uint32_t)((r.y >> sx) - (r.x >> sx) + 1) * (uint32_t)((r.w >> sy) - (r.z >> sy) + 1);
@@ -556,7 +558,7 @@ k_tile_filter(const uint32_t* __restrict__ super_sorted, const int2* __restrict_
 
 void launch_sorted_count(const ProjView& pv, const uint32_t* order, int64_t n, int sx, int sy,
                          ushort4* rect_d, uint32_t* ccnt, int64_t* blk, cudaStream_t st) {
-    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.cnt, pv.rect, order, n,
+    k_sorted_count<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pv.rect, order, n,
                                                                     sx, sy, rect_d, ccnt, blk);
 }
 
