@@ -1465,7 +1465,6 @@ static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int 
     L.pv.dkey = ws.template take<uint32_t>(nv);
     L.pv.dsort = ws.template take<uint32_t>(nv);
     L.pv.rect = ws.template take<ushort4>(nv);
-    L.pv.cnt = ws.template take<uint32_t>(nv);
     L.nlanes = std::min(kLanes, n_views);
     for (int l = 0; l < L.nlanes; ++l) {
         ViewLane& V = L.lane[l];
@@ -1876,7 +1875,7 @@ __global__ void k_export_projection(ProjView pv, int64_t n, float* __restrict__ 
     colors[3 * g + 2] = pv.p2[g];
     depth[g] = __uint_as_float(pv.dkey[g]);
     const ushort4 r = pv.rect[g];
-    const bool any = pv.cnt[g] > 0;
+    const bool any = r.y >= r.x;  // x1 < x0: no tiles
     rects[4 * g] = any ? r.x : 0;
     rects[4 * g + 1] = any ? r.y : -1;
     rects[4 * g + 2] = any ? r.z : 0;

@@ -37,14 +37,12 @@ struct ProjView {
     float* p2;
     uint32_t* dkey;   // bits of the camera-space depth
     uint32_t* dsort;  // depth-sort key: dkey, or 0xffffffff for a Gaussian without pairs
-    ushort4* rect;    // inclusive tile rectangle x0, x1, y0, y1
-    uint32_t* cnt;    // tiles in the rectangle (0 = no pairs)
+    ushort4* rect;    // inclusive tile rectangle x0, x1, y0, y1 (x1 < x0: no pairs)
 
     // View v's records inside the [view][n] arrays.
     ProjView view(int v, int64_t n) const {
         const size_t o = (size_t)v * n;
-        return ProjView{p0 + o, p1 + o, p2 + o, dkey ? dkey + o : nullptr, dsort + o, rect + o,
-                        cnt + o};
+        return ProjView{p0 + o, p1 + o, p2 + o, dkey ? dkey + o : nullptr, dsort + o, rect + o};
     }
 };
 

@@ -210,7 +210,6 @@ k_train_project(GConst P, int64_t n, int64_t row_begin, int64_t row_end,
             if (pv.dkey != nullptr) pv.dkey[o] = __float_as_uint(z);
             pv.dsort[o] = count > 0 ? __float_as_uint(z) : 0xffffffffu;
             pv.rect[o] = rc;
-            pv.cnt[o] = count;
             if (visible) nvis += 1.0f;
             if (count > 0) {
                 touched |= 1ull << v;
@@ -303,7 +302,7 @@ k_pair_offsets(const uint32_t* __restrict__ ccnt, int64_t n,
 // super-tiles ((cells_x + 1) x cells_y ints, after the tile grid's). Summed in shared
 // memory per block when both grids fit `smem_bins`, then added to the global arrays.
 __global__ void __launch_bounds__(1024)
-k_tile_diff(const ushort4* __restrict__ rect, const uint32_t* __restrict__ cnt, int64_t n,
+k_tile_diff(const ushort4* __restrict__ rect, int64_t n,
             int tiles_x, int tiles_y, int sx, int sy, int smem_bins, int* __restrict__ diff) {
     extern __shared__ int s_diff[];
     const int gw = tiles_x + 1;
@@ -319,9 +318,8 @@ k_tile_diff(const ushort4* __restrict__ rect, const uint32_t* __restrict__ cnt, 
     }
     for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < n;
          g += (int64_t)gridDim.x * blockDim.x) {
-        const uint32_t c = cnt[g];
         const ushort4 r = rect[g];
-        if (c == 0u) continue;
+        if (r.y < r.x) continue;  // no tiles
         for (int y = r.z; y <= (int)r.w; ++y) {
             atomicAdd(&d[y * gw + r.x], 1);
             atomicAdd(&d[y * gw + r.y + 1], -1);
@@ -588,8 +586,13 @@ gs_status launch_tile_counts(const ProjView& pv, int64_t n, int tiles_x, int til
     GS_CUDA_CHECK(cudaMemsetAsync(diff, 0, (size_t)bins * sizeof(int), st));
     GS_CUDA_CHECK(cudaFuncSetAttribute(k_tile_diff, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)(kSmemBins * sizeof(int))));
-    const int grid = (int)std::min<int64_t>(2 * kNumSMs, div_up(n, 1024));
-    k_tile_diff<<<grid, 1024, smem, st>>>(pv.rect, pv.cnt, n, tiles_x, tiles_y, sx, sy,
+#ifndef GS_TILE_DIFF_BLOCKS_PER_SM
+#define GS_TILE_DIFF_BLOCKS_PER_SM 2
+#endif
+    // every block merges its shared copy into the global arrays with atomics, so fewer
+    // blocks mean fewer merges
+    const int grid = (int)std::min<int64_t>(GS_TILE_DIFF_BLOCKS_PER_SM * kNumSMs, div_up(n, 1024));
+    k_tile_diff<<<grid, 1024, smem, st>>>(pv.rect, n, tiles_x, tiles_y, sx, sy,
                                           smem ? kSmemBins : 0, diff);
     GS_CHECK_LAUNCH();
     // block 0: tile ranges; block 1: super-tile ranges; the sort's digit offsets from the

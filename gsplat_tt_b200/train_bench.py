@@ -57,8 +57,8 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, launches_per_step
     * train_project (all of the rank's views in one pass over the rows; the step's
       launches split the N rows -- one launch, or one per row chunk when the next step's
       projection follows the multicast update chunk by chunk): the SH3 parameters once
-      (236 B per Gaussian) and per view the 52 B record (mean 8, conic 12, colour 12,
-      opacity 4, depth key 4, rectangle 8, pair count 4);
+      (236 B per Gaussian) and per view the 48 B record (mean 8, conic 12, colour 12,
+      opacity 4, depth key 4, rectangle 8);
     * radix_pass32 (one pass of the depth sort over N): 4 B key + 4 B value read and written;
     * tile_filter (the per-tile lists from the sorted super-tile lists): 4 B per (Gaussian,
       tile) pair written, a lower bound (its reads are per super-tile item);
@@ -76,7 +76,7 @@ def _kernel_bytes(name: str, n: int, views: int, pairs: float, launches_per_step
     passes of the super-tile sort (tile_sort_emit, tile_sort_pass) move per super-tile item
     bytes whose count the timer does not see, and have no entry either."""
     if name == "train_project":
-        return (n * 236.0 + views * n * 52.0) / max(launches_per_step, 1.0)
+        return (n * 236.0 + views * n * 48.0) / max(launches_per_step, 1.0)
     if name == "radix_pass32":
         return n * 16.0
     if name == "tile_filter":

@@ -36,7 +36,7 @@ def test_summary_picks_largest_hbm_kernel_and_scales_traffic():
     assert "raster_bwd 37.1 ms" in roof["note"]
     assert per_kernel["tile_filter"]["algorithmic_bytes"] == pytest.approx(pairs * 4)
     assert sort["ms_per_step"] == pytest.approx((14.8 + 16.0 + 8.8 + 6.0) / 2)
-    assert per_kernel["train_project"]["algorithmic_bytes"] == pytest.approx(n * 236 + views * n * 52)
+    assert per_kernel["train_project"]["algorithmic_bytes"] == pytest.approx(n * 236 + views * n * 48)
 
 
 def test_summary_without_traffic_entry():
@@ -58,7 +58,7 @@ def test_chunked_and_owner_sharded_launches_are_charged_their_own_rows():
     assert pb["frac_hbm"] < 1.0
     # the next step's projection, one launch per row chunk behind the update
     tp = per_kernel["train_project"]
-    assert tp["algorithmic_bytes"] == pytest.approx((n * 236.0 + views * n * 52.0) / 4)
+    assert tp["algorithmic_bytes"] == pytest.approx((n * 236.0 + views * n * 48.0) / 4)
     assert tp["frac_hbm"] < 1.0
     mc = per_kernel["sparse_adam_mc"]
     assert "frac_hbm" not in mc
