@@ -58,25 +58,32 @@ __device__ __forceinline__ uint32_t ld_volatile(const uint32_t* p) {
 __device__ __forceinline__ void st_volatile(uint32_t* p, uint32_t v) { *(volatile uint32_t*)p = v; }
 
 // Items from global key / value arrays; vals == null stands for the item's index (iota).
+// A source fills a thread's keys first (load) and its values only after the ranking and
+// the look-back (load_vals), so the values do not hold registers across them.
 template <typename KeyT>
 struct GlobalSource {
     const KeyT* keys;
     const uint32_t* vals;
+    static constexpr bool kValsInSmem = false;  // load_vals reads global memory only
 
     __device__ __forceinline__ void load(SortSmem<KeyT>& S, uint32_t tile, int64_t base, int valid,
-                                         int64_t n, KeyT pad, KeyT (&key)[kSortItems],
-                                         uint32_t (&val)[kSortItems]) const {
+                                         int64_t n, KeyT pad, KeyT (&key)[kSortItems]) const {
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
         for (int j = 0; j < kSortItems; ++j) {
             const int li = warp * (kSortItems * 32) + j * 32 + lane;
-            if (li < valid) {
-                key[j] = keys[base + li];
-                val[j] = vals ? vals[base + li] : (uint32_t)(base + li);
-            } else {  // pads get the largest digit so they rank after every real item
-                key[j] = pad;
-                val[j] = 0;
-            }
+            // pads get the largest digit so they rank after every real item
+            key[j] = (li < valid) ? keys[base + li] : pad;
+        }
+    }
+
+    __device__ __forceinline__ void load_vals(const SortSmem<KeyT>& S, int64_t base, int valid,
+                                              uint32_t (&val)[kSortItems]) const {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+        for (int j = 0; j < kSortItems; ++j) {
+            const int li = warp * (kSortItems * 32) + j * 32 + lane;
+            val[j] = (li < valid) ? (vals ? vals[base + li] : (uint32_t)(base + li)) : 0u;
         }
     }
 };
@@ -86,8 +93,19 @@ struct GlobalSource {
 // it is at most n_host; a larger *n_dev (a capacity overflow, which the caller reports)
 // sorts nothing, so no write can land past the caller's buffers. keys_out may be null on
 // the last pass (values only).
+// Resident blocks per SM the register budget is set for: 64-bit keys 3 (their shared
+// staging allows no more), 32-bit keys from global arrays GS_SORT_BLOCKS_U32, 32-bit keys
+// from a generating source (more shared memory) 4.
+#ifndef GS_SORT_BLOCKS_U32
+#define GS_SORT_BLOCKS_U32 4
+#endif
 template <typename KeyT, typename Src>
-__global__ void __launch_bounds__(kSortThreads, sizeof(KeyT) == 4 ? 4 : 3)
+constexpr int sort_min_blocks() {
+    return sizeof(KeyT) == 8 ? 3 : (Src::kValsInSmem ? 4 : GS_SORT_BLOCKS_U32);
+}
+
+template <typename KeyT, typename Src>
+__global__ void __launch_bounds__(kSortThreads, (sort_min_blocks<KeyT, Src>()))
 k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
                 const int64_t* __restrict__ n_dev, int64_t n_host, int shift, int digit_bits,
                 const uint32_t* __restrict__ digit_offsets, uint32_t* __restrict__ lookback,
@@ -107,9 +125,8 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
     const int valid = (int)min((int64_t)kTileItems, n - base);
 
     KeyT key[kSortItems];
-    uint32_t val[kSortItems];
     const uint32_t dmax = (1u << digit_bits) - 1u;  // pads' digit
-    src.load(S, tile, base, valid, n, (KeyT)dmax << shift, key, val);
+    src.load(S, tile, base, valid, n, (KeyT)dmax << shift, key);
 #define GS_DIGIT(k) ((uint32_t)((k) >> shift) & dmax)
 
     // Warp-level multisplit: rank of each item among the warp's items of its digit.
@@ -219,13 +236,22 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
     }
     __syncthreads();
 
-    // Scatter into shared memory in digit-sorted order.
+    // Scatter into shared memory in digit-sorted order: the keys, then the values, which are
+    // loaded only now (each item's slot stays in rank[]).
 #pragma unroll
     for (int j = 0; j < kSortItems; ++j) {
         const uint32_t dj = GS_DIGIT(key[j]);
-        const uint32_t pos = S.local_off[dj] + S.warp_hist[warp][dj] + rank[j];
-        S.keys[pos] = key[j];
-        S.vals[pos] = val[j];
+        rank[j] += S.local_off[dj] + S.warp_hist[warp][dj];
+        S.keys[rank[j]] = key[j];
+    }
+    {
+        uint32_t val[kSortItems];
+        src.load_vals(S, base, valid, val);
+        // a source that staged its values in S.vals: every thread has read its own before
+        // any slot is overwritten
+        if (Src::kValsInSmem) __syncthreads();
+#pragma unroll
+        for (int j = 0; j < kSortItems; ++j) S.vals[rank[j]] = val[j];
     }
     __syncthreads();
 

@@ -105,6 +105,10 @@ gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64
     const size_t smem = sizeof(SortSmem<KeyT>);
     GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<KeyT, GlobalSource<KeyT>>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    // all of the SM's unified memory as shared memory: the passes are occupancy-bound and
+    // read their inputs once
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<KeyT, GlobalSource<KeyT>>,
+                                       cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     const KeyT* kin = keys;
     const uint32_t* vin = vals;
     const unsigned int grid = (unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1);
@@ -188,6 +192,8 @@ gs_status radix_sort_rect_pairs(const RectPairArgs& src, const int64_t* n_dev, i
     const size_t smem = sizeof(SortSmem<uint32_t>);
     GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, GlobalSource<uint32_t>>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, GlobalSource<uint32_t>>,
+                                       cudaFuncAttributePreferredSharedMemoryCarveout, 100));
     const unsigned int grid = (unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1);
     {
         KernelTimer kt("tile_sort_emit", st);

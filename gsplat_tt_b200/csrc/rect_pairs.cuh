@@ -64,10 +64,21 @@ struct RectPairSource : RectPairArgs {
         }
     }
 
+    static constexpr bool kValsInSmem = true;  // load_vals reads the staged S.vals
+
+    __device__ __forceinline__ void load_vals(const SortSmem<uint32_t>& S, int64_t base, int valid,
+                                              uint32_t (&val)[kSortItems]) const {
+        const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+        for (int j = 0; j < kSortItems; ++j) {
+            const int li = warp * (kSortItems * 32) + j * 32 + lane;
+            val[j] = (li < valid) ? S.vals[li] : 0u;
+        }
+    }
+
     __device__ __forceinline__ void load(SortSmem<uint32_t>& S, uint32_t tile, int64_t base,
                                          int valid, int64_t n, uint32_t pad,
-                                         uint32_t (&key)[kSortItems],
-                                         uint32_t (&val)[kSortItems]) const {
+                                         uint32_t (&key)[kSortItems]) const {
         // Queue of long runs, double-buffered by chunk parity: chunk k writes buffer k & 1
         // before its first barrier, and chunk k + 2 (the next writer of that buffer) starts
         // only after every warp has passed chunk k + 1's first barrier. Each counter is
@@ -133,13 +144,9 @@ struct RectPairSource : RectPairArgs {
 #pragma unroll
         for (int j = 0; j < kSortItems; ++j) {
             const int li = warp * (kSortItems * 32) + j * 32 + lane;
-            if (li < valid) {
-                key[j] = S.keys[li];
-                val[j] = S.vals[li];
-            } else {  // pads get the largest digit so they rank after every real item
-                key[j] = pad;
-                val[j] = 0u;
-            }
+            // pads get the largest digit so they rank after every real item; the values stay
+            // in S.vals until load_vals
+            key[j] = (li < valid) ? S.keys[li] : pad;
         }
     }
 };
