@@ -586,7 +586,10 @@ struct SsimBwdSmem {
 // channel mu_x, mu_y, E_xx, E_yy, E_xy (zero padding), S, and the maps d_mu, d_xx, d_xy
 // (scaled by -lambda / n; planar [3][H][W]) that the second pass filters. Sums |x - y|
 // and S. The image patch is read once for all three channels, row segments contiguous.
-__global__ void __launch_bounds__(256)
+#ifndef GS_SSIM_FWD_BLOCKS
+#define GS_SSIM_FWD_BLOCKS 1
+#endif
+__global__ void __launch_bounds__(256, GS_SSIM_FWD_BLOCKS)
 k_ssim_fwd(const float* __restrict__ img, const float* __restrict__ tgt, LossCfg L,
            float* __restrict__ dmu, float* __restrict__ dxx, float* __restrict__ dxy,
            double* __restrict__ acc) {

@@ -90,7 +90,10 @@ constexpr int kProjThreads = 256;
 #define GS_FILTER_THREADS 256
 #endif
 constexpr int kFilterThreads = GS_FILTER_THREADS;  // warps x 32 sharing a super-tile in the tile filter
-constexpr int kFilterAhead = 4;      // 32-item steps whose loads the filter issues together
+#ifndef GS_FILTER_AHEAD
+#define GS_FILTER_AHEAD 8
+#endif
+constexpr int kFilterAhead = GS_FILTER_AHEAD;  // 32-item steps whose loads the filter issues together
 constexpr int kMaxViews = 64;  // views per training step (one bit each in the touched mask)
 constexpr int kMaxTileRows = 4096;  // tile rows the tile-count kernel handles
 
