@@ -25,7 +25,20 @@ constexpr int kRadix = 1 << kRadixBits;
 constexpr int kSortThreads = 256;
 constexpr int kSortWarps = kSortThreads / 32;
 constexpr int kSortItems = 16;
-constexpr int kTileItems = kSortThreads * kSortItems;  // 4096
+constexpr int kTileItems = kSortThreads * kSortItems;  // 4096 (32-bit keys)
+// Items per thread and per tile by key width: 64-bit keys may take fewer per thread, which
+// shrinks their shared staging so more blocks fit an SM.
+#ifndef GS_SORT_ITEMS_U64
+#define GS_SORT_ITEMS_U64 16
+#endif
+template <typename KeyT>
+struct SortShape {
+    static constexpr int kItems = sizeof(KeyT) == 8 ? GS_SORT_ITEMS_U64 : kSortItems;
+    static constexpr int kTile = kSortThreads * kItems;
+};
+__host__ __device__ constexpr int sort_tile_items(int key_bytes) {
+    return key_bytes == 8 ? SortShape<uint64_t>::kTile : SortShape<uint32_t>::kTile;
+}
 constexpr unsigned int kFlagAgg = 1u << 30;
 constexpr unsigned int kFlagInc = 2u << 30;
 constexpr unsigned int kValueMask = (1u << 30) - 1;
@@ -43,8 +56,8 @@ static_assert(kSortThreads == kRadix, "one thread per digit in the look-back");
 
 template <typename KeyT>
 struct SortSmem {
-    KeyT keys[kTileItems];
-    uint32_t vals[kTileItems];
+    KeyT keys[SortShape<KeyT>::kTile];
+    uint32_t vals[SortShape<KeyT>::kTile];
     uint32_t warp_hist[kSortWarps][kRadix];
     uint32_t local_off[kRadix];
     uint32_t gbase[kRadix];  // digit's global offset minus its block-local offset
@@ -66,23 +79,25 @@ struct GlobalSource {
     const uint32_t* vals;
     static constexpr bool kValsInSmem = false;  // load_vals reads global memory only
 
+    static constexpr int kItems = SortShape<KeyT>::kItems;
+
     __device__ __forceinline__ void load(SortSmem<KeyT>& S, uint32_t tile, int64_t base, int valid,
-                                         int64_t n, KeyT pad, KeyT (&key)[kSortItems]) const {
+                                         int64_t n, KeyT pad, KeyT (&key)[kItems]) const {
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-        for (int j = 0; j < kSortItems; ++j) {
-            const int li = warp * (kSortItems * 32) + j * 32 + lane;
+        for (int j = 0; j < kItems; ++j) {
+            const int li = warp * (kItems * 32) + j * 32 + lane;
             // pads get the largest digit so they rank after every real item
             key[j] = (li < valid) ? keys[base + li] : pad;
         }
     }
 
     __device__ __forceinline__ void load_vals(const SortSmem<KeyT>& S, int64_t base, int valid,
-                                              uint32_t (&val)[kSortItems]) const {
+                                              uint32_t (&val)[kItems]) const {
         const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 #pragma unroll
-        for (int j = 0; j < kSortItems; ++j) {
-            const int li = warp * (kSortItems * 32) + j * 32 + lane;
+        for (int j = 0; j < kItems; ++j) {
+            const int li = warp * (kItems * 32) + j * 32 + lane;
             val[j] = (li < valid) ? (vals ? vals[base + li] : (uint32_t)(base + li)) : 0u;
         }
     }
@@ -99,9 +114,12 @@ struct GlobalSource {
 #ifndef GS_SORT_BLOCKS_U32
 #define GS_SORT_BLOCKS_U32 4
 #endif
+#ifndef GS_SORT_BLOCKS_U64
+#define GS_SORT_BLOCKS_U64 3
+#endif
 template <typename KeyT, typename Src>
 constexpr int sort_min_blocks() {
-    return sizeof(KeyT) == 8 ? 3 : (Src::kValsInSmem ? 4 : GS_SORT_BLOCKS_U32);
+    return sizeof(KeyT) == 8 ? GS_SORT_BLOCKS_U64 : (Src::kValsInSmem ? 4 : GS_SORT_BLOCKS_U32);
 }
 
 template <typename KeyT, typename Src>
@@ -120,11 +138,12 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
     for (int i = tid; i < kSortWarps * kRadix; i += kSortThreads) (&S.warp_hist[0][0])[i] = 0;
     __syncthreads();
     const uint32_t tile = S.tile;
-    const int64_t base = (int64_t)tile * kTileItems;
+    constexpr int kItems = SortShape<KeyT>::kItems, kTile = SortShape<KeyT>::kTile;
+    const int64_t base = (int64_t)tile * kTile;
     if (base >= n) return;
-    const int valid = (int)min((int64_t)kTileItems, n - base);
+    const int valid = (int)min((int64_t)kTile, n - base);
 
-    KeyT key[kSortItems];
+    KeyT key[kItems];
     const uint32_t dmax = (1u << digit_bits) - 1u;  // pads' digit
     src.load(S, tile, base, valid, n, (KeyT)dmax << shift, key);
 #define GS_DIGIT(k) ((uint32_t)((k) >> shift) & dmax)
@@ -133,10 +152,10 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
     // Peers are found with one ballot per digit bit (pure ALU, pipelines across items);
     // each peer group's leader claims the group's slots with one shared atomic, kept in
     // item order by __syncwarp.
-    uint32_t rank[kSortItems];
+    uint32_t rank[kItems];
     const uint32_t lt_mask = (1u << lane) - 1u;
 #pragma unroll
-    for (int j = 0; j < kSortItems; ++j) {
+    for (int j = 0; j < kItems; ++j) {
         const uint32_t d = GS_DIGIT(key[j]);
         uint32_t peers = 0xffffffffu;
         if (digit_bits == kRadixBits) {
@@ -170,7 +189,7 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
         S.warp_hist[w][d] = count;
         count += c;
     }
-    const uint32_t pads = ((uint32_t)d == dmax) ? (uint32_t)(kTileItems - valid) : 0u;
+    const uint32_t pads = ((uint32_t)d == dmax) ? (uint32_t)(kTile - valid) : 0u;
     count -= pads;
 
     // Decoupled look-back over earlier tiles of this pass, kLookWindow predecessors per
@@ -239,19 +258,19 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
     // Scatter into shared memory in digit-sorted order: the keys, then the values, which are
     // loaded only now (each item's slot stays in rank[]).
 #pragma unroll
-    for (int j = 0; j < kSortItems; ++j) {
+    for (int j = 0; j < kItems; ++j) {
         const uint32_t dj = GS_DIGIT(key[j]);
         rank[j] += S.local_off[dj] + S.warp_hist[warp][dj];
         S.keys[rank[j]] = key[j];
     }
     {
-        uint32_t val[kSortItems];
+        uint32_t val[kItems];
         src.load_vals(S, base, valid, val);
         // a source that staged its values in S.vals: every thread has read its own before
         // any slot is overwritten
         if (Src::kValsInSmem) __syncthreads();
 #pragma unroll
-        for (int j = 0; j < kSortItems; ++j) S.vals[rank[j]] = val[j];
+        for (int j = 0; j < kItems; ++j) S.vals[rank[j]] = val[j];
     }
     __syncthreads();
 

@@ -55,7 +55,8 @@ __global__ void k_radix_hist_scan(uint32_t* __restrict__ hist, int npass) {
 
 size_t radix_workspace_bytes(int64_t n, int key_bits, int key_bytes) {
     const int npass = (key_bits + kRadixBits - 1) / kRadixBits;
-    const int64_t ntiles = (n + kTileItems - 1) / kTileItems + 1;
+    const int tile_items = sort_tile_items(key_bytes);
+    const int64_t ntiles = (n + tile_items - 1) / tile_items + 1;
     WorkspaceSizer s;
     s.take<unsigned int>(1);                            // error word (first: see gs_workspace_error)
     s.take<uint32_t>((size_t)npass * kRadix);          // histograms / offsets
@@ -74,7 +75,8 @@ gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64
                              void* workspace, size_t workspace_bytes, cudaStream_t st,
                              unsigned int** err_out, unsigned int* err_ext) {
     const int npass = radix_num_passes(key_bits);
-    const int64_t ntiles = (n_cap + kTileItems - 1) / kTileItems + 1;
+    constexpr int kTile = SortShape<KeyT>::kTile;
+    const int64_t ntiles = (n_cap + kTile - 1) / kTile + 1;
     Workspace ws(workspace, workspace_bytes);
     unsigned int* err = ws.take<unsigned int>(1);
     uint32_t* hist = ws.take<uint32_t>((size_t)npass * kRadix);
