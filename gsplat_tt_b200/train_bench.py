@@ -14,7 +14,6 @@ small ncu captures; the benchmark line then names the reduced workload).
 from __future__ import annotations
 
 import os
-import time
 
 import numpy as np
 import torch
@@ -225,22 +224,45 @@ def run(args, rank: int, world: int, local: int) -> dict:
 
     # e2e: the public API given the step's inputs (target images) in pinned host memory --
     # the library copies every view's target host -> device each step, on its own stream
-    # overlapped with the other views' work -- and the loss read back to the host.
+    # overlapped with the other views' work -- and every step's loss read back to the host.
+    # The loss of step i is copied to pinned memory at the end of step i and read on the
+    # host once step i + 1 has been enqueued (as a training loop that logs its losses does),
+    # so the GPU is not left idle while the host waits; the last step's loss is read inside
+    # the timed region too. The same loop with a blocking read after every step is reported
+    # beside it.
     pinned = [torch.from_numpy(t).pin_memory() for t in targets_host]
-    for _ in range(2):
-        tr.step(cams, pinned, next_cams=nxt)
-        loss_host = tr.losses.sum().item()
-    barrier(world)
-    torch.cuda.synchronize()
-    t0 = time.perf_counter()
-    e0.record()
-    for _ in range(args.steps):
-        tr.step(cams, pinned, next_cams=nxt)
-        loss_host = tr.losses.sum().item()
-    e1.record()
-    torch.cuda.synchronize()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
-    del loss_host, t0
+    loss_pin = torch.zeros(args.steps, dtype=torch.float32).pin_memory()
+    done = [torch.cuda.Event() for _ in range(args.steps)]
+    losses_read = []
+
+    def e2e_loop(blocking: bool) -> float:
+        for _ in range(2):
+            tr.step(cams, pinned, next_cams=nxt)
+            tr.losses.sum().item()
+        barrier(world)
+        torch.cuda.synchronize()
+        losses_read.clear()
+        e0.record()
+        for i in range(args.steps):
+            tr.step(cams, pinned, next_cams=nxt)
+            if blocking:
+                losses_read.append(tr.losses.sum().item())
+                continue
+            loss_pin[i:i + 1].copy_(tr.losses.sum().reshape(1), non_blocking=True)
+            done[i].record()
+            if i > 0:
+                done[i - 1].synchronize()
+                losses_read.append(float(loss_pin[i - 1]))
+        if not blocking:
+            done[args.steps - 1].synchronize()
+            losses_read.append(float(loss_pin[args.steps - 1]))
+        e1.record()
+        torch.cuda.synchronize()
+        assert len(losses_read) == args.steps and all(np.isfinite(losses_read))
+        return max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+
+    e2e_ms = e2e_loop(blocking=False)
+    e2e_blocking_ms = e2e_loop(blocking=True)
 
     # per-kernel device times (CUDA events on the launching stream), one more short loop;
     # with the timer on the library runs the views on one stream, so launches do not overlap
@@ -280,7 +302,9 @@ def run(args, rank: int, world: int, local: int) -> dict:
                    "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},
         "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
                 "h2d_bytes_per_step": int(sum(t.size * 4 for t in targets_host)),
-                "d2h_bytes_per_step": 4},
+                "d2h_bytes_per_step": 4,
+                "loss_read": "every step; step i's loss read on the host after step i + 1 is enqueued",
+                "value_blocking_read": total_px / (e2e_blocking_ms / 1e3) / 1e6},
         # the library's kernels launched in the timed region, summed over the ranks
         "gpu_launches": int(sum_over_ranks(float(launches), world)),
         "ms_per_step_by_rank": ms_by_rank,

@@ -111,3 +111,18 @@ def test_device_logf_reproduces_host_logf():
         yh = od.logf_array(x)
         bad += int((yd.cpu().numpy().view(np.uint32) != yh.view(np.uint32)).sum())
     assert bad == 0
+
+
+def test_launch_count_counts_the_sort_kernels(gd):
+    """gs_launch_count (the bench's gpu_launches) grows by the sort's kernels: the histogram
+    and its scan, then one pass per 8 key bits (here 40 bits: five passes)."""
+    from gsplat_tt_b200._lib import lib
+    rng = np.random.default_rng(3)
+    n = 10000
+    keys = rng.integers(0, 1 << 40, n, dtype=np.uint64)
+    vals = np.arange(n, dtype=np.uint32)
+    run(gd, keys, vals, 40)  # first call: module load and attributes
+    c0 = lib.gs_launch_count()
+    run(gd, keys, vals, 40)
+    launched = lib.gs_launch_count() - c0
+    assert launched >= 2 + 5, launched
