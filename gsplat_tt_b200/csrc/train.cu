@@ -341,6 +341,35 @@ __device__ __forceinline__ void warp_sum9(const float (&v)[9], int lane, float& 
     s1 = d;
 }
 
+// The backward's pair records as copied from global memory, before staging: projected
+// records p0 / p1 / p2, the forward's coefficient cache qc / qcols, and the Gaussian id.
+struct __align__(16) BRaw {  // 64 bytes
+    float4 p0, p1, qc;
+    float p2;
+    uint32_t qcols, gid, pad;
+};
+
+// Asynchronous global -> shared copies (cp.async): 16 bytes through L2 only, or 4 bytes.
+__device__ __forceinline__ void cp_async16_cg(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async4_ca(void* smem, const void* gmem) {
+    const unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+
+// 1: the backward copies the next batch's pair records into shared memory with cp.async
+// while it replays the current batch, and loads the Gaussian ids of the batch after that
+// into registers; 0: each batch's records are loaded synchronously between two barriers.
+#ifndef GS_BWD_PREFETCH
+#define GS_BWD_PREFETCH 0
+#endif
+// Minimum resident blocks per SM the backward's register budget is set for (0: none).
+#ifndef GS_BWD_MIN_BLOCKS
+#define GS_BWD_MIN_BLOCKS 0
+#endif
+
 struct __align__(16) BPair {  // 80 bytes: five 16-byte shared-memory loads
     RPair q;
     float mxl, myl, A, B, C;
@@ -355,13 +384,22 @@ struct __align__(16) BPair {  // 80 bytes: five 16-byte shared-memory loads
 // G u^2, G uv, G v^2, G u, G v with G = dL/dpower) are summed over the thread's PPT pixels
 // in registers, over the warp with shuffles, over the tile in shared memory, and added once
 // per pair into the view's per-Gaussian rows with float4 atomics.
-template <int TILE, int PPT>
-__global__ void __launch_bounds__(TILE * TILE / PPT)
+//
+// DET (deterministic mode): instead of the atomics, pair (g, tile) stores its sums in slot
+// doff[g] + j, j the tile's row-major index inside g's rectangle (every staged pair, zero
+// sums included; the caller zeroes the slots first), and k_det_reduce adds each Gaussian's
+// slots in j order. Only for 16x16 tiles: the two warps of such a block add onto zero in
+// shared memory, which gives the same bits in either order.
+template <int TILE, int PPT, bool DET>
+__global__ void __launch_bounds__(TILE * TILE / PPT, TILE == 16 ? GS_BWD_MIN_BLOCKS : 0)
 k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals, ProjView pv,
             TCfg cfg, int H, int W, const float* __restrict__ dimg,
             const float* __restrict__ final_T, const int32_t* __restrict__ n_contrib,
             const float4* __restrict__ qc, const uint32_t* __restrict__ qcols,
-            float* __restrict__ grad2d) {
+            float* __restrict__ grad2d, const int64_t* __restrict__ doff,
+            float4* __restrict__ dslots, int64_t slot_cap) {
+    static_assert(!DET || (TILE == 16 && TILE * TILE / PPT <= 64),
+                  "the deterministic mode needs at most two warps per tile");
     using LY = PixLayout<TILE, PPT>;
     constexpr int NB = kBwdBatch;
     constexpr int NP = PPT / 2;  // pixel pairs per thread (packed fp32x2 math)
@@ -419,9 +457,70 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
     if (my_max > 0) atomicMax(&s_max, my_max);
     __syncthreads();
     const int maxl = s_max;
+#if GS_BWD_PREFETCH
+    // Batches run back to front: batch b is [max(0, maxl - (b + 1) NB), maxl - b NB). Thread t
+    // stages slots t + k kThreads of a batch. While batch b is replayed, batch b + 1's
+    // records are in flight (cp.async into raw) and batch b + 2's ids in registers.
+    constexpr int kSPT = (NB + LY::kThreads - 1) / LY::kThreads;
+    __shared__ BRaw raw[NB];
+    uint32_t gnext[kSPT];
+    auto load_ids = [&](int hi_) {
+        const int lo_ = max(0, hi_ - NB);
+#pragma unroll
+        for (int k = 0; k < kSPT; ++k) {
+            const int s = threadIdx.x + k * LY::kThreads;
+            gnext[k] = (hi_ > 0 && s < hi_ - lo_) ? svals[rg.x + lo_ + s] : 0u;
+        }
+    };
+    auto issue = [&](int hi_) {
+        const int lo_ = max(0, hi_ - NB);
+#pragma unroll
+        for (int k = 0; k < kSPT; ++k) {
+            const int s = threadIdx.x + k * LY::kThreads;
+            if (hi_ > 0 && s < hi_ - lo_) {
+                const uint32_t g = gnext[k];
+                const int64_t pi = (int64_t)rg.x + lo_ + s;
+                raw[s].gid = g;
+                cp_async16_cg(&raw[s].p0, &pv.p0[g]);
+                cp_async16_cg(&raw[s].p1, &pv.p1[g]);
+                cp_async16_cg(&raw[s].qc, &qc[pi]);
+                cp_async4_ca(&raw[s].p2, &pv.p2[g]);
+                cp_async4_ca(&raw[s].qcols, &qcols[pi]);
+            }
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+    };
+    if (maxl > 0) {
+        load_ids(maxl);
+        issue(maxl);
+        load_ids(maxl - NB);
+    }
+#endif
     for (int hi = maxl; hi > 0; hi -= NB) {
         const int lo = max(0, hi - NB);
         const int nb = hi - lo;
+#if GS_BWD_PREFETCH
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        __syncthreads();  // every thread's copies of this batch landed; the last epilogue is done
+        for (int s = threadIdx.x; s < nb; s += LY::kThreads) {
+            const BRaw& r = raw[s];
+            const float4 p0 = r.p0, p1 = r.p1;
+            BPair bp;
+            bp.q = stage_pair_cached(p0, p1, r.p2, r.qc, r.qcols, ox, oy, bp.mxl, bp.myl);
+            bp.A = p0.z;
+            bp.B = p0.w;
+            bp.C = p1.x;
+            bp.gid = r.gid;
+            sp[s] = bp;
+#pragma unroll
+            for (int k = 0; k < 9; ++k) acc[k][s] = 0.0f;
+        }
+        __syncthreads();  // the batch is staged; raw may be refilled
+        if (lo > 0) {
+            issue(lo);
+            load_ids(lo - NB);
+        }
+#else
         __syncthreads();
         for (int s = threadIdx.x; s < nb; s += LY::kThreads) {
             const uint32_t g = svals[rg.x + lo + s];
@@ -438,6 +537,7 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             for (int k = 0; k < 9; ++k) acc[k][s] = 0.0f;
         }
         __syncthreads();
+#endif
         for (int j = nb - 1; j >= 0; --j) {
             const int idx = lo + j;
             float2 v[9];
@@ -506,8 +606,18 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             const float s0 = acc[0][s], s1 = acc[1][s], s2 = acc[2][s], s3 = acc[3][s];
             const float Suu = acc[4][s], Suv = acc[5][s], Svv = acc[6][s], Su = acc[7][s];
             const float Sv = acc[8][s];
-            if (s0 != 0.0f || s1 != 0.0f || s2 != 0.0f || s3 != 0.0f || Su != 0.0f || Sv != 0.0f ||
-                Suu != 0.0f || Suv != 0.0f || Svv != 0.0f) {
+            if constexpr (DET) {
+                const ushort4 r = pv.rect[bp.gid];
+                const int64_t slot = doff[bp.gid] + (int64_t)(ty - (int)r.z) * ((int)r.y - (int)r.x + 1) +
+                                     (tx - (int)r.x);
+                if (slot >= 0 && slot < slot_cap) {
+                    float4* d = dslots + 3 * slot;
+                    d[0] = make_float4(bp.A * Su + bp.B * Sv, bp.B * Su + bp.C * Sv, -0.5f * Suu, -Suv);
+                    d[1] = make_float4(-0.5f * Svv, s0, s1, s2);
+                    d[2] = make_float4(s3, 0.0f, 0.0f, 0.0f);
+                }
+            } else if (s0 != 0.0f || s1 != 0.0f || s2 != 0.0f || s3 != 0.0f || Su != 0.0f ||
+                       Sv != 0.0f || Suu != 0.0f || Suv != 0.0f || Svv != 0.0f) {
                 float4* gr = reinterpret_cast<float4*>(grad2d + (size_t)bp.gid * kGradStride);
                 atomicAdd(&gr[0], make_float4(bp.A * Su + bp.B * Sv, bp.B * Su + bp.C * Sv,
                                               -0.5f * Suu, -Suv));
@@ -516,6 +626,63 @@ k_train_bwd(const int2* __restrict__ ranges, const uint32_t* __restrict__ svals,
             }
         }
     }
+}
+
+// Tiles of an inclusive tile rectangle (x0, x1, y0, y1); x1 < x0 means none.
+__device__ __forceinline__ int64_t rect_tiles(ushort4 r) {
+    return (r.y >= r.x) ? (int64_t)(r.y - r.x + 1) * (int64_t)(r.w - r.z + 1) : 0;
+}
+
+// Deterministic mode: each Gaussian's first slot, the exclusive prefix of the tile counts
+// in Gaussian order (gsplat/blend_backward_ref.py:32-36 P[g]); blk_off holds the exclusive
+// offsets of the projection's 256-Gaussian blocks.
+__global__ void __launch_bounds__(kProjThreads)
+k_det_offsets(const ushort4* __restrict__ rect, int64_t n, const int64_t* __restrict__ blk_off,
+              int64_t* __restrict__ doff) {
+    __shared__ int64_t smem[33];
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t c = (i < n) ? rect_tiles(rect[i]) : 0;
+    int64_t total;
+    const int64_t ex = block_exclusive_scan<int64_t>(c, smem, &total);
+    if (i < n) doff[i] = blk_off[blockIdx.x] + ex;
+}
+
+// Zero the view's used slots: 3 float4 per pair, pairs = min(*pairs, cap).
+__global__ void k_det_zero(float4* __restrict__ slots, const int64_t* __restrict__ pairs,
+                           int64_t cap) {
+    const int64_t m = 3 * min(*pairs, cap);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < m;
+         i += (int64_t)gridDim.x * blockDim.x)
+        slots[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+}
+
+// Deterministic mode: each Gaussian's 2D-gradient row = its slots summed j = 0, 1, ... in
+// fp32 (gsplat/blend_backward_ref.py:239-244), stored over the row the projection zeroed.
+__global__ void k_det_reduce(const ushort4* __restrict__ rect, const int64_t* __restrict__ doff,
+                             const float4* __restrict__ slots, int64_t n, int64_t cap,
+                             float* __restrict__ grad2d) {
+    const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (g >= n) return;
+    const int64_t c = rect_tiles(rect[g]);
+    if (c == 0) return;
+    const int64_t o = doff[g];
+    if (o + c > cap) return;  // overflowed view: its tile lists are empty, nothing was written
+    float4 a[3];
+#pragma unroll
+    for (int k = 0; k < 3; ++k) a[k] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int64_t j = 0; j < c; ++j) {
+#pragma unroll
+        for (int k = 0; k < 3; ++k) {
+            const float4 s = slots[3 * (o + j) + k];
+            a[k].x = __fadd_rn(a[k].x, s.x);
+            a[k].y = __fadd_rn(a[k].y, s.y);
+            a[k].z = __fadd_rn(a[k].z, s.z);
+            a[k].w = __fadd_rn(a[k].w, s.w);
+        }
+    }
+    float4* gr = reinterpret_cast<float4*>(grad2d + (size_t)g * kGradStride);
+#pragma unroll
+    for (int k = 0; k < 3; ++k) gr[k] = a[k];
 }
 
 // ------------------------------------------------------------------ loss
@@ -1431,6 +1598,10 @@ struct ViewLane {
     float* dxx;
     float* dxy;
     float* target;     // staging copy of a view's target when the caller passes host memory
+    // deterministic mode only (null otherwise): slot offset of each Gaussian (exclusive
+    // prefix of the tile counts, Gaussian order) and the per-pair gradient slots, 3 float4
+    int64_t* doff;
+    float4* dslots;
 };
 
 struct TrainWs {
@@ -1449,7 +1620,7 @@ struct TrainWs {
 
 template <typename WS>
 static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int W, int tile,
-                         int64_t cap) {
+                         int64_t cap, bool det = false) {
     const int tiles = ((W + tile - 1) / tile) * ((H + tile - 1) / tile);
     const int tile_bits = bits_for(tiles > 1 ? tiles - 1 : 1);
     const int64_t nb = div_up(n, kProjThreads) + 1;
@@ -1501,6 +1672,13 @@ static void train_layout(WS& ws, TrainWs& L, int64_t n, int n_views, int H, int 
         V.target = ws.template take<float>(px * 3);
     }
     L.loss_acc = ws.template take<double>(2 * (size_t)n_views);
+    // The deterministic mode's slots come last, so the layout before them does not depend on
+    // the mode and a deterministic workspace serves every other call unchanged.
+    for (int l = 0; l < L.nlanes; ++l) {
+        ViewLane& V = L.lane[l];
+        V.doff = det ? ws.template take<int64_t>(n) : nullptr;
+        V.dslots = det ? ws.template take<float4>(3 * (size_t)cap) : nullptr;
+    }
 }
 
 struct SizerAdapter {
@@ -1554,6 +1732,15 @@ static gs_status check_cfg(const gs_train_config* cfg) {
     GS_ARG_CHECK(cfg != nullptr, "train: null config");
     GS_ARG_CHECK(cfg->sh_degree >= 0 && cfg->sh_degree <= 3, "train: sh_degree must be 0..3");
     GS_ARG_CHECK(cfg->tile_size == 16 || cfg->tile_size == 32, "train: tile_size must be 16 or 32");
+    GS_ARG_CHECK(cfg->deterministic == 0 || cfg->deterministic == 1,
+                 "train: deterministic must be 0 or 1");
+    if (cfg->deterministic && cfg->tile_size != 16) {
+        // a 32x32 tile's backward block has eight warps adding into the same shared-memory
+        // sums in whatever order they arrive; with 16x16 tiles two warps add onto zero, which
+        // is order-independent
+        set_error("train: deterministic mode needs tile_size 16");
+        return GS_ERR_UNSUPPORTED;
+    }
     return GS_OK;
 }
 
@@ -1582,6 +1769,30 @@ extern "C" size_t gs_train_workspace_size(int64_t n, int32_t sh_degree, int32_t 
     TrainWs L;
     train_layout(s, L, n, n_views, height, width, tile_size, pair_capacity);
     return s.s.bytes();
+}
+
+extern "C" size_t gs_train_deterministic_workspace_size(int64_t n, int32_t sh_degree,
+                                                        int32_t n_views, int32_t height,
+                                                        int32_t width, int32_t tile_size,
+                                                        int64_t pair_capacity) {
+    (void)sh_degree;
+    if (n < 1) n = 1;
+    if (n_views < 1) n_views = 1;
+    if (tile_size < 1) tile_size = 16;
+    if (pair_capacity < 1) pair_capacity = 1;
+    SizerAdapter s;
+    TrainWs L;
+    train_layout(s, L, n, n_views, height, width, tile_size, pair_capacity, true);
+    return s.s.bytes();
+}
+
+// Size of the workspace a call with this config lays out.
+static size_t train_ws_bytes(const gs_train_config& cfg, int64_t n, int n_views, int H, int W,
+                             int64_t cap) {
+    return cfg.deterministic
+               ? gs_train_deterministic_workspace_size(n, cfg.sh_degree, n_views, H, W,
+                                                       cfg.tile_size, cap)
+               : gs_train_workspace_size(n, cfg.sh_degree, n_views, H, W, cfg.tile_size, cap);
 }
 
 // Every view's projection in one pass over the parameters (cameras already in L.cams),
@@ -1772,16 +1983,39 @@ static gs_status launch_loss(const float* img, const float* target, int vh, int 
 
 // Backward rasteriser of one view: 2D-gradient rows g2 from dimg and the lane's final T /
 // counts of the same view's forward.
+// With the workspace's deterministic slots (V.doff non-null: cfg.deterministic), the
+// per-pair sums go through the slots instead of atomics; blk_off = the view's scanned
+// projection block offsets, pairs = its pair total (device), n Gaussians, cap the capacity.
 static gs_status launch_raster_bwd(const TCfg& c, const ViewLane& V, const ProjView& pvv, int vh,
-                                   int vw, const float* dimg, float* g2, cudaStream_t st) {
+                                   int vw, const float* dimg, float* g2, const int64_t* blk_off,
+                                   const int64_t* pairs, int64_t n, int64_t cap, cudaStream_t st) {
     KernelTimer kt("raster_bwd", st);
     const unsigned int tiles = (unsigned int)(c.tiles_x * c.tiles_y);
+    if (V.doff != nullptr) {
+        if (c.tile != 16) {
+            set_error("train: deterministic mode needs tile_size 16");
+            return GS_ERR_UNSUPPORTED;
+        }
+        k_det_offsets<<<div_up(n, kProjThreads), kProjThreads, 0, st>>>(pvv.rect, n, blk_off, V.doff);
+        GS_CHECK_LAUNCH();
+        k_det_zero<<<kNumSMs * 4, 256, 0, st>>>(V.dslots, pairs, cap);
+        GS_CHECK_LAUNCH();
+        k_train_bwd<16, kBwdPPT, true><<<tiles, 256 / kBwdPPT, 0, st>>>(
+            V.ranges, V.svals, pvv, c, vh, vw, dimg, V.final_T, V.ncon, V.qc, V.qcols, g2, V.doff,
+            V.dslots, cap);
+        GS_CHECK_LAUNCH();
+        k_det_reduce<<<div_up(n, 256), 256, 0, st>>>(pvv.rect, V.doff, V.dslots, n, cap, g2);
+        GS_CHECK_LAUNCH();
+        return GS_OK;
+    }
     if (c.tile == 16)
-        k_train_bwd<16, kBwdPPT><<<tiles, 256 / kBwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
-                                                                        V.final_T, V.ncon, V.qc, V.qcols, g2);
+        k_train_bwd<16, kBwdPPT, false><<<tiles, 256 / kBwdPPT, 0, st>>>(
+            V.ranges, V.svals, pvv, c, vh, vw, dimg, V.final_T, V.ncon, V.qc, V.qcols, g2, nullptr,
+            nullptr, 0);
     else
-        k_train_bwd<32, kBwdPPT><<<tiles, 1024 / kBwdPPT, 0, st>>>(V.ranges, V.svals, pvv, c, vh, vw, dimg,
-                                                                         V.final_T, V.ncon, V.qc, V.qcols, g2);
+        k_train_bwd<32, kBwdPPT, false><<<tiles, 1024 / kBwdPPT, 0, st>>>(
+            V.ranges, V.svals, pvv, c, vh, vw, dimg, V.final_T, V.ncon, V.qc, V.qcols, g2, nullptr,
+            nullptr, 0);
     GS_CHECK_LAUNCH();
     return GS_OK;
 }
@@ -1820,7 +2054,8 @@ static gs_status run_view(int64_t n, int v, const gs_camera& cam, const gs_train
                     L.loss_acc + 2 * v, view_losses + v, st);
     if (s != GS_OK) return s;
     if (host_target && LS != nullptr) GS_CUDA_CHECK(cudaEventRecord(LS->consumed[lane], st));
-    s = launch_raster_bwd(c, V, pvv, vh, vw, V.dimg, L.grad2d + (size_t)v * n * kGradStride, st);
+    s = launch_raster_bwd(c, V, pvv, vh, vw, V.dimg, L.grad2d + (size_t)v * n * kGradStride,
+                          L.blk + (size_t)v * L.blk_stride, L.pairs + v, n, cap, st);
     if (s != GS_OK) return s;
     if (grad2d_out) {
         k_export_grad2d<<<div_up(n, 256), 256, 0, st>>>(L.grad2d, L.touch, n, v,
@@ -1964,10 +2199,9 @@ static gs_status stage_layout(const char* who, int64_t n, const gs_camera* cam,
     GS_ARG_CHECK(image_fits(cam->height, cam->width, cfg->tile_size),
                  "%s: image must be 1..%d tile rows and 1..65535 tile columns", who, kMaxTileRows);
     Workspace ws(workspace, workspace_bytes);
-    train_layout(ws, L, n, 1, cam->height, cam->width, cfg->tile_size, cap);
+    train_layout(ws, L, n, 1, cam->height, cam->width, cfg->tile_size, cap, cfg->deterministic != 0);
     GS_ARG_CHECK(ws.ok(), "%s: workspace too small (%zu < %zu)", who, workspace_bytes,
-                 gs_train_workspace_size(n, cfg->sh_degree, 1, cam->height, cam->width,
-                                         cfg->tile_size, cap));
+                 train_ws_bytes(*cfg, n, 1, cam->height, cam->width, cap));
     return GS_OK;
 }
 
@@ -2067,7 +2301,8 @@ extern "C" gs_status gs_render_bwd(int64_t n, const gs_camera* cam, const gs_tra
     if (s != GS_OK) return s;
     const int H = cam->height, W = cam->width;
     const TCfg c = make_tcfg(*cfg, H, W);
-    s = launch_raster_bwd(c, L.lane[0], L.pv.view(0, n), H, W, dL_dimage, L.grad2d, st);
+    s = launch_raster_bwd(c, L.lane[0], L.pv.view(0, n), H, W, dL_dimage, L.grad2d, L.blk, L.pairs,
+                          n, pair_capacity, st);
     if (s != GS_OK) return s;
     if (grad2d) {
         k_export_grad2d<<<div_up(n, 256), 256, 0, st>>>(L.grad2d, L.touch, n, 0, grad2d);
@@ -2370,10 +2605,9 @@ extern "C" gs_status gs_train_step(const gs_gaussians* params, const gs_gaussian
     }
     Workspace ws(workspace, workspace_bytes);
     TrainWs L;
-    train_layout(ws, L, n, n_views, H, W, cfg->tile_size, pair_capacity);
+    train_layout(ws, L, n, n_views, H, W, cfg->tile_size, pair_capacity, cfg->deterministic != 0);
     GS_ARG_CHECK(ws.ok(), "gs_train_step: workspace too small (%zu < %zu)", workspace_bytes,
-                 gs_train_workspace_size(n, cfg->sh_degree, n_views, H, W, cfg->tile_size,
-                                         pair_capacity));
+                 train_ws_bytes(*cfg, n, n_views, H, W, pair_capacity));
     const GConst P = gconst(params);
     GS_CUDA_CHECK(cudaMemsetAsync(L.err, 0, sizeof(unsigned int), st));
     GS_CUDA_CHECK(cudaMemsetAsync(L.loss_acc, 0, 2 * n_views * sizeof(double), st));

@@ -51,7 +51,7 @@ class GsTrainConfig(ctypes.Structure):
                 ("lr_quats", ctypes.c_float), ("lr_opacity", ctypes.c_float),
                 ("lr_sh_dc", ctypes.c_float), ("lr_sh_rest", ctypes.c_float),
                 ("beta1", ctypes.c_float), ("beta2", ctypes.c_float), ("eps", ctypes.c_float),
-                ("bf16_moments", ctypes.c_int32)]
+                ("bf16_moments", ctypes.c_int32), ("deterministic", ctypes.c_int32)]
 
 
 _G = ctypes.POINTER(GsGaussians)
@@ -63,6 +63,8 @@ lib.gs_train_step.argtypes = [_G, _G, _G, _G, _vp, _i64, _i64, _C, ctypes.POINTE
                               _CFG, _i32, _vp, _vp, _vp, _vp, _i64, _vp, _sz, _vp]
 lib.gs_train_workspace_size.restype = _sz
 lib.gs_train_workspace_size.argtypes = [_i64, _i32, _i32, _i32, _i32, _i32, _i64]
+lib.gs_train_deterministic_workspace_size.restype = _sz
+lib.gs_train_deterministic_workspace_size.argtypes = [_i64, _i32, _i32, _i32, _i32, _i32, _i64]
 lib.gs_train_count_pairs.restype = ctypes.c_int
 lib.gs_train_count_pairs.argtypes = [_G, _i64, _C, _i32, _CFG, ctypes.POINTER(_i64), _vp, _sz, _vp]
 lib.gs_sparse_adam.restype = ctypes.c_int
@@ -106,6 +108,14 @@ class TrainConfig:
     betas: tuple = (0.9, 0.999)
     eps: float = 1e-15
     bf16_moments: bool = False
+    # fixed-order gradient sums in the backward rasteriser (same bits on every run; tile 16)
+    deterministic: bool = False
+
+    def workspace_size(self, n: int, n_views: int, height: int, width: int, cap: int) -> int:
+        """Bytes of the training workspace a call with this config needs."""
+        fn = (lib.gs_train_deterministic_workspace_size if self.deterministic
+              else lib.gs_train_workspace_size)
+        return int(fn(n, self.sh_degree, n_views, height, width, self.tile_size, cap))
 
     def c_struct(self) -> GsTrainConfig:
         c = GsTrainConfig()
@@ -120,6 +130,7 @@ class TrainConfig:
         c.lr_sh_dc, c.lr_sh_rest = self.lr["sh_dc"], self.lr["sh_rest"]
         c.beta1, c.beta2, c.eps = self.betas[0], self.betas[1], self.eps
         c.bf16_moments = int(bool(self.bf16_moments))
+        c.deterministic = int(bool(self.deterministic))
         return c
 
 
@@ -285,8 +296,7 @@ class Trainer:
     def _alloc(self, capacity: int) -> None:
         self._projected = None
         self.capacity = capacity
-        nb = lib.gs_train_workspace_size(self.n, self.cfg.sh_degree, self.n_views, self.H, self.W,
-                                         self.cfg.tile_size, capacity)
+        nb = self.cfg.workspace_size(self.n, self.n_views, self.H, self.W, capacity)
         self.ws = None
         torch.cuda.empty_cache()
         self.ws = torch.empty(nb, dtype=torch.uint8, device=self.device)
@@ -541,8 +551,7 @@ class StagedView:
         self.tr = trainer
         self.H, self.W = int(height), int(width)
         cfg = trainer.cfg
-        self.ws = torch.empty(lib.gs_train_workspace_size(trainer.n, cfg.sh_degree, 1, self.H, self.W,
-                                                          cfg.tile_size, trainer.capacity),
+        self.ws = torch.empty(cfg.workspace_size(trainer.n, 1, self.H, self.W, trainer.capacity),
                               dtype=torch.uint8, device=trainer.device)
         self.lws = torch.empty(lib.gs_loss_workspace_size(self.H, self.W), dtype=torch.uint8,
                                device=trainer.device)

@@ -39,8 +39,11 @@ def view_targets(cams, first_index: int) -> list[np.ndarray]:
 
 
 def train_cfg() -> TrainConfig:
+    # GS_BENCH_DETERMINISTIC=1 times the fixed-order (slot) gradient sums instead of the
+    # atomics; the bench line then says so in its config
+    det = os.environ.get("GS_BENCH_DETERMINISTIC", "0") == "1"
     return TrainConfig(sh_degree=3, tile_size=16, use_ssim=True, lambda_dssim=0.2,
-                       lr=dict(LR_BASELINE), betas=(0.9, 0.999), eps=1e-15)
+                       lr=dict(LR_BASELINE), betas=(0.9, 0.999), eps=1e-15, deterministic=det)
 
 
 # Measured NVLink rate used as the multicast update's denominator: a peer copy of 770 GB/s
@@ -299,6 +302,8 @@ def run(args, rank: int, world: int, local: int) -> dict:
                        "; each step projects the next step's views after its update"
                        + (", row chunk by row chunk as the chunks land" if tr.multicast else "")
                        if nxt is not None else ""),
+                   "gradient_sums": "fixed-order slots (deterministic mode)" if cfg.deterministic
+                   else "float atomics",
                    "l2": "inputs larger than L2 (params 1.4 GB, pairs per view > 100 MB)"},
         "e2e": {"value": total_px / (e2e_ms / 1e3) / 1e6, "unit": "Mpix/s",
                 "h2d_bytes_per_step": int(sum(t.size * 4 for t in targets_host)),

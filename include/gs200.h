@@ -241,6 +241,16 @@ typedef struct gs_train_config {
     int32_t bf16_moments;    /* moments stored as bfloat16 (round to nearest even): the
                                 exp_avg / exp_avg_sq arrays then hold 2-byte values and their
                                 gs_gaussians pointers are read as 16-bit arrays */
+    int32_t deterministic;   /* 1: the backward rasteriser sums each Gaussian's per-tile
+                                gradient terms in a fixed order instead of with float
+                                atomics, so the same inputs give the same bits on every run
+                                (the reference's slot layout, gsplat/blend_backward_ref.py:32-36,
+                                239-244: pair (g, tile) writes slot P[g] + j, j the tile's
+                                row-major index in g's rectangle, P the exclusive prefix of the
+                                Gaussians' tile counts; the slots are then summed j ascending).
+                                A debugging mode: slower, tile_size 16 only (GS_ERR_UNSUPPORTED
+                                otherwise), and the workspace of
+                                gs_train_deterministic_workspace_size. 0: atomics (default). */
 } gs_train_config;
 
 /* One training step over n_views views (<= 64) of one rank.
@@ -304,6 +314,13 @@ gs_status gs_train_project_rows(const gs_gaussians* params, float* vis_counts, i
                                 void* stream);
 size_t gs_train_workspace_size(int64_t n, int32_t sh_degree, int32_t n_views, int32_t height,
                                int32_t width, int32_t tile_size, int64_t pair_capacity);
+/* The workspace of a step, gs_render_fwd or gs_render_bwd whose config sets
+ * deterministic = 1: gs_train_workspace_size plus, per lane, pair_capacity 48-byte gradient
+ * slots and n slot offsets (the layout before them is the same, so every other call taking
+ * the workspace accepts it too). gsplat/blend_backward_ref.py:239-244 slot array. */
+size_t gs_train_deterministic_workspace_size(int64_t n, int32_t sh_degree, int32_t n_views,
+                                             int32_t height, int32_t width, int32_t tile_size,
+                                             int64_t pair_capacity);
 
 /* Pair count of each view (projection + tile rectangles only), synchronising, to size
  * pair_capacity. pairs_host: n_views int64 in host memory. */

@@ -6,7 +6,7 @@ both of its paths -- the fused one (has_render_fused / render_fused) and the sta
 signatures and every render knob the Pipeline pushes landing on an attribute the backend
 has. The check runs in a child process with the reference project on sys.path; it is
 skipped where the reference is absent (the reference root is $GSPLAT_TT_REFERENCE, else the
-location the build driver mounts it at)."""
+`reference_path` recorded in BASELINE.json)."""
 import os
 import subprocess
 import sys

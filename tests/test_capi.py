@@ -136,3 +136,44 @@ def test_stage_entry_points_argument_errors_need_no_device():
     assert lib.gs_loss(p, p, 64, 64, ctypes.byref(cfg), p, p, ws, 16, None) == GS_ERR_ARG
     assert b"workspace too small" in lib.gs_last_error()
     assert lib.gs_loss(p, None, 64, 64, ctypes.byref(cfg), p, p, ws, 1 << 30, None) == GS_ERR_ARG
+
+
+def test_deterministic_mode_checks_and_workspace_need_no_device():
+    """deterministic = 1 asks for 16x16 tiles (GS_ERR_UNSUPPORTED with 32) and a workspace
+    with one 48-byte slot per pair and one 8-byte offset per Gaussian in every lane; the
+    workspace before the slots is the default layout, and a default-sized workspace is
+    rejected on the host before any device call."""
+    from gsplat_tt_b200._lib import GS_ERR_ARG, GS_ERR_UNSUPPORTED
+    from gsplat_tt_b200.train import GsCamera, GsGaussians, TrainConfig, camera_struct, lib
+    import numpy as np
+    n, cap, H, W = 1000, 50000, 64, 64
+    for views, lanes in ((1, 1), (3, 3), (9, 4)):
+        base = lib.gs_train_workspace_size(n, 3, views, H, W, 16, cap)
+        det = lib.gs_train_deterministic_workspace_size(n, 3, views, H, W, 16, cap)
+        extra = det - base
+        assert lanes * (cap * 48 + n * 8) <= extra <= lanes * (cap * 48 + n * 8 + 2 * 256)
+        assert TrainConfig(deterministic=True).workspace_size(n, views, H, W, cap) == det
+        assert TrainConfig().workspace_size(n, views, H, W, cap) == base
+    g = GsGaussians(16, 16, 16, 16, 16)  # fake aligned addresses: never dereferenced
+    cams = (GsCamera * 1)(camera_struct(np.eye(4), np.eye(3), H, W))
+    tg = (ctypes.c_void_p * 1)(16)
+    ws = ctypes.c_void_p(256)
+
+    def step(cfg, ws_bytes):
+        return lib.gs_train_step(ctypes.byref(g), ctypes.byref(g), ctypes.byref(g),
+                                 ctypes.byref(g), ctypes.c_void_p(16), n, 0, cams, tg, 1,
+                                 ctypes.byref(cfg), 1, ctypes.c_void_p(16), None, None, None, cap,
+                                 ws, ws_bytes, None)
+    assert step(TrainConfig(tile_size=32, deterministic=True).c_struct(), 1 << 40) == GS_ERR_UNSUPPORTED
+    assert b"tile_size 16" in lib.gs_last_error()
+    bad = TrainConfig().c_struct()
+    bad.deterministic = 2
+    assert step(bad, 1 << 40) == GS_ERR_ARG
+    assert b"deterministic" in lib.gs_last_error()
+    base = lib.gs_train_workspace_size(n, 3, 1, H, W, 16, cap)
+    assert step(TrainConfig(deterministic=True).c_struct(), base) == GS_ERR_ARG
+    assert b"workspace too small" in lib.gs_last_error()
+    cam = camera_struct(np.eye(4), np.eye(3), H, W)
+    assert lib.gs_render_bwd(n, ctypes.byref(cam), ctypes.byref(TrainConfig(deterministic=True).c_struct()),
+                             ctypes.c_void_p(16), None, cap, ws, base, None) == GS_ERR_ARG
+    assert b"workspace too small" in lib.gs_last_error()
