@@ -68,8 +68,10 @@ def cpu_sort_baseline(keys, vals, budget_s: float = 15.0) -> dict:
         el = time.perf_counter() - t0
         if el > budget_s or iters >= 20:
             break
-    return {"value": n * iters / el, "unit": "pairs/s", "cores": cores, "kind": kind,
-            "sample": f"{iters} full C2 sorts of {n} pairs", **info}
+    v = n * iters / el
+    # per core as well: the host's core count differs between boxes
+    return {"value": v, "unit": "pairs/s", "cores": cores, "value_per_core": v / cores,
+            "kind": kind, "sample": f"{iters} full C2 sorts of {n} pairs", **info}
 
 
 def _train_sample(name: str, views: int):
@@ -111,7 +113,8 @@ def train_cpu_baseline(name: str, budget_s: float = 20.0, max_steps: int = 3) ->
             if el > budget_s or iters >= max_steps:
                 break
     s = SAMPLE_SCALE
-    return {"value": workers * H * W * iters / el / 1e6, "unit": "Mpix/s", "cores": workers,
+    v = workers * H * W * iters / el / 1e6
+    return {"value": v, "unit": "Mpix/s", "cores": workers, "value_per_core": v / workers,
             "kind": "port",
             "sample": f"{iters} oracle steps of {workers} views {W}x{H} (one per worker process) "
                       f"with {n} Gaussians ({name.upper()} at 1/{s * s} of the pixels and "
