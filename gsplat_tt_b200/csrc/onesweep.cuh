@@ -122,12 +122,16 @@ constexpr int sort_min_blocks() {
     return sizeof(KeyT) == 8 ? GS_SORT_BLOCKS_U64 : (Src::kValsInSmem ? 4 : GS_SORT_BLOCKS_U32);
 }
 
-template <typename KeyT, typename Src>
+// The pass writes keys as KeyOutT, shifted right by out_shift: a 64-bit sort whose caller
+// wants only the values narrows its keys to 32 bits once the bits below
+// key_bits - 32 are sorted, so the remaining passes move 4-byte keys.
+template <typename KeyT, typename Src, typename KeyOutT = KeyT>
 __global__ void __launch_bounds__(kSortThreads, (sort_min_blocks<KeyT, Src>()))
-k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
+k_onesweep_pass(Src src, KeyOutT* __restrict__ keys_out, uint32_t* __restrict__ vals_out,
                 const int64_t* __restrict__ n_dev, int64_t n_host, int shift, int digit_bits,
                 const uint32_t* __restrict__ digit_offsets, uint32_t* __restrict__ lookback,
-                uint32_t* __restrict__ tile_counter, unsigned int* __restrict__ err) {
+                uint32_t* __restrict__ tile_counter, unsigned int* __restrict__ err,
+                int out_shift) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     SortSmem<KeyT>& S = *reinterpret_cast<SortSmem<KeyT>*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -280,7 +284,7 @@ k_onesweep_pass(Src src, KeyT* __restrict__ keys_out, uint32_t* __restrict__ val
         const KeyT k = S.keys[i];
         const uint32_t dd = GS_DIGIT(k);
         const uint32_t out = S.gbase[dd] + (uint32_t)i;
-        if (keys_out) keys_out[out] = k;
+        if (keys_out) keys_out[out] = (KeyOutT)(k >> out_shift);
         vals_out[out] = S.vals[i];
     }
 #undef GS_DIGIT

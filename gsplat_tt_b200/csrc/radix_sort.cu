@@ -114,18 +114,59 @@ gs_status radix_sort_pairs_t(const KeyT* keys, const uint32_t* vals, const int64
     const KeyT* kin = keys;
     const uint32_t* vin = vals;
     const unsigned int grid = (unsigned int)(ntiles - 1 > 0 ? ntiles - 1 : 1);
-    for (int p = 0; p < npass; ++p) {
+    // Only the values wanted and more than 32 key bits: the first `wide` passes sort the
+    // 64-bit keys, the last of them writes each key's bits [8 wide, 8 wide + 32) -- every
+    // bit a later pass reads -- as a 32-bit key, and the remaining passes move 4-byte keys.
+    // Same digits, same stable passes: the same order as sorting the 64-bit keys throughout.
+    const int wide = (sizeof(KeyT) == 8 && keys_out == nullptr && key_bits > 32)
+                         ? (key_bits - 32 + kRadixBits - 1) / kRadixBits : npass;
+    if (wide < npass) {
+        GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<KeyT, GlobalSource<KeyT>, uint32_t>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+        GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<KeyT, GlobalSource<KeyT>, uint32_t>,
+                                           cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+    }
+    for (int p = 0; p < wide; ++p) {
         const bool last = (p == npass - 1);
         KeyT* kout = last ? keys_out : ((p & 1) ? kb : ka);
         uint32_t* vout = last ? vals_out : ((p & 1) ? vb : va);
         KernelTimer kt(sizeof(KeyT) == 8 ? "radix_pass" : "radix_pass32", st);
-        k_onesweep_pass<KeyT><<<grid, kSortThreads, smem, st>>>(
-            GlobalSource<KeyT>{kin, vin}, kout, vout, n_dev, n_cap, p * kRadixBits,
-            std::min(kRadixBits, key_bits - p * kRadixBits), hist + p * kRadix,
-            look + (size_t)p * ntiles * kRadix, counters + p, err);
+        if (p == wide - 1 && wide < npass) {
+            k_onesweep_pass<KeyT, GlobalSource<KeyT>, uint32_t><<<grid, kSortThreads, smem, st>>>(
+                GlobalSource<KeyT>{kin, vin}, (uint32_t*)kout, vout, n_dev, n_cap, p * kRadixBits,
+                kRadixBits, hist + p * kRadix, look + (size_t)p * ntiles * kRadix, counters + p,
+                err, wide * kRadixBits);
+        } else {
+            k_onesweep_pass<KeyT><<<grid, kSortThreads, smem, st>>>(
+                GlobalSource<KeyT>{kin, vin}, kout, vout, n_dev, n_cap, p * kRadixBits,
+                std::min(kRadixBits, key_bits - p * kRadixBits), hist + p * kRadix,
+                look + (size_t)p * ntiles * kRadix, counters + p, err, 0);
+        }
         GS_CHECK_LAUNCH();
         kin = kout;
         vin = vout;
+    }
+    if (wide < npass) {
+        const size_t smem32 = sizeof(SortSmem<uint32_t>);
+        GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, GlobalSource<uint32_t>>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem32));
+        GS_CUDA_CHECK(cudaFuncSetAttribute(k_onesweep_pass<uint32_t, GlobalSource<uint32_t>>,
+                                           cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        const unsigned int grid32 = (unsigned int)std::max<int64_t>(1, div_up(n_cap, kTileItems));
+        const uint32_t* kin32 = (const uint32_t*)kin;
+        for (int p = wide; p < npass; ++p) {
+            const bool last = (p == npass - 1);
+            uint32_t* kout = last ? nullptr : (uint32_t*)((p & 1) ? kb : ka);
+            uint32_t* vout = last ? vals_out : ((p & 1) ? vb : va);
+            KernelTimer kt("radix_pass_n32", st);
+            k_onesweep_pass<uint32_t><<<grid32, kSortThreads, smem32, st>>>(
+                GlobalSource<uint32_t>{kin32, vin}, kout, vout, n_dev, n_cap,
+                (p - wide) * kRadixBits, std::min(kRadixBits, key_bits - p * kRadixBits),
+                hist + p * kRadix, look + (size_t)p * ntiles * kRadix, counters + p, err, 0);
+            GS_CHECK_LAUNCH();
+            kin32 = kout;
+            vin = vout;
+        }
     }
     return GS_OK;
 }
@@ -164,7 +205,7 @@ static gs_status launch_rect_pass(const RectPairArgs& a, uint32_t* keys_out, uin
     RectPairSource<SX, SY> src;
     static_cast<RectPairArgs&>(src) = a;
     k_onesweep_pass<uint32_t, RectPairSource<SX, SY>><<<grid, kSortThreads, smem, st>>>(
-        src, keys_out, vals_out, n_dev, n_cap, 0, digit_bits, digit_offsets, look, counter, err);
+        src, keys_out, vals_out, n_dev, n_cap, 0, digit_bits, digit_offsets, look, counter, err, 0);
     GS_CHECK_LAUNCH();
     return GS_OK;
 }
@@ -225,7 +266,7 @@ gs_status radix_sort_rect_pairs(const RectPairArgs& src, const int64_t* n_dev, i
         k_onesweep_pass<uint32_t, GlobalSource<uint32_t>><<<grid, kSortThreads, smem, st>>>(
             GlobalSource<uint32_t>{kin, vin}, kout, vout, n_dev, n_cap, p * kRadixBits,
             std::min(kRadixBits, key_bits - p * kRadixBits), digit_offsets + p * kRadix,
-            look + (size_t)p * ntiles * kRadix, counters + p, err);
+            look + (size_t)p * ntiles * kRadix, counters + p, err, 0);
         GS_CHECK_LAUNCH();
         kin = kout;
         vin = vout;

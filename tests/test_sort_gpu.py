@@ -70,6 +70,44 @@ def test_bits_above_key_bits_are_ignored(gd, bits):
     np.testing.assert_array_equal(kg, keys[order])
 
 
+def run_values(gd, keys, vals, key_bits):
+    import torch
+    v = gd.sort_pairs(torch.from_numpy(keys.view(np.int64)), torch.from_numpy(vals.view(np.int32)),
+                      key_bits)
+    return v.cpu().numpy().view(np.uint32)
+
+
+@pytest.mark.parametrize("bits", [33, 40, 45, 48, 57, 64])
+def test_values_only_sort_with_narrowed_keys(gd, bits):
+    """Without keys_out, a sort of more than 32 key bits narrows its keys to 32 bits once
+    the bits below key_bits - 32 are sorted (the later passes move 4-byte keys); the values
+    must come out in the full-width stable order. Keys carry set bits above key_bits and
+    heavy duplicates; values are a permutation."""
+    rng = np.random.default_rng(200 + bits)
+    n = 300_000
+    keys = rng.integers(0, 1 << 63, n, dtype=np.uint64)
+    keys |= rng.integers(0, 2, n, dtype=np.uint64) << np.uint64(63)
+    keys[::3] = keys[0]
+    vals = rng.permutation(n).astype(np.uint32)
+    low = keys if bits == 64 else keys & np.uint64((1 << bits) - 1)
+    np.testing.assert_array_equal(run_values(gd, keys, vals, bits),
+                                  vals[np.argsort(low, kind="stable")])
+
+
+@pytest.mark.parametrize("n", [1, 4095, 4097, 65539])
+def test_values_only_zipf_sizes_vs_oracle(gd, n):
+    keys, vals = scenes.c2_pairs(n=n, seed=n)
+    _, vo = od.sort_pairs(keys, vals)
+    np.testing.assert_array_equal(run_values(gd, keys, vals, 45), vo)
+
+
+def test_c2_values_only_matches_reference_golden(gd):
+    """The benchmark's call: C2 with values only (narrowed keys after two passes)."""
+    G = np.load(os.path.join(GOLDEN, "sort.npz"))
+    keys, vals = scenes.c2_pairs()
+    assert sha(run_values(gd, keys, vals, 45)) == str(G["sha_sorted_values"])
+
+
 def test_c2_full_matches_reference_golden(gd):
     G = np.load(os.path.join(GOLDEN, "sort.npz"))
     keys, vals = scenes.c2_pairs()
