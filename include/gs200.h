@@ -160,7 +160,10 @@ size_t gs_sort_and_bin_workspace_size(int64_t p, int32_t tiles_x, int32_t tiles_
 /* Stable ascending LSD radix sort of (uint64 key, uint32 value) pairs over the low
  * `key_bits` bits of the key (the higher bits must be zero); the order sort_and_bin
  * produces for key = tile << 32 | depth bits (src/gsplat_cpu/sort.cpp:24-27, the
- * reference's sort microbenchmark input). keys_out may be NULL. */
+ * reference's sort microbenchmark input). keys_out may be NULL: with more than 32 key
+ * bits the sort then narrows its keys to 32 bits once only bits below bit 8 w + 32 are
+ * left to sort (w = ceil((key_bits - 32) / 8) passes on 64-bit keys), so the later passes
+ * move 4-byte keys; the values come out in the same order. */
 gs_status gs_sort_pairs(const uint64_t* keys, const uint32_t* values, int64_t n,
                         int32_t key_bits, uint64_t* keys_out, uint32_t* values_out,
                         void* workspace, size_t workspace_bytes, void* stream);

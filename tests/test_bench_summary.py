@@ -69,3 +69,18 @@ def test_chunked_and_owner_sharded_launches_are_charged_their_own_rows():
     per_kernel, _, _ = tb.summarize_kernels({"sparse_adam": (1.0, 1)}, 1, n, views, 1.0, 1,
                                             PEAKS, adam_rows=n // world, world=world)
     assert per_kernel["sparse_adam"]["algorithmic_bytes"] == pytest.approx(n // world * 59 * 28)
+
+
+def test_sort_byte_model_counts_the_narrowed_passes():
+    """The sort line's own-bytes model: six passes for 45 key bits, the first on 64-bit
+    keys, the second writing keys narrowed to 32 bits, three on 32-bit keys, the last
+    writing values only; up to 32 key bits every pass moves 64-bit keys."""
+    import bench
+    assert bench.sort_pass_bytes(45) == [24, 20, 16, 16, 16, 12]
+    assert bench.sort_pass_bytes(64) == [24, 24, 24, 20, 16, 16, 16, 12]
+    assert bench.sort_pass_bytes(33) == [20, 16, 16, 16, 12]
+    assert bench.sort_pass_bytes(32) == [24, 24, 24, 16]
+    per_launch, per_sort = bench.sort_algorithmic_bytes(1 << 24, 45)
+    assert per_sort == (104 + 8) * (1 << 24)
+    assert per_launch == 104 * (1 << 24) / 6
+    assert bench.SORT_PASS_BYTES_PER_PAIR * 6 + 8 == 152
